@@ -1,0 +1,85 @@
+// Shared helpers for the sm_100a kernels of minispeed_b200.
+//
+// The .cu translation units include only CUDA headers and this file; the
+// PyTorch binding layer (bindings.cpp) passes raw device pointers, sizes and
+// the current stream.  Keeping ATen out of the .cu files keeps each nvcc
+// invocation to a few seconds.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+#include "kernels_api.h"
+
+namespace msb {
+
+// Host-side count of kernel launches issued by this library (bench evidence).
+void count_launch(int n = 1);
+
+inline void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+  }
+}
+
+#define MSB_CHECK_LAUNCH(name)                                  \
+  do {                                                          \
+    ::msb::check_cuda(cudaGetLastError(), name);                \
+    ::msb::count_launch();                                      \
+  } while (0)
+
+constexpr int kNumSMs = 148;
+
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+
+__device__ __forceinline__ bool finite_f32(float x) {
+  // exponent all ones <=> inf or nan
+  return (__float_as_uint(x) & 0x7f800000u) != 0x7f800000u;
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ unsigned warp_or(unsigned v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v |= __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Dispatch a functor over the three float dtypes.
+#define MSB_DISPATCH_FLOAT(code, T, ...)                                      \
+  switch (code) {                                                             \
+    case ::msb::kF32: { using T = float; __VA_ARGS__; break; }                \
+    case ::msb::kF16: { using T = __half; __VA_ARGS__; break; }               \
+    case ::msb::kBF16: { using T = __nv_bfloat16; __VA_ARGS__; break; }       \
+    default: throw std::runtime_error("unsupported dtype code");             \
+  }
+
+inline int grid_for(long long work_items, int threads, int max_blocks) {
+  long long b = (work_items + threads - 1) / threads;
+  if (b < 1) b = 1;
+  if (b > max_blocks) b = max_blocks;
+  return static_cast<int>(b);
+}
+
+}  // namespace msb

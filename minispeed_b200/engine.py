@@ -1,0 +1,309 @@
+"""The training engine: ``initialize`` and :class:`DeepSpeedEngine`.
+
+Public behaviour follows the reference engine (``minispeed/engine.py``):
+
+* ``initialize(model, model_parameters, config)`` returns the engine, which
+  also unpacks as ``engine, optimizer, _, lr_scheduler`` (``engine.py:221-224,
+  372-389``);
+* init order: config -> device -> ``model.to`` -> rank-0 broadcast -> flat
+  groups -> fp32 master snapshot -> cast params to the training dtype ->
+  (stage 3) partition -> optimizer -> scheduler -> loss scaler
+  (``engine.py:90-155``);
+* ``backward`` scales the loss by ``loss_scale / gas`` (the ``/gas`` only when
+  ``scale_wrt_gas`` and gas > 1) and counts micro-steps (``engine.py:227-251``);
+* ``step`` acts only at a not-yet-consumed accumulation boundary and returns
+  whether an update was applied; an inf/nan step halves the loss scale, is
+  counted in ``skipped_steps``, and does not step the scheduler
+  (``engine.py:254-322``).
+
+The optimizer step itself is the device pipeline of
+:meth:`minispeed_b200.zero.ZeROOptimizer.boundary_step` (one host
+synchronization per step instead of three, one fused kernel per stage of
+work).  Device-side phase timers (CUDA events) complement the wall-clock
+``engine.timers``.
+"""
+
+from __future__ import annotations
+
+import logging
+from typing import Iterator, List, Optional
+
+import torch
+from torch import nn
+
+from . import checkpoint as ckpt
+from . import comm
+from .config import DeepSpeedConfig, load_config
+from .flat import FlatParamGroup, build_flat_groups
+from .optim import build_scheduler
+from .precision import DynamicLossScaler
+from .utils import Timers
+from .zero import build_zero_optimizer, make_collectives
+
+logger = logging.getLogger("minispeed_b200")
+
+
+def _normalize_param_groups(model: nn.Module, model_parameters, defaults: dict) -> List[dict]:
+    """torch.optim-style groups from None, an iterable of params, a dict or a
+    list of group dicts; config optimizer params are the group defaults
+    (reference ``engine.py:44-78``)."""
+    if model_parameters is None:
+        raw = [list(model.parameters())]
+    elif isinstance(model_parameters, dict):
+        raw = [model_parameters]
+    else:
+        items = list(model_parameters)
+        raw = items if items and isinstance(items[0], dict) else [items]
+    groups = []
+    for grp in raw:
+        if isinstance(grp, dict):
+            params, opts = grp.get("params", []), {k: v for k, v in grp.items() if k != "params"}
+        else:
+            params, opts = grp, {}
+        if isinstance(params, torch.Tensor):
+            params = [params]
+        merged = dict(defaults)
+        merged.update(opts)
+        merged["params"] = [p for p in params if isinstance(p, nn.Parameter) and p.requires_grad]
+        if merged["params"]:
+            groups.append(merged)
+    if not groups:
+        raise ValueError("No trainable parameters found")
+    return groups
+
+
+class DeepSpeedEngine:
+    """Wraps an ``nn.Module`` with ZeRO data parallelism and mixed precision."""
+
+    def __init__(self, model: nn.Module, config, model_parameters=None):
+        self.config: DeepSpeedConfig = load_config(config, world_size=comm.get_world_size())
+        self.rank = comm.get_rank()
+        self.world_size = comm.get_world_size()
+        self.device = comm.resolve_device()
+        if self.device.type == "cuda":
+            torch.cuda.set_device(self.device)
+        self.timers = Timers()
+        self.module = model.to(self.device)
+        self._broadcast_model()
+
+        groups = _normalize_param_groups(model, model_parameters, self.config.optimizer_params)
+        self.flat_groups: List[FlatParamGroup]
+        self.flat_groups, option_groups = build_flat_groups(
+            groups, rank=self.rank, world_size=self.world_size,
+            zero_stage=self.config.zero_stage, device=self.device)
+        for g in self.flat_groups:
+            g.copy_model_to_flat()  # params are still in their original dtype here
+
+        self._param_dtype = None
+        if self.config.dtype != "fp32":
+            self._param_dtype = self.config.torch_dtype
+            for g in self.flat_groups:
+                g.cast_params(self._param_dtype)
+        if self.config.zero_stage >= 3:
+            for g in self.flat_groups:
+                g.partition_params()
+
+        coll = make_collectives(self.world_size, self.rank, self.device,
+                                self.config.b200.comm, self.config.b200)
+        self.optimizer = build_zero_optimizer(self.flat_groups, option_groups,
+                                              zero_stage=self.config.zero_stage,
+                                              collectives=coll)
+        self.lr_scheduler = build_scheduler(self.optimizer, self.config.scheduler_type,
+                                            self.config.scheduler_params)
+        fp16 = self.config.fp16_enabled
+        self.loss_scaler = DynamicLossScaler(enabled=fp16, init_scale=self.config.loss_scale,
+                                             scale_window=self.config.loss_scale_window)
+        if fp16 and self.config.loss_scale == 0:
+            self.loss_scaler.set_scale_from_power(self.config.initial_scale_power)
+
+        self.micro_steps = 0
+        self.global_steps = 0
+        self.skipped_steps = 0
+        self._consumed_boundary = -1
+        self.grad_norm: Optional[float] = None
+        self._window_open = False
+
+    # ----------------------------------------------------------- properties
+    @property
+    def gas(self) -> int:
+        return self.config.gas
+
+    @property
+    def is_gradient_accumulation_boundary(self) -> bool:
+        return self.micro_steps > 0 and self.micro_steps % self.gas == 0
+
+    @property
+    def _boundary_pending(self) -> bool:
+        return self.is_gradient_accumulation_boundary and self._consumed_boundary != self.micro_steps
+
+    @property
+    def loss_scale(self) -> float:
+        return self.loss_scaler.loss_scale_factor
+
+    @property
+    def parameters(self):
+        return self.module.parameters()
+
+    @property
+    def collectives(self) -> str:
+        """Name of the gradient/parameter communication strategy in use."""
+        return self.optimizer.coll.name
+
+    # --------------------------------------------------------- nn surface
+    def _cast_inputs(self, obj):
+        """Cast floating-point inputs to the model dtype, recursively
+        (reference ``engine.py:182-198``)."""
+        dt = self._param_dtype
+        if dt is None:
+            return obj
+        if isinstance(obj, torch.Tensor):
+            return obj.to(dt) if obj.is_floating_point() and obj.dtype != dt else obj
+        if isinstance(obj, dict):
+            return {k: self._cast_inputs(v) for k, v in obj.items()}
+        if isinstance(obj, tuple):
+            return tuple(self._cast_inputs(v) for v in obj)
+        if isinstance(obj, list):
+            return [self._cast_inputs(v) for v in obj]
+        return obj
+
+    def _open_window(self) -> None:
+        """First forward of an accumulation window: bind the gradient arenas
+        so autograd accumulates straight into them."""
+        if self._window_open or not torch.is_grad_enabled() or not self.module.training:
+            return
+        for g in self.flat_groups:
+            if g.params_materialized:
+                g.rebind()
+                g.ensure_grad_arena()
+        self._window_open = True
+
+    def forward(self, *args, **kwargs):
+        if not self.optimizer.params_gathered:
+            with self.timers.timer("gather"):
+                self.optimizer.gather_parameters()
+        self._open_window()
+        return self.module(*self._cast_inputs(args), **self._cast_inputs(kwargs))
+
+    def __call__(self, *args, **kwargs):
+        return self.forward(*args, **kwargs)
+
+    def train(self, mode: bool = True):
+        self.module.train(mode)
+        return self
+
+    def eval(self):
+        self.module.eval()
+        return self
+
+    def __iter__(self) -> Iterator:
+        return iter((self, self.optimizer, None, self.lr_scheduler))
+
+    # ------------------------------------------------------------ backward
+    def _scale_loss(self, loss: torch.Tensor, scale_wrt_gas: bool) -> torch.Tensor:
+        factor = self.loss_scaler.loss_scale_factor
+        if scale_wrt_gas and self.gas > 1:
+            factor /= self.gas
+        return loss if factor == 1.0 else loss * factor
+
+    def backward(self, loss: torch.Tensor, scale_wrt_gas: bool = True,
+                 retain_graph: bool = False, create_graph: bool = False) -> None:
+        with self.timers.timer("backward"):
+            self._scale_loss(loss, scale_wrt_gas).backward(retain_graph=retain_graph,
+                                                           create_graph=create_graph)
+        self.micro_steps += 1
+
+    # ---------------------------------------------------------------- step
+    def step(self) -> bool:
+        """Apply the optimizer at a pending accumulation boundary.
+
+        Returns True only when an update was applied."""
+        if not self._boundary_pending:
+            return False
+        self._consumed_boundary = self.micro_steps
+        with self.timers.timer("step"):
+            return self._take_optimizer_step()
+
+    @torch.no_grad()
+    def _take_optimizer_step(self) -> bool:
+        scale = self.loss_scaler.loss_scale_factor
+        with self.timers.timer("reduce"):
+            applied, norm = self.optimizer.boundary_step(scale, self.config.gradient_clipping)
+        self.optimizer.after_step(applied)
+        self._window_open = False
+        if not applied:
+            self.loss_scaler.update(overflow=True)
+            self.skipped_steps += 1
+            self.optimizer.zero_grad()
+            if self.skipped_steps % max(1, self.config.steps_per_print) == 0:
+                logger.warning("rank %d: inf/nan gradients at micro_step=%d, step skipped "
+                               "(loss_scale=%.1f, skipped=%d)", self.rank, self.micro_steps,
+                               self.loss_scaler.scale, self.skipped_steps)
+            return False
+        self.grad_norm = norm
+        self.loss_scaler.update(overflow=False)
+        self.lr_scheduler.step()
+        self.optimizer.zero_grad()
+        self.global_steps += 1
+        return True
+
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        for g in self.flat_groups:
+            g.zero_grad()
+        for p in self.module.parameters():
+            p.grad = None
+        self._window_open = False
+
+    # ------------------------------------------------------- checkpointing
+    def save_checkpoint(self, save_dir: str, tag: Optional[str] = None, **kwargs):
+        return ckpt.save_checkpoint(self, save_dir, tag=tag, **kwargs)
+
+    def load_checkpoint(self, load_dir: str, tag: Optional[str] = None, **kwargs):
+        return ckpt.load_checkpoint(self, load_dir, tag=tag, **kwargs)
+
+    def state_dict(self):
+        self.optimizer.gather_parameters()
+        return self.module.state_dict()
+
+    def load_state_dict(self, state_dict):
+        self.optimizer.gather_parameters()
+        self.module.load_state_dict(state_dict)
+        for g in self.flat_groups:
+            g.copy_model_to_flat()
+
+    # -------------------------------------------------------------- helpers
+    @torch.no_grad()
+    def _broadcast_model(self) -> None:
+        if not comm.is_distributed():
+            return
+        tensors = [p.data for p in self.module.parameters()]
+        tensors += [b.data for b in self.module.buffers()]
+        comm.broadcast_tensors(tensors, src=0)
+
+    def get_loss_scale(self) -> float:
+        return self.loss_scaler.scale
+
+    def get_gradient_norm(self) -> Optional[float]:
+        return self.grad_norm
+
+    def close(self) -> None:
+        """Release communication resources (peer mappings, buffers)."""
+        self.optimizer.close()
+
+    def __repr__(self) -> str:  # pragma: no cover
+        return (f"DeepSpeedEngine({self.config!r}, global_steps={self.global_steps}, "
+                f"micro_steps={self.micro_steps})")
+
+
+def initialize(model: Optional[nn.Module] = None, model_parameters=None, config=None,
+               model_args=None):
+    """Initialize distributed state and build the engine.
+
+    ``engine, optimizer, _, lr_scheduler = initialize(...)`` also works."""
+    if model is None:
+        raise ValueError("model is required")
+    comm.init_distributed()
+    engine = DeepSpeedEngine(model, config, model_parameters=model_parameters)
+    if comm.get_rank() == 0:
+        logger.info("minispeed_b200 initialized: %s (collectives=%s)", engine.config,
+                    engine.collectives)
+    return engine

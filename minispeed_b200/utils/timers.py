@@ -1,0 +1,130 @@
+"""Named timers.
+
+:class:`Timers` keeps the reference's wall-clock API (``engine.timers``,
+reference ``minispeed/utils.py:14-60``): ``timers("name")``,
+``with timers.timer("name")``, ``names()``, ``reset()`` and a rank-0
+``log()`` string ``"name: 0.123s | ..."``.  Like the reference it does not
+synchronize the GPU, so on CUDA it measures host time.
+
+:class:`DeviceTimers` measures the same kind of named sections on the GPU
+with CUDA events recorded on the current stream; ``elapsed_ms()`` syncs
+once and sums every completed interval.  ``max_over_ranks`` reduces a value
+with MAX across the process group, which is how multi-GPU times are
+reported.
+"""
+
+from __future__ import annotations
+
+import time
+from contextlib import contextmanager
+from typing import Dict, Iterator, List
+
+import torch
+
+
+class Timer:
+    def __init__(self, name: str):
+        self.name = name
+        self.elapsed = 0.0
+        self.started_at = None
+
+    @contextmanager
+    def section(self) -> Iterator[None]:
+        t0 = time.perf_counter()
+        try:
+            yield
+        finally:
+            self.elapsed += time.perf_counter() - t0
+
+    def start(self) -> None:
+        self.started_at = time.perf_counter()
+
+    def stop(self) -> None:
+        if self.started_at is not None:
+            self.elapsed += time.perf_counter() - self.started_at
+            self.started_at = None
+
+    def reset(self) -> None:
+        self.elapsed = 0.0
+
+
+class Timers:
+    def __init__(self) -> None:
+        self._timers: Dict[str, Timer] = {}
+
+    def __call__(self, name: str) -> Timer:
+        t = self._timers.get(name)
+        if t is None:
+            t = self._timers[name] = Timer(name)
+        return t
+
+    @contextmanager
+    def timer(self, name: str) -> Iterator[None]:
+        with self(name).section():
+            yield
+
+    def names(self) -> List[str]:
+        return list(self._timers)
+
+    def reset(self) -> None:
+        for t in self._timers.values():
+            t.reset()
+
+    def log(self, rank0_only: bool = True) -> str:
+        from .. import comm
+
+        if rank0_only and comm.get_rank() != 0:
+            return ""
+        return " | ".join(f"{n}: {t.elapsed:.3f}s" for n, t in self._timers.items())
+
+
+class DeviceTimers:
+    """CUDA-event section timers (no-ops on CPU)."""
+
+    def __init__(self) -> None:
+        self._pending: Dict[str, list] = {}
+        self._done: Dict[str, float] = {}
+
+    @contextmanager
+    def timer(self, name: str) -> Iterator[None]:
+        if not torch.cuda.is_available():
+            yield
+            return
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        try:
+            yield
+        finally:
+            b.record()
+            self._pending.setdefault(name, []).append((a, b))
+
+    def elapsed_ms(self) -> Dict[str, float]:
+        if self._pending:
+            torch.cuda.synchronize()
+        for name, pairs in self._pending.items():
+            self._done[name] = self._done.get(name, 0.0) + sum(a.elapsed_time(b) for a, b in pairs)
+        self._pending.clear()
+        return dict(self._done)
+
+    def reset(self) -> None:
+        self._pending.clear()
+        self._done.clear()
+
+
+def max_over_ranks(value: float) -> float:
+    from .. import comm
+
+    if not comm.is_distributed():
+        return float(value)
+    dev = torch.device("cuda", torch.cuda.current_device()) if (
+        torch.cuda.is_available() and torch.distributed.get_backend() == "nccl") else "cpu"
+    t = torch.tensor([float(value)], dtype=torch.float64, device=dev)
+    comm.all_reduce(t, op="max")
+    return float(t.item())
+
+
+def set_seed(seed: int) -> None:
+    torch.manual_seed(seed)
+    if torch.cuda.is_available():
+        torch.cuda.manual_seed_all(seed)

@@ -1,0 +1,114 @@
+"""Two ranks on gloo/CPU must reproduce a single-process run on the union batch.
+
+Each rank trains on its half of every micro-batch; the averaged gradient equals
+the union-batch gradient, so trajectories agree up to fp32 summation order.
+Covers stages 0-3, the exact global clipping norm (including stage 1) and the
+partitioning of optimizer state.
+"""
+
+import os
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import minispeed_b200 as ms
+from tests.helpers import config, free_port, make_data, make_net, rank_slice, run, set_rank_env
+
+WORLD, STEPS, GAS, MICRO = 2, 5, 2, 4
+
+
+def _worker(rank, stage, port, out_dir, clip, dtype):
+    set_rank_env(rank, WORLD, port, "gloo", "cpu")
+    engine = ms.initialize(model=make_net(), config=config(
+        micro=MICRO, gas=GAS, stage=stage, clip=clip, dtype=dtype))
+    x, y = make_data(STEPS, GAS, WORLD, MICRO)
+    losses = run(engine, rank_slice(x, rank, MICRO), rank_slice(y, rank, MICRO), STEPS, GAS)
+    params = {k: v.clone() for k, v in engine.state_dict().items()}
+    engine.optimizer.sync_master_weights()
+    torch.save({"losses": torch.tensor(losses), "params": params,
+                "steps": engine.global_steps, "norm": engine.grad_norm,
+                "exp_avg": [s["exp_avg"].clone() for s in engine.optimizer.state],
+                "opt_step": engine.optimizer.state[0]["step"],
+                "masters": engine.flat_groups[0].data.clone(),
+                "coll": engine.collectives},
+               os.path.join(out_dir, f"r{rank}.pt"))
+    ms.comm.destroy()
+
+
+def padded_total():
+    total = sum(p.numel() for p in make_net().parameters())
+    return -(-total // WORLD) * WORLD
+
+
+def _single(clip, dtype):
+    engine = ms.initialize(model=make_net(), config=config(
+        micro=MICRO * WORLD, gas=GAS, stage=0, clip=clip, dtype=dtype))
+    x, y = make_data(STEPS, GAS, WORLD, MICRO)
+    losses = run(engine, x, y, STEPS, GAS)
+    return torch.tensor(losses), engine.state_dict(), engine.grad_norm
+
+
+def _spawn(stage, tmp_path, clip=1.0, dtype="fp32"):
+    mp.spawn(_worker, args=(stage, free_port(), str(tmp_path), clip, dtype), nprocs=WORLD,
+             join=True)
+    return [torch.load(tmp_path / f"r{r}.pt", weights_only=False) for r in range(WORLD)]
+
+
+@pytest.mark.parametrize("stage", [0, 1, 2, 3])
+def test_two_ranks_match_union_batch(stage, tmp_path):
+    r0, r1 = _spawn(stage, tmp_path)
+    ref_losses, ref_params, _ = _single(1.0, "fp32")
+    assert r0["steps"] == r1["steps"] == STEPS
+    assert r0["coll"] == "gloo"
+    torch.testing.assert_close((r0["losses"] + r1["losses"]) / 2, ref_losses,
+                               rtol=5e-3, atol=1e-4)
+    num = den = 0.0
+    for k, ref in ref_params.items():
+        torch.testing.assert_close(r0["params"][k], r1["params"][k], rtol=0, atol=0)
+        num += float((r0["params"][k] - ref).pow(2).sum())
+        den += float(ref.pow(2).sum())
+    assert (num / den) ** 0.5 < 1e-4
+    if stage < 3:   # full fp32 masters agree across ranks once synced
+        torch.testing.assert_close(r0["masters"], r1["masters"], rtol=0, atol=0)
+    else:           # stage 3 keeps disjoint shards
+        assert r0["masters"].numel() == r1["masters"].numel() == padded_total() // WORLD
+
+
+@pytest.mark.parametrize("stage", [1, 2, 3])
+def test_clipping_uses_exact_global_norm(stage, tmp_path):
+    """Tiny clip threshold: every step clips, so the norm must be global."""
+    r0, r1 = _spawn(stage, tmp_path, clip=0.01)
+    _, ref_params, ref_norm = _single(0.01, "fp32")
+    assert r0["norm"] == pytest.approx(r1["norm"], rel=0, abs=0)
+    assert r0["norm"] == pytest.approx(ref_norm, rel=1e-3)
+    num = den = 0.0
+    for k, ref in ref_params.items():
+        num += float((r0["params"][k] - ref).pow(2).sum())
+        den += float(ref.pow(2).sum())
+    assert (num / den) ** 0.5 < 1e-4
+
+
+@pytest.mark.parametrize("stage", [0, 1, 2, 3])
+def test_optimizer_state_is_partitioned(stage, tmp_path):
+    r0, r1 = _spawn(stage, tmp_path)
+    total = sum(p.numel() for p in make_net().parameters())
+    padded = -(-total // WORLD) * WORLD
+    n0 = [t.numel() for t in r0["exp_avg"]]
+    assert n0 == [t.numel() for t in r1["exp_avg"]]
+    assert r0["opt_step"] == STEPS
+    if stage == 0:
+        assert n0 == [padded]
+        torch.testing.assert_close(r0["exp_avg"][0], r1["exp_avg"][0])
+    else:
+        assert n0 == [padded // WORLD]
+        assert not torch.equal(r0["exp_avg"][0], r1["exp_avg"][0])
+
+
+def test_bf16_two_ranks_stage2(tmp_path):
+    r0, r1 = _spawn(2, tmp_path, dtype="bf16")
+    ref_losses, _, _ = _single(1.0, "bf16")
+    torch.testing.assert_close((r0["losses"] + r1["losses"]) / 2, ref_losses,
+                               rtol=3e-2, atol=3e-3)
+    for k in r0["params"]:
+        torch.testing.assert_close(r0["params"][k], r1["params"][k], rtol=0, atol=0)
