@@ -1,0 +1,77 @@
+"""GEMM throughput of the tcgen05 kernel vs the library product on the
+GPT-2-small training shapes (M = 16 x 1024 tokens).
+
+    python benchmarks/gemm_bench.py [--tokens 16384] [--iters 20]
+
+Times each product with CUDA events after warm-up; inputs are re-used, the
+operand set of each shape is < L2 for the small products, so this measures
+kernel throughput (compare with the cuBLAS column, same conditions).
+"""
+
+import argparse
+import json
+import os
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from minispeed_b200.ops import gemm  # noqa: E402
+
+
+def timeit(fn, iters):
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args()
+    T, C, V = args.tokens, 768, 50257
+    Vp = 50304
+    rows = []
+    shapes = [("qkv", 3 * C, C), ("proj", C, C), ("fc", 4 * C, C), ("fc2", C, 4 * C), ("head", V, C)]
+    for name, N, K in shapes:
+        x = torch.randn(T, K, device="cuda").half()
+        w = (torch.randn(N, K, device="cuda") * 0.02).half()
+        if name == "head":
+            dy = torch.randn(T, Vp, device="cuda").half()[:, :V]
+        else:
+            dy = torch.randn(T, N, device="cuda").half()
+        for kind in ("fwd", "dgrad", "wgrad"):
+            if kind == "fwd":
+                ours = lambda: gemm.gemm(x, w, a_kmajor=True, b_kmajor=True)
+                lib = lambda: torch.mm(x, w.t())
+            elif kind == "dgrad":
+                ours = lambda: gemm.gemm(dy, w, a_kmajor=True, b_kmajor=False)
+                lib = lambda: torch.mm(dy, w)
+            else:
+                ours = lambda: gemm.gemm(dy, x, a_kmajor=False, b_kmajor=False)
+                lib = lambda: torch.mm(dy.t(), x)
+            flops = 2.0 * T * N * K
+            t_o = timeit(ours, args.iters)
+            gemm.check()
+            t_l = timeit(lib, args.iters)
+            rows.append({"gemm": f"{name}.{kind}", "M_N_K": [T if kind != "wgrad" else N,
+                                                            N if kind == "fwd" else (K if kind == "dgrad" else K),
+                                                            K if kind == "fwd" else (N if kind == "dgrad" else T)],
+                         "ours_ms": round(t_o, 4), "ours_tflops": round(flops / t_o / 1e9, 1),
+                         "cublas_ms": round(t_l, 4), "cublas_tflops": round(flops / t_l / 1e9, 1)})
+            print(json.dumps(rows[-1]), flush=True)
+    tot_o = sum(r["ours_ms"] for r in rows)
+    tot_l = sum(r["cublas_ms"] for r in rows)
+    print(json.dumps({"total_ours_ms": round(tot_o, 3), "total_cublas_ms": round(tot_l, 3)}))
+
+
+if __name__ == "__main__":
+    main()

@@ -102,6 +102,202 @@ void cast_scale(const at::Tensor& src, const at::Tensor& dst, double mul) {
                   (float)mul, stream_of(src));
 }
 
+using OptT = c10::optional<at::Tensor>;
+
+const void* optr(const OptT& t) {
+  return (t.has_value() && t->defined()) ? t->data_ptr() : nullptr;
+}
+void* optr_mut(const OptT& t) {
+  return (t.has_value() && t->defined()) ? t->data_ptr() : nullptr;
+}
+float* optr_f(const OptT& t) {
+  if (!(t.has_value() && t->defined())) return nullptr;
+  TORCH_CHECK(t->scalar_type() == at::kFloat);
+  return t->data_ptr<float>();
+}
+
+void add_norm_fwd(const at::Tensor& x, const OptT& delta, const at::Tensor& w, const OptT& b,
+                  const OptT& s_out, const at::Tensor& y, const OptT& mean,
+                  const at::Tensor& rstd, double eps, bool rms) {
+  check_cuda_contig(x, "x");
+  check_cuda_contig(y, "y");
+  const int64_t C = x.size(-1), M = x.numel() / C;
+  TORCH_CHECK(C % 8 == 0, "hidden size must be a multiple of 8");
+  TORCH_CHECK(w.numel() == C && y.numel() == x.numel() && rstd.numel() >= M);
+  c10::cuda::CUDAGuard g(x.device());
+  msb::add_norm_fwd(x.data_ptr(), optr(delta), w.data_ptr(), optr(b), optr_mut(s_out),
+                    y.data_ptr(), optr_f(mean), rstd.data_ptr<float>(), (int)M, (int)C,
+                    (float)eps, rms, dtype_code(x), stream_of(x));
+}
+
+int64_t norm_bwd(const at::Tensor& dy, const at::Tensor& s, const at::Tensor& w,
+                 const OptT& mean, const at::Tensor& rstd, const OptT& dres,
+                 const at::Tensor& dx, const at::Tensor& dw_part, const OptT& db_part, bool rms,
+                 int64_t max_blocks) {
+  check_cuda_contig(dy, "dy");
+  check_cuda_contig(s, "s");
+  const int64_t C = s.size(-1), M = s.numel() / C;
+  TORCH_CHECK(dw_part.numel() >= max_blocks * C, "dw partial buffer too small");
+  c10::cuda::CUDAGuard g(s.device());
+  return msb::norm_bwd(dy.data_ptr(), s.data_ptr(), w.data_ptr(), optr_f(mean),
+                       rstd.data_ptr<float>(), optr(dres), dx.data_ptr(),
+                       dw_part.data_ptr<float>(), optr_f(db_part), (int)M, (int)C, rms,
+                       dtype_code(s), (int)max_blocks, stream_of(s));
+}
+
+void check_rows(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1 && t.stride(0) >= t.size(1),
+              name, " must be a row-major matrix (unit column stride)");
+}
+
+int64_t colsum_partial(const at::Tensor& a, const at::Tensor& part, int64_t max_chunks) {
+  check_rows(a, "a");
+  const int64_t N = a.size(1), M = a.size(0);
+  TORCH_CHECK(part.numel() >= max_chunks * N, "partial buffer too small");
+  c10::cuda::CUDAGuard g(a.device());
+  return msb::colsum_partial(a.data_ptr(), part.data_ptr<float>(), (int)M, (int)N, a.stride(0),
+                             dtype_code(a), (int)max_chunks, stream_of(a));
+}
+
+void colsum_finish(const at::Tensor& part, int64_t nparts, const at::Tensor& out) {
+  c10::cuda::CUDAGuard g(out.device());
+  msb::colsum_finish(part.data_ptr<float>(), (int)nparts, (int)out.numel(), out.data_ptr(),
+                     dtype_code(out), stream_of(out));
+}
+
+void bias_gelu_fwd(const at::Tensor& u, const OptT& bias, const at::Tensor& h) {
+  check_cuda_contig(u, "u");
+  check_cuda_contig(h, "h");
+  TORCH_CHECK(u.size(-1) % 8 == 0);
+  c10::cuda::CUDAGuard g(u.device());
+  msb::bias_gelu_fwd(u.data_ptr(), optr(bias), h.data_ptr(), u.numel(), (int)u.size(-1),
+                     dtype_code(u), stream_of(u));
+}
+
+void gelu_bwd(const at::Tensor& dh, const at::Tensor& u, const at::Tensor& du) {
+  check_cuda_contig(dh, "dh");
+  check_cuda_contig(u, "u");
+  TORCH_CHECK(u.numel() % 8 == 0);
+  c10::cuda::CUDAGuard g(u.device());
+  msb::gelu_bwd(dh.data_ptr(), u.data_ptr(), du.data_ptr(), u.numel(), dtype_code(u),
+                stream_of(u));
+}
+
+void swiglu_fwd(const at::Tensor& gu, const at::Tensor& h) {
+  check_cuda_contig(gu, "gu");
+  const int64_t F = h.size(-1);
+  TORCH_CHECK(gu.size(-1) == 2 * F && F % 8 == 0);
+  c10::cuda::CUDAGuard g(gu.device());
+  msb::swiglu_fwd(gu.data_ptr(), h.data_ptr(), h.numel() / F, (int)F, dtype_code(gu),
+                  stream_of(gu));
+}
+
+void swiglu_bwd(const at::Tensor& dh, const at::Tensor& gu, const at::Tensor& dgu) {
+  const int64_t F = dh.size(-1);
+  c10::cuda::CUDAGuard g(gu.device());
+  msb::swiglu_bwd(dh.data_ptr(), gu.data_ptr(), dgu.data_ptr(), dh.numel() / F, (int)F,
+                  dtype_code(gu), stream_of(gu));
+}
+
+void cross_entropy_fwd(const at::Tensor& logits, const at::Tensor& tgt, const at::Tensor& lse,
+                       const at::Tensor& loss_rows, const at::Tensor& loss,
+                       const at::Tensor& inv_count, int64_t ignore_index) {
+  check_rows(logits, "logits");
+  check_cuda_contig(tgt, "targets");
+  TORCH_CHECK(tgt.scalar_type() == at::kLong, "targets must be int64");
+  const int64_t V = logits.size(1), M = logits.size(0);
+  TORCH_CHECK(tgt.numel() == M && lse.numel() >= M && loss_rows.numel() >= M);
+  c10::cuda::CUDAGuard g(logits.device());
+  msb::cross_entropy_fwd(logits.data_ptr(), reinterpret_cast<const long long*>(tgt.data_ptr<int64_t>()),
+                         lse.data_ptr<float>(), loss_rows.data_ptr<float>(), loss.data_ptr<float>(),
+                         inv_count.data_ptr<float>(), M, (int)V, logits.stride(0), ignore_index,
+                         dtype_code(logits), stream_of(logits));
+}
+
+void cross_entropy_bwd(const at::Tensor& logits, const at::Tensor& tgt, const at::Tensor& lse,
+                       const at::Tensor& grad_out, const at::Tensor& inv_count,
+                       int64_t ignore_index) {
+  check_rows(logits, "logits");
+  TORCH_CHECK(grad_out.scalar_type() == at::kFloat && grad_out.is_cuda());
+  const int64_t V = logits.size(1), M = logits.size(0);
+  c10::cuda::CUDAGuard g(logits.device());
+  msb::cross_entropy_bwd(logits.data_ptr(), reinterpret_cast<const long long*>(tgt.data_ptr<int64_t>()),
+                         lse.data_ptr<float>(), grad_out.data_ptr<float>(),
+                         inv_count.data_ptr<float>(), M, (int)V, logits.stride(0), ignore_index,
+                         dtype_code(logits), stream_of(logits));
+}
+
+void embedding_fwd(const at::Tensor& idx, const at::Tensor& wte, const OptT& wpe,
+                   const at::Tensor& out, int64_t T) {
+  check_cuda_contig(idx, "idx");
+  TORCH_CHECK(idx.scalar_type() == at::kLong);
+  const int64_t C = wte.size(-1);
+  TORCH_CHECK(C % 8 == 0);
+  c10::cuda::CUDAGuard g(wte.device());
+  msb::embedding_fwd(reinterpret_cast<const long long*>(idx.data_ptr<int64_t>()), wte.data_ptr(), optr(wpe), out.data_ptr(),
+                     idx.numel(), (int)T, (int)C, wte.size(0), dtype_code(wte), stream_of(wte));
+}
+
+void embedding_bwd(const at::Tensor& dout, const at::Tensor& idx, const at::Tensor& dwte,
+                   const OptT& dwpe, int64_t T) {
+  check_cuda_contig(dout, "dout");
+  TORCH_CHECK(dwte.scalar_type() == at::kFloat);
+  const int64_t C = dout.size(-1);
+  c10::cuda::CUDAGuard g(dout.device());
+  msb::embedding_bwd(dout.data_ptr(), reinterpret_cast<const long long*>(idx.data_ptr<int64_t>()), dwte.data_ptr<float>(),
+                     optr_f(dwpe), idx.numel(), (int)T, (int)C, dwte.size(0), dtype_code(dout),
+                     stream_of(dout));
+}
+
+void rope(const at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t, int64_t BT,
+          int64_t T, int64_t H, int64_t D, int64_t row_stride, bool inverse) {
+  TORCH_CHECK(x.is_cuda() && cos_t.scalar_type() == at::kFloat);
+  c10::cuda::CUDAGuard g(x.device());
+  msb::rope(x.data_ptr(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), BT, (int)T, (int)H,
+            (int)D, row_stride, inverse, dtype_code(x), stream_of(x));
+}
+
+// C[M,N] (+)= A * B^T with A given as [M,K] (a_kmajor) or [K,M], B as [N,K]
+// (b_kmajor) or [K,N]; every matrix row-major with unit column stride.
+void gemm(const at::Tensor& a, const at::Tensor& b, bool a_kmajor, bool b_kmajor,
+          const OptT& bias, const at::Tensor& out, bool accumulate, const at::Tensor& err,
+          double timeout_s) {
+  check_rows(a, "A");
+  check_rows(b, "B");
+  check_rows(out, "C");
+  TORCH_CHECK(a.scalar_type() == b.scalar_type() && a.scalar_type() == out.scalar_type(),
+              "gemm operands and output must share one 16-bit dtype");
+  TORCH_CHECK(a.scalar_type() == at::kHalf || a.scalar_type() == at::kBFloat16,
+              "tcgen05 gemm takes fp16 or bf16");
+  const int64_t M = a_kmajor ? a.size(0) : a.size(1);
+  const int64_t K = a_kmajor ? a.size(1) : a.size(0);
+  const int64_t N = b_kmajor ? b.size(0) : b.size(1);
+  const int64_t Kb = b_kmajor ? b.size(1) : b.size(0);
+  TORCH_CHECK(K == Kb, "gemm K mismatch: ", K, " vs ", Kb);
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm output shape mismatch");
+  TORCH_CHECK(err.is_cuda() && err.scalar_type() == at::kInt && err.numel() >= 1);
+  if (bias.has_value() && bias->defined()) {
+    TORCH_CHECK(bias->numel() == N && bias->scalar_type() == a.scalar_type(), "bias mismatch");
+  }
+  c10::cuda::CUDAGuard g(a.device());
+  int bn = 0, splits = 1;
+  const long long need = msb::gemm_plan((int)M, (int)N, (int)K, 148, &bn, &splits);
+  at::Tensor ws;
+  if (need > 0) ws = at::empty({need}, a.options().dtype(at::kFloat));
+  msb::gemm_tcgen05(a.data_ptr(), a.stride(0), a_kmajor ? 0 : 1, b.data_ptr(), b.stride(0),
+                    b_kmajor ? 0 : 1, out.data_ptr(), out.stride(0), optr(bias), (int)M, (int)N,
+                    (int)K, dtype_code(a), accumulate ? 1 : 0,
+                    need > 0 ? ws.data_ptr<float>() : nullptr, need,
+                    reinterpret_cast<unsigned*>(err.data_ptr<int>()), timeout_s, stream_of(a));
+}
+
+std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K) {
+  int bn = 0, splits = 1;
+  const long long need = msb::gemm_plan((int)M, (int)N, (int)K, 148, &bn, &splits);
+  return {bn, splits, need};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, mod) {
@@ -112,4 +308,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, mod) {
   mod.def("adamw", &adamw);
   mod.def("cast_scale", &cast_scale);
   mod.def("launch_count", &msb::launch_count);
+  mod.def("add_norm_fwd", &add_norm_fwd);
+  mod.def("norm_bwd", &norm_bwd);
+  mod.def("colsum_partial", &colsum_partial);
+  mod.def("colsum_finish", &colsum_finish);
+  mod.def("bias_gelu_fwd", &bias_gelu_fwd);
+  mod.def("gelu_bwd", &gelu_bwd);
+  mod.def("swiglu_fwd", &swiglu_fwd);
+  mod.def("swiglu_bwd", &swiglu_bwd);
+  mod.def("cross_entropy_fwd", &cross_entropy_fwd);
+  mod.def("cross_entropy_bwd", &cross_entropy_bwd);
+  mod.def("embedding_fwd", &embedding_fwd);
+  mod.def("embedding_bwd", &embedding_bwd);
+  mod.def("rope", &rope);
+  mod.def("gemm", &gemm);
+  mod.def("gemm_plan", &gemm_plan_py);
 }

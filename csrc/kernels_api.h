@@ -22,4 +22,41 @@ void adamw(float* master, float* m, float* v, const void* grad, int gdtype, void
 void cast_scale(const void* src, int sdtype, void* dst, int ddtype, long long n, float mul,
                 cudaStream_t stream);
 
+// ---- model kernels (nn_kernels.cu)
+void add_norm_fwd(const void* x, const void* delta, const void* w, const void* b, void* s_out,
+                  void* y, float* mean, float* rstd, int M, int C, float eps, bool rms,
+                  int dtype, cudaStream_t st);
+int norm_bwd(const void* dy, const void* s, const void* w, const float* mean, const float* rstd,
+             const void* dres, void* dx, float* dw_part, float* db_part, int M, int C, bool rms,
+             int dtype, int max_blocks, cudaStream_t st);
+int colsum_partial(const void* a, float* part, int M, int N, long long ld, int dtype,
+                   int max_chunks, cudaStream_t st);
+void colsum_finish(const float* part, int nparts, int N, void* out, int dtype, cudaStream_t st);
+void bias_gelu_fwd(void* u, const void* bias, void* h, long long total, int N, int dtype,
+                   cudaStream_t st);
+void gelu_bwd(const void* dh, const void* u, void* du, long long total, int dtype,
+              cudaStream_t st);
+void swiglu_fwd(const void* gu, void* h, long long rows, int F, int dtype, cudaStream_t st);
+void swiglu_bwd(const void* dh, const void* gu, void* dgu, long long rows, int F, int dtype,
+                cudaStream_t st);
+void cross_entropy_fwd(const void* logits, const long long* tgt, float* lse, float* loss_rows,
+                       float* loss, float* inv_count, long long M, int V, long long ld,
+                       long long ignore_index, int dtype, cudaStream_t st);
+void cross_entropy_bwd(void* logits, const long long* tgt, const float* lse,
+                       const float* grad_out, const float* inv_count, long long M, int V,
+                       long long ld, long long ignore_index, int dtype, cudaStream_t st);
+void embedding_fwd(const long long* idx, const void* wte, const void* wpe, void* out, long long M,
+                   int T_len, int C, long long V, int dtype, cudaStream_t st);
+void embedding_bwd(const void* dout, const long long* idx, float* dwte, float* dwpe, long long M,
+                   int T_len, int C, long long V, int dtype, cudaStream_t st);
+void rope(void* x, const float* cos_t, const float* sin_t, long long BT, int T_len, int H, int D,
+          long long row_stride, bool inverse, int dtype, cudaStream_t st);
+
+// ---- tcgen05 GEMM (gemm_tcgen05.cu)
+long long gemm_plan(int M, int N, int K, int num_sms, int* bn_out, int* splits_out);
+void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
+                  void* C, long long ldc, const void* bias, int M, int N, int K, int dtype,
+                  int accumulate, float* ws, long long ws_floats, unsigned* err,
+                  double timeout_s, cudaStream_t st);
+
 }  // namespace msb

@@ -1,0 +1,753 @@
+// Memory-bound model kernels of the GPT / Llama blocks.
+//
+//   add_layernorm_fwd  s = x (+ delta); y = LN(s) * w + b  (or RMSNorm: no
+//                      mean, no bias); saves mean/rstd per row.  Fusing the
+//                      residual add into the norm removes one read+write of
+//                      the residual stream per add.
+//   layernorm_bwd      dx = LN'(dy) (+ dresidual), per-block fp32 partial
+//                      column sums for dw/db (deterministic second pass)
+//   colsum_*           column sums of [M,N] (bias grads) via partials
+//   bias_gelu_fwd      u += b; h = gelu(u)  (exact erf GELU, as nn.GELU())
+//   gelu_bwd           du = dh * gelu'(u)
+//   swiglu_fwd/bwd     h = silu(g) * u and its gradient
+//   cross_entropy_*    fused softmax cross-entropy over model-dtype logits:
+//                      forward = one online-softmax pass per row (loss, lse),
+//                      backward = one pass writing dlogits in place; the fp32
+//                      logits the reference materializes never exist.
+//   embedding_*        token (+ position) gather-add and its scatter-add
+//   rope_*             rotary position embedding on q/k in place
+#include "common.cuh"
+
+namespace msb {
+namespace {
+
+template <typename T>
+struct alignas(16) Pack8 {
+  T v[8];
+};
+
+// 8-element accesses: one 16-byte transaction when the address allows it,
+// element-wise otherwise.  Parameters are views into a flat arena at
+// arbitrary element offsets, so weights and biases need not be aligned.
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&f)[8]) {
+  if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    Pack8<T> r = *reinterpret_cast<const Pack8<T>*>(p);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) f[k] = to_f32(r.v[k]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) f[k] = to_f32(p[k]);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&f)[8]) {
+  if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    Pack8<T> r;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) r.v[k] = from_f32<T>(f[k]);
+    *reinterpret_cast<Pack8<T>*>(p) = r;
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) p[k] = from_f32<T>(f[k]);
+  }
+}
+
+// ------------------------------------------------------------ layernorm
+// One warp per row; the row stays in registers (NV vectors of 8 per lane).
+template <typename T, int NV, bool RMS>
+__global__ void __launch_bounds__(256)
+add_norm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ delta,
+                    const T* __restrict__ w, const T* __restrict__ b, T* __restrict__ s_out,
+                    T* __restrict__ y, float* __restrict__ mean_out,
+                    float* __restrict__ rstd_out, int M, int C, float eps) {
+  const int warps = blockDim.x >> 5;
+  const int row = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const int nvec = C >> 3;
+  const size_t base = (size_t)row * C;
+  float v[NV][8];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (lane + i * 32) << 3;
+    if ((lane + i * 32) < nvec) {
+      load8(x + base + c, v[i]);
+      if (delta != nullptr) {
+        float d[8];
+        load8(delta + base + c, d);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[i][k] += d[k];
+        // the residual stream is stored in the model dtype: normalise the
+        // rounded value so that forward and backward see the same input
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[i][k] = to_f32(from_f32<T>(v[i][k]));
+        if (s_out != nullptr) store8(s_out + base + c, v[i]);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) sum += v[i][k];
+    }
+  }
+  float mean = 0.f;
+  if (!RMS) mean = warp_sum(sum) / (float)C;
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+    if ((lane + i * 32) < nvec) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float d = v[i][k] - mean;
+        sq += d * d;
+      }
+    }
+  const float var = warp_sum(sq) / (float)C;
+  const float rstd = rsqrtf(var + eps);
+  if (lane == 0) {
+    if (mean_out != nullptr) mean_out[row] = mean;
+    rstd_out[row] = rstd;
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (lane + i * 32) << 3;
+    if ((lane + i * 32) < nvec) {
+      float wf[8], o[8];
+      load8(w + c, wf);
+      if (RMS) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = (v[i][k] * rstd) * wf[k];
+      } else {
+        float bf[8];
+        load8(b + c, bf);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = ((v[i][k] - mean) * rstd) * wf[k] + bf[k];
+      }
+      store8(y + base + c, o);
+    }
+  }
+}
+
+template <int NV>
+__device__ __forceinline__ void block_colsum(float (&acc)[NV][8], float* red, float* out, int C,
+                                             int nvec, int warp, int lane, int warps) {
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (lane + i * 32) << 3;
+    if ((lane + i * 32) < nvec)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) red[warp * C + c + k] = acc[i][k];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float t = 0.f;
+    for (int q = 0; q < warps; ++q) t += red[q * C + c];
+    out[(size_t)blockIdx.x * C + c] = t;
+  }
+  __syncthreads();
+}
+
+// Backward: one warp per row, ROWS_PER_WARP rows per warp; every lane owns
+// fixed columns and accumulates dw/db for them in registers; the block then
+// writes one partial row per block (deterministic).
+template <typename T, int NV, bool RMS>
+__global__ void __launch_bounds__(256)
+norm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ s, const T* __restrict__ w,
+                const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                const T* __restrict__ dres, T* __restrict__ dx, float* __restrict__ dw_part,
+                float* __restrict__ db_part, int M, int C, int rows_per_block) {
+  const int warps = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nvec = C >> 3;
+  float dwacc[NV][8], dbacc[NV][8];
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) dwacc[i][k] = dbacc[i][k] = 0.f;
+
+  const int row0 = blockIdx.x * rows_per_block;
+  const int row1 = min(M, row0 + rows_per_block);
+  for (int row = row0 + warp; row < row1; row += warps) {
+    const size_t base = (size_t)row * C;
+    const float mean = RMS ? 0.f : mean_in[row];
+    const float rstd = rstd_in[row];
+    float xh[NV][8], g[NV][8];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (lane + i * 32) << 3;
+      if ((lane + i * 32) < nvec) {
+        float sv[8], dyv[8], wv[8];
+        load8(s + base + c, sv);
+        load8(dy + base + c, dyv);
+        load8(w + c, wv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          xh[i][k] = (sv[k] - mean) * rstd;
+          g[i][k] = dyv[k] * wv[k];
+          s1 += g[i][k];
+          s2 += g[i][k] * xh[i][k];
+          dwacc[i][k] += dyv[k] * xh[i][k];
+          dbacc[i][k] += dyv[k];
+        }
+      }
+    }
+    s1 = warp_sum(s1) / (float)C;
+    s2 = warp_sum(s2) / (float)C;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (lane + i * 32) << 3;
+      if ((lane + i * 32) < nvec) {
+        float o[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          o[k] = RMS ? rstd * (g[i][k] - xh[i][k] * s2)
+                     : rstd * (g[i][k] - s1 - xh[i][k] * s2);
+        if (dres != nullptr) {
+          float r[8];
+          load8(dres + base + c, r);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) o[k] += r[k];
+        }
+        store8(dx + base + c, o);
+      }
+    }
+  }
+  // block reduction of the per-lane column partials through shared memory
+  extern __shared__ float red[];  // [warps][C]
+  block_colsum<NV>(dwacc, red, dw_part, C, nvec, warp, lane, warps);
+  if (!RMS) block_colsum<NV>(dbacc, red, db_part, C, nvec, warp, lane, warps);
+}
+
+// Column sums of a [M, N] matrix (row stride ld) into partials
+// [gridDim.y, N]: block (x, y) sums rows [y*rpb, (y+1)*rpb) of a 256-column
+// slab; each thread owns 8 adjacent columns (16-byte loads), each warp a row.
+template <typename T>
+__global__ void __launch_bounds__(256)
+colsum_partial_kernel(const T* __restrict__ a, float* __restrict__ part, int M, int N,
+                      long long ld, int rows_per_block) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c0 = blockIdx.x * 256 + lane * 8;
+  const int r0 = blockIdx.y * rows_per_block;
+  const int r1 = min(M, r0 + rows_per_block);
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (c0 < N) {
+    for (int r = r0 + warp; r < r1; r += 8) {
+      float f[8];
+      const T* p = a + (long long)r * ld + c0;
+      if (c0 + 8 <= N) {
+        load8(p, f);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) f[k] = (c0 + k < N) ? to_f32(p[k]) : 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] += f[k];
+    }
+  }
+  __shared__ float red[8][256 + 8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) red[warp][lane * 8 + k] = acc[k];
+  __syncthreads();
+  const int c = blockIdx.x * 256 + threadIdx.x;
+  if (c < N) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w][threadIdx.x];
+    part[(size_t)blockIdx.y * N + c] = t;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+colsum_finish_kernel(const float* __restrict__ part, int nparts, int N, T* __restrict__ out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= N) return;
+  float t = 0.f;
+  for (int p = 0; p < nparts; ++p) t += part[(size_t)p * N + c];
+  out[c] = from_f32<T>(t);
+}
+
+// ---------------------------------------------------------------- GELU
+__device__ __forceinline__ float gelu_f(float u) {
+  return 0.5f * u * (1.f + erff(u * 0.70710678118654752f));
+}
+__device__ __forceinline__ float gelu_grad_f(float u) {
+  const float cdf = 0.5f * (1.f + erff(u * 0.70710678118654752f));
+  const float pdf = expf(-0.5f * u * u) * 0.39894228040143268f;
+  return cdf + u * pdf;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+bias_gelu_fwd_kernel(T* __restrict__ u, const T* __restrict__ bias, T* __restrict__ h,
+                     long long total, int N) {
+  const long long nvec = total >> 3;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long e = i << 3;
+    const int c = (int)(e % N);
+    float f[8], bf[8], o[8];
+    load8(u + e, f);
+    if (bias != nullptr) {
+      load8(bias + c, bf);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) f[k] += bf[k];
+      store8(u + e, f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) f[k] = to_f32(from_f32<T>(f[k]));
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = gelu_f(f[k]);
+    store8(h + e, o);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+gelu_bwd_kernel(const T* __restrict__ dh, const T* __restrict__ u, T* __restrict__ du,
+                long long total) {
+  const long long nvec = total >> 3;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
+       i += (long long)gridDim.x * blockDim.x) {
+    float a[8], b[8], o[8];
+    load8(dh + (i << 3), a);
+    load8(u + (i << 3), b);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = a[k] * gelu_grad_f(b[k]);
+    store8(du + (i << 3), o);
+  }
+}
+
+// -------------------------------------------------------------- SwiGLU
+// gu = [.., 2F] with gate in [0,F) and up in [F,2F) of each row; h = silu(gate)*up
+template <typename T>
+__global__ void __launch_bounds__(256)
+swiglu_fwd_kernel(const T* __restrict__ gu, T* __restrict__ h, long long rows, int F) {
+  const long long nvec = rows * (F >> 3);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / (F >> 3);
+    const int c = (int)(i % (F >> 3)) << 3;
+    float g[8], u[8], o[8];
+    load8(gu + r * 2 * F + c, g);
+    load8(gu + r * 2 * F + F + c, u);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = (g[k] / (1.f + expf(-g[k]))) * u[k];
+    store8(h + r * F + c, o);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+swiglu_bwd_kernel(const T* __restrict__ dh, const T* __restrict__ gu, T* __restrict__ dgu,
+                  long long rows, int F) {
+  const long long nvec = rows * (F >> 3);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / (F >> 3);
+    const int c = (int)(i % (F >> 3)) << 3;
+    float d[8], g[8], u[8], dg[8], du[8];
+    load8(dh + r * F + c, d);
+    load8(gu + r * 2 * F + c, g);
+    load8(gu + r * 2 * F + F + c, u);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float sg = 1.f / (1.f + expf(-g[k]));
+      const float silu = g[k] * sg;
+      du[k] = d[k] * silu;
+      dg[k] = d[k] * u[k] * (sg * (1.f + g[k] * (1.f - sg)));
+    }
+    store8(dgu + r * 2 * F + c, dg);
+    store8(dgu + r * 2 * F + F + c, du);
+  }
+}
+
+// -------------------------------------------------------- cross entropy
+// Walk one row of V elements starting at an arbitrary 2-byte address with
+// 16-byte loads in the aligned middle.
+template <typename T, typename F>
+__device__ __forceinline__ void for_row(const T* row, int V, F&& f) {
+  const int head = (int)(((16 - (reinterpret_cast<uintptr_t>(row) & 15)) & 15) / sizeof(T));
+  const int h = min(head, V);
+  for (int i = threadIdx.x; i < h; i += blockDim.x) f(i, to_f32(row[i]));
+  const int nvec = (V - h) / 8;
+  const T* mid = row + h;
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    float v[8];
+    load8(mid + i * 8, v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) f(h + i * 8 + k, v[k]);
+  }
+  for (int i = h + nvec * 8 + threadIdx.x; i < V; i += blockDim.x) f(i, to_f32(row[i]));
+}
+
+__device__ __forceinline__ void softmax_merge(float& m, float& s, float m2, float s2) {
+  const float mx = fmaxf(m, m2);
+  if (mx == -INFINITY) return;
+  s = s * expf(m - mx) + s2 * expf(m2 - mx);
+  m = mx;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(512)
+ce_fwd_kernel(const T* __restrict__ logits, const long long* __restrict__ tgt,
+              float* __restrict__ lse_out, float* __restrict__ loss_rows, int V, long long ld,
+              long long ignore_index) {
+  const long long r = blockIdx.x;
+  const T* row = logits + r * ld;
+  float m = -INFINITY, s = 0.f;
+  for_row(row, V, [&](int, float v) {
+    if (v > m) {
+      s = s * expf(m - v) + 1.f;
+      m = v;
+    } else {
+      s += expf(v - m);
+    }
+  });
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    softmax_merge(m, s, m2, s2);
+  }
+  __shared__ float sm[32], ss[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sm[warp] = m;
+    ss[warp] = s;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    m = lane < nw ? sm[lane] : -INFINITY;
+    s = lane < nw ? ss[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      softmax_merge(m, s, m2, s2);
+    }
+    if (lane == 0) {
+      const float lse = m + logf(s);
+      lse_out[r] = lse;
+      const long long t = tgt[r];
+      // ignored (or out-of-range) targets contribute nothing
+      const bool valid = t != ignore_index && t >= 0 && t < V;
+      loss_rows[r] = valid ? lse - to_f32(row[t]) : 0.f;
+    }
+  }
+}
+
+// loss = sum(loss_rows) / count(valid); deterministic single block
+__global__ void __launch_bounds__(1024)
+ce_reduce_kernel(const float* __restrict__ loss_rows, const long long* __restrict__ tgt,
+                 long long M, int V, long long ignore_index, float* __restrict__ out_loss,
+                 float* __restrict__ out_inv_count) {
+  double acc = 0.0;
+  long long cnt = 0;
+  for (long long i = threadIdx.x; i < M; i += blockDim.x) {
+    acc += loss_rows[i];
+    cnt += tgt[i] != ignore_index && tgt[i] >= 0 && tgt[i] < V;
+  }
+  __shared__ double sa[1024];
+  __shared__ long long sc[1024];
+  sa[threadIdx.x] = acc;
+  sc[threadIdx.x] = cnt;
+  __syncthreads();
+  for (int w = 512; w > 0; w >>= 1) {
+    if (threadIdx.x < w) {
+      sa[threadIdx.x] += sa[threadIdx.x + w];
+      sc[threadIdx.x] += sc[threadIdx.x + w];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const double c = sc[0] > 0 ? (double)sc[0] : 0.0;
+    out_loss[0] = c > 0 ? (float)(sa[0] / c) : NAN;
+    out_inv_count[0] = c > 0 ? (float)(1.0 / c) : 0.f;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(512)
+ce_bwd_kernel(T* __restrict__ logits, const long long* __restrict__ tgt,
+              const float* __restrict__ lse, const float* __restrict__ grad_out,
+              const float* __restrict__ inv_count, int V, long long ld, long long ignore_index) {
+  const long long r = blockIdx.x;
+  T* row = logits + r * ld;
+  const long long t = tgt[r];
+  const float scale =
+      (t == ignore_index || t < 0 || t >= V) ? 0.f : grad_out[0] * inv_count[0];
+  const float l = lse[r];
+  const int head = (int)(((16 - (reinterpret_cast<uintptr_t>(row) & 15)) & 15) / sizeof(T));
+  const int h = min(head, V);
+  auto g = [&](int i, float v) { return (expf(v - l) - (i == t ? 1.f : 0.f)) * scale; };
+  for (int i = threadIdx.x; i < h; i += blockDim.x) row[i] = from_f32<T>(g(i, to_f32(row[i])));
+  const int nvec = (V - h) / 8;
+  T* mid = row + h;
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    float v[8];
+    load8(mid + i * 8, v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = g(h + i * 8 + k, v[k]);
+    store8(mid + i * 8, v);
+  }
+  for (int i = h + nvec * 8 + threadIdx.x; i < V; i += blockDim.x)
+    row[i] = from_f32<T>(g(i, to_f32(row[i])));
+}
+
+// ------------------------------------------------------------ embedding
+template <typename T>
+__global__ void __launch_bounds__(256)
+embedding_fwd_kernel(const long long* __restrict__ idx, const T* __restrict__ wte,
+                     const T* __restrict__ wpe, T* __restrict__ out, long long M, int T_len,
+                     int C, long long V) {
+  const int nvec = C >> 3;
+  const long long total = M * nvec;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long m = i / nvec;
+    const int c = (int)(i % nvec) << 3;
+    const long long tok = idx[m];
+    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (tok >= 0 && tok < V) load8(wte + tok * C + c, a);
+    if (wpe != nullptr) {
+      float b[8];
+      load8(wpe + (long long)(m % T_len) * C + c, b);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) a[k] += b[k];
+    }
+    store8(out + m * C + c, a);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+embedding_bwd_kernel(const T* __restrict__ dout, const long long* __restrict__ idx,
+                     float* __restrict__ dwte, float* __restrict__ dwpe, long long M,
+                     int T_len, int C, long long V) {
+  const int nvec = C >> 3;
+  const long long total = M * nvec;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long m = i / nvec;
+    const int c = (int)(i % nvec) << 3;
+    float a[8];
+    load8(dout + m * C + c, a);
+    const long long tok = idx[m];
+    if (tok >= 0 && tok < V) {
+      float* te = dwte + tok * C + c;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) atomicAdd(te + k, a[k]);
+    }
+    if (dwpe != nullptr) {
+      float* pe = dwpe + (long long)(m % T_len) * C + c;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) atomicAdd(pe + k, a[k]);
+    }
+  }
+}
+
+// ----------------------------------------------------------------- RoPE
+// x: [B, T, H, D] viewed with row stride `row_stride` elements between
+// consecutive (b, t); rotates pairs (i, i + D/2) (the "rotate_half" form).
+template <typename T>
+__global__ void __launch_bounds__(256)
+rope_kernel(T* __restrict__ x, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+            long long BT, int T_len, int H, int D, long long row_stride, int inverse) {
+  const int half = D >> 1;
+  const long long total = BT * H * half;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int j = (int)(i % half);
+    const long long hb = i / half;
+    const int h = (int)(hb % H);
+    const long long bt = hb / H;
+    const int t = (int)(bt % T_len);
+    T* p = x + bt * row_stride + (long long)h * D;
+    const float c = cos_t[(size_t)t * half + j];
+    const float s = inverse ? -sin_t[(size_t)t * half + j] : sin_t[(size_t)t * half + j];
+    const float a = to_f32(p[j]), b = to_f32(p[j + half]);
+    p[j] = from_f32<T>(a * c - b * s);
+    p[j + half] = from_f32<T>(b * c + a * s);
+  }
+}
+
+}  // namespace
+
+// =============================================================== host API
+template <typename T, int NVV>
+static void launch_norm_fwd(const void* x, const void* delta, const void* w, const void* b,
+                            void* s_out, void* y, float* mean, float* rstd, int M, int C,
+                            float eps, bool rms, int blocks, cudaStream_t st) {
+  if (rms)
+    add_norm_fwd_kernel<T, NVV, true><<<blocks, 256, 0, st>>>(
+        (const T*)x, (const T*)delta, (const T*)w, (const T*)b, (T*)s_out, (T*)y, mean, rstd, M,
+        C, eps);
+  else
+    add_norm_fwd_kernel<T, NVV, false><<<blocks, 256, 0, st>>>(
+        (const T*)x, (const T*)delta, (const T*)w, (const T*)b, (T*)s_out, (T*)y, mean, rstd, M,
+        C, eps);
+}
+
+void add_norm_fwd(const void* x, const void* delta, const void* w, const void* b, void* s_out,
+                  void* y, float* mean, float* rstd, int M, int C, float eps, bool rms,
+                  int dtype, cudaStream_t st) {
+  const int nv = (C / 8 + 31) / 32;
+  const int blocks = (M + 7) / 8;
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    if (nv <= 1) launch_norm_fwd<T, 1>(x, delta, w, b, s_out, y, mean, rstd, M, C, eps, rms, blocks, st);
+    else if (nv <= 2) launch_norm_fwd<T, 2>(x, delta, w, b, s_out, y, mean, rstd, M, C, eps, rms, blocks, st);
+    else if (nv <= 3) launch_norm_fwd<T, 3>(x, delta, w, b, s_out, y, mean, rstd, M, C, eps, rms, blocks, st);
+    else if (nv <= 4) launch_norm_fwd<T, 4>(x, delta, w, b, s_out, y, mean, rstd, M, C, eps, rms, blocks, st);
+    else if (nv <= 8) launch_norm_fwd<T, 8>(x, delta, w, b, s_out, y, mean, rstd, M, C, eps, rms, blocks, st);
+    else if (nv <= 16) launch_norm_fwd<T, 16>(x, delta, w, b, s_out, y, mean, rstd, M, C, eps, rms, blocks, st);
+    else throw std::runtime_error("norm: hidden size too large");
+  });
+  MSB_CHECK_LAUNCH("add_norm_fwd");
+}
+
+template <typename T, int NVV>
+static void launch_norm_bwd(const void* dy, const void* s, const void* w, const float* mean,
+                            const float* rstd, const void* dres, void* dx, float* dw_part,
+                            float* db_part, int M, int C, bool rms, int blocks, int rpb,
+                            size_t smem, cudaStream_t st) {
+  auto kern = rms ? norm_bwd_kernel<T, NVV, true> : norm_bwd_kernel<T, NVV, false>;
+  check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+             "norm_bwd smem");
+  kern<<<blocks, 256, smem, st>>>((const T*)dy, (const T*)s, (const T*)w, mean, rstd,
+                                  (const T*)dres, (T*)dx, dw_part, db_part, M, C, rpb);
+}
+
+int norm_bwd(const void* dy, const void* s, const void* w, const float* mean, const float* rstd,
+             const void* dres, void* dx, float* dw_part, float* db_part, int M, int C, bool rms,
+             int dtype, int max_blocks, cudaStream_t st) {
+  const int nv = (C / 8 + 31) / 32;
+  const int warps = 8;
+  int blocks = min(max_blocks, (M + warps - 1) / warps);
+  if (blocks < 1) blocks = 1;
+  const int rpb = (M + blocks - 1) / blocks;
+  blocks = (M + rpb - 1) / rpb;
+  const size_t smem = (size_t)warps * C * sizeof(float);
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    if (nv <= 1) launch_norm_bwd<T, 1>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, blocks, rpb, smem, st);
+    else if (nv <= 2) launch_norm_bwd<T, 2>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, blocks, rpb, smem, st);
+    else if (nv <= 3) launch_norm_bwd<T, 3>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, blocks, rpb, smem, st);
+    else if (nv <= 4) launch_norm_bwd<T, 4>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, blocks, rpb, smem, st);
+    else if (nv <= 8) launch_norm_bwd<T, 8>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, blocks, rpb, smem, st);
+    else if (nv <= 16) launch_norm_bwd<T, 16>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, blocks, rpb, smem, st);
+    else throw std::runtime_error("norm_bwd: hidden size too large");
+  });
+  MSB_CHECK_LAUNCH("norm_bwd");
+  return blocks;
+}
+
+int colsum_partial(const void* a, float* part, int M, int N, long long ld, int dtype,
+                   int max_chunks, cudaStream_t st) {
+  int chunks = min(max_chunks, max(1, (M + 63) / 64));
+  const int rpb = (M + chunks - 1) / chunks;
+  chunks = (M + rpb - 1) / rpb;
+  dim3 grid((N + 255) / 256, chunks);
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    colsum_partial_kernel<T><<<grid, 256, 0, st>>>((const T*)a, part, M, N, ld, rpb);
+  });
+  MSB_CHECK_LAUNCH("colsum_partial");
+  return chunks;
+}
+
+void colsum_finish(const float* part, int nparts, int N, void* out, int dtype, cudaStream_t st) {
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    colsum_finish_kernel<T><<<(N + 255) / 256, 256, 0, st>>>(part, nparts, N, (T*)out);
+  });
+  MSB_CHECK_LAUNCH("colsum_finish");
+}
+
+void bias_gelu_fwd(void* u, const void* bias, void* h, long long total, int N, int dtype,
+                   cudaStream_t st) {
+  const int blocks = grid_for(total / 8, 256, kNumSMs * 16);
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    bias_gelu_fwd_kernel<T><<<blocks, 256, 0, st>>>((T*)u, (const T*)bias, (T*)h, total, N);
+  });
+  MSB_CHECK_LAUNCH("bias_gelu_fwd");
+}
+
+void gelu_bwd(const void* dh, const void* u, void* du, long long total, int dtype,
+              cudaStream_t st) {
+  const int blocks = grid_for(total / 8, 256, kNumSMs * 16);
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    gelu_bwd_kernel<T><<<blocks, 256, 0, st>>>((const T*)dh, (const T*)u, (T*)du, total);
+  });
+  MSB_CHECK_LAUNCH("gelu_bwd");
+}
+
+void swiglu_fwd(const void* gu, void* h, long long rows, int F, int dtype, cudaStream_t st) {
+  const int blocks = grid_for(rows * (F / 8), 256, kNumSMs * 16);
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    swiglu_fwd_kernel<T><<<blocks, 256, 0, st>>>((const T*)gu, (T*)h, rows, F);
+  });
+  MSB_CHECK_LAUNCH("swiglu_fwd");
+}
+
+void swiglu_bwd(const void* dh, const void* gu, void* dgu, long long rows, int F, int dtype,
+                cudaStream_t st) {
+  const int blocks = grid_for(rows * (F / 8), 256, kNumSMs * 16);
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    swiglu_bwd_kernel<T><<<blocks, 256, 0, st>>>((const T*)dh, (const T*)gu, (T*)dgu, rows, F);
+  });
+  MSB_CHECK_LAUNCH("swiglu_bwd");
+}
+
+void cross_entropy_fwd(const void* logits, const long long* tgt, float* lse, float* loss_rows,
+                       float* loss, float* inv_count, long long M, int V, long long ld,
+                       long long ignore_index, int dtype, cudaStream_t st) {
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    ce_fwd_kernel<T><<<(unsigned)M, 512, 0, st>>>((const T*)logits, tgt, lse, loss_rows, V, ld,
+                                                 ignore_index);
+  });
+  MSB_CHECK_LAUNCH("ce_fwd");
+  ce_reduce_kernel<<<1, 1024, 0, st>>>(loss_rows, tgt, M, V, ignore_index, loss, inv_count);
+  MSB_CHECK_LAUNCH("ce_reduce");
+}
+
+void cross_entropy_bwd(void* logits, const long long* tgt, const float* lse,
+                       const float* grad_out, const float* inv_count, long long M, int V,
+                       long long ld, long long ignore_index, int dtype, cudaStream_t st) {
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    ce_bwd_kernel<T><<<(unsigned)M, 512, 0, st>>>((T*)logits, tgt, lse, grad_out, inv_count, V,
+                                                 ld, ignore_index);
+  });
+  MSB_CHECK_LAUNCH("ce_bwd");
+}
+
+void embedding_fwd(const long long* idx, const void* wte, const void* wpe, void* out, long long M,
+                   int T_len, int C, long long V, int dtype, cudaStream_t st) {
+  const int blocks = grid_for(M * (C / 8), 256, kNumSMs * 16);
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    embedding_fwd_kernel<T><<<blocks, 256, 0, st>>>(idx, (const T*)wte, (const T*)wpe, (T*)out,
+                                                    M, T_len, C, V);
+  });
+  MSB_CHECK_LAUNCH("embedding_fwd");
+}
+
+void embedding_bwd(const void* dout, const long long* idx, float* dwte, float* dwpe, long long M,
+                   int T_len, int C, long long V, int dtype, cudaStream_t st) {
+  const int blocks = grid_for(M * (C / 8), 256, kNumSMs * 16);
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    embedding_bwd_kernel<T><<<blocks, 256, 0, st>>>((const T*)dout, idx, dwte, dwpe, M, T_len,
+                                                    C, V);
+  });
+  MSB_CHECK_LAUNCH("embedding_bwd");
+}
+
+void rope(void* x, const float* cos_t, const float* sin_t, long long BT, int T_len, int H, int D,
+          long long row_stride, bool inverse, int dtype, cudaStream_t st) {
+  const int blocks = grid_for(BT * H * (D / 2), 256, kNumSMs * 16);
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    rope_kernel<T><<<blocks, 256, 0, st>>>((T*)x, cos_t, sin_t, BT, T_len, H, D, row_stride,
+                                           inverse ? 1 : 0);
+  });
+  MSB_CHECK_LAUNCH("rope");
+}
+
+}  // namespace msb

@@ -1,0 +1,112 @@
+"""GEMM entry points of the linear layers.
+
+Three products per linear layer, all with 16-bit operands and fp32
+accumulation:
+
+* ``linear_fwd``   y[M,N]  = x[M,K] @ W[N,K]^T (+ b)   both operands K-major
+* ``linear_dgrad`` dx[M,K] = dy[M,N] @ W[N,K]           W is N-major
+* ``linear_wgrad`` dW[N,K] = dy[M,N]^T @ x[M,K]         both M-major
+
+On CUDA they run the tcgen05/TMEM kernel of ``csrc/gemm_tcgen05.cu``
+(TMA-fed shared-memory ring, accumulators in tensor memory, epilogue with
+bias / accumulate, split-K for small outputs).  TMA needs 16-byte aligned
+operand bases and row strides; an operand that is not (e.g. a parameter view
+at an odd arena offset) is copied into an aligned buffer first.
+``MSB_GEMM=torch`` selects the library product instead (comparison baseline
+in the GEMM tests and benchmarks).
+
+Each launch carries a device error word; kernels whose bounded waits time
+out set it and return.  :func:`check` reads it (one host sync) and raises.
+"""
+
+from __future__ import annotations
+
+import os
+from typing import Dict, Optional
+
+import torch
+
+from . import _ext
+
+_MODE = os.environ.get("MSB_GEMM", "auto")
+TIMEOUT_S = float(os.environ.get("MSB_KERNEL_TIMEOUT_S", "2.0"))
+_ERR: Dict[int, torch.Tensor] = {}
+
+
+class KernelTimeoutError(RuntimeError):
+    """A device-side bounded wait expired (the kernel returned early)."""
+
+
+def error_word(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _ERR.get(idx)
+    if t is None:
+        t = _ERR[idx] = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", idx))
+    return t
+
+
+def check(device: Optional[torch.device] = None) -> None:
+    """Raise :class:`KernelTimeoutError` if any GEMM on ``device`` timed out."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    w = error_word(dev)
+    code = int(w[0].item())
+    if code:
+        w.zero_()
+        raise KernelTimeoutError(f"tcgen05 gemm wait expired (code {code})")
+
+
+def native_enabled() -> bool:
+    return _MODE != "torch" and _ext.available() and hasattr(_ext.get(), "gemm")
+
+
+def _tma_ready(t: torch.Tensor) -> torch.Tensor:
+    """Row-major view whose base and row stride are 16-byte aligned."""
+    ok = (t.stride(-1) == 1 and t.data_ptr() % 16 == 0 and (t.stride(0) * t.element_size()) % 16 == 0
+          and t.stride(0) >= t.shape[1])
+    if ok:
+        return t
+    rows, cols = t.shape
+    ld = -(-cols // 8) * 8
+    buf = torch.empty(rows, ld, dtype=t.dtype, device=t.device)[:, :cols]
+    buf.copy_(t)
+    return buf
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, *, a_kmajor: bool, b_kmajor: bool,
+         bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+         accumulate: bool = False) -> torch.Tensor:
+    """C[M,N] (+)= A @ B^T (+ bias) in the tcgen05 operand convention.
+
+    ``a`` holds A as [M,K] (``a_kmajor``) or [K,M]; ``b`` holds B as [N,K]
+    (``b_kmajor``) or [K,N]."""
+    M = a.shape[0] if a_kmajor else a.shape[1]
+    N = b.shape[0] if b_kmajor else b.shape[1]
+    if out is None:
+        out = torch.empty(M, N, dtype=a.dtype, device=a.device)
+    if a.is_cuda and a.dtype in (torch.float16, torch.bfloat16) and native_enabled():
+        _ext.get().gemm(_tma_ready(a), _tma_ready(b), a_kmajor, b_kmajor, bias, out,
+                        accumulate, error_word(a.device), TIMEOUT_S)
+        return out
+    A = a if a_kmajor else a.t()
+    B = b.t() if b_kmajor else b
+    if accumulate:
+        out.add_(A @ B)
+    elif bias is not None:
+        torch.addmm(bias, A, B, out=out)
+    else:
+        torch.mm(A, B, out=out)
+    return out
+
+
+def linear_fwd(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    return gemm(x, w, a_kmajor=True, b_kmajor=True, bias=bias, out=out)
+
+
+def linear_dgrad(dy: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    return gemm(dy, w, a_kmajor=True, b_kmajor=False)
+
+
+def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, out: Optional[torch.Tensor] = None,
+                 accumulate: bool = False) -> torch.Tensor:
+    return gemm(dy, x, a_kmajor=False, b_kmajor=False, out=out, accumulate=accumulate)

@@ -1,0 +1,106 @@
+"""Engine behaviour on one GPU: fp16 loss scaling, inf/nan skip, the fused
+step pipeline against the CPU pipeline, and the GPT model."""
+
+import pytest
+import torch
+
+import minispeed_b200 as ms
+from minispeed_b200.models import GPT, GPTConfig, init_gpt2_
+from tests.helpers import config, make_data, make_net, mse, run
+
+pytestmark = pytest.mark.gpu
+STEPS, GAS, MICRO = 6, 2, 4
+
+
+def test_fp16_trains_and_scale_grows():
+    x, y = make_data(STEPS, GAS, 1, MICRO, device="cuda")
+    model = make_net(device="cuda")
+    engine = ms.initialize(model=model, config=config(micro=MICRO, gas=GAS, dtype="fp16",
+                                                      scale_power=4, window=3, lr=1e-2))
+    losses = run(engine, x, y, STEPS, GAS, device="cuda")
+    assert all(map(lambda v: v == v, losses)) and losses[-1] < losses[0]
+    assert next(model.parameters()).dtype == torch.float16
+    assert engine.flat_groups[0].data.dtype == torch.float32
+    assert engine.get_loss_scale() > 16.0
+    assert engine.loss_scaler.skipped_steps == 0
+    assert engine.grad_norm is not None and engine.grad_norm > 0
+
+
+def test_forced_inf_skips_step_everything_untouched():
+    x, y = make_data(STEPS, GAS, 1, MICRO, device="cuda")
+    model = make_net(device="cuda")
+    engine = ms.initialize(model=model, config=config(
+        micro=MICRO, gas=GAS, dtype="fp16", scale_power=6, lr=1e-2, warmup=5))
+    run(engine, x, y, 1, GAS, device="cuda")
+    for m in range(GAS):
+        engine.backward(mse(engine(x[1, m]), y[1, m]))
+    next(p for p in model.parameters()).grad.view(-1)[0] = float("inf")
+    before = {n: p.detach().clone() for n, p in model.named_parameters()}
+    masters = engine.flat_groups[0].data.clone()
+    state = engine.optimizer.state[0]["exp_avg"].clone()
+    steps, scale, lr = engine.global_steps, engine.get_loss_scale(), \
+        engine.lr_scheduler.get_last_lr()
+    assert engine.step() is False
+    assert engine.global_steps == steps and engine.skipped_steps == 1
+    assert engine.get_loss_scale() == scale / 2
+    assert engine.lr_scheduler.get_last_lr() == lr
+    for n, p in model.named_parameters():
+        assert torch.equal(p, before[n])
+    assert torch.equal(engine.flat_groups[0].data, masters)
+    assert torch.equal(engine.optimizer.state[0]["exp_avg"], state)
+    losses = run(engine, x[2:], y[2:], 2, GAS, device="cuda")
+    assert all(v == v for v in losses) and engine.global_steps == steps + 2
+
+
+@pytest.mark.parametrize("stage", [0, 1, 2, 3])
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+def test_gpu_pipeline_matches_cpu_pipeline(stage, dtype, monkeypatch):
+    x, y = make_data(STEPS, GAS, 1, MICRO)
+    cfg = config(micro=MICRO, gas=GAS, dtype=dtype, stage=stage, clip=0.05)
+    monkeypatch.setenv("MINISPEED_DEVICE", "cpu")
+    cpu = ms.initialize(model=make_net(), config=cfg)
+    lc = run(cpu, x, y, STEPS, GAS)
+    monkeypatch.setenv("MINISPEED_DEVICE", "cuda:0")
+    gpu = ms.initialize(model=make_net(), config=cfg)
+    lg = run(gpu, x, y, STEPS, GAS, device="cuda")
+    tol = 1e-4 if dtype == "fp32" else 2e-2
+    torch.testing.assert_close(torch.tensor(lg), torch.tensor(lc), rtol=tol, atol=tol)
+    assert gpu.grad_norm == pytest.approx(cpu.grad_norm, rel=1e-3 if dtype == "fp32" else 5e-2)
+    pc, pg = cpu.state_dict(), gpu.state_dict()
+    for k in pc:
+        torch.testing.assert_close(pg[k].cpu().float(), pc[k].float(), rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+def test_gpt_trains_on_gpu(dtype):
+    torch.manual_seed(0)
+    cfg = GPTConfig(vocab_size=1000, block_size=128, n_layer=2, n_head=4, n_embd=128)
+    model = init_gpt2_(GPT(cfg))
+    engine = ms.initialize(model=model, config={
+        "train_micro_batch_size_per_gpu": 4, "gradient_accumulation_steps": 1,
+        "gradient_clipping": 1.0, "dtype": dtype,
+        "fp16": {"enabled": dtype == "fp16", "initial_scale_power": 12},
+        "zero_optimization": {"stage": 2},
+        "optimizer": {"type": "AdamW", "params": {"lr": 3e-3}}})
+    data = torch.randint(0, 1000, (4, 129), device="cuda")
+    losses = []
+    for _ in range(15):
+        loss = engine(data[:, :-1], targets=data[:, 1:])
+        engine.backward(loss)
+        engine.step()
+        losses.append(float(loss))
+    assert losses[-1] < losses[0] - 1.0, losses
+
+
+def test_gpt_matches_cpu_fp32_forward():
+    torch.manual_seed(0)
+    cfg = GPTConfig(vocab_size=512, block_size=64, n_layer=2, n_head=4, n_embd=128)
+    cpu = init_gpt2_(GPT(cfg))
+    gpu = GPT(cfg).cuda()
+    gpu.load_state_dict(cpu.state_dict())
+    gpu.half()
+    idx = torch.randint(0, 512, (2, 64))
+    tgt = torch.roll(idx, -1, 1)
+    lc = cpu(idx, targets=tgt)
+    lg = gpu(idx.cuda(), targets=tgt.cuda())
+    assert float(lg) == pytest.approx(float(lc), rel=2e-3)

@@ -1,0 +1,98 @@
+"""tcgen05 GEMM numerics against an fp32 PyTorch product."""
+
+import pytest
+import torch
+
+from minispeed_b200.ops import _ext, gemm
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(A, B, bias=None):
+    r = A.float() @ B.float().t()
+    if bias is not None:
+        r = r + bias.float()
+    return r
+
+
+def _check(out, ref, K):
+    # fp32 accumulation; the only rounding is the final 16-bit cast
+    scale = ref.abs().max().item() + 1e-6
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 1e-2 * scale + 1e-3, (err, scale, K)
+
+
+@pytest.fixture(autouse=True)
+def _native():
+    assert gemm.native_enabled(), "tcgen05 gemm must be built"
+    yield
+    gemm.check()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("a_k,b_k", [(True, True), (True, False), (False, False), (False, True)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 192), (300, 200, 130),
+                                   (1000, 768, 768)])
+def test_gemm_majors(dtype, a_k, b_k, M, N, K):
+    torch.manual_seed(M + N + K)
+    A = torch.randn(M, K, device="cuda").to(dtype)
+    B = torch.randn(N, K, device="cuda").to(dtype)
+    a = A if a_k else A.t().contiguous()
+    b = B if b_k else B.t().contiguous()
+    out = gemm.gemm(a, b, a_kmajor=a_k, b_kmajor=b_k)
+    torch.cuda.synchronize()
+    _check(out, _ref(A, B), K)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_gemm_bias_and_padded_output(dtype):
+    M, N, K = 513, 1001, 256
+    A = torch.randn(M, K, device="cuda").to(dtype)
+    B = torch.randn(N, K, device="cuda").to(dtype)
+    bias = torch.randn(N, device="cuda").to(dtype)
+    buf = torch.full((M, 1024), 7.0, device="cuda", dtype=dtype)
+    out = buf[:, :N]
+    gemm.gemm(A, B, a_kmajor=True, b_kmajor=True, bias=bias, out=out)
+    _check(out, _ref(A, B, bias), K)
+    assert torch.all(buf[:, N:] == 7.0)  # padding untouched
+
+
+@pytest.mark.parametrize("M,N,K", [(2304, 768, 16384), (768, 3072, 4096), (64, 64, 8192)])
+def test_gemm_wgrad_shapes_split_k(M, N, K):
+    """dW = dY^T X with both operands M-major and a long reduction (split-K)."""
+    dy = (torch.randn(K, M, device="cuda") * 0.1).half()
+    x = (torch.randn(K, N, device="cuda") * 0.1).half()
+    plan = _ext.get().gemm_plan(M, N, K)
+    out = gemm.gemm(dy, x, a_kmajor=False, b_kmajor=False)
+    _check(out, dy.float().t() @ x.float(), K)
+    assert plan[0] in (128, 256)
+
+
+def test_gemm_accumulate():
+    M, N, K = 640, 384, 512
+    A = torch.randn(M, K, device="cuda").half()
+    B = torch.randn(N, K, device="cuda").half()
+    C0 = torch.randn(M, N, device="cuda").half()
+    out = C0.clone()
+    gemm.gemm(A, B, a_kmajor=True, b_kmajor=True, out=out, accumulate=True)
+    _check(out, _ref(A, B) + C0.float(), K)
+
+
+def test_gemm_unaligned_operand_is_copied():
+    W = torch.randn(777 * 65 + 3, device="cuda").half()
+    w = W[3:].view(777, 65)[:, :64]   # odd base offset and odd row stride
+    x = torch.randn(200, 64, device="cuda").half()
+    out = gemm.gemm(x, w, a_kmajor=True, b_kmajor=True)
+    _check(out, _ref(x, w), 64)
+
+
+def test_gpt2_shapes_match_library():
+    """The GPT-2-small training shapes, fwd/dgrad/wgrad, against fp32."""
+    Mt, C = 4096, 768
+    for N, K in ((2304, C), (C, C), (4 * C, C), (C, 4 * C)):
+        x = (torch.randn(Mt, K, device="cuda") * 0.5).half()
+        w = (torch.randn(N, K, device="cuda") * 0.05).half()
+        dy = (torch.randn(Mt, N, device="cuda") * 0.5).half()
+        _check(gemm.linear_fwd(x, w, None), _ref(x, w), K)
+        _check(gemm.linear_dgrad(dy, w), dy.float() @ w.float(), N)
+        _check(gemm.linear_wgrad(dy, x), dy.float().t() @ x.float(), Mt)
