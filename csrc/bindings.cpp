@@ -160,10 +160,21 @@ int64_t colsum_partial(const at::Tensor& a, const at::Tensor& part, int64_t max_
                              dtype_code(a), (int)max_chunks, stream_of(a));
 }
 
-void colsum_finish(const at::Tensor& part, int64_t nparts, const at::Tensor& out) {
+void colsum_finish(const at::Tensor& part, int64_t nparts, const at::Tensor& out,
+                   bool accumulate) {
+  check_cuda_contig(out, "out");
   c10::cuda::CUDAGuard g(out.device());
   msb::colsum_finish(part.data_ptr<float>(), (int)nparts, (int)out.numel(), out.data_ptr(),
-                     dtype_code(out), stream_of(out));
+                     dtype_code(out), accumulate ? 1 : 0, stream_of(out));
+}
+
+void accum_cast(const at::Tensor& src, const at::Tensor& dst, bool accumulate) {
+  check_cuda_contig(src, "src");
+  check_cuda_contig(dst, "dst");
+  TORCH_CHECK(src.scalar_type() == at::kFloat && src.numel() == dst.numel());
+  c10::cuda::CUDAGuard g(dst.device());
+  msb::accum_cast(src.data_ptr<float>(), dst.data_ptr(), dst.numel(), dtype_code(dst),
+                  accumulate ? 1 : 0, stream_of(dst));
 }
 
 void bias_gelu_fwd(const at::Tensor& u, const OptT& bias, const at::Tensor& h) {
@@ -262,7 +273,7 @@ void rope(const at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t,
 // (b_kmajor) or [K,N]; every matrix row-major with unit column stride.
 void gemm(const at::Tensor& a, const at::Tensor& b, bool a_kmajor, bool b_kmajor,
           const OptT& bias, const at::Tensor& out, bool accumulate, const at::Tensor& err,
-          double timeout_s) {
+          double timeout_s, int64_t mode, const OptT& aux) {
   check_rows(a, "A");
   check_rows(b, "B");
   check_rows(out, "C");
@@ -280,14 +291,26 @@ void gemm(const at::Tensor& a, const at::Tensor& b, bool a_kmajor, bool b_kmajor
   if (bias.has_value() && bias->defined()) {
     TORCH_CHECK(bias->numel() == N && bias->scalar_type() == a.scalar_type(), "bias mismatch");
   }
+  TORCH_CHECK(mode >= 0 && mode <= 2, "gemm epilogue mode must be 0, 1 or 2");
+  void* auxp = nullptr;
+  int64_t ld_aux = 0;
+  if (mode != 0) {
+    TORCH_CHECK(aux.has_value() && aux->defined(), "gemm epilogue mode needs aux");
+    check_rows(*aux, "aux");
+    TORCH_CHECK(aux->size(0) == M && aux->size(1) == N && aux->scalar_type() == a.scalar_type());
+    auxp = aux->data_ptr();
+    ld_aux = aux->stride(0);
+    TORCH_CHECK(!accumulate, "gemm epilogue modes do not accumulate");
+  }
   c10::cuda::CUDAGuard g(a.device());
   int bn = 0, splits = 1;
-  const long long need = msb::gemm_plan((int)M, (int)N, (int)K, 148, &bn, &splits);
+  long long need = msb::gemm_plan((int)M, (int)N, (int)K, 148, &bn, &splits);
+  if (mode != 0) need = 0;
   at::Tensor ws;
   if (need > 0) ws = at::empty({need}, a.options().dtype(at::kFloat));
   msb::gemm_tcgen05(a.data_ptr(), a.stride(0), a_kmajor ? 0 : 1, b.data_ptr(), b.stride(0),
                     b_kmajor ? 0 : 1, out.data_ptr(), out.stride(0), optr(bias), (int)M, (int)N,
-                    (int)K, dtype_code(a), accumulate ? 1 : 0,
+                    (int)K, dtype_code(a), accumulate ? 1 : 0, (int)mode, auxp, ld_aux,
                     need > 0 ? ws.data_ptr<float>() : nullptr, need,
                     reinterpret_cast<unsigned*>(err.data_ptr<int>()), timeout_s, stream_of(a));
 }
@@ -312,6 +335,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, mod) {
   mod.def("norm_bwd", &norm_bwd);
   mod.def("colsum_partial", &colsum_partial);
   mod.def("colsum_finish", &colsum_finish);
+  mod.def("accum_cast", &accum_cast);
   mod.def("bias_gelu_fwd", &bias_gelu_fwd);
   mod.def("gelu_bwd", &gelu_bwd);
   mod.def("swiglu_fwd", &swiglu_fwd);

@@ -66,6 +66,16 @@ __device__ __forceinline__ unsigned warp_or(unsigned v) {
   return v;
 }
 
+// exact (erf) GELU and its derivative, as torch.nn.GELU()
+__device__ __forceinline__ float gelu_f(float u) {
+  return 0.5f * u * (1.f + erff(u * 0.70710678118654752f));
+}
+__device__ __forceinline__ float gelu_grad_f(float u) {
+  const float cdf = 0.5f * (1.f + erff(u * 0.70710678118654752f));
+  const float pdf = expf(-0.5f * u * u) * 0.39894228040143268f;
+  return cdf + u * pdf;
+}
+
 // Dispatch a functor over the three float dtypes.
 #define MSB_DISPATCH_FLOAT(code, T, ...)                                      \
   switch (code) {                                                             \

@@ -30,6 +30,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <string>
 
 #include "common.cuh"
@@ -40,7 +41,8 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 x 16-bit = 128 bytes = one swizzle row
 constexpr int STAGES = 4;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two warps per TMEM lane quarter
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 struct Params {
   int M, N, K;
@@ -54,6 +56,13 @@ struct Params {
   float* ws;         // [splits][M][N] fp32 when splits > 1
   int a_mn, b_mn;    // 1 = MN-major operand
   int accumulate;    // C += result
+  int c_vec;         // C base and row stride allow 16-byte stores
+  int ws_vec;        // workspace rows allow 16-byte stores
+  int nfast;         // tile order: 1 = all N tiles of an M block back to back
+  int mode;          // 0 plain, 1 bias+GELU (C = u, aux = gelu(u)), 2 C = acc * gelu'(aux)
+  void* aux;         // second output (mode 1) or input (mode 2), row stride ld_aux
+  long long ld_aux;
+  int aux_vec;
   uint32_t idesc;
   unsigned* err;
   unsigned long long timeout_ns;
@@ -194,54 +203,110 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile
   }
 }
 
-template <int BN>
+template <int BN, int TM = BM>
 __device__ __forceinline__ void unit_coords(const Params& p, int u, int& m0, int& n0, int& kb0,
                                             int& kb1, int& split) {
   const int tiles = p.tiles_m * p.tiles_n;
   split = u / tiles;
   const int t = u - split * tiles;
-  m0 = (t % p.tiles_m) * BM;
-  n0 = (t / p.tiles_m) * BN;
+  // Walk along the operand that is re-read less: with nfast the CTAs that run
+  // together share one row block of A (the larger operand) through L2.
+  if (p.nfast) {
+    m0 = (t / p.tiles_n) * TM;
+    n0 = (t % p.tiles_n) * BN;
+  } else {
+    m0 = (t % p.tiles_m) * TM;
+    n0 = (t / p.tiles_m) * BN;
+  }
   kb0 = split * p.kb_per_split;
   kb1 = min(p.kb_total, kb0 + p.kb_per_split);
 }
 
+// 32 consecutive values of one row, 16-byte accesses when `vec`
 template <typename T>
-__device__ __forceinline__ void store_row_chunk(const Params& p, int row, int col, const float* v,
-                                                int nvalid) {
-  T* c = static_cast<T*>(p.C) + (long long)row * p.ldc + col;
-  const T* bias = static_cast<const T*>(p.bias);
-  float o[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    float x = v[j];
-    if (bias != nullptr && j < nvalid) x += to_f32(bias[col + j]);
-    o[j] = x;
-  }
-  const bool vec = nvalid == 32 && (reinterpret_cast<uintptr_t>(c) & 15) == 0;
-  if (vec) {
+__device__ __forceinline__ void store32(T* c, bool vec, const float (&v)[32], int nvalid,
+                                        int accumulate) {
+  if (nvalid == 32 && vec) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       uint4 pack;
       T* h = reinterpret_cast<T*>(&pack);
-      if (p.accumulate) {
-        uint4 old = *reinterpret_cast<const uint4*>(c + q * 8);
+      if (accumulate) {
+        const uint4 old = *reinterpret_cast<const uint4*>(c + q * 8);
         const T* oh = reinterpret_cast<const T*>(&old);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) h[j] = from_f32<T>(o[q * 8 + j] + to_f32(oh[j]));
+        for (int j = 0; j < 8; ++j) h[j] = from_f32<T>(v[q * 8 + j] + to_f32(oh[j]));
       } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) h[j] = from_f32<T>(o[q * 8 + j]);
+        for (int j = 0; j < 8; ++j) h[j] = from_f32<T>(v[q * 8 + j]);
       }
       *reinterpret_cast<uint4*>(c + q * 8) = pack;
     }
-  } else {
-    for (int j = 0; j < nvalid; ++j) {
-      float x = o[j];
-      if (p.accumulate) x += to_f32(c[j]);
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j < nvalid) {
+      float x = v[j];
+      if (accumulate) x += to_f32(c[j]);
       c[j] = from_f32<T>(x);
     }
   }
+}
+
+template <typename T>
+__device__ __forceinline__ void load32(const T* a, bool vec, float (&v)[32], int nvalid) {
+  if (nvalid == 32 && vec) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 pack = *reinterpret_cast<const uint4*>(a + q * 8);
+      const T* h = reinterpret_cast<const T*>(&pack);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[q * 8 + j] = to_f32(h[j]);
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = j < nvalid ? to_f32(a[j]) : 0.f;
+}
+
+// Epilogue of one 32-column chunk of an output row (v = acc + bias).
+template <typename T>
+__device__ __forceinline__ void store_chunk(const Params& p, int row, int col, float (&v)[32],
+                                            int nvalid) {
+  T* c = static_cast<T*>(p.C) + (long long)row * p.ldc + col;
+  if (p.mode == 1) {
+    // pre-activation u is stored in the model dtype; GELU sees the rounded u
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = to_f32(from_f32<T>(v[j]));
+    store32<T>(c, p.c_vec, v, nvalid, 0);
+    float h[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) h[j] = gelu_f(v[j]);
+    store32<T>(static_cast<T*>(p.aux) + (long long)row * p.ld_aux + col, p.aux_vec, h, nvalid, 0);
+    return;
+  }
+  if (p.mode == 2) {
+    float u[32];
+    load32<T>(static_cast<const T*>(p.aux) + (long long)row * p.ld_aux + col, p.aux_vec, u, nvalid);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = to_f32(from_f32<T>(v[j])) * gelu_grad_f(u[j]);
+  }
+  store32<T>(c, p.c_vec, v, nvalid, p.accumulate);
+}
+
+__device__ __forceinline__ void store_ws_chunk(const Params& p, int split, int row, int col,
+                                               const float (&v)[32], int nvalid) {
+  float* w = p.ws + ((long long)split * p.M + row) * p.N + col;
+  if (nvalid == 32 && p.ws_vec) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      reinterpret_cast<float4*>(w)[q] = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j < nvalid) w[j] = v[j];
 }
 
 template <typename T, int BN>
@@ -267,7 +332,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&bars->tfull[b]), 1);
-      mbar_init(smem_u32(&bars->tempty[b]), 4);
+      mbar_init(smem_u32(&bars->tempty[b]), kEpiWarps);
     }
     mbar_init(smem_u32(&bars->drain), 1);
     bars->abort = 0;
@@ -374,8 +439,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     }
   } else if (warp >= 2) {
     // ---------------------------------------------------------- epilogue
-    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int quarter = warp & 3;           // TMEM lanes this warp may access
+    const int half = (warp - 2) / 4;        // which interleaved half of the chunks
     const int row_in_tile = quarter * 32 + lane;
+    const bool has_bias = p.bias != nullptr && p.splits == 1;
     int it = 0;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++it) {
       int m0, n0, kb0, kb1, split;
@@ -389,29 +456,21 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       tc_fence_after();
       const int row = m0 + row_in_tile;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half; c < BN / 32; c += 2) {
         uint32_t r[32];
         tmem_ld32(tmem_base + ((quarter * 32) << 16) + buf * BN + c * 32, r);
         tmem_ld_wait();
-        const int col = n0 + c * 32;
-        if (row < p.M && col < p.N) {
-          const int nvalid = min(32, p.N - col);
-          float v[32];
+        const int col = n0 + c * 32;  // warp-uniform
+        if (col >= p.N) continue;
+        const int nvalid = min(32, p.N - col);
+        float bl = 0.f;
+        if (has_bias && lane < nvalid) bl = to_f32(static_cast<const T*>(p.bias)[col + lane]);
+        float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          if (p.splits > 1) {
-            float* w = p.ws + ((long long)split * p.M + row) * p.N + col;
-            if (nvalid == 32 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) {
-#pragma unroll
-              for (int q = 0; q < 8; ++q)
-                reinterpret_cast<float4*>(w)[q] =
-                    make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
-            } else {
-              for (int j = 0; j < nvalid; ++j) w[j] = v[j];
-            }
-          } else {
-            store_row_chunk<T>(p, row, col, v, nvalid);
-          }
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + __shfl_sync(0xffffffffu, bl, j);
+        if (row < p.M) {
+          if (p.splits > 1) store_ws_chunk(p, split, row, col, v, nvalid);
+          else store_chunk<T>(p, row, col, v, nvalid);
         }
       }
       tc_fence_before();
@@ -427,6 +486,322 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
+
+
+// ======================================================================
+// 2-CTA variant: a cluster of two CTAs on two SMs computes a 256 x 256
+// tile with tcgen05.mma.cta_group::2 (M = 256 split over the pair's tensor
+// memories).  Each CTA stages only its 128 rows of A and its 128 rows of B
+// per K slice, so the L2 -> SM traffic per FLOP is 2/3 of the 1-CTA kernel
+// and six ring stages fit in shared memory.  The even CTA ("leader") issues
+// the MMAs; both CTAs' TMA loads signal the leader's stage barrier
+// (.cta_group::2 form), each commit is sent to both CTAs' barriers, and both
+// epilogues release the accumulator on the leader's barrier.  Every TMA load
+// is a plain per-CTA tile load.
+// ======================================================================
+namespace pair {
+
+constexpr int TM = 256;        // M rows per CTA pair
+constexpr int BN2 = 256;       // N columns per tile
+constexpr int HALF = 128;      // rows of A and of B staged per CTA
+constexpr int STAGES2 = 6;
+constexpr int A2_BYTES = HALF * BK * 2;
+constexpr int B2_BYTES = HALF * BK * 2;
+
+__device__ __forceinline__ uint32_t cta_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+__device__ __forceinline__ void remote_arrive(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ bool try_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool wait2(uint32_t bar, uint32_t parity, volatile int* abort,
+                                      const Params& p, unsigned code) {
+  if (try_cluster(bar, parity)) return true;
+  const uint64_t t0 = gtime();
+  while (true) {
+    if (try_cluster(bar, parity)) return true;
+    if (*abort) return false;
+    if (gtime() - t0 > p.timeout_ns) {
+      *abort = 1;
+      atomicCAS(p.err, 0u, code);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                              int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.cta_group::2"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void alloc2(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void relinquish2() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void mma2(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrive (when the issued MMAs retire) on the barrier at this offset in
+// both CTAs of the pair: one commit per barrier, the peer's addressed
+// through its shared::cluster window
+__device__ __forceinline__ void commit2_to(uint32_t cluster_bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          cluster_bar)
+      : "memory");
+}
+__device__ __forceinline__ void commit2_both(uint32_t bar) {
+  commit2_to(bar);
+  commit2_to(mapa(bar, 1));
+}
+__device__ __forceinline__ void commit2_local(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+
+struct alignas(8) Bars2 {
+  uint64_t full[STAGES2];
+  uint64_t empty[STAGES2];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t smem_bytes2() {
+  return 1024 + STAGES2 * (A2_BYTES + B2_BYTES) + sizeof(Bars2);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+             const Params p) {
+  constexpr uint32_t TMEM_COLS = 2 * BN2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES2 * A2_BYTES;
+  Bars2* bars = reinterpret_cast<Bars2*>(sB + STAGES2 * B2_BYTES);
+  volatile int* abort = &bars->abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cta_rank();
+  const bool leader = rank == 0;
+  const int pair_id = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(smem_u32(&bars->full[s]), 1);
+      mbar_init(smem_u32(&bars->empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&bars->tfull[b]), 1);
+      mbar_init(smem_u32(&bars->tempty[b]), 2 * kEpiWarps);
+    }
+    mbar_init(smem_u32(&bars->drain), 1);
+    bars->abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  // both CTAs are running and their barriers initialised before any remote use
+  cluster_sync();
+  if (warp == 1) {
+    alloc2(smem_u32(&bars->tmem_base), TMEM_COLS);
+    relinquish2();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------ TMA producer
+    int stage = 0;
+    uint32_t phase = 0;
+    int pending[STAGES2];
+#pragma unroll
+    for (int s = 0; s < STAGES2; ++s) pending[s] = -1;
+    bool ok = true;
+    for (int u = pair_id; u < p.units && ok; u += npairs) {
+      int m0, n0, kb0, kb1, split;
+      unit_coords<BN2, TM>(p, u, m0, n0, kb0, kb1, split);
+      const int am = m0 + HALF * rank, bn = n0 + HALF * rank;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!wait2(smem_u32(&bars->empty[stage]), phase ^ 1, abort, p, 11)) {
+          ok = false;
+          break;
+        }
+        const uint32_t full_local = smem_u32(&bars->full[stage]);
+        const uint32_t full_leader = mapa(full_local, 0);
+        if (leader) mbar_expect_tx(full_local, 2 * (A2_BYTES + B2_BYTES));
+        const uint32_t a_dst = smem_u32(sA + stage * A2_BYTES);
+        const uint32_t b_dst = smem_u32(sB + stage * B2_BYTES);
+        const int k0 = kb * BK;
+        if (p.a_mn) {
+          tma_load_pair(a_dst, &tmA, full_leader, am, k0);
+          tma_load_pair(a_dst + 8192, &tmA, full_leader, am + 64, k0);
+        } else {
+          tma_load_pair(a_dst, &tmA, full_leader, k0, am);
+        }
+        if (p.b_mn) {
+          tma_load_pair(b_dst, &tmB, full_leader, bn, k0);
+          tma_load_pair(b_dst + 8192, &tmB, full_leader, bn + 64, k0);
+        } else {
+          tma_load_pair(b_dst, &tmB, full_leader, k0, bn);
+        }
+        pending[stage] = static_cast<int>(phase);
+        if (++stage == STAGES2) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    if (leader) {
+      // the leader's stage barriers count both CTAs' bytes: wait for them
+      for (int s = 0; s < STAGES2; ++s) {
+        if (pending[s] < 0) continue;
+        const uint64_t t0 = gtime();
+        while (!try_cluster(smem_u32(&bars->full[s]), static_cast<uint32_t>(pending[s])) &&
+               gtime() - t0 < p.timeout_ns) {
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ------------------------------------------------------- MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    int it = 0;
+    bool ok = true;
+    for (int u = pair_id; u < p.units && ok; u += npairs, ++it) {
+      int m0, n0, kb0, kb1, split;
+      unit_coords<BN2, TM>(p, u, m0, n0, kb0, kb1, split);
+      const int buf = it & 1;
+      const uint32_t tphase = (it >> 1) & 1;
+      if (!wait2(smem_u32(&bars->tempty[buf]), tphase ^ 1, abort, p, 12)) break;
+      tc_fence_after();
+      const uint32_t d = tmem_base + buf * BN2;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!wait2(smem_u32(&bars->full[stage]), phase, abort, p, 13)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(sA + stage * A2_BYTES);
+        const uint32_t b_base = smem_u32(sB + stage * B2_BYTES);
+#pragma unroll
+        for (int ks = 0; ks < BK / 16; ++ks)
+          mma2(d, operand_desc(a_base, p.a_mn, ks), operand_desc(b_base, p.b_mn, ks), p.idesc,
+               (kb > kb0 || ks > 0) ? 1u : 0u);
+        commit2_both(smem_u32(&bars->empty[stage]));
+        if (++stage == STAGES2) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (ok) commit2_both(smem_u32(&bars->tfull[buf]));
+    }
+    commit2_local(smem_u32(&bars->drain));
+    const uint64_t t0 = gtime();
+    while (!mbar_try(smem_u32(&bars->drain), 0) && gtime() - t0 < p.timeout_ns) {
+    }
+  } else if (warp >= 2) {
+    // ---------------------------------------------------------- epilogue
+    const int quarter = warp & 3;
+    const int half = (warp - 2) / 4;
+    const int row_in_tile = HALF * rank + quarter * 32 + lane;
+    const bool has_bias = p.bias != nullptr && p.splits == 1;
+    const uint32_t tempty_leader0 = mapa(smem_u32(&bars->tempty[0]), 0);
+    const uint32_t tempty_leader1 = mapa(smem_u32(&bars->tempty[1]), 0);
+    int it = 0;
+    for (int u = pair_id; u < p.units; u += npairs, ++it) {
+      int m0, n0, kb0, kb1, split;
+      unit_coords<BN2, TM>(p, u, m0, n0, kb0, kb1, split);
+      const int buf = it & 1;
+      const uint32_t tphase = (it >> 1) & 1;
+      int ok = lane == 0 ? (wait2(smem_u32(&bars->tfull[buf]), tphase, abort, p, 14) ? 1 : 0) : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const int row = m0 + row_in_tile;
+#pragma unroll 1
+      for (int c = half; c < BN2 / 32; c += 2) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((quarter * 32) << 16) + buf * BN2 + c * 32, r);
+        tmem_ld_wait();
+        const int col = n0 + c * 32;
+        if (col >= p.N) continue;
+        const int nvalid = min(32, p.N - col);
+        float bl = 0.f;
+        if (has_bias && lane < nvalid) bl = to_f32(static_cast<const T*>(p.bias)[col + lane]);
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + __shfl_sync(0xffffffffu, bl, j);
+        if (row < p.M) {
+          if (p.splits > 1) store_ws_chunk(p, split, row, col, v, nvalid);
+          else store_chunk<T>(p, row, col, v, nvalid);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) remote_arrive(buf ? tempty_leader1 : tempty_leader0);
+    }
+  }
+
+  // every role of both CTAs is done before tensor memory is released and
+  // before either CTA's shared memory can go away
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    dealloc2(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace pair
 
 // C = sum_s ws[s] (+ bias) (+ C)
 template <typename T>
@@ -461,12 +836,26 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// The driver-level encode needs a current context.  A host thread that only
+// ever ran on the default device (autograd's backward worker) may not have
+// made it current yet: cudaSetDevice binds the primary context (CUDA >= 12).
+void bind_context() {
+  thread_local int bound = -1;
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (bound != dev) {
+    check_cuda(cudaSetDevice(dev), "cudaSetDevice");
+    bound = dev;
+  }
+}
+
 // 2-D map over a row-major matrix [outer, inner] with row stride ld elements.
 CUtensorMap make_map(const void* ptr, int dtype, long long inner, long long outer, long long ld,
                      int box_inner, int box_outer) {
   if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0)
     throw std::runtime_error("gemm operand must be 16-byte aligned");
   if ((ld * 2) % 16 != 0) throw std::runtime_error("gemm operand row stride must be 16-byte aligned");
+  bind_context();
   CUtensorMap m;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
@@ -501,24 +890,82 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int g
   kern<<<grid, kThreads, smem_bytes<BN>(), st>>>(ta, tb, p);
 }
 
+template <typename T>
+int pair_capacity(const Params& p, cudaStream_t st) {
+  // how many 2-CTA clusters of this kernel can be resident at once
+  static int cached = -1;
+  if (cached < 0) {
+    auto kern = pair::gemm2_kernel<T>;
+    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)pair::smem_bytes2()),
+               "gemm2 smem attribute");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 74);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = pair::smem_bytes2();
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    check_cuda(cudaOccupancyMaxActiveClusters(&n, kern, &cfg), "gemm2 occupancy");
+    cached = n > 0 ? n : 1;
+  }
+  (void)p;
+  return cached;
+}
+
+template <typename T>
+void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int npairs,
+                 cudaStream_t st) {
+  auto kern = pair::gemm2_kernel<T>;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * npairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = pair::smem_bytes2();
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  check_cuda(cudaLaunchKernelEx(&cfg, kern, ta, tb, p), "gemm2 launch");
+}
+
 }  // namespace tc
 
 // Pick the N tile (256 or 128) and the split-K factor from a simple time
 // model: waves * K-slices * per-slice time, plus the fp32 workspace round
 // trip of split-K.  Returns the workspace floats the plan needs.
+// bn_out = 256 or 128 (one CTA per tile) or 512 (a 2-CTA pair per 256 x 256 tile).
 long long gemm_plan(int M, int N, int K, int num_sms, int* bn_out, int* splits_out) {
   const int kb = (K + tc::BK - 1) / tc::BK;
   double best = 1e30;
   int best_bn = N > 128 ? 256 : 128, best_s = 1;
-  for (int bn : {256, 128}) {
+  const char* force = std::getenv("MSB_GEMM_VARIANT");
+  for (int bn : {512, 256, 128}) {
+    if (force != nullptr) {
+      if (std::string(force) == "1cta" && bn == 512) continue;
+      if (std::string(force) == "2cta" && bn != 512) continue;
+    }
     if (bn == 256 && N <= 128) continue;
-    const double t_slice = bn == 256 ? 0.27 : 0.15;  // us per 64-deep K slice
-    const long long tiles = (long long)((M + tc::BM - 1) / tc::BM) * ((N + bn - 1) / bn);
+    // us per 64-deep K slice per tile; the pair kernel moves 2/3 of the bytes
+    const double t_slice = bn == 512 ? 0.22 : (bn == 256 ? 0.27 : 0.15);
+    const int tm = bn == 512 ? 256 : tc::BM;
+    const int tn = bn == 512 ? 256 : bn;
+    const int slots = bn == 512 ? num_sms / 2 : num_sms;
+    const long long tiles = (long long)((M + tm - 1) / tm) * ((N + tn - 1) / tn);
     for (int s = 1; s <= 16; ++s) {
       const int per = (kb + s - 1) / s;
       if (s > 1 && per < 4) break;
       if ((kb + per - 1) / per != s) continue;
-      const double waves = std::ceil((double)(tiles * s) / num_sms);
+      const double waves = std::ceil((double)(tiles * s) / slots);
       double t = waves * per * t_slice;
       if (s > 1) t += (2.0 * s * (double)M * N * 4.0 + (double)M * N * 2.0) / 6.0e12 * 1e6 + 3.0;
       if (t < best - 1e-9) {
@@ -535,15 +982,18 @@ long long gemm_plan(int M, int N, int K, int num_sms, int* bn_out, int* splits_o
 
 void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
                   void* C, long long ldc, const void* bias, int M, int N, int K, int dtype,
-                  int accumulate, float* ws, long long ws_floats, unsigned* err,
-                  double timeout_s, cudaStream_t st) {
+                  int accumulate, int mode, void* aux, long long ld_aux, float* ws,
+                  long long ws_floats, unsigned* err, double timeout_s, cudaStream_t st) {
   using namespace tc;
   int bn, splits;
   const long long need = gemm_plan(M, N, K, kNumSMs, &bn, &splits);
-  if (need > ws_floats || ws == nullptr) {
+  if (need > ws_floats || ws == nullptr || mode != 0) {
     splits = 1;
-    bn = N > 128 ? 256 : 128;
+    if (bn != 512) bn = N > 128 ? 256 : 128;
   }
+  const bool two_cta = bn == 512;
+  const int tm = two_cta ? 256 : BM;
+  const int tn = two_cta ? 256 : bn;
   Params p;
   p.M = M;
   p.N = N;
@@ -551,8 +1001,9 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
   p.kb_total = (K + BK - 1) / BK;
   p.kb_per_split = (p.kb_total + splits - 1) / splits;
   p.splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
-  p.tiles_m = (M + BM - 1) / BM;
-  p.tiles_n = (N + bn - 1) / bn;
+  p.tiles_m = (M + tm - 1) / tm;
+  p.tiles_n = (N + tn - 1) / tn;
+  p.nfast = (long long)M > (long long)N ? 1 : 0;  // A (M x K) larger than B (N x K)
   p.units = p.tiles_m * p.tiles_n * p.splits;
   p.C = C;
   p.ldc = ldc;
@@ -561,20 +1012,39 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
   p.a_mn = a_mn;
   p.b_mn = b_mn;
   p.accumulate = p.splits > 1 ? 0 : accumulate;
+  p.c_vec = ((reinterpret_cast<uintptr_t>(C) & 15) == 0 && (ldc % 8) == 0) ? 1 : 0;
+  p.mode = mode;
+  p.aux = aux;
+  p.ld_aux = ld_aux;
+  p.aux_vec = ((reinterpret_cast<uintptr_t>(aux) & 15) == 0 && (ld_aux % 8) == 0) ? 1 : 0;
+  p.ws_vec = ((reinterpret_cast<uintptr_t>(ws) & 15) == 0 && (N % 4) == 0) ? 1 : 0;
   const uint32_t fmt = dtype == kBF16 ? 1u : 0u;
   p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(a_mn) << 15) |
-            (static_cast<uint32_t>(b_mn) << 16) | (static_cast<uint32_t>(bn >> 3) << 17) |
-            (static_cast<uint32_t>(BM >> 4) << 24);
+            (static_cast<uint32_t>(b_mn) << 16) | (static_cast<uint32_t>(tn >> 3) << 17) |
+            (static_cast<uint32_t>(tm >> 4) << 24);
   p.err = err;
   p.timeout_ns = static_cast<unsigned long long>(timeout_s * 1e9);
 
-  // operand maps: K-major [rows, K] -> box {64, rows-tile}; MN-major [K, rows] -> box {64, 64}
+  // operand maps: K-major [rows, K] -> box {64, rows staged per CTA};
+  // MN-major [K, rows] -> box {64, 64}
+  const int a_rows = two_cta ? pair::HALF : BM;
+  const int b_rows = two_cta ? pair::HALF : bn;
   const CUtensorMap ta = a_mn ? make_map(A, dtype, M, K, lda, 64, 64)
-                              : make_map(A, dtype, K, M, lda, 64, BM);
+                              : make_map(A, dtype, K, M, lda, 64, a_rows);
   const CUtensorMap tb = b_mn ? make_map(B, dtype, N, K, ldb, 64, 64)
-                              : make_map(B, dtype, K, N, ldb, 64, bn);
+                              : make_map(B, dtype, K, N, ldb, 64, b_rows);
   const int grid = std::min(p.units, kNumSMs);
-  if (dtype == kF16) {
+  if (two_cta) {
+    if (dtype == kF16) {
+      const int npairs = std::min(p.units, pair_capacity<__half>(p, st));
+      launch_pair<__half>(ta, tb, p, npairs, st);
+    } else if (dtype == kBF16) {
+      const int npairs = std::min(p.units, pair_capacity<__nv_bfloat16>(p, st));
+      launch_pair<__nv_bfloat16>(ta, tb, p, npairs, st);
+    } else {
+      throw std::runtime_error("tcgen05 gemm takes fp16/bf16 operands");
+    }
+  } else if (dtype == kF16) {
     if (bn == 256) launch<__half, 256>(ta, tb, p, grid, st);
     else launch<__half, 128>(ta, tb, p, grid, st);
   } else if (dtype == kBF16) {

@@ -31,7 +31,10 @@ int norm_bwd(const void* dy, const void* s, const void* w, const float* mean, co
              int dtype, int max_blocks, cudaStream_t st);
 int colsum_partial(const void* a, float* part, int M, int N, long long ld, int dtype,
                    int max_chunks, cudaStream_t st);
-void colsum_finish(const float* part, int nparts, int N, void* out, int dtype, cudaStream_t st);
+void colsum_finish(const float* part, int nparts, int N, void* out, int dtype, int accumulate,
+                   cudaStream_t st);
+void accum_cast(const float* src, void* dst, long long n, int dtype, int accumulate,
+                cudaStream_t st);
 void bias_gelu_fwd(void* u, const void* bias, void* h, long long total, int N, int dtype,
                    cudaStream_t st);
 void gelu_bwd(const void* dh, const void* u, void* du, long long total, int dtype,
@@ -56,7 +59,7 @@ void rope(void* x, const float* cos_t, const float* sin_t, long long BT, int T_l
 long long gemm_plan(int M, int N, int K, int num_sms, int* bn_out, int* splits_out);
 void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
                   void* C, long long ldc, const void* bias, int M, int N, int K, int dtype,
-                  int accumulate, float* ws, long long ws_floats, unsigned* err,
-                  double timeout_s, cudaStream_t st);
+                  int accumulate, int mode, void* aux, long long ld_aux, float* ws,
+                  long long ws_floats, unsigned* err, double timeout_s, cudaStream_t st);
 
 }  // namespace msb

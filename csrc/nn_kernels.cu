@@ -258,26 +258,41 @@ colsum_partial_kernel(const T* __restrict__ a, float* __restrict__ part, int M, 
   }
 }
 
+// out[c] (+)= sum_p part[p][c]: block = 32 columns x 8 warps over the parts.
 template <typename T>
 __global__ void __launch_bounds__(256)
-colsum_finish_kernel(const float* __restrict__ part, int nparts, int N, T* __restrict__ out) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= N) return;
+colsum_finish_kernel(const float* __restrict__ part, int nparts, int N, T* __restrict__ out,
+                     int accumulate) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x * 32 + lane;
   float t = 0.f;
-  for (int p = 0; p < nparts; ++p) t += part[(size_t)p * N + c];
-  out[c] = from_f32<T>(t);
+  if (c < N)
+    for (int q = warp; q < nparts; q += 8) t += part[(size_t)q * N + c];
+  __shared__ float red[8][33];
+  red[warp][lane] = t;
+  __syncthreads();
+  if (warp == 0 && c < N) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) acc += red[w][lane];
+    if (accumulate) acc += to_f32(out[c]);
+    out[c] = from_f32<T>(acc);
+  }
+}
+
+// dst (+)= float(src) for a float32 source (accumulating gradients in place)
+template <typename T>
+__global__ void __launch_bounds__(256)
+accum_cast_kernel(const float* __restrict__ src, T* __restrict__ dst, long long n, int accumulate) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    float v = src[i];
+    if (accumulate) v += to_f32(dst[i]);
+    dst[i] = from_f32<T>(v);
+  }
 }
 
 // ---------------------------------------------------------------- GELU
-__device__ __forceinline__ float gelu_f(float u) {
-  return 0.5f * u * (1.f + erff(u * 0.70710678118654752f));
-}
-__device__ __forceinline__ float gelu_grad_f(float u) {
-  const float cdf = 0.5f * (1.f + erff(u * 0.70710678118654752f));
-  const float pdf = expf(-0.5f * u * u) * 0.39894228040143268f;
-  return cdf + u * pdf;
-}
-
 template <typename T>
 __global__ void __launch_bounds__(256)
 bias_gelu_fwd_kernel(T* __restrict__ u, const T* __restrict__ bias, T* __restrict__ h,
@@ -656,11 +671,21 @@ int colsum_partial(const void* a, float* part, int M, int N, long long ld, int d
   return chunks;
 }
 
-void colsum_finish(const float* part, int nparts, int N, void* out, int dtype, cudaStream_t st) {
+void colsum_finish(const float* part, int nparts, int N, void* out, int dtype, int accumulate,
+                   cudaStream_t st) {
   MSB_DISPATCH_FLOAT(dtype, T, {
-    colsum_finish_kernel<T><<<(N + 255) / 256, 256, 0, st>>>(part, nparts, N, (T*)out);
+    colsum_finish_kernel<T><<<(N + 31) / 32, 256, 0, st>>>(part, nparts, N, (T*)out, accumulate);
   });
   MSB_CHECK_LAUNCH("colsum_finish");
+}
+
+void accum_cast(const float* src, void* dst, long long n, int dtype, int accumulate,
+                cudaStream_t st) {
+  const int blocks = grid_for(n, 256, kNumSMs * 16);
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    accum_cast_kernel<T><<<blocks, 256, 0, st>>>(src, (T*)dst, n, accumulate);
+  });
+  MSB_CHECK_LAUNCH("accum_cast");
 }
 
 void bias_gelu_fwd(void* u, const void* bias, void* h, long long total, int N, int dtype,

@@ -85,7 +85,7 @@ class Block(nn.Module):
         a = self.attn(h)
         x, h = ops.add_norm(x, a, self.ln2.weight, self.ln2.bias, self.eps)
         fc, fc2 = self.mlp[0], self.mlp[2]
-        m = ops.linear(ops.linear_gelu(h, fc.weight, fc.bias), fc2.weight, fc2.bias)
+        m = ops.mlp_gelu(h, fc.weight, fc.bias, fc2.weight, fc2.bias)
         return x, m
 
 

@@ -72,29 +72,45 @@ def _tma_ready(t: torch.Tensor) -> torch.Tensor:
     return buf
 
 
+EPI_PLAIN, EPI_BIAS_GELU, EPI_DGELU = 0, 1, 2
+
+
 def gemm(a: torch.Tensor, b: torch.Tensor, *, a_kmajor: bool, b_kmajor: bool,
          bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-         accumulate: bool = False) -> torch.Tensor:
+         accumulate: bool = False, mode: int = EPI_PLAIN,
+         aux: Optional[torch.Tensor] = None) -> torch.Tensor:
     """C[M,N] (+)= A @ B^T (+ bias) in the tcgen05 operand convention.
 
     ``a`` holds A as [M,K] (``a_kmajor``) or [K,M]; ``b`` holds B as [N,K]
-    (``b_kmajor``) or [K,N]."""
+    (``b_kmajor``) or [K,N].  Epilogue modes: ``EPI_BIAS_GELU`` stores
+    u = A@B^T + bias into ``out`` and gelu(u) into ``aux``; ``EPI_DGELU``
+    stores (A@B^T) * gelu'(aux) into ``out``."""
     M = a.shape[0] if a_kmajor else a.shape[1]
     N = b.shape[0] if b_kmajor else b.shape[1]
     if out is None:
         out = torch.empty(M, N, dtype=a.dtype, device=a.device)
     if a.is_cuda and a.dtype in (torch.float16, torch.bfloat16) and native_enabled():
         _ext.get().gemm(_tma_ready(a), _tma_ready(b), a_kmajor, b_kmajor, bias, out,
-                        accumulate, error_word(a.device), TIMEOUT_S)
+                        accumulate, error_word(a.device), TIMEOUT_S, mode, aux)
         return out
     A = a if a_kmajor else a.t()
     B = b.t() if b_kmajor else b
+    r = A.float() @ B.float()
+    if bias is not None:
+        r = r + bias.float()
+    if mode == EPI_BIAS_GELU:
+        u = r.to(out.dtype)
+        out.copy_(u)
+        aux.copy_(torch.nn.functional.gelu(u.float()).to(aux.dtype))
+        return out
+    if mode == EPI_DGELU:
+        from .nn import gelu_grad_reference
+
+        r = r.to(out.dtype).float() * gelu_grad_reference(aux.float())
     if accumulate:
-        out.add_(A @ B)
-    elif bias is not None:
-        torch.addmm(bias, A, B, out=out)
+        out.copy_((out.float() + r).to(out.dtype))
     else:
-        torch.mm(A, B, out=out)
+        out.copy_(r.to(out.dtype))
     return out
 
 

@@ -27,7 +27,7 @@ import torch.nn.functional as F
 from . import _ext, gemm
 
 _COLSUM_CHUNKS = 256   # row chunks of a column-sum reduction
-_NORM_BLOCKS = 148 * 8  # norm backward blocks (one partial row of dw/db each)
+_NORM_BLOCKS = 148 * 2  # norm backward blocks (one partial row of dw/db each)
 
 
 def _C():
@@ -47,14 +47,44 @@ def as_matrix(t: torch.Tensor, n: int) -> torch.Tensor:
     return m
 
 
-def _colsum(a2d: torch.Tensor, dtype) -> torch.Tensor:
-    """Column sums of a [M, N] CUDA matrix (bias gradients)."""
+def grad_sink(p: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    """The parameter's existing ``.grad`` if gradients can be accumulated into
+    it in place (the engine binds every ``p.grad`` to a view of its flat
+    gradient arena), else None.
+
+    Backward kernels write into a sink directly (GEMM epilogue accumulate,
+    column-sum accumulate) and report no gradient to autograd for that input,
+    which is what autograd's own accumulation would have produced."""
+    if p is None or not isinstance(p, torch.nn.Parameter):
+        return None
+    g = p.grad
+    if g is None or g.dtype != p.dtype or g.shape != p.shape or not g.is_contiguous():
+        return None
+    return g
+
+
+def _colsum(a2d: torch.Tensor, dtype, sink: Optional[torch.Tensor] = None
+            ) -> Optional[torch.Tensor]:
+    """Column sums of a [M, N] CUDA matrix (bias gradients); accumulated into
+    ``sink`` (returns None) or returned as a new tensor."""
     n = a2d.shape[-1]
     part = _scratch(a2d.device, _COLSUM_CHUNKS * n)
     nb = _C().colsum_partial(a2d, part, _COLSUM_CHUNKS)
+    if sink is not None:
+        _C().colsum_finish(part, nb, sink, True)
+        return None
     out = torch.empty(n, dtype=dtype, device=a2d.device)
-    _C().colsum_finish(part, nb, out)
+    _C().colsum_finish(part, nb, out, False)
     return out
+
+
+def _wgrad(dy2: torch.Tensor, x2: torch.Tensor, w: torch.Tensor) -> Optional[torch.Tensor]:
+    """dW = dy^T x, accumulated into w's gradient sink when it has one."""
+    sink = grad_sink(w)
+    if sink is not None:
+        gemm.linear_wgrad(dy2, x2, out=sink.view(sink.shape[0], -1), accumulate=True)
+        return None
+    return gemm.linear_wgrad(dy2, x2)
 
 
 # --------------------------------------------------------------- norms
@@ -70,6 +100,7 @@ class _AddNorm(torch.autograd.Function):
         _C().add_norm_fwd(x, delta, w, b, s, y, mean, rstd, eps, rms)
         saved = s if s is not None else x
         ctx.save_for_backward(saved, w, mean, rstd)
+        ctx.params = (w, b)
         ctx.rms = rms
         ctx.has_delta = delta is not None
         ctx.has_bias = b is not None
@@ -94,12 +125,21 @@ class _AddNorm(torch.autograd.Function):
             ds = ds.contiguous()
         nb = _C().norm_bwd(dy, s, w, mean, rstd, ds, dx, dw_part, db_part, ctx.rms,
                            _NORM_BLOCKS)
-        dw = torch.empty_like(w)
-        _C().colsum_finish(dw_part, nb, dw)
-        db = None
+        w_p, b_p = ctx.params
+        dw = db = None
+        sink = grad_sink(w_p)
+        if sink is not None:
+            _C().colsum_finish(dw_part, nb, sink, True)
+        else:
+            dw = torch.empty_like(w)
+            _C().colsum_finish(dw_part, nb, dw, False)
         if ctx.has_bias:
-            db = torch.empty_like(w)
-            _C().colsum_finish(db_part, nb, db)
+            sink = grad_sink(b_p)
+            if sink is not None:
+                _C().colsum_finish(db_part, nb, sink, True)
+            else:
+                db = torch.empty_like(w)
+                _C().colsum_finish(db_part, nb, db, False)
         if ctx.has_delta:
             return dx, dx, dw, db, None, None
         return dx, None, dw, db, None, None
@@ -132,7 +172,7 @@ def norm(x: torch.Tensor, w, b, eps: float = 1e-5, rms: bool = False) -> torch.T
 # -------------------------------------------------------------- linears
 class _Linear(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, w, b, act, pad):
+    def forward(ctx, x, w, b, pad):
         shp = x.shape
         x2 = as_matrix(x, shp[-1])
         N = w.shape[0]
@@ -142,38 +182,58 @@ class _Linear(torch.autograd.Function):
             # that every row starts 16-byte aligned (TMA / vector access)
             ld = -(-N // pad) * pad
             out = torch.empty(x2.shape[0], ld, dtype=x.dtype, device=x.device)[:, :N]
-        if act == "gelu":
-            u = gemm.linear_fwd(x2, w, None)
-            h = torch.empty_like(u)
-            _C().bias_gelu_fwd(u, b, h)
-            ctx.save_for_backward(x2, w, u)
-            out = h
-        else:
-            out = gemm.linear_fwd(x2, w, b, out=out)
-            ctx.save_for_backward(x2, w)
-        ctx.act = act
-        ctx.has_bias = b is not None
+        out = gemm.linear_fwd(x2, w, b, out=out)
+        ctx.save_for_backward(x2, w)
+        ctx.params = (w, b)
         ctx.shape = shp
         return out.view(*shp[:-1], N)
 
     @staticmethod
     def backward(ctx, dy):
-        if ctx.act == "gelu":
-            x2, w, u = ctx.saved_tensors
-        else:
-            x2, w = ctx.saved_tensors
+        x2, w = ctx.saved_tensors
+        w_p, b_p = ctx.params
         dy2 = as_matrix(dy, w.shape[0])
-        if ctx.act == "gelu":
-            dy2 = dy2.contiguous()
-            du = torch.empty_like(u)
-            _C().gelu_bwd(dy2, u, du)
-            dy2 = du
         dx = gemm.linear_dgrad(dy2, w) if ctx.needs_input_grad[0] else None
-        dw = gemm.linear_wgrad(dy2, x2)
-        db = _colsum(dy2, w.dtype) if ctx.has_bias else None
+        dw = _wgrad(dy2, x2, w_p)
+        db = _colsum(dy2, w.dtype, grad_sink(b_p)) if b_p is not None else None
         if dx is not None:
             dx = dx.view(ctx.shape)
-        return dx, dw, db, None, None
+        return dx, dw, db, None
+
+
+class _MlpGelu(torch.autograd.Function):
+    """fc2(gelu(fc(x))) with both GELU passes fused into GEMM epilogues:
+    forward  fc : u = x W1^T + b1 and a = gelu(u) written by one epilogue
+    backward fc2-dgrad: du = (dout W2) * gelu'(u) written by one epilogue."""
+
+    @staticmethod
+    def forward(ctx, x, w1, b1, w2, b2):
+        shp = x.shape
+        x2 = as_matrix(x, shp[-1])
+        M, F_ = x2.shape[0], w1.shape[0]
+        u = torch.empty(M, F_, dtype=x.dtype, device=x.device)
+        a = torch.empty_like(u)
+        gemm.gemm(x2, w1, a_kmajor=True, b_kmajor=True, bias=b1, out=u,
+                  mode=gemm.EPI_BIAS_GELU, aux=a)
+        out = gemm.linear_fwd(a, w2, b2)
+        ctx.save_for_backward(x2, w1, u, a, w2)
+        ctx.params = (w1, b1, w2, b2)
+        ctx.shape = shp
+        return out.view(*shp[:-1], w2.shape[0])
+
+    @staticmethod
+    def backward(ctx, dout):
+        x2, w1, u, a, w2 = ctx.saved_tensors
+        w1_p, b1_p, w2_p, b2_p = ctx.params
+        d2 = as_matrix(dout, w2.shape[0])
+        dw2 = _wgrad(d2, a, w2_p)
+        db2 = _colsum(d2, w2.dtype, grad_sink(b2_p)) if b2_p is not None else None
+        du = torch.empty_like(u)
+        gemm.gemm(d2, w2, a_kmajor=True, b_kmajor=False, out=du, mode=gemm.EPI_DGELU, aux=u)
+        dw1 = _wgrad(du, x2, w1_p)
+        db1 = _colsum(du, w1.dtype, grad_sink(b1_p)) if b1_p is not None else None
+        dx = gemm.linear_dgrad(du, w1).view(ctx.shape) if ctx.needs_input_grad[0] else None
+        return dx, dw1, db1, dw2, db2
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
@@ -182,15 +242,50 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
     stride rounded up to a multiple of ``pad_out`` (the returned tensor is a
     view with the logical width)."""
     if x.is_cuda:
-        return _Linear.apply(x, w, b, None, pad_out)
+        return _Linear.apply(x, w, b, pad_out)
     return F.linear(x, w, b)
+
+
+def mlp_gelu(x: torch.Tensor, w1: torch.Tensor, b1: Optional[torch.Tensor], w2: torch.Tensor,
+             b2: Optional[torch.Tensor]) -> torch.Tensor:
+    """``fc2(gelu(fc(x)))`` (exact erf GELU)."""
+    if x.is_cuda:
+        return _MlpGelu.apply(x, w1, b1, w2, b2)
+    return F.linear(F.gelu(F.linear(x, w1, b1)), w2, b2)
 
 
 def linear_gelu(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None
                 ) -> torch.Tensor:
+    """``gelu(x @ w.T + b)`` (pre-activation kept for backward)."""
     if x.is_cuda:
-        return _Linear.apply(x, w, b, "gelu", 0)
+        return _LinearGelu.apply(x, w, b)
     return F.gelu(F.linear(x, w, b))
+
+
+class _LinearGelu(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, b):
+        shp = x.shape
+        x2 = as_matrix(x, shp[-1])
+        u = torch.empty(x2.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+        h = torch.empty_like(u)
+        gemm.gemm(x2, w, a_kmajor=True, b_kmajor=True, bias=b, out=u,
+                  mode=gemm.EPI_BIAS_GELU, aux=h)
+        ctx.save_for_backward(x2, w, u)
+        ctx.params = (w, b)
+        ctx.shape = shp
+        return h.view(*shp[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dh):
+        x2, w, u = ctx.saved_tensors
+        w_p, b_p = ctx.params
+        du = torch.empty_like(u)
+        _C().gelu_bwd(as_matrix(dh, w.shape[0]).contiguous(), u, du)
+        dw = _wgrad(du, x2, w_p)
+        db = _colsum(du, w.dtype, grad_sink(b_p)) if b_p is not None else None
+        dx = gemm.linear_dgrad(du, w).view(ctx.shape) if ctx.needs_input_grad[0] else None
+        return dx, dw, db
 
 
 class _SwiGLU(torch.autograd.Function):
@@ -267,6 +362,7 @@ class _Embedding(torch.autograd.Function):
         idx = idx.contiguous()
         _C().embedding_fwd(idx, wte, wpe, out, T)
         ctx.save_for_backward(idx)
+        ctx.params = (wte, wpe)
         ctx.shapes = (wte.shape, None if wpe is None else wpe.shape, wte.dtype, T)
         return out
 
@@ -274,11 +370,22 @@ class _Embedding(torch.autograd.Function):
     def backward(ctx, dout):
         (idx,) = ctx.saved_tensors
         wte_shape, wpe_shape, dtype, T = ctx.shapes
+        wte_p, wpe_p = ctx.params
         dwte = torch.zeros(wte_shape, dtype=torch.float32, device=dout.device)
         dwpe = None if wpe_shape is None else torch.zeros(wpe_shape, dtype=torch.float32,
                                                           device=dout.device)
         _C().embedding_bwd(dout.contiguous(), idx, dwte, dwpe, T)
-        return None, dwte.to(dtype), None if dwpe is None else dwpe.to(dtype)
+        return None, _to_sink(dwte, wte_p, dtype), (None if dwpe is None
+                                                     else _to_sink(dwpe, wpe_p, dtype))
+
+
+def _to_sink(g32: torch.Tensor, param, dtype) -> Optional[torch.Tensor]:
+    """Add an fp32 gradient into the param's sink, or return it cast."""
+    sink = grad_sink(param)
+    if sink is not None:
+        _C().accum_cast(g32, sink, True)
+        return None
+    return g32.to(dtype)
 
 
 def embedding(idx: torch.Tensor, wte: torch.Tensor, wpe: Optional[torch.Tensor] = None
@@ -339,3 +446,8 @@ def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch
 
 def gelu_reference(x: torch.Tensor) -> torch.Tensor:
     return 0.5 * x * (1.0 + torch.erf(x / math.sqrt(2.0)))
+
+
+def gelu_grad_reference(u: torch.Tensor) -> torch.Tensor:
+    cdf = 0.5 * (1.0 + torch.erf(u / math.sqrt(2.0)))
+    return cdf + u * torch.exp(-0.5 * u * u) / math.sqrt(2.0 * math.pi)
