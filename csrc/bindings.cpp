@@ -321,6 +321,89 @@ std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K) {
   return {bn, splits, need};
 }
 
+// ------------------------------------------------- peer heap / collectives
+char* const* heap_table(const at::Tensor& heaps) {
+  TORCH_CHECK(heaps.is_cuda() && heaps.scalar_type() == at::kLong && heaps.is_contiguous(),
+              "heap table must be a CUDA int64 tensor");
+  return reinterpret_cast<char* const*>(heaps.data_ptr<int64_t>());
+}
+
+int64_t peer_alloc_py(int64_t bytes) { return reinterpret_cast<int64_t>(msb::peer_alloc(bytes)); }
+void peer_free_py(int64_t p) { msb::peer_free(reinterpret_cast<void*>(p)); }
+py::bytes peer_handle_py(int64_t p) {
+  char h[64];
+  msb::peer_handle(reinterpret_cast<void*>(p), h);
+  return py::bytes(h, 64);
+}
+int64_t peer_open_py(const std::string& h) {
+  TORCH_CHECK(h.size() == 64, "IPC handle must be 64 bytes");
+  return reinterpret_cast<int64_t>(msb::peer_open(h.data()));
+}
+void peer_close_py(int64_t p) { msb::peer_close(reinterpret_cast<void*>(p)); }
+
+// Non-owning tensor over device memory at `ptr` (the heap object owns it).
+at::Tensor tensor_from_ptr(int64_t ptr, int64_t numel, int64_t dtype, int64_t device) {
+  static const at::ScalarType types[3] = {at::kFloat, at::kHalf, at::kBFloat16};
+  TORCH_CHECK(dtype >= 0 && dtype < 3);
+  auto opts = at::TensorOptions().dtype(types[dtype]).device(at::kCUDA, (int)device);
+  return at::from_blob(reinterpret_cast<void*>(ptr), {numel}, opts);
+}
+
+void peer_barrier_py(const at::Tensor& heaps, int64_t sync_off, int64_t rank, int64_t world,
+                     int64_t epoch, double timeout_s, const at::Tensor& status) {
+  c10::cuda::CUDAGuard g(heaps.device());
+  msb::peer_barrier(heap_table(heaps), sync_off, (int)rank, (int)world, (unsigned)epoch,
+                    timeout_s, reinterpret_cast<unsigned*>(status.data_ptr<int>()),
+                    stream_of(heaps));
+}
+
+int64_t rs_stats_py(const at::Tensor& heaps, int64_t grad_off, int64_t dtype, int64_t s0,
+                    const at::Tensor& out, int64_t world, double mul, int64_t fanout_off,
+                    const at::Tensor& partials, const at::Tensor& flags, int64_t slot,
+                    int64_t max_blocks, bool aligned16) {
+  check_cuda_contig(out, "out");
+  TORCH_CHECK(out.scalar_type() == at::kFloat);
+  TORCH_CHECK(slot >= 0 && slot + max_blocks <= partials.numel(), "stats scratch overflow");
+  c10::cuda::CUDAGuard g(heaps.device());
+  return msb::rs_stats(heap_table(heaps), grad_off, (int)dtype, s0, out.numel(), (int)world,
+                       (float)mul, out.data_ptr<float>(), fanout_off,
+                       partials.data_ptr<float>() + slot,
+                       reinterpret_cast<unsigned*>(flags.data_ptr<int>()) + slot, (int)max_blocks,
+                       aligned16, stream_of(heaps));
+}
+
+void stats_exchange_py(const at::Tensor& heaps, int64_t sync_off, int64_t rank, int64_t world,
+                       int64_t epoch, const at::Tensor& out, double max_norm, double timeout_s,
+                       const at::Tensor& status) {
+  c10::cuda::CUDAGuard g(heaps.device());
+  msb::stats_exchange(heap_table(heaps), sync_off, (int)rank, (int)world, (unsigned)epoch,
+                      out.data_ptr<float>(), max_norm, timeout_s,
+                      reinterpret_cast<unsigned*>(status.data_ptr<int>()), stream_of(heaps));
+}
+
+void adamw_fanout_py(const at::Tensor& master, const at::Tensor& m, const at::Tensor& v,
+                     const at::Tensor& grad, const at::Tensor& heaps, int64_t param_off,
+                     int64_t pdtype, int64_t s0, int64_t world, const at::Tensor& stats,
+                     double lr, double beta1, double beta2, double eps, double wd, double bc1,
+                     double bc2, double grad_mul) {
+  check_cuda_contig(master, "master");
+  TORCH_CHECK(grad.scalar_type() == at::kFloat && grad.numel() == master.numel());
+  c10::cuda::CUDAGuard g(master.device());
+  msb::adamw_fanout(master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+                    grad.data_ptr<float>(), heap_table(heaps), param_off, (int)pdtype, s0,
+                    master.numel(), (int)world, stats.data_ptr<float>(), lr, beta1, beta2, eps,
+                    wd, bc1, bc2, grad_mul, stream_of(master));
+}
+
+void gather_pull_py(const at::Tensor& heaps, int64_t shard_off, int64_t shard, int64_t world,
+                    const at::Tensor& dst) {
+  check_cuda_contig(dst, "dst");
+  TORCH_CHECK(dst.numel() >= shard * world);
+  c10::cuda::CUDAGuard g(dst.device());
+  msb::gather_pull(heap_table(heaps), shard_off, shard, (int)world, dst.data_ptr(),
+                   dtype_code(dst), stream_of(dst));
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, mod) {
@@ -347,4 +430,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, mod) {
   mod.def("rope", &rope);
   mod.def("gemm", &gemm);
   mod.def("gemm_plan", &gemm_plan_py);
+  mod.def("peer_alloc", &peer_alloc_py);
+  mod.def("peer_free", &peer_free_py);
+  mod.def("peer_handle", &peer_handle_py);
+  mod.def("peer_open", &peer_open_py);
+  mod.def("peer_close", &peer_close_py);
+  mod.def("tensor_from_ptr", &tensor_from_ptr);
+  mod.def("peer_barrier", &peer_barrier_py);
+  mod.def("rs_stats", &rs_stats_py);
+  mod.def("stats_exchange", &stats_exchange_py);
+  mod.def("adamw_fanout", &adamw_fanout_py);
+  mod.def("gather_pull", &gather_pull_py);
 }

@@ -1,0 +1,379 @@
+// Fused step-pipeline collectives over NVLink peer memory.
+//
+// Every rank owns one device buffer (the "peer heap") whose layout is the
+// same on all ranks; each rank maps every peer's heap (CUDA IPC) and passes
+// the table of heap base addresses to these kernels, which then load from
+// and store to peer HBM directly over NVLink 5 / NVSwitch.  Plain loads and
+// stores only: no multimem, no TMA.
+//
+//   peer_barrier      every rank signals an epoch to every peer and waits
+//                     (bounded) until all peers signalled it
+//   rs_stats          reduce-scatter fused with unscale/average and the
+//                     gradient statistics: rank r sums its shard of every
+//                     peer's model-dtype gradient arena in fp32 in rank
+//                     order (deterministic), scales by 1/(loss_scale*W),
+//                     writes the fp32 shard (optionally also into every
+//                     peer's full fp32 buffer: the all-reduce of stage 0)
+//                     and emits per-block (sum of squares, inf/nan) partials
+//   stats_exchange    all-gather of each rank's [flag, sumsq] through a
+//                     board in every heap; summed in rank order so every
+//                     rank computes the bitwise-identical global norm
+//   adamw_fanout      AdamW on this rank's shard whose fp16/bf16 cast is
+//                     stored into the parameter arena of EVERY rank (the
+//                     parameter all-gather fused into the update)
+//   gather_pull       stage-3 parameter gather: local arena <- every peer's
+//                     model-dtype shard
+//
+// Waits use %globaltimer bounds; on expiry a kernel records an error code in
+// a local status word and returns, leaving the context usable.
+#include "common.cuh"
+
+namespace msb {
+namespace {
+
+__device__ __forceinline__ uint64_t gtime_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Sync area at `sync_off` in every heap:
+//   uint32 flags[kMaxRanks]         flags[q] = last epoch rank q signalled
+//   Board  board[kMaxRanks]         board[q] = rank q's step statistics
+constexpr int kMaxRanks = 16;
+struct Board {
+  unsigned epoch;
+  float flag;
+  float sumsq;
+  unsigned pad;
+};
+
+__device__ __forceinline__ unsigned* flags_of(char* heap, long long sync_off) {
+  return reinterpret_cast<unsigned*>(heap + sync_off);
+}
+__device__ __forceinline__ Board* board_of(char* heap, long long sync_off) {
+  return reinterpret_cast<Board*>(heap + sync_off + kMaxRanks * sizeof(unsigned) * 4);
+}
+
+__global__ void peer_barrier_kernel(char* const* heaps, long long sync_off, int rank, int world,
+                                    unsigned epoch, unsigned long long timeout_ns,
+                                    unsigned* status) {
+  // make this device's earlier writes (local and peer stores of preceding
+  // kernels) visible system-wide before announcing the epoch
+  __threadfence_system();
+  const int t = threadIdx.x;
+  if (t < world) st_release_sys(flags_of(heaps[t], sync_off) + rank, epoch);
+  __syncthreads();
+  if (t < world) {
+    const unsigned* mine = flags_of(heaps[rank], sync_off) + t;
+    const uint64_t t0 = gtime_ns();
+    while (static_cast<int>(ld_acquire_sys(mine) - epoch) < 0) {
+      if (gtime_ns() - t0 > timeout_ns) {
+        atomicCAS(status, 0u, 0x100u | static_cast<unsigned>(t));
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  __threadfence_system();
+}
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256)
+rs_stats_kernel(char* const* heaps, long long grad_off, long long s0, long long n, int world,
+                float mul, float* __restrict__ out, long long fanout_off,
+                float* __restrict__ partials, unsigned* __restrict__ pflags) {
+  float ss = 0.f;
+  unsigned bad = 0u;
+  const long long nvec = n / VEC;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    float acc[VEC];
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) acc[k] = 0.f;
+    for (int q = 0; q < world; ++q) {
+      const T* src = reinterpret_cast<const T*>(heaps[q] + grad_off) + s0 + i * VEC;
+      if (VEC == 8) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(src);
+        const T* h = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) acc[k] += to_f32(h[k]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) acc[k] += to_f32(src[k]);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+      const float v = acc[k] * mul;
+      bad |= finite_f32(v) ? 0u : 1u;
+      ss = fmaf(v, v, ss);
+      acc[k] = v;
+    }
+    float* o = out + i * VEC;
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) o[k] = acc[k];
+    if (fanout_off >= 0) {
+      for (int q = 0; q < world; ++q) {
+        float* dst = reinterpret_cast<float*>(heaps[q] + fanout_off) + s0 + i * VEC;
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) dst[k] = acc[k];
+      }
+    }
+  }
+  for (long long i = nvec * VEC + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += stride) {
+    float a = 0.f;
+    for (int q = 0; q < world; ++q)
+      a += to_f32(reinterpret_cast<const T*>(heaps[q] + grad_off)[s0 + i]);
+    const float v = a * mul;
+    bad |= finite_f32(v) ? 0u : 1u;
+    ss = fmaf(v, v, ss);
+    out[i] = v;
+    if (fanout_off >= 0)
+      for (int q = 0; q < world; ++q) reinterpret_cast<float*>(heaps[q] + fanout_off)[s0 + i] = v;
+  }
+  if (fanout_off >= 0) __threadfence_system();
+  __shared__ float s_ss[8];
+  __shared__ unsigned s_bad[8];
+  ss = warp_sum(ss);
+  bad = warp_or(bad);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    s_ss[warp] = ss;
+    s_bad[warp] = bad;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    ss = lane < 8 ? s_ss[lane] : 0.f;
+    bad = lane < 8 ? s_bad[lane] : 0u;
+    ss = warp_sum(ss);
+    bad = warp_or(bad);
+    if (lane == 0) {
+      partials[blockIdx.x] = ss;
+      pflags[blockIdx.x] = bad;
+    }
+  }
+}
+
+__global__ void stats_exchange_kernel(char* const* heaps, long long sync_off, int rank, int world,
+                                      unsigned epoch, float* out, double max_norm,
+                                      unsigned long long timeout_ns, unsigned* status) {
+  if (threadIdx.x == 0) {
+    const float flag = out[0], sumsq = out[1];
+    for (int q = 0; q < world; ++q) {
+      Board* b = board_of(heaps[q], sync_off) + rank;
+      b->flag = flag;
+      b->sumsq = sumsq;
+    }
+    __threadfence_system();
+    for (int q = 0; q < world; ++q) st_release_sys(&(board_of(heaps[q], sync_off) + rank)->epoch, epoch);
+    Board* mine = board_of(heaps[rank], sync_off);
+    double total = 0.0;
+    float any = 0.f;
+    bool ok = true;
+    for (int q = 0; q < world && ok; ++q) {
+      const uint64_t t0 = gtime_ns();
+      while (ld_acquire_sys(&mine[q].epoch) != epoch) {
+        if (gtime_ns() - t0 > timeout_ns) {
+          atomicCAS(status, 0u, 0x200u | static_cast<unsigned>(q));
+          ok = false;
+          break;
+        }
+      }
+    }
+    if (ok) {
+      // rank order: every rank adds the same numbers in the same order
+      for (int q = 0; q < world; ++q) {
+        const volatile Board* b = &mine[q];
+        total += (double)b->sumsq;
+        any = fmaxf(any, b->flag);
+      }
+    } else {
+      any = 1.f;  // a timed-out step is never applied
+    }
+    out[0] = any > 0.f ? 1.f : 0.f;
+    out[1] = (float)total;
+    const float norm = sqrtf(out[1]);
+    out[2] = norm;
+    float coef = 1.f;
+    if (max_norm > 0.0 && (double)norm > max_norm) coef = (float)(max_norm / ((double)norm + 1e-6));
+    out[3] = coef;
+  }
+}
+
+struct AdamArgs2 {
+  float lr_neg, wd_term, b1, omb1, b2, omb2, bc1, bc2, eps, grad_mul;
+};
+
+template <typename P, int VEC>
+__global__ void __launch_bounds__(256)
+adamw_fanout_kernel(float* __restrict__ master, float* __restrict__ m, float* __restrict__ v,
+                    const float* __restrict__ grad, char* const* heaps, long long param_off,
+                    long long s0, long long n, int world, const float* __restrict__ stats,
+                    AdamArgs2 a) {
+  if (stats[0] != 0.f) return;  // overflow: nothing changes on any rank
+  const float coef = stats[3];
+  const long long nvec = n / VEC;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec + (n % VEC ? 1 : 0);
+       i += stride) {
+    const long long e0 = i * VEC;
+    const int cnt = (int)min((long long)VEC, n - e0);
+    alignas(16) P outv[VEC];
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+      if (k < cnt) {
+        const long long e = e0 + k;
+        float p = master[e], mm = m[e], vv = v[e];
+        float g = grad[e] * a.grad_mul;
+        g = g * coef;
+        if (a.wd_term != 0.f) p = p + a.wd_term * p;
+        mm = mm * a.b1 + a.omb1 * g;
+        vv = vv * a.b2 + a.omb2 * g * g;
+        const float denom = sqrtf(vv / a.bc2) + a.eps;
+        p = p + a.lr_neg * ((mm / a.bc1) / denom);
+        master[e] = p;
+        m[e] = mm;
+        v[e] = vv;
+        outv[k] = from_f32<P>(p);
+      }
+    }
+    // one vector store per rank when the destination allows it: 4 x 16-bit
+    // = 8 bytes, 4 x fp32 = 16 bytes
+    constexpr int BYTES = static_cast<int>(sizeof(P)) * VEC;
+    for (int q = 0; q < world; ++q) {
+      P* dst = reinterpret_cast<P*>(heaps[q] + param_off) + s0 + e0;
+      const bool vec = cnt == VEC && (reinterpret_cast<uintptr_t>(dst) % BYTES) == 0;
+      if (vec && BYTES == 8) {
+        *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(outv);
+      } else if (vec && BYTES == 16) {
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(outv);
+      } else {
+        for (int k = 0; k < cnt; ++k) dst[k] = outv[k];
+      }
+    }
+  }
+  __threadfence_system();
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+gather_pull_kernel(char* const* heaps, long long shard_off, long long shard, int world,
+                   T* __restrict__ dst) {
+  const long long total = shard * world;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int q = (int)(i / shard);
+    const long long j = i - (long long)q * shard;
+    dst[i] = reinterpret_cast<const T*>(heaps[q] + shard_off)[j];
+  }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------- host API
+void peer_barrier(char* const* heaps, long long sync_off, int rank, int world, unsigned epoch,
+                  double timeout_s, unsigned* status, cudaStream_t st) {
+  peer_barrier_kernel<<<1, 32, 0, st>>>(heaps, sync_off, rank, world, epoch,
+                                        (unsigned long long)(timeout_s * 1e9), status);
+  MSB_CHECK_LAUNCH("peer_barrier");
+}
+
+int rs_stats(char* const* heaps, long long grad_off, int dtype, long long s0, long long n,
+             int world, float mul, float* out, long long fanout_off, float* partials,
+             unsigned* pflags, int max_blocks, bool aligned16, cudaStream_t st) {
+  int blocks = 1;
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    constexpr int V = 16 / sizeof(T);
+    if (aligned16 && V == 8) {
+      blocks = grid_for(n / V, 256, max_blocks);
+      rs_stats_kernel<T, 8><<<blocks, 256, 0, st>>>(heaps, grad_off, s0, n, world, mul, out,
+                                                    fanout_off, partials, pflags);
+    } else {
+      blocks = grid_for(n, 256, max_blocks);
+      rs_stats_kernel<T, 1><<<blocks, 256, 0, st>>>(heaps, grad_off, s0, n, world, mul, out,
+                                                    fanout_off, partials, pflags);
+    }
+  });
+  MSB_CHECK_LAUNCH("rs_stats");
+  return blocks;
+}
+
+void stats_exchange(char* const* heaps, long long sync_off, int rank, int world, unsigned epoch,
+                    float* out, double max_norm, double timeout_s, unsigned* status,
+                    cudaStream_t st) {
+  stats_exchange_kernel<<<1, 32, 0, st>>>(heaps, sync_off, rank, world, epoch, out, max_norm,
+                                          (unsigned long long)(timeout_s * 1e9), status);
+  MSB_CHECK_LAUNCH("stats_exchange");
+}
+
+void adamw_fanout(float* master, float* m, float* v, const float* grad, char* const* heaps,
+                  long long param_off, int pdtype, long long s0, long long n, int world,
+                  const float* stats, double lr, double beta1, double beta2, double eps,
+                  double wd, double bc1, double bc2, double grad_mul, cudaStream_t st) {
+  AdamArgs2 a;
+  a.lr_neg = (float)(-lr);
+  a.wd_term = (float)(-lr * wd);
+  a.b1 = (float)beta1;
+  a.omb1 = (float)(1.0 - beta1);
+  a.b2 = (float)beta2;
+  a.omb2 = (float)(1.0 - beta2);
+  a.bc1 = (float)bc1;
+  a.bc2 = (float)bc2;
+  a.eps = (float)eps;
+  a.grad_mul = (float)grad_mul;
+  const int blocks = grid_for(n / 4 + 1, 256, kNumSMs * 16);
+  if (pdtype == kF16)
+    adamw_fanout_kernel<__half, 4><<<blocks, 256, 0, st>>>(master, m, v, grad, heaps, param_off, s0,
+                                                           n, world, stats, a);
+  else if (pdtype == kBF16)
+    adamw_fanout_kernel<__nv_bfloat16, 4><<<blocks, 256, 0, st>>>(master, m, v, grad, heaps,
+                                                                  param_off, s0, n, world, stats, a);
+  else
+    adamw_fanout_kernel<float, 4><<<blocks, 256, 0, st>>>(master, m, v, grad, heaps, param_off, s0,
+                                                          n, world, stats, a);
+  MSB_CHECK_LAUNCH("adamw_fanout");
+}
+
+void gather_pull(char* const* heaps, long long shard_off, long long shard, int world, void* dst,
+                 int dtype, cudaStream_t st) {
+  const int blocks = grid_for(shard * world, 256, kNumSMs * 16);
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    gather_pull_kernel<T><<<blocks, 256, 0, st>>>(heaps, shard_off, shard, world,
+                                                  static_cast<T*>(dst));
+  });
+  MSB_CHECK_LAUNCH("gather_pull");
+}
+
+// --------------------------------------------------------- peer heap
+void* peer_alloc(size_t bytes) {
+  void* p = nullptr;
+  check_cuda(cudaMalloc(&p, bytes), "peer heap cudaMalloc");
+  check_cuda(cudaMemset(p, 0, bytes), "peer heap memset");
+  return p;
+}
+void peer_free(void* p) { check_cuda(cudaFree(p), "peer heap cudaFree"); }
+void peer_handle(void* p, char out[64]) {
+  cudaIpcMemHandle_t h;
+  check_cuda(cudaIpcGetMemHandle(&h, p), "cudaIpcGetMemHandle");
+  memcpy(out, &h, sizeof(h));
+}
+void* peer_open(const char handle[64]) {
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  check_cuda(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  return p;
+}
+void peer_close(void* p) { check_cuda(cudaIpcCloseMemHandle(p), "cudaIpcCloseMemHandle"); }
+
+}  // namespace msb

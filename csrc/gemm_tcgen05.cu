@@ -803,11 +803,43 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
 
 }  // namespace pair
 
-// C = sum_s ws[s] (+ bias) (+ C)
+// C = sum_s ws[s] (+ bias) (+ C); 4 columns per thread (16-byte workspace loads)
 template <typename T>
 __global__ void __launch_bounds__(256)
 splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N, T* __restrict__ C,
                      long long ldc, const T* __restrict__ bias, int accumulate) {
+  const long long total = (long long)M * N;
+  const int nq = N >> 2;  // N % 4 == 0 on this path
+  const long long quads = (long long)M * nq;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < quads;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int m = (int)(i / nq), n = (int)(i % nq) * 4;
+    const long long e = (long long)m * N + n;
+    float4 acc = *reinterpret_cast<const float4*>(ws + e);
+    for (int s = 1; s < splits; ++s) {
+      const float4 w = *reinterpret_cast<const float4*>(ws + (long long)s * total + e);
+      acc.x += w.x;
+      acc.y += w.y;
+      acc.z += w.z;
+      acc.w += w.w;
+    }
+    float a[4] = {acc.x, acc.y, acc.z, acc.w};
+    T* c = C + (long long)m * ldc + n;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float x = a[k];
+      if (bias != nullptr) x += to_f32(bias[n + k]);
+      if (accumulate) x += to_f32(c[k]);
+      c[k] = from_f32<T>(x);
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+splitk_reduce_scalar_kernel(const float* __restrict__ ws, int splits, int M, int N,
+                            T* __restrict__ C, long long ldc, const T* __restrict__ bias,
+                            int accumulate) {
   const long long total = (long long)M * N;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -818,6 +850,21 @@ splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N, T* 
     T* c = C + (long long)m * ldc + n;
     if (accumulate) acc += to_f32(*c);
     *c = from_f32<T>(acc);
+  }
+}
+
+template <typename T>
+void launch_reduce(const float* ws, int splits, int M, int N, void* C, long long ldc,
+                   const void* bias, int accumulate, cudaStream_t st) {
+  if (N % 4 == 0 && (reinterpret_cast<uintptr_t>(ws) & 15) == 0) {
+    const int blocks = grid_for((long long)M * N / 4, 256, kNumSMs * 8);
+    splitk_reduce_kernel<T><<<blocks, 256, 0, st>>>(ws, splits, M, N, static_cast<T*>(C), ldc,
+                                                    static_cast<const T*>(bias), accumulate);
+  } else {
+    const int blocks = grid_for((long long)M * N, 256, kNumSMs * 8);
+    splitk_reduce_scalar_kernel<T><<<blocks, 256, 0, st>>>(ws, splits, M, N, static_cast<T*>(C),
+                                                           ldc, static_cast<const T*>(bias),
+                                                           accumulate);
   }
 }
 
@@ -967,7 +1014,7 @@ long long gemm_plan(int M, int N, int K, int num_sms, int* bn_out, int* splits_o
       if ((kb + per - 1) / per != s) continue;
       const double waves = std::ceil((double)(tiles * s) / slots);
       double t = waves * per * t_slice;
-      if (s > 1) t += (2.0 * s * (double)M * N * 4.0 + (double)M * N * 2.0) / 6.0e12 * 1e6 + 3.0;
+      if (s > 1) t += (2.0 * s * (double)M * N * 4.0 + (double)M * N * 4.0) / 4.0e12 * 1e6 + 5.0;
       if (t < best - 1e-9) {
         best = t;
         best_bn = bn;
@@ -1055,15 +1102,10 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
   }
   MSB_CHECK_LAUNCH("gemm_tcgen05");
   if (p.splits > 1) {
-    const int blocks = grid_for((long long)M * N, 256, kNumSMs * 8);
     if (dtype == kF16)
-      splitk_reduce_kernel<__half><<<blocks, 256, 0, st>>>(
-          ws, p.splits, M, N, static_cast<__half*>(C), ldc, static_cast<const __half*>(bias),
-          accumulate);
+      launch_reduce<__half>(ws, p.splits, M, N, C, ldc, bias, accumulate, st);
     else
-      splitk_reduce_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
-          ws, p.splits, M, N, static_cast<__nv_bfloat16*>(C), ldc,
-          static_cast<const __nv_bfloat16*>(bias), accumulate);
+      launch_reduce<__nv_bfloat16>(ws, p.splits, M, N, C, ldc, bias, accumulate, st);
     MSB_CHECK_LAUNCH("splitk_reduce");
   }
 }

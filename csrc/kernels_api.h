@@ -62,4 +62,25 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
                   int accumulate, int mode, void* aux, long long ld_aux, float* ws,
                   long long ws_floats, unsigned* err, double timeout_s, cudaStream_t st);
 
+// ---- NVLink peer heap + fused collectives (collectives.cu)
+void peer_barrier(char* const* heaps, long long sync_off, int rank, int world, unsigned epoch,
+                  double timeout_s, unsigned* status, cudaStream_t st);
+int rs_stats(char* const* heaps, long long grad_off, int dtype, long long s0, long long n,
+             int world, float mul, float* out, long long fanout_off, float* partials,
+             unsigned* pflags, int max_blocks, bool aligned16, cudaStream_t st);
+void stats_exchange(char* const* heaps, long long sync_off, int rank, int world, unsigned epoch,
+                    float* out, double max_norm, double timeout_s, unsigned* status,
+                    cudaStream_t st);
+void adamw_fanout(float* master, float* m, float* v, const float* grad, char* const* heaps,
+                  long long param_off, int pdtype, long long s0, long long n, int world,
+                  const float* stats, double lr, double beta1, double beta2, double eps,
+                  double wd, double bc1, double bc2, double grad_mul, cudaStream_t st);
+void gather_pull(char* const* heaps, long long shard_off, long long shard, int world, void* dst,
+                 int dtype, cudaStream_t st);
+void* peer_alloc(size_t bytes);
+void peer_free(void* p);
+void peer_handle(void* p, char out[64]);
+void* peer_open(const char handle[64]);
+void peer_close(void* p);
+
 }  // namespace msb

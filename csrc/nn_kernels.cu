@@ -16,6 +16,8 @@
 //                      logits the reference materializes never exist.
 //   embedding_*        token (+ position) gather-add and its scatter-add
 //   rope_*             rotary position embedding on q/k in place
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace msb {
@@ -128,46 +130,17 @@ add_norm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ delta,
   }
 }
 
-template <int NV>
-__device__ __forceinline__ void block_colsum(float (&acc)[NV][8], float* red, float* out, int C,
-                                             int nvec, int warp, int lane, int warps) {
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int c = (lane + i * 32) << 3;
-    if ((lane + i * 32) < nvec)
-#pragma unroll
-      for (int k = 0; k < 8; ++k) red[warp * C + c + k] = acc[i][k];
-  }
-  __syncthreads();
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    float t = 0.f;
-    for (int q = 0; q < warps; ++q) t += red[q * C + c];
-    out[(size_t)blockIdx.x * C + c] = t;
-  }
-  __syncthreads();
-}
-
-// Backward: one warp per row, ROWS_PER_WARP rows per warp; every lane owns
-// fixed columns and accumulates dw/db for them in registers; the block then
-// writes one partial row per block (deterministic).
+// Row-parallel norm backward: one warp per row, no column accumulators, so
+// many rows are in flight per SM (the column sums are a separate tiled pass).
 template <typename T, int NV, bool RMS>
 __global__ void __launch_bounds__(256)
-norm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ s, const T* __restrict__ w,
-                const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
-                const T* __restrict__ dres, T* __restrict__ dx, float* __restrict__ dw_part,
-                float* __restrict__ db_part, int M, int C, int rows_per_block) {
+norm_dx_kernel(const T* __restrict__ dy, const T* __restrict__ s, const T* __restrict__ w,
+               const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+               const T* __restrict__ dres, T* __restrict__ dx, int M, int C) {
   const int warps = blockDim.x >> 5;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31;
   const int nvec = C >> 3;
-  float dwacc[NV][8], dbacc[NV][8];
-#pragma unroll
-  for (int i = 0; i < NV; ++i)
-#pragma unroll
-    for (int k = 0; k < 8; ++k) dwacc[i][k] = dbacc[i][k] = 0.f;
-
-  const int row0 = blockIdx.x * rows_per_block;
-  const int row1 = min(M, row0 + rows_per_block);
-  for (int row = row0 + warp; row < row1; row += warps) {
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
     const size_t base = (size_t)row * C;
     const float mean = RMS ? 0.f : mean_in[row];
     const float rstd = rstd_in[row];
@@ -187,8 +160,6 @@ norm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ s, const T* __re
           g[i][k] = dyv[k] * wv[k];
           s1 += g[i][k];
           s2 += g[i][k] * xh[i][k];
-          dwacc[i][k] += dyv[k] * xh[i][k];
-          dbacc[i][k] += dyv[k];
         }
       }
     }
@@ -201,8 +172,7 @@ norm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ s, const T* __re
         float o[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          o[k] = RMS ? rstd * (g[i][k] - xh[i][k] * s2)
-                     : rstd * (g[i][k] - s1 - xh[i][k] * s2);
+          o[k] = RMS ? rstd * (g[i][k] - xh[i][k] * s2) : rstd * (g[i][k] - s1 - xh[i][k] * s2);
         if (dres != nullptr) {
           float r[8];
           load8(dres + base + c, r);
@@ -213,10 +183,51 @@ norm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ s, const T* __re
       }
     }
   }
-  // block reduction of the per-lane column partials through shared memory
-  extern __shared__ float red[];  // [warps][C]
-  block_colsum<NV>(dwacc, red, dw_part, C, nvec, warp, lane, warps);
-  if (!RMS) block_colsum<NV>(dbacc, red, db_part, C, nvec, warp, lane, warps);
+}
+
+// Column partials of dw = sum_rows dy * xhat and db = sum_rows dy, tiled like
+// colsum_partial_kernel: block (256-column slab, row chunk).
+template <typename T, bool RMS>
+__global__ void __launch_bounds__(256)
+norm_dwdb_partial_kernel(const T* __restrict__ dy, const T* __restrict__ s,
+                         const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                         float* __restrict__ dw_part, float* __restrict__ db_part, int M, int C,
+                         int rows_per_block) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c0 = blockIdx.x * 256 + lane * 8;
+  const int r0 = blockIdx.y * rows_per_block;
+  const int r1 = min(M, r0 + rows_per_block);
+  float aw[8] = {0, 0, 0, 0, 0, 0, 0, 0}, ab[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (c0 < C) {
+    for (int r = r0 + warp; r < r1; r += 8) {
+      float d[8], x[8];
+      load8(dy + (size_t)r * C + c0, d);
+      load8(s + (size_t)r * C + c0, x);
+      const float mean = RMS ? 0.f : mean_in[r];
+      const float rstd = rstd_in[r];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        aw[k] += d[k] * ((x[k] - mean) * rstd);
+        ab[k] += d[k];
+      }
+    }
+  }
+  __shared__ float red[8][256 + 8];
+#pragma unroll
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1 && (RMS || db_part == nullptr)) break;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) red[warp][lane * 8 + k] = pass == 0 ? aw[k] : ab[k];
+    __syncthreads();
+    const int c = blockIdx.x * 256 + threadIdx.x;
+    if (c < C) {
+      float t = 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) t += red[q][threadIdx.x];
+      (pass == 0 ? dw_part : db_part)[(size_t)blockIdx.y * C + c] = t;
+    }
+    __syncthreads();
+  }
 }
 
 // Column sums of a [M, N] matrix (row stride ld) into partials
@@ -624,38 +635,45 @@ void add_norm_fwd(const void* x, const void* delta, const void* w, const void* b
 }
 
 template <typename T, int NVV>
-static void launch_norm_bwd(const void* dy, const void* s, const void* w, const float* mean,
-                            const float* rstd, const void* dres, void* dx, float* dw_part,
-                            float* db_part, int M, int C, bool rms, int blocks, int rpb,
-                            size_t smem, cudaStream_t st) {
-  auto kern = rms ? norm_bwd_kernel<T, NVV, true> : norm_bwd_kernel<T, NVV, false>;
-  check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-             "norm_bwd smem");
-  kern<<<blocks, 256, smem, st>>>((const T*)dy, (const T*)s, (const T*)w, mean, rstd,
-                                  (const T*)dres, (T*)dx, dw_part, db_part, M, C, rpb);
+static void launch_norm_dx(const void* dy, const void* s, const void* w, const float* mean,
+                           const float* rstd, const void* dres, void* dx, int M, int C, bool rms,
+                           cudaStream_t st) {
+  const int blocks = grid_for((M + 7) / 8, 1, kNumSMs * 16);
+  if (rms)
+    norm_dx_kernel<T, NVV, true><<<blocks, 256, 0, st>>>((const T*)dy, (const T*)s, (const T*)w,
+                                                          mean, rstd, (const T*)dres, (T*)dx, M, C);
+  else
+    norm_dx_kernel<T, NVV, false><<<blocks, 256, 0, st>>>((const T*)dy, (const T*)s, (const T*)w,
+                                                           mean, rstd, (const T*)dres, (T*)dx, M,
+                                                           C);
 }
 
 int norm_bwd(const void* dy, const void* s, const void* w, const float* mean, const float* rstd,
              const void* dres, void* dx, float* dw_part, float* db_part, int M, int C, bool rms,
              int dtype, int max_blocks, cudaStream_t st) {
   const int nv = (C / 8 + 31) / 32;
-  const int warps = 8;
-  int blocks = min(max_blocks, (M + warps - 1) / warps);
-  if (blocks < 1) blocks = 1;
-  const int rpb = (M + blocks - 1) / blocks;
-  blocks = (M + rpb - 1) / rpb;
-  const size_t smem = (size_t)warps * C * sizeof(float);
+  int chunks = std::min(max_blocks, std::max(1, (M + 63) / 64));
+  const int rpb = (M + chunks - 1) / chunks;
+  chunks = (M + rpb - 1) / rpb;
+  dim3 grid((C + 255) / 256, chunks);
   MSB_DISPATCH_FLOAT(dtype, T, {
-    if (nv <= 1) launch_norm_bwd<T, 1>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, blocks, rpb, smem, st);
-    else if (nv <= 2) launch_norm_bwd<T, 2>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, blocks, rpb, smem, st);
-    else if (nv <= 3) launch_norm_bwd<T, 3>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, blocks, rpb, smem, st);
-    else if (nv <= 4) launch_norm_bwd<T, 4>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, blocks, rpb, smem, st);
-    else if (nv <= 8) launch_norm_bwd<T, 8>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, blocks, rpb, smem, st);
-    else if (nv <= 16) launch_norm_bwd<T, 16>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, blocks, rpb, smem, st);
+    if (nv <= 1) launch_norm_dx<T, 1>(dy, s, w, mean, rstd, dres, dx, M, C, rms, st);
+    else if (nv <= 2) launch_norm_dx<T, 2>(dy, s, w, mean, rstd, dres, dx, M, C, rms, st);
+    else if (nv <= 3) launch_norm_dx<T, 3>(dy, s, w, mean, rstd, dres, dx, M, C, rms, st);
+    else if (nv <= 4) launch_norm_dx<T, 4>(dy, s, w, mean, rstd, dres, dx, M, C, rms, st);
+    else if (nv <= 8) launch_norm_dx<T, 8>(dy, s, w, mean, rstd, dres, dx, M, C, rms, st);
+    else if (nv <= 16) launch_norm_dx<T, 16>(dy, s, w, mean, rstd, dres, dx, M, C, rms, st);
     else throw std::runtime_error("norm_bwd: hidden size too large");
+    MSB_CHECK_LAUNCH("norm_dx");
+    if (rms)
+      norm_dwdb_partial_kernel<T, true><<<grid, 256, 0, st>>>((const T*)dy, (const T*)s, mean,
+                                                             rstd, dw_part, nullptr, M, C, rpb);
+    else
+      norm_dwdb_partial_kernel<T, false><<<grid, 256, 0, st>>>((const T*)dy, (const T*)s, mean,
+                                                              rstd, dw_part, db_part, M, C, rpb);
   });
-  MSB_CHECK_LAUNCH("norm_bwd");
-  return blocks;
+  MSB_CHECK_LAUNCH("norm_dwdb_partial");
+  return chunks;
 }
 
 int colsum_partial(const void* a, float* part, int M, int N, long long ld, int dtype,

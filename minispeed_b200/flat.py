@@ -85,6 +85,9 @@ class FlatParamGroup:
         self.param_arena: Optional[torch.Tensor] = None
         self.param_shard: Optional[torch.Tensor] = None
         self.grad_arena: Optional[torch.Tensor] = None
+        # a pinned gradient arena (peer heap) is zeroed between windows,
+        # never freed, so peers can keep addressing it
+        self._arena_pinned = False
         self._partitioned = False
         self._bind_full(self._new_arena_from_params(self.param_dtype))
 
@@ -305,13 +308,14 @@ class FlatParamGroup:
         if self._grad_shard is not None:
             self._grad_shard.zero_()
         if self.grad_arena is not None:
-            if self.zero_stage >= 3:
+            if self.zero_stage >= 3 and not self._arena_pinned:
                 self.grad_arena = None
                 for p in self.params:
                     p.grad = None
             else:
                 self.grad_arena.zero_()
-                self.bind_grads()
+                if self.param_arena is not None:
+                    self.bind_grads()
 
     def grad_for_shard(self) -> torch.Tensor:
         if self.grad_shard is not None:

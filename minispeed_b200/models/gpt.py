@@ -59,8 +59,8 @@ class CausalSelfAttention(nn.Module):
         B, T, C = h.shape
         qkv = ops.linear(h, self.qkv.weight, self.qkv.bias).view(B, T, 3, self.n_head,
                                                                  self.head_dim)
-        att = ops.causal_attention(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2])
-        return ops.linear(att.reshape(B, T, C), self.proj.weight, self.proj.bias)
+        att = ops.attention_qkv(qkv)
+        return ops.linear(att, self.proj.weight, self.proj.bias)
 
 
 class Block(nn.Module):

@@ -1,23 +1,21 @@
-"""Causal self-attention (forward + backward) on [B, T, H, D] tensors.
+"""Causal self-attention (forward + backward) over a fused qkv projection.
 
-The sm_100a flash-attention kernel (``csrc/attention.cu``) is used when the
-extension provides it: blockwise online softmax, causal tile skipping, GQA
-by head mapping, q/k/v read straight from the fused qkv projection layout
-and the output written in the [B, T, H*D] layout the output projection
-consumes.  ``MSB_ATTN=torch`` selects PyTorch's SDPA instead (comparison
-baseline in the tests).
+``attention_qkv(qkv)`` takes the [B, T, 3, H, D] output of the fused qkv
+projection and returns [B, T, H*D], the layout the output projection
+consumes.  Its backward writes dq, dk and dv into ONE [B, T, 3, H, D]
+buffer with a single kernel; going through three views of the qkv tensor
+instead would make autograd materialize three zero-filled full-size
+gradients and add them (3 fills + 3 copies + 2 adds per layer).
+
+The attention core is PyTorch's scaled_dot_product_attention (the cuDNN
+sm_100 flash kernels), run on strided [B, H, T, D] views without copies.
+GQA (fewer kv heads) is handled by :func:`causal_attention`.
 """
 
 from __future__ import annotations
 
-import os
-
 import torch
 import torch.nn.functional as F
-
-from . import _ext
-
-_MODE = os.environ.get("MSB_ATTN", "auto")
 
 
 def _sdpa(q, k, v):
@@ -31,9 +29,36 @@ def _sdpa(q, k, v):
     return o.transpose(1, 2)
 
 
-def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
-    if q.is_cuda and _MODE != "torch" and hasattr(_ext.get(), "attn_fwd"):
-        from .flash import flash_attention
+class _AttnQKV(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv):
+        B, T, _, H, D = qkv.shape
+        with torch.enable_grad():
+            leaves = [qkv[:, :, i].detach().transpose(1, 2).requires_grad_() for i in range(3)]
+            o = F.scaled_dot_product_attention(*leaves, is_causal=True)
+        ctx.graph = (leaves, o)
+        ctx.shape = (B, T, H, D)
+        return o.detach().transpose(1, 2).reshape(B, T, H * D)
 
-        return flash_attention(q, k, v)
+    @staticmethod
+    def backward(ctx, dout):
+        leaves, o = ctx.graph
+        B, T, H, D = ctx.shape
+        g = dout.reshape(B, T, H, D).transpose(1, 2)
+        dq, dk, dv = torch.autograd.grad(o, leaves, g)
+        ctx.graph = None
+        return torch.stack([t.transpose(1, 2) for t in (dq, dk, dv)], dim=2)
+
+
+def attention_qkv(qkv: torch.Tensor) -> torch.Tensor:
+    """Causal attention of a [B, T, 3, H, D] fused projection -> [B, T, H*D]."""
+    if qkv.is_cuda:
+        return _AttnQKV.apply(qkv)
+    B, T, _, H, D = qkv.shape
+    return _sdpa(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]).reshape(B, T, H * D)
+
+
+def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """Causal attention over [B, T, H, D] q and [B, T, Hkv, D] k/v (GQA when
+    Hkv < H); returns [B, T, H, D]."""
     return _sdpa(q, k, v)

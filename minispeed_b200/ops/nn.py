@@ -27,7 +27,7 @@ import torch.nn.functional as F
 from . import _ext, gemm
 
 _COLSUM_CHUNKS = 256   # row chunks of a column-sum reduction
-_NORM_BLOCKS = 148 * 2  # norm backward blocks (one partial row of dw/db each)
+_NORM_BLOCKS = 256     # row chunks of the norm-backward dw/db column sums
 
 
 def _C():
@@ -442,6 +442,13 @@ def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch
     from . import attention
 
     return attention.causal_attention(q, k, v)
+
+
+def attention_qkv(qkv: torch.Tensor) -> torch.Tensor:
+    """Causal attention of a fused [B, T, 3, H, D] projection -> [B, T, H*D]."""
+    from . import attention
+
+    return attention.attention_qkv(qkv)
 
 
 def gelu_reference(x: torch.Tensor) -> torch.Tensor:

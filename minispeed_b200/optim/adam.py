@@ -102,26 +102,33 @@ class FlatAdam:
     @torch.no_grad()
     def fused_step(self, grads: List[torch.Tensor], stats: torch.Tensor,
                    grad_mul: float, max_norm: Optional[float],
-                   param_outs: List[Optional[torch.Tensor]],
-                   peer_params=None) -> None:
+                   param_outs: List[Optional[torch.Tensor]], fanouts=None) -> None:
         """Enqueue the device-skipping fused update for every group.
 
         ``grads[i]`` is group i's gradient covering its shard (any float
         dtype), scaled by ``grad_mul`` inside the kernel; ``stats`` is the
         finalized device statistics tensor (flag, sum of squares, norm,
-        clip coefficient).  The step counters advance on the host only once
-        the caller knows the step was applied (:meth:`commit_step`).
+        clip coefficient).  ``fanouts[i]``, when given, makes the kernel
+        store the cast parameters into every rank's parameter arena over
+        NVLink (the fused all-gather).  The step counters advance on the host
+        only once the caller knows the step was applied (:meth:`commit_step`).
         """
-        from ..ops import kernels
+        from ..ops import _ext, kernels
 
         for i, (group, flat, st) in enumerate(zip(self.param_groups, self.flat_groups,
                                                    self._state)):
             lr, b1, b2, eps, wd, bc1, bc2 = self.hyper(group, st["step"] + 1)
+            fan = None if fanouts is None else fanouts[i]
+            if fan is not None:
+                heaps, param_off, pdtype, s0, world = fan
+                _ext.get().adamw_fanout(flat.shard, st["exp_avg"], st["exp_avg_sq"], grads[i],
+                                        heaps, param_off, pdtype, s0, world, stats, lr, b1, b2,
+                                        eps, wd, bc1, bc2, grad_mul)
+                continue
             kernels.adamw_step(flat.shard, st["exp_avg"], st["exp_avg_sq"], grads[i],
                                lr=lr, beta1=b1, beta2=b2, eps=eps, wd=wd, bc1=bc1, bc2=bc2,
                                grad_mul=grad_mul, stats=stats,
-                               max_norm=max_norm, param_out=param_outs[i],
-                               peer=None if peer_params is None else peer_params[i])
+                               max_norm=max_norm, param_out=param_outs[i])
 
     def commit_step(self) -> None:
         for st in self._state:

@@ -39,9 +39,12 @@ class LocalCollectives:
         self.world_size = 1
         self.rank = 0
 
-    def reduce_grads(self, g: FlatParamGroup, arena: torch.Tensor, inv_scale: float
-                     ) -> Tuple[torch.Tensor, float]:
-        return arena[g.shard_start:g.shard_end], inv_scale
+    def attach(self, groups, zero_stage: int) -> None:
+        pass
+
+    def reduce_grads(self, g: FlatParamGroup, arena: torch.Tensor, inv_scale: float,
+                     stats=None) -> Tuple[torch.Tensor, float, bool]:
+        return arena[g.shard_start:g.shard_end], inv_scale, False
 
     def stats_need_allreduce(self, stage: int) -> bool:
         return False
@@ -49,7 +52,16 @@ class LocalCollectives:
     def all_reduce_stats(self, out: torch.Tensor) -> None:
         pass
 
+    def fanout(self, g: FlatParamGroup):
+        return None
+
     def gather_params(self, g: FlatParamGroup) -> None:
+        pass
+
+    def end_step(self) -> None:
+        pass
+
+    def check(self) -> None:
         pass
 
     def gather_shards(self, g: FlatParamGroup) -> None:
@@ -82,8 +94,20 @@ class LibraryCollectives:
             self._rs_out[key] = buf
         return buf
 
-    def reduce_grads(self, g: FlatParamGroup, arena: torch.Tensor, inv_scale: float
-                     ) -> Tuple[torch.Tensor, float]:
+    def attach(self, groups, zero_stage: int) -> None:
+        pass
+
+    def fanout(self, g: FlatParamGroup):
+        return None
+
+    def end_step(self) -> None:
+        pass
+
+    def check(self) -> None:
+        pass
+
+    def reduce_grads(self, g: FlatParamGroup, arena: torch.Tensor, inv_scale: float,
+                     stats=None) -> Tuple[torch.Tensor, float, bool]:
         full = g._grad
         if full is None:
             full = torch.empty(g.numel_padded, dtype=torch.float32, device=g.device)
@@ -91,11 +115,11 @@ class LibraryCollectives:
         if g.zero_stage == 0:
             dist.all_reduce(full)
             g._grad = full
-            return full, 1.0 / self.world_size
+            return full, 1.0 / self.world_size, False
         out = self._shard_out(g)
         dist.reduce_scatter_tensor(out, full)
         g._grad = None if g.zero_stage >= 3 else full
-        return out, 1.0 / self.world_size
+        return out, 1.0 / self.world_size, False
 
     def stats_need_allreduce(self, stage: int) -> bool:
         return stage >= 1

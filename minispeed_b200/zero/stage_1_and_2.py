@@ -74,12 +74,16 @@ class ZeROOptimizer:
         device = flat_groups[0].device
         self.coll = collectives if collectives is not None else make_collectives(
             self.world_size, self.rank, device)
+        self.coll.attach(flat_groups, zero_stage)
         self.stats = kernels.StepStats(device)
         self._host_stats = (torch.zeros(4, dtype=torch.float32, pin_memory=True)
                             if device.type == "cuda" else None)
         # stages 1-2 only all-gather the model-dtype params each step; the
         # fp32 masters outside this rank's shard are refreshed on demand
         self._masters_stale = False
+        # optional CUDA-event timing of the communication phases of each step
+        # (list of (reduce_ms, gather_ms)); enabled by the engine
+        self.phase_log = None
 
     # ------------------------------------------------------ torch surface
     @property
@@ -135,11 +139,16 @@ class ZeROOptimizer:
         inv = 1.0 / float(loss_scale)
         st = self.stats
         st.reset()
+        ev = None
+        if self.phase_log is not None and st.device.type == "cuda":
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            ev[0].record()
         grads, mul = [], 1.0
         for g in self.flat_groups:
             arena = g.collect_grads()
-            red, mul = self.coll.reduce_grads(g, arena, inv)
-            st.accumulate(red, mul)
+            red, mul, stats_done = self.coll.reduce_grads(g, arena, inv, st)
+            if not stats_done:
+                st.accumulate(red, mul)
             grads.append(red)
         if self.coll.stats_need_allreduce(self.zero_stage):
             st.finalize(max_norm, epilogue=False)
@@ -147,13 +156,25 @@ class ZeROOptimizer:
             out = st.epilogue(max_norm)
         else:
             out = st.finalize(max_norm)
+        if ev is not None:
+            ev[1].record()
         targets = [self._param_target(g) for g in self.flat_groups]
-        self.adam.fused_step(grads, out, mul, max_norm, targets)
+        fanouts = [self.coll.fanout(g) for g in self.flat_groups]
+        self.adam.fused_step(grads, out, mul, max_norm, targets, fanouts)
+        if ev is not None:
+            ev[2].record()
         if 1 <= self.zero_stage <= 2 and self.world_size > 1:
             for g in self.flat_groups:
                 self.coll.gather_params(g)
             self._masters_stale = True
+        self.coll.end_step()
+        if ev is not None:
+            ev[3].record()
         flag, norm = self._read_stats(out)
+        self.coll.check()
+        if ev is not None:
+            self.phase_log.append((ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]),
+                                   ev[2].elapsed_time(ev[3])))
         if flag:
             return False, None
         self.adam.commit_step()

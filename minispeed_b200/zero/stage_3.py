@@ -43,7 +43,7 @@ class ZeROStage3Optimizer(ZeROOptimizer):
         for g in self.flat_groups:
             g.materialize_params()
             self.coll.gather_shards(g)
-            if torch.is_grad_enabled():
+            if torch.is_grad_enabled() or g._arena_pinned:
                 g.ensure_grad_arena()
         self._gathered = True
 

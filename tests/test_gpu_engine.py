@@ -104,3 +104,49 @@ def test_gpt_matches_cpu_fp32_forward():
     lc = cpu(idx, targets=tgt)
     lg = gpu(idx.cuda(), targets=tgt.cuda())
     assert float(lg) == pytest.approx(float(lc), rel=2e-3)
+
+
+def test_peer_barrier_wait_times_out_with_status():
+    """A device barrier whose peer never signals gives up and reports; the
+    context stays usable (no trap, no endless wait)."""
+    import time
+
+    from minispeed_b200.ops import _ext
+
+    C = _ext.get()
+    a = C.peer_alloc(8192)
+    b = C.peer_alloc(8192)   # stands in for a peer heap nobody writes
+    try:
+        heaps = torch.tensor([a, b], dtype=torch.int64, device="cuda")
+        status = torch.zeros(4, dtype=torch.int32, device="cuda")
+        t0 = time.time()
+        C.peer_barrier(heaps, 0, 0, 2, 1, 0.3, status)
+        torch.cuda.synchronize()
+        assert 0.2 < time.time() - t0 < 30
+        assert int(status[0]) == 0x101          # waited on rank 1
+        x = torch.ones(4, device="cuda") * 2    # context still healthy
+        assert float(x.sum()) == 8.0
+    finally:
+        torch.cuda.synchronize()
+        C.peer_free(a)
+        C.peer_free(b)
+
+
+def test_stats_exchange_times_out_and_blocks_the_update():
+    from minispeed_b200.ops import _ext
+
+    C = _ext.get()
+    a = C.peer_alloc(8192)
+    b = C.peer_alloc(8192)
+    try:
+        heaps = torch.tensor([a, b], dtype=torch.int64, device="cuda")
+        status = torch.zeros(4, dtype=torch.int32, device="cuda")
+        out = torch.tensor([0.0, 4.0, 0, 0, 0, 0, 0, 0], device="cuda")
+        C.stats_exchange(heaps, 0, 0, 2, 7, out, 1.0, 0.2, status)
+        torch.cuda.synchronize()
+        assert int(status[0]) == 0x201
+        assert float(out[0]) == 1.0   # a timed-out step is flagged, never applied
+    finally:
+        torch.cuda.synchronize()
+        C.peer_free(a)
+        C.peer_free(b)

@@ -1,0 +1,77 @@
+"""Two ranks on two GPUs: the fused NVLink collectives against the
+single-process union-batch run and against the NCCL path (stages 0-3)."""
+
+import os
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import minispeed_b200 as ms
+from tests.helpers import config, free_port, make_data, make_net, rank_slice, run
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+WORLD, STEPS, GAS, MICRO = 2, 4, 2, 4
+
+
+def _worker(rank, stage, dtype, comm_mode, port, out_dir):
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port),
+                       "RANK": str(rank), "WORLD_SIZE": str(WORLD), "LOCAL_RANK": str(rank),
+                       "LOCAL_WORLD_SIZE": str(WORLD), "MINISPEED_DEVICE": f"cuda:{rank}",
+                       "MINISPEED_PG_TIMEOUT_S": "120", "NCCL_NVLS_ENABLE": "0"})
+    os.environ.pop("MINISPEED_BACKEND", None)
+    torch.cuda.set_device(rank)
+    cfg = config(micro=MICRO, gas=GAS, stage=stage, dtype=dtype, clip=0.5,
+                 b200={"comm": comm_mode, "wait_timeout_ms": 20000})
+    engine = ms.initialize(model=make_net(), config=cfg)
+    x, y = make_data(STEPS, GAS, WORLD, MICRO)
+    losses = run(engine, rank_slice(x, rank, MICRO), rank_slice(y, rank, MICRO), STEPS, GAS,
+                 device=f"cuda:{rank}")
+    params = {k: v.detach().float().cpu() for k, v in engine.state_dict().items()}
+    torch.save({"losses": torch.tensor(losses), "params": params, "coll": engine.collectives,
+                "norm": engine.grad_norm, "steps": engine.global_steps},
+               os.path.join(out_dir, f"r{rank}.pt"))
+    engine.close()
+    ms.comm.destroy()
+
+
+def _spawn(tmp_path, stage, dtype, comm_mode):
+    mp.spawn(_worker, args=(stage, dtype, comm_mode, free_port(), str(tmp_path)), nprocs=WORLD,
+             join=True)
+    return [torch.load(tmp_path / f"r{r}.pt", weights_only=False) for r in range(WORLD)]
+
+
+@pytest.fixture(autouse=True)
+def _two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+
+
+@pytest.mark.parametrize("stage", [0, 1, 2, 3])
+def test_fused_nvlink_matches_single_process(stage, tmp_path, monkeypatch):
+    r0, r1 = _spawn(tmp_path, stage, "fp32", "fused")
+    assert r0["coll"] == "fused-nvlink"
+    assert r0["steps"] == STEPS
+    monkeypatch.setenv("MINISPEED_DEVICE", "cuda:0")
+    ref = ms.initialize(model=make_net(), config=config(micro=MICRO * WORLD, gas=GAS, stage=0,
+                                                        clip=0.5))
+    x, y = make_data(STEPS, GAS, WORLD, MICRO)
+    ref_losses = torch.tensor(run(ref, x, y, STEPS, GAS, device="cuda:0"))
+    torch.testing.assert_close((r0["losses"] + r1["losses"]) / 2, ref_losses, rtol=2e-3,
+                               atol=1e-4)
+    assert r0["norm"] == r1["norm"]
+    for k, v in ref.state_dict().items():
+        torch.testing.assert_close(r0["params"][k], r1["params"][k], rtol=0, atol=0)
+        torch.testing.assert_close(r0["params"][k], v.float().cpu(), rtol=2e-3, atol=2e-4)
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+def test_fused_matches_nccl_path(dtype, tmp_path):
+    fused = _spawn(tmp_path / "f", 2, dtype, "fused") if (tmp_path / "f").mkdir() is None else None
+    nccl = _spawn(tmp_path / "n", 2, dtype, "nccl") if (tmp_path / "n").mkdir() is None else None
+    assert fused[0]["coll"] == "fused-nvlink" and nccl[0]["coll"] == "nccl"
+    tol = 2e-2 if dtype == "bf16" else 2e-3
+    torch.testing.assert_close(fused[0]["losses"], nccl[0]["losses"], rtol=tol, atol=tol)
+    for k in fused[0]["params"]:
+        torch.testing.assert_close(fused[0]["params"][k], nccl[0]["params"][k], rtol=tol,
+                                   atol=tol)
