@@ -62,3 +62,37 @@ def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch
     """Causal attention over [B, T, H, D] q and [B, T, Hkv, D] k/v (GQA when
     Hkv < H); returns [B, T, H, D]."""
     return _sdpa(q, k, v)
+
+
+class _AttnGQA(torch.autograd.Function):
+    """Causal GQA attention over a fused [B, T, H + 2*Hkv, D] projection."""
+
+    @staticmethod
+    def forward(ctx, qkv, H, Hkv):
+        B, T, _, D = qkv.shape
+        with torch.enable_grad():
+            parts = (qkv[:, :, :H], qkv[:, :, H:H + Hkv], qkv[:, :, H + Hkv:])
+            leaves = [t.detach().transpose(1, 2).requires_grad_() for t in parts]
+            o = F.scaled_dot_product_attention(*leaves, is_causal=True, enable_gqa=Hkv != H)
+        ctx.graph = (leaves, o)
+        ctx.shape = (B, T, H, D)
+        return o.detach().transpose(1, 2).reshape(B, T, H * D)
+
+    @staticmethod
+    def backward(ctx, dout):
+        leaves, o = ctx.graph
+        B, T, H, D = ctx.shape
+        g = dout.reshape(B, T, H, D).transpose(1, 2)
+        dq, dk, dv = torch.autograd.grad(o, leaves, g)
+        ctx.graph = None
+        return torch.cat([t.transpose(1, 2) for t in (dq, dk, dv)], dim=2), None, None
+
+
+def attention_gqa(qkv: torch.Tensor, n_head: int, n_kv_head: int) -> torch.Tensor:
+    """Causal attention of a fused [B, T, H + 2*Hkv, D] projection -> [B, T, H*D]."""
+    if qkv.is_cuda:
+        return _AttnGQA.apply(qkv, n_head, n_kv_head)
+    B, T, _, D = qkv.shape
+    H, Hkv = n_head, n_kv_head
+    o = _sdpa(qkv[:, :, :H], qkv[:, :, H:H + Hkv], qkv[:, :, H + Hkv:])
+    return o.reshape(B, T, H * D)

@@ -424,6 +424,46 @@ class _Rope(torch.autograd.Function):
         return dx, None, None
 
 
+class _RopeQK(torch.autograd.Function):
+    """Rotary embedding of the q and k heads of a fused [B, T, H+2Hkv, D]
+    projection (v passes through)."""
+
+    @staticmethod
+    def forward(ctx, qkv, cos, sin, H, Hkv):
+        B, T, Ht, D = qkv.shape
+        y = qkv.contiguous().clone()
+        _C().rope(y, cos, sin, B * T, T, H + Hkv, D, Ht * D, False)
+        ctx.save_for_backward(cos, sin)
+        ctx.heads = (H, Hkv)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        cos, sin = ctx.saved_tensors
+        H, Hkv = ctx.heads
+        B, T, Ht, D = dy.shape
+        dx = dy.contiguous().clone()
+        _C().rope(dx, cos, sin, B * T, T, H + Hkv, D, Ht * D, True)
+        return dx, None, None, None, None
+
+
+def rope_qk(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, n_head: int,
+            n_kv_head: int) -> torch.Tensor:
+    """Rotate the first ``n_head + n_kv_head`` heads (q and k) of a fused
+    [B, T, H+2Hkv, D] projection."""
+    if qkv.is_cuda:
+        return _RopeQK.apply(qkv, cos, sin, n_head, n_kv_head)
+    n = n_head + n_kv_head
+    return torch.cat([rope(qkv[:, :, :n], cos, sin), qkv[:, :, n:]], dim=2)
+
+
+def attention_gqa(qkv: torch.Tensor, n_head: int, n_kv_head: int) -> torch.Tensor:
+    """Causal GQA attention of a fused [B, T, H+2Hkv, D] projection -> [B, T, H*D]."""
+    from . import attention
+
+    return attention.attention_gqa(qkv, n_head, n_kv_head)
+
+
 def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     """Rotary embedding of ``x`` [B, T, H, D] (rotate-half convention)."""
     if x.is_cuda:

@@ -150,3 +150,52 @@ def test_stats_exchange_times_out_and_blocks_the_update():
         torch.cuda.synchronize()
         C.peer_free(a)
         C.peer_free(b)
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+def test_llama_matches_cpu_fp32_and_trains(dtype):
+    from minispeed_b200.models import Llama, LlamaConfig, init_llama_
+
+    torch.manual_seed(0)
+    cfg = LlamaConfig(vocab_size=512, block_size=64, n_layer=2, n_head=4, n_kv_head=2,
+                      n_embd=128, ffn_hidden=256)
+    cpu = init_llama_(Llama(cfg))
+    gpu = Llama(cfg).cuda()
+    gpu.load_state_dict(cpu.state_dict())
+    gpu.to(torch.float16 if dtype == "fp16" else torch.bfloat16)
+    idx = torch.randint(0, 512, (2, 64))
+    tgt = torch.roll(idx, -1, 1)
+    lc = cpu(idx, targets=tgt)
+    lg = gpu(idx.cuda(), targets=tgt.cuda())
+    assert float(lg) == pytest.approx(float(lc), rel=5e-3 if dtype == "fp16" else 2e-2)
+    model = init_llama_(Llama(cfg))
+    engine = ms.initialize(model=model, config={
+        "train_micro_batch_size_per_gpu": 2, "dtype": dtype, "gradient_clipping": 1.0,
+        "fp16": {"enabled": dtype == "fp16", "initial_scale_power": 12},
+        "zero_optimization": {"stage": 3},
+        "optimizer": {"type": "AdamW", "params": {"lr": 3e-3}}})
+    data = torch.randint(0, 512, (2, 65), device="cuda")
+    losses = []
+    for _ in range(12):
+        loss = engine(data[:, :-1], targets=data[:, 1:])
+        engine.backward(loss)
+        engine.step()
+        losses.append(float(loss.detach()))
+    assert losses[-1] < losses[0] - 1.0, losses
+
+
+def test_gqa_attention_and_rope_grads_match_fp32():
+    from minispeed_b200.ops import nn as ops
+
+    torch.manual_seed(1)
+    B, T, H, Hkv, D = 2, 64, 4, 2, 64
+    qkv = torch.randn(B, T, H + 2 * Hkv, D, device="cuda").half().requires_grad_()
+    cos, sin = ops.rope_tables(T, D, 500000.0, "cuda")
+    out = ops.attention_gqa(ops.rope_qk(qkv, cos, sin, H, Hkv), H, Hkv)
+    g = torch.randn_like(out)
+    out.backward(g)
+    ref_in = qkv.detach().float().cpu().requires_grad_()
+    ref = ops.attention_gqa(ops.rope_qk(ref_in, cos.cpu(), sin.cpu(), H, Hkv), H, Hkv)
+    ref.backward(g.float().cpu())
+    torch.testing.assert_close(out.float().cpu(), ref.detach(), rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(qkv.grad.float().cpu(), ref_in.grad, rtol=3e-2, atol=3e-2)
