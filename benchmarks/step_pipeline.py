@@ -51,7 +51,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--sizes", default="20,24,27,29,31")
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--dtype", default="fp16", choices=["fp16", "bf16"])
     args = ap.parse_args()
@@ -94,7 +94,7 @@ def main():
                 p.grad = grad_src.clone()
             else:
                 p.grad.copy_(grad_src)
-            inject = rank == 0 and i >= args.warmup and (i - args.warmup) % 100 == 50
+            inject = rank == 0 and i >= args.warmup and (i - args.warmup) % 100 == 10
             if inject:
                 p.grad.view(-1)[n // 2] = float("inf")
             engine.micro_steps += 1

@@ -6,6 +6,12 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+
 #include "kernels_api.h"
 
 namespace {
@@ -269,6 +275,82 @@ void rope(const at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t,
             (int)D, row_stride, inverse, dtype_code(x), stream_of(x));
 }
 
+void cuda_ok(cudaError_t e, const char* what) {
+  TORCH_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e));
+}
+
+// ---- GEMM tile/split selection by measurement.  The first call of each
+// (shape, operand majorness, dtype, epilogue kind) times every candidate
+// configuration into a scratch output (no accumulate, so the real output is
+// untouched) and caches the fastest; later calls use the cache.
+struct PlanKey {
+  int64_t M, N, K;
+  int a_mn, b_mn, dtype, fused;
+  bool operator<(const PlanKey& o) const {
+    return std::tie(M, N, K, a_mn, b_mn, dtype, fused) <
+           std::tie(o.M, o.N, o.K, o.a_mn, o.b_mn, o.dtype, o.fused);
+  }
+};
+std::map<PlanKey, std::pair<int, int>> g_plans;
+std::mutex g_plan_mutex;
+bool g_autotune = std::getenv("MSB_GEMM_AUTOTUNE") == nullptr ||
+                  std::string(std::getenv("MSB_GEMM_AUTOTUNE")) != "0";
+
+std::pair<int, int> tune_gemm(const at::Tensor& a, const at::Tensor& b, int a_mn, int b_mn,
+                              int64_t M, int64_t N, int64_t K, bool fused, const at::Tensor& err,
+                              double timeout_s, cudaStream_t st) {
+  std::vector<std::pair<int, int>> cands;
+  const int kb = (int)((K + 63) / 64);
+  const char* force = std::getenv("MSB_GEMM_VARIANT");
+  const std::string fv = force ? force : "";
+  for (int bn : {512, 256, 128}) {
+    if (fv == "1cta" && bn == 512) continue;
+    if (fv == "2cta" && bn != 512) continue;
+    if (bn == 256 && N <= 128) continue;
+    for (int s : {1, 2, 4, 8}) {
+      if (fused && s > 1) continue;
+      if (s > 1 && kb / s < 4) continue;
+      if (s > 1 && (long long)s * M * N > (1LL << 31)) continue;
+      cands.push_back({bn, s});
+    }
+  }
+  if (cands.size() <= 1) return cands.empty() ? std::make_pair(0, 0) : cands[0];
+  const int64_t ldn = (N + 7) / 8 * 8;  // aligned rows, as the real outputs use
+  at::Tensor scratch = at::empty({M, ldn}, a.options());
+  long long ws_need = 0;
+  for (auto& c : cands) ws_need = std::max<long long>(ws_need, c.second > 1 ? c.second * M * N : 0);
+  at::Tensor ws;
+  if (ws_need > 0) ws = at::empty({ws_need}, a.options().dtype(at::kFloat));
+  cudaEvent_t e0, e1;
+  cuda_ok(cudaEventCreate(&e0), "event");
+  cuda_ok(cudaEventCreate(&e1), "event");
+  float best = 1e30f;
+  std::pair<int, int> pick = cands[0];
+  for (auto& c : cands) {
+    float t = 1e30f;
+    for (int rep = 0; rep < 3; ++rep) {
+      cuda_ok(cudaEventRecord(e0, st), "event");
+      msb::gemm_tcgen05(a.data_ptr(), a.stride(0), a_mn, b.data_ptr(), b.stride(0), b_mn,
+                        scratch.data_ptr(), ldn, nullptr, (int)M, (int)N, (int)K, dtype_code(a), 0,
+                        0, nullptr, 0, ws_need > 0 ? ws.data_ptr<float>() : nullptr, ws_need,
+                        reinterpret_cast<unsigned*>(err.data_ptr<int>()), timeout_s, st, c.first,
+                        c.second);
+      cuda_ok(cudaEventRecord(e1, st), "event");
+      cuda_ok(cudaEventSynchronize(e1), "event");
+      float ms = 0.f;
+      cuda_ok(cudaEventElapsedTime(&ms, e0, e1), "event");
+      if (rep > 0) t = std::min(t, ms);
+    }
+    if (t < best) {
+      best = t;
+      pick = c;
+    }
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  return pick;
+}
+
 // C[M,N] (+)= A * B^T with A given as [M,K] (a_kmajor) or [K,M], B as [N,K]
 // (b_kmajor) or [K,N]; every matrix row-major with unit column stride.
 void gemm(const at::Tensor& a, const at::Tensor& b, bool a_kmajor, bool b_kmajor,
@@ -303,16 +385,42 @@ void gemm(const at::Tensor& a, const at::Tensor& b, bool a_kmajor, bool b_kmajor
     TORCH_CHECK(!accumulate, "gemm epilogue modes do not accumulate");
   }
   c10::cuda::CUDAGuard g(a.device());
-  int bn = 0, splits = 1;
-  long long need = msb::gemm_plan((int)M, (int)N, (int)K, 148, &bn, &splits);
+  cudaStream_t st = stream_of(a);
+  const int a_mn = a_kmajor ? 0 : 1, b_mn = b_kmajor ? 0 : 1;
+  int bn = 0, splits = 0;
+  if (g_autotune) {
+    const PlanKey key{M, N, K, a_mn, b_mn, dtype_code(a), mode != 0 ? 1 : 0};
+    std::lock_guard<std::mutex> lock(g_plan_mutex);
+    auto it = g_plans.find(key);
+    if (it == g_plans.end())
+      it = g_plans.emplace(key, tune_gemm(a, b, a_mn, b_mn, M, N, K, mode != 0, err, timeout_s,
+                                          st)).first;
+    bn = it->second.first;
+    splits = it->second.second;
+  }
+  long long need = 0;
+  if (bn > 0) {
+    need = splits > 1 ? (long long)splits * M * N : 0;
+  } else {
+    int pbn = 0, ps = 1;
+    need = msb::gemm_plan((int)M, (int)N, (int)K, 148, &pbn, &ps);
+  }
   if (mode != 0) need = 0;
   at::Tensor ws;
   if (need > 0) ws = at::empty({need}, a.options().dtype(at::kFloat));
-  msb::gemm_tcgen05(a.data_ptr(), a.stride(0), a_kmajor ? 0 : 1, b.data_ptr(), b.stride(0),
-                    b_kmajor ? 0 : 1, out.data_ptr(), out.stride(0), optr(bias), (int)M, (int)N,
-                    (int)K, dtype_code(a), accumulate ? 1 : 0, (int)mode, auxp, ld_aux,
+  msb::gemm_tcgen05(a.data_ptr(), a.stride(0), a_mn, b.data_ptr(), b.stride(0), b_mn,
+                    out.data_ptr(), out.stride(0), optr(bias), (int)M, (int)N, (int)K,
+                    dtype_code(a), accumulate ? 1 : 0, (int)mode, auxp, ld_aux,
                     need > 0 ? ws.data_ptr<float>() : nullptr, need,
-                    reinterpret_cast<unsigned*>(err.data_ptr<int>()), timeout_s, stream_of(a));
+                    reinterpret_cast<unsigned*>(err.data_ptr<int>()), timeout_s, st, bn, splits);
+}
+
+std::vector<int64_t> gemm_cached_plan(int64_t M, int64_t N, int64_t K, int64_t a_mn,
+                                      int64_t b_mn, int64_t dtype, int64_t fused) {
+  std::lock_guard<std::mutex> lock(g_plan_mutex);
+  auto it = g_plans.find(PlanKey{M, N, K, (int)a_mn, (int)b_mn, (int)dtype, (int)fused});
+  if (it == g_plans.end()) return {};
+  return {it->second.first, it->second.second};
 }
 
 std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K) {
@@ -430,6 +538,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, mod) {
   mod.def("rope", &rope);
   mod.def("gemm", &gemm);
   mod.def("gemm_plan", &gemm_plan_py);
+  mod.def("gemm_cached_plan", &gemm_cached_plan);
   mod.def("peer_alloc", &peer_alloc_py);
   mod.def("peer_free", &peer_free_py);
   mod.def("peer_handle", &peer_handle_py);

@@ -119,8 +119,14 @@ rs_stats_kernel(char* const* heaps, long long grad_off, long long s0, long long 
       acc[k] = v;
     }
     float* o = out + i * VEC;
+    if (VEC == 8) {
+      // out is a fresh fp32 buffer (16-byte aligned): two 16-byte stores
+      reinterpret_cast<float4*>(o)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      reinterpret_cast<float4*>(o)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
 #pragma unroll
-    for (int k = 0; k < VEC; ++k) o[k] = acc[k];
+      for (int k = 0; k < VEC; ++k) o[k] = acc[k];
+    }
     if (fanout_off >= 0) {
       for (int q = 0; q < world; ++q) {
         float* dst = reinterpret_cast<float*>(heaps[q] + fanout_off) + s0 + i * VEC;
@@ -214,7 +220,20 @@ struct AdamArgs2 {
   float lr_neg, wd_term, b1, omb1, b2, omb2, bc1, bc2, eps, grad_mul;
 };
 
-template <typename P, int VEC>
+__device__ __forceinline__ float adam_one(float& p, float& mm, float& vv, float graw, float coef,
+                                          const AdamArgs2& a) {
+  float g = graw * a.grad_mul;
+  g = g * coef;
+  if (a.wd_term != 0.f) p = p + a.wd_term * p;
+  mm = mm * a.b1 + a.omb1 * g;
+  vv = vv * a.b2 + a.omb2 * g * g;
+  const float denom = sqrtf(vv / a.bc2) + a.eps;
+  p = p + a.lr_neg * ((mm / a.bc1) / denom);
+  return p;
+}
+
+// VECLOAD: master/m/v/grad are 16-byte aligned -> float4 accesses
+template <typename P, bool VECLOAD>
 __global__ void __launch_bounds__(256)
 adamw_fanout_kernel(float* __restrict__ master, float* __restrict__ m, float* __restrict__ v,
                     const float* __restrict__ grad, char* const* heaps, long long param_off,
@@ -222,34 +241,41 @@ adamw_fanout_kernel(float* __restrict__ master, float* __restrict__ m, float* __
                     AdamArgs2 a) {
   if (stats[0] != 0.f) return;  // overflow: nothing changes on any rank
   const float coef = stats[3];
-  const long long nvec = n / VEC;
+  constexpr int VEC = 4;
+  constexpr int BYTES = static_cast<int>(sizeof(P)) * VEC;
+  const long long groups = (n + VEC - 1) / VEC;
   const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec + (n % VEC ? 1 : 0);
-       i += stride) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < groups; i += stride) {
     const long long e0 = i * VEC;
     const int cnt = (int)min((long long)VEC, n - e0);
     alignas(16) P outv[VEC];
+    if (VECLOAD && cnt == VEC) {
+      float4 p4 = *reinterpret_cast<const float4*>(master + e0);
+      float4 m4 = *reinterpret_cast<const float4*>(m + e0);
+      float4 v4 = *reinterpret_cast<const float4*>(v + e0);
+      const float4 g4 = *reinterpret_cast<const float4*>(grad + e0);
+      outv[0] = from_f32<P>(adam_one(p4.x, m4.x, v4.x, g4.x, coef, a));
+      outv[1] = from_f32<P>(adam_one(p4.y, m4.y, v4.y, g4.y, coef, a));
+      outv[2] = from_f32<P>(adam_one(p4.z, m4.z, v4.z, g4.z, coef, a));
+      outv[3] = from_f32<P>(adam_one(p4.w, m4.w, v4.w, g4.w, coef, a));
+      *reinterpret_cast<float4*>(master + e0) = p4;
+      *reinterpret_cast<float4*>(m + e0) = m4;
+      *reinterpret_cast<float4*>(v + e0) = v4;
+    } else {
 #pragma unroll
-    for (int k = 0; k < VEC; ++k) {
-      if (k < cnt) {
-        const long long e = e0 + k;
-        float p = master[e], mm = m[e], vv = v[e];
-        float g = grad[e] * a.grad_mul;
-        g = g * coef;
-        if (a.wd_term != 0.f) p = p + a.wd_term * p;
-        mm = mm * a.b1 + a.omb1 * g;
-        vv = vv * a.b2 + a.omb2 * g * g;
-        const float denom = sqrtf(vv / a.bc2) + a.eps;
-        p = p + a.lr_neg * ((mm / a.bc1) / denom);
-        master[e] = p;
-        m[e] = mm;
-        v[e] = vv;
-        outv[k] = from_f32<P>(p);
+      for (int k = 0; k < VEC; ++k) {
+        if (k < cnt) {
+          const long long e = e0 + k;
+          float p = master[e], mm = m[e], vv = v[e];
+          outv[k] = from_f32<P>(adam_one(p, mm, vv, grad[e], coef, a));
+          master[e] = p;
+          m[e] = mm;
+          v[e] = vv;
+        }
       }
     }
     // one vector store per rank when the destination allows it: 4 x 16-bit
     // = 8 bytes, 4 x fp32 = 16 bytes
-    constexpr int BYTES = static_cast<int>(sizeof(P)) * VEC;
     for (int q = 0; q < world; ++q) {
       P* dst = reinterpret_cast<P*>(heaps[q] + param_off) + s0 + e0;
       const bool vec = cnt == VEC && (reinterpret_cast<uintptr_t>(dst) % BYTES) == 0;
@@ -294,7 +320,8 @@ int rs_stats(char* const* heaps, long long grad_off, int dtype, long long s0, lo
   int blocks = 1;
   MSB_DISPATCH_FLOAT(dtype, T, {
     constexpr int V = 16 / sizeof(T);
-    if (aligned16 && V == 8) {
+    // vector loads need 16-byte aligned sources, vector stores an aligned out
+    if (aligned16 && V == 8 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
       blocks = grid_for(n / V, 256, max_blocks);
       rs_stats_kernel<T, 8><<<blocks, 256, 0, st>>>(heaps, grad_off, s0, n, world, mul, out,
                                                     fanout_off, partials, pflags);
@@ -332,15 +359,23 @@ void adamw_fanout(float* master, float* m, float* v, const float* grad, char* co
   a.eps = (float)eps;
   a.grad_mul = (float)grad_mul;
   const int blocks = grid_for(n / 4 + 1, 256, kNumSMs * 16);
-  if (pdtype == kF16)
-    adamw_fanout_kernel<__half, 4><<<blocks, 256, 0, st>>>(master, m, v, grad, heaps, param_off, s0,
-                                                           n, world, stats, a);
-  else if (pdtype == kBF16)
-    adamw_fanout_kernel<__nv_bfloat16, 4><<<blocks, 256, 0, st>>>(master, m, v, grad, heaps,
-                                                                  param_off, s0, n, world, stats, a);
-  else
-    adamw_fanout_kernel<float, 4><<<blocks, 256, 0, st>>>(master, m, v, grad, heaps, param_off, s0,
-                                                          n, world, stats, a);
+  auto al = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  const bool vl = al(master) && al(m) && al(v) && al(grad);
+#define MSB_FANOUT(P)                                                                        \
+  if (vl)                                                                                    \
+    adamw_fanout_kernel<P, true><<<blocks, 256, 0, st>>>(master, m, v, grad, heaps, param_off, \
+                                                         s0, n, world, stats, a);            \
+  else                                                                                       \
+    adamw_fanout_kernel<P, false><<<blocks, 256, 0, st>>>(master, m, v, grad, heaps,         \
+                                                          param_off, s0, n, world, stats, a);
+  if (pdtype == kF16) {
+    MSB_FANOUT(__half)
+  } else if (pdtype == kBF16) {
+    MSB_FANOUT(__nv_bfloat16)
+  } else {
+    MSB_FANOUT(float)
+  }
+#undef MSB_FANOUT
   MSB_CHECK_LAUNCH("adamw_fanout");
 }
 

@@ -1030,11 +1030,17 @@ long long gemm_plan(int M, int N, int K, int num_sms, int* bn_out, int* splits_o
 void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
                   void* C, long long ldc, const void* bias, int M, int N, int K, int dtype,
                   int accumulate, int mode, void* aux, long long ld_aux, float* ws,
-                  long long ws_floats, unsigned* err, double timeout_s, cudaStream_t st) {
+                  long long ws_floats, unsigned* err, double timeout_s, cudaStream_t st,
+                  int force_bn, int force_splits) {
   using namespace tc;
   int bn, splits;
   const long long need = gemm_plan(M, N, K, kNumSMs, &bn, &splits);
-  if (need > ws_floats || ws == nullptr || mode != 0) {
+  if (force_bn > 0) {
+    bn = force_bn;
+    splits = force_splits > 0 ? force_splits : 1;
+    if (splits > 1 && (long long)splits * M * N > ws_floats) splits = 1;
+  }
+  if ((splits > 1 && (ws == nullptr || (long long)splits * M * N > ws_floats)) || mode != 0) {
     splits = 1;
     if (bn != 512) bn = N > 128 ? 256 : 128;
   }

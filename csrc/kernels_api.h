@@ -60,7 +60,8 @@ long long gemm_plan(int M, int N, int K, int num_sms, int* bn_out, int* splits_o
 void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
                   void* C, long long ldc, const void* bias, int M, int N, int K, int dtype,
                   int accumulate, int mode, void* aux, long long ld_aux, float* ws,
-                  long long ws_floats, unsigned* err, double timeout_s, cudaStream_t st);
+                  long long ws_floats, unsigned* err, double timeout_s, cudaStream_t st,
+                  int force_bn = 0, int force_splits = 0);
 
 // ---- NVLink peer heap + fused collectives (collectives.cu)
 void peer_barrier(char* const* heaps, long long sync_off, int rank, int world, unsigned epoch,
