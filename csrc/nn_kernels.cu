@@ -28,6 +28,15 @@ struct alignas(16) Pack8 {
   T v[8];
 };
 
+// 2^x on the special-function unit; e^x = 2^(x * log2(e))
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // 8-element accesses: one 16-byte transaction when the address allows it,
 // element-wise otherwise.  Parameters are views into a flat arena at
 // arbitrary element offsets, so weights and biases need not be aligned.
@@ -408,10 +417,11 @@ __device__ __forceinline__ void for_row(const T* row, int V, F&& f) {
   for (int i = h + nvec * 8 + threadIdx.x; i < V; i += blockDim.x) f(i, to_f32(row[i]));
 }
 
+// running (max, sum) pairs in base-2 units: value y = x * log2(e)
 __device__ __forceinline__ void softmax_merge(float& m, float& s, float m2, float s2) {
   const float mx = fmaxf(m, m2);
   if (mx == -INFINITY) return;
-  s = s * expf(m - mx) + s2 * expf(m2 - mx);
+  s = s * ex2_approx(m - mx) + s2 * ex2_approx(m2 - mx);
   m = mx;
 }
 
@@ -424,11 +434,12 @@ ce_fwd_kernel(const T* __restrict__ logits, const long long* __restrict__ tgt,
   const T* row = logits + r * ld;
   float m = -INFINITY, s = 0.f;
   for_row(row, V, [&](int, float v) {
-    if (v > m) {
-      s = s * expf(m - v) + 1.f;
-      m = v;
+    const float y = v * kLog2e;
+    if (y > m) {
+      s = s * ex2_approx(m - y) + 1.f;
+      m = y;
     } else {
-      s += expf(v - m);
+      s += ex2_approx(y - m);
     }
   });
 #pragma unroll
@@ -455,7 +466,7 @@ ce_fwd_kernel(const T* __restrict__ logits, const long long* __restrict__ tgt,
       softmax_merge(m, s, m2, s2);
     }
     if (lane == 0) {
-      const float lse = m + logf(s);
+      const float lse = m * kLn2 + logf(s);
       lse_out[r] = lse;
       const long long t = tgt[r];
       // ignored (or out-of-range) targets contribute nothing
@@ -508,7 +519,9 @@ ce_bwd_kernel(T* __restrict__ logits, const long long* __restrict__ tgt,
   const float l = lse[r];
   const int head = (int)(((16 - (reinterpret_cast<uintptr_t>(row) & 15)) & 15) / sizeof(T));
   const int h = min(head, V);
-  auto g = [&](int i, float v) { return (expf(v - l) - (i == t ? 1.f : 0.f)) * scale; };
+  auto g = [&](int i, float v) {
+    return (ex2_approx((v - l) * kLog2e) - (i == t ? 1.f : 0.f)) * scale;
+  };
   for (int i = threadIdx.x; i < h; i += blockDim.x) row[i] = from_f32<T>(g(i, to_f32(row[i])));
   const int nvec = (V - h) / 8;
   T* mid = row + h;
