@@ -8,7 +8,10 @@ loss scaling (initial_scale_power 16, window 1000), ZeRO stage 2, micro-batch
 16 per GPU, gas 1, AdamW, WarmupDecayLR, gradient clipping 1.0.  Synthetic
 uniform-random token ids, GPT-2 random init (std 0.02) for both arms.
 
-``--impl ours`` runs minispeed_b200 (fused sm_100a kernels); ``--impl
+``--impl ours`` runs minispeed_b200 (fused sm_100a kernels) through
+``engine.train_batch`` with ``b200.cuda_graph`` on: after two eager warm-up
+micro-steps the forward + backward is replayed as one captured CUDA graph and
+the optimizer step runs eagerly after it (one host read per step); ``--impl
 reference`` runs the unmodified reference engine installed in
 ``baseline/_ref`` through its public API with a stock-PyTorch GPT-2 of the
 same architecture (nn.Linear/nn.LayerNorm/nn.GELU/SDPA, the reference
@@ -196,9 +199,12 @@ def main():
         torch.manual_seed(1234)
         model = RefGPT()
 
-        def loss_fn(eng, x, y):
+        def micro_step(eng, x, y):
             logits = eng(x)
-            return F.cross_entropy(logits.reshape(-1, logits.size(-1)).float(), y.reshape(-1))
+            loss = F.cross_entropy(logits.reshape(-1, logits.size(-1)).float(), y.reshape(-1))
+            eng.backward(loss)
+            eng.step()
+            return loss
     else:
         sys.path.insert(0, ROOT)
         import minispeed_b200 as lib
@@ -208,13 +214,17 @@ def main():
         model = GPT(GPTConfig(vocab_size=VOCAB, block_size=SEQ, n_layer=LAYERS, n_head=HEADS,
                               n_embd=EMBD))
 
-        def loss_fn(eng, x, y):
-            return eng(x, targets=y)
+        def micro_step(eng, x, y):
+            # forward + backward replayed as one CUDA graph, then the step
+            return eng.train_batch(x, targets=y)
 
     _init(model)
     lcomm.init_distributed()
+    cfg = ds_config(world, args.warmup + 2 * args.steps)
+    if args.impl == "ours":
+        cfg["b200"] = {"cuda_graph": True}
     engine, _, _, _ = lib.initialize(model=model, model_parameters=model.parameters(),
-                                     config=ds_config(world, args.warmup + 2 * args.steps))
+                                     config=cfg)
     dist = torch.distributed
     distributed = dist.is_available() and dist.is_initialized() and world > 1
 
@@ -228,9 +238,7 @@ def main():
         t = dev_pool[i % n_pool]
         loss = None
         for _ in range(GAS):
-            loss = loss_fn(engine, t[:, :-1], t[:, 1:])
-            engine.backward(loss)
-            engine.step()
+            loss = micro_step(engine, t[:, :-1], t[:, 1:])
         return loss
 
     def sync_all():
@@ -289,9 +297,7 @@ def main():
         x, y = t[:, :-1], t[:, 1:]
         loss = None
         for _ in range(GAS):
-            loss = loss_fn(engine, x, y)
-            engine.backward(loss)
-            engine.step()
+            loss = micro_step(engine, x, y)
         losses.append(float(loss.item()))
     e1.record()
     sync_all()

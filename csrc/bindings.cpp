@@ -392,11 +392,19 @@ void gemm(const at::Tensor& a, const at::Tensor& b, bool a_kmajor, bool b_kmajor
     const PlanKey key{M, N, K, a_mn, b_mn, dtype_code(a), mode != 0 ? 1 : 0};
     std::lock_guard<std::mutex> lock(g_plan_mutex);
     auto it = g_plans.find(key);
-    if (it == g_plans.end())
-      it = g_plans.emplace(key, tune_gemm(a, b, a_mn, b_mn, M, N, K, mode != 0, err, timeout_s,
-                                          st)).first;
-    bn = it->second.first;
-    splits = it->second.second;
+    if (it == g_plans.end()) {
+      // timing candidates synchronizes: never inside a CUDA-graph capture
+      // (a shape first seen there runs the heuristic plan, untuned)
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      cuda_ok(cudaStreamIsCapturing(st, &cs), "cudaStreamIsCapturing");
+      if (cs == cudaStreamCaptureStatusNone)
+        it = g_plans.emplace(key, tune_gemm(a, b, a_mn, b_mn, M, N, K, mode != 0, err, timeout_s,
+                                            st)).first;
+    }
+    if (it != g_plans.end()) {
+      bn = it->second.first;
+      splits = it->second.second;
+    }
   }
   long long need = 0;
   if (bn > 0) {
@@ -522,6 +530,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, mod) {
   mod.def("adamw", &adamw);
   mod.def("cast_scale", &cast_scale);
   mod.def("launch_count", &msb::launch_count);
+  mod.def("count_launches", [](int64_t n) { msb::count_launch((int)n); },
+          "add n to the launch counter (kernels replayed from a captured CUDA graph)");
   mod.def("add_norm_fwd", &add_norm_fwd);
   mod.def("norm_bwd", &norm_bwd);
   mod.def("colsum_partial", &colsum_partial);

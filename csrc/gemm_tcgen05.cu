@@ -7,17 +7,19 @@
 // which covers the three products of a linear layer without transposes:
 // forward (both K-major), dgrad (B MN-major) and wgrad (both MN-major).
 //
-// CTA = 6 warps, one CTA per SM, persistent over output tiles (128 x BN):
+// CTA = 10 warps, one CTA per SM, persistent over output tiles (128 x BN):
 //   warp 0     TMA producer: 64-deep K slices of A and B into a 4-stage
 //              shared-memory ring (128-byte swizzle), one mbarrier per stage
 //   warp 1     owns the tensor memory (allocates 2 x BN fp32 columns) and
 //              issues tcgen05.mma (M=128, N=BN, K=16) from one thread;
 //              tcgen05.commit frees a ring stage once its MMAs retire and
 //              signals "accumulator full" after a tile's last K slice
-//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time (one TMEM lane =
-//              one output row per thread), bias, cast, store; release the
-//              accumulator buffer so the MMA warp can start the tile after
-//              next while this one drains (double-buffered accumulators)
+//   warps 2-9  epilogue: tcgen05.ld 32 columns at a time (one TMEM lane =
+//              one output row per thread), bias, activation, cast; each
+//              32 x 32 chunk is staged in shared memory and written by a TMA
+//              bulk tensor store; then release the accumulator buffer so the
+//              MMA warp can start the tile after next while this one drains
+//              (double-buffered accumulators)
 //
 // Split-K (for wgrad products whose output has too few tiles to fill 148
 // SMs) writes fp32 partial tiles to a workspace reduced by a second kernel.
@@ -63,6 +65,7 @@ struct Params {
   void* aux;         // second output (mode 1) or input (mode 2), row stride ld_aux
   long long ld_aux;
   int aux_vec;
+  int staged;        // epilogue through shared memory + TMA stores (tmC / tmX valid)
   uint32_t idesc;
   unsigned* err;
   unsigned long long timeout_ns;
@@ -295,6 +298,116 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int col, f
   store32<T>(c, p.c_vec, v, nvalid, p.accumulate);
 }
 
+// ------------------------------------------------ staged (TMA-store) epilogue
+// Each epilogue warp owns two 2 KB staging buffers: one 32-row x 32-column
+// chunk of the output in the model dtype, 64 bytes per row, 16-byte pieces
+// XOR-swizzled by bits 7-8 of the address (the tensor map's 64-byte swizzle;
+// the eight rows one 16-byte store phase touches land in eight different
+// bank groups).  Lane 0 writes the chunk to global memory with one TMA bulk
+// tensor store: whole 128-byte lines, asynchronous, off the load/store unit.
+constexpr int kStageBytes = 2048;
+constexpr int kEpiStageBytes = kEpiWarps * 2 * kStageBytes;
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// wait until at most N of this thread's bulk groups still read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ void stage_row(uint8_t* buf, int r, const float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 pack;
+    T* h = reinterpret_cast<T*>(&pack);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) h[e] = from_f32<T>(v[j * 8 + e]);
+    *reinterpret_cast<uint4*>(buf + r * 64 + ((j ^ ((r >> 1) & 3)) << 4)) = pack;
+  }
+}
+
+// v += bias[col .. col+31]; every lane reads the same addresses (broadcast)
+template <typename T>
+__device__ __forceinline__ void add_bias(const Params& p, int col, int nvalid, float (&v)[32]) {
+  const T* b = static_cast<const T*>(p.bias) + col;
+  if (nvalid == 32 && (reinterpret_cast<uintptr_t>(b) & 15) == 0) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 pack = *reinterpret_cast<const uint4*>(b + q * 8);
+      const T* h = reinterpret_cast<const T*>(&pack);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[q * 8 + j] += to_f32(h[j]);
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j < nvalid) v[j] += to_f32(b[j]);
+}
+
+// One 32 x 32 chunk of C, rows row0.. and columns col.. all inside C (warp-
+// uniform), through the staging buffers.  Modes as store_chunk; accumulate
+// and split-K never come here.  sbuf alternates the two buffers in modes 0
+// and 2.
+template <typename T>
+__device__ __forceinline__ void staged_chunk(const Params& p, const CUtensorMap* tmC,
+                                             const CUtensorMap* tmX, uint8_t* stg, int& sbuf,
+                                             int row0, int lane, int col, int nvalid,
+                                             float (&v)[32]) {
+  const int row = row0 + lane;
+  if (p.mode == 1) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = to_f32(from_f32<T>(v[j]));
+    float h[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) h[j] = gelu_f(v[j]);
+    if (lane == 0) bulk_wait_read<0>();
+    __syncwarp();
+    stage_row<T>(stg, lane, v);
+    stage_row<T>(stg + kStageBytes, lane, h);
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmC, smem_u32(stg), col, row0);
+      tma_store_2d(tmX, smem_u32(stg + kStageBytes), col, row0);
+      bulk_commit();
+    }
+    return;
+  }
+  if (p.mode == 2) {
+    float u[32];
+    load32<T>(static_cast<const T*>(p.aux) + (long long)row * p.ld_aux + col, p.aux_vec, u, nvalid);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = to_f32(from_f32<T>(v[j])) * gelu_grad_f(u[j]);
+  }
+  if (lane == 0) bulk_wait_read<1>();
+  __syncwarp();
+  uint8_t* buf = stg + sbuf * kStageBytes;
+  stage_row<T>(buf, lane, v);
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmC, smem_u32(buf), col, row0);
+    bulk_commit();
+  }
+  sbuf ^= 1;
+}
+
 __device__ __forceinline__ void store_ws_chunk(const Params& p, int split, int row, int col,
                                                const float (&v)[32], int nvalid) {
   float* w = p.ws + ((long long)split * p.M + row) * p.N + col;
@@ -312,6 +425,7 @@ __device__ __forceinline__ void store_ws_chunk(const Params& p, int split, int r
 template <typename T, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+            const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX,
             const Params p) {
   constexpr int A_BYTES = BM * BK * 2;
   constexpr int B_BYTES = BN * BK * 2;
@@ -321,7 +435,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  Barriers* bars = reinterpret_cast<Barriers*>(sB + STAGES * B_BYTES);
+  uint8_t* sStage = sB + STAGES * B_BYTES;
+  Barriers* bars = reinterpret_cast<Barriers*>(sStage + kEpiStageBytes);
   volatile int* abort = &bars->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -443,6 +558,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     const int half = (warp - 2) / 4;        // which interleaved half of the chunks
     const int row_in_tile = quarter * 32 + lane;
     const bool has_bias = p.bias != nullptr && p.splits == 1;
+    uint8_t* stg = sStage + (warp - 2) * 2 * kStageBytes;
+    int sbuf = 0;
     int it = 0;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++it) {
       int m0, n0, kb0, kb1, split;
@@ -454,6 +571,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
+      const int row0 = m0 + quarter * 32;
       const int row = m0 + row_in_tile;
 #pragma unroll 1
       for (int c = half; c < BN / 32; c += 2) {
@@ -461,14 +579,17 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         tmem_ld32(tmem_base + ((quarter * 32) << 16) + buf * BN + c * 32, r);
         tmem_ld_wait();
         const int col = n0 + c * 32;  // warp-uniform
-        if (col >= p.N) continue;
+        if (col >= p.N || row0 >= p.M) continue;
         const int nvalid = min(32, p.N - col);
-        float bl = 0.f;
-        if (has_bias && lane < nvalid) bl = to_f32(static_cast<const T*>(p.bias)[col + lane]);
         float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + __shfl_sync(0xffffffffu, bl, j);
-        if (row < p.M) {
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (has_bias) add_bias<T>(p, col, nvalid, v);
+        // TMA stores only for chunks wholly inside C: ragged edges are
+        // stored per thread, so no write depends on the map's bound clipping
+        if (p.staged && nvalid == 32 && row0 + 32 <= p.M) {
+          staged_chunk<T>(p, &tmC, &tmX, stg, sbuf, row0, lane, col, nvalid, v);
+        } else if (row < p.M) {
           if (p.splits > 1) store_ws_chunk(p, split, row, col, v, nvalid);
           else store_chunk<T>(p, row, col, v, nvalid);
         }
@@ -477,6 +598,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bars->tempty[buf]));
     }
+    // the staging buffers are read and the stores performed before exit
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -610,12 +734,13 @@ struct alignas(8) Bars2 {
 };
 
 constexpr size_t smem_bytes2() {
-  return 1024 + STAGES2 * (A2_BYTES + B2_BYTES) + sizeof(Bars2);
+  return 1024 + STAGES2 * (A2_BYTES + B2_BYTES) + kEpiStageBytes + sizeof(Bars2);
 }
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+             const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX,
              const Params p) {
   constexpr uint32_t TMEM_COLS = 2 * BN2;
   extern __shared__ uint8_t smem_raw[];
@@ -623,7 +748,8 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES2 * A2_BYTES;
-  Bars2* bars = reinterpret_cast<Bars2*>(sB + STAGES2 * B2_BYTES);
+  uint8_t* sStage = sB + STAGES2 * B2_BYTES;
+  Bars2* bars = reinterpret_cast<Bars2*>(sStage + kEpiStageBytes);
   volatile int* abort = &bars->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -755,6 +881,8 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     const bool has_bias = p.bias != nullptr && p.splits == 1;
     const uint32_t tempty_leader0 = mapa(smem_u32(&bars->tempty[0]), 0);
     const uint32_t tempty_leader1 = mapa(smem_u32(&bars->tempty[1]), 0);
+    uint8_t* stg = sStage + (warp - 2) * 2 * kStageBytes;
+    int sbuf = 0;
     int it = 0;
     for (int u = pair_id; u < p.units; u += npairs, ++it) {
       int m0, n0, kb0, kb1, split;
@@ -765,6 +893,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
+      const int row0 = m0 + HALF * rank + quarter * 32;
       const int row = m0 + row_in_tile;
 #pragma unroll 1
       for (int c = half; c < BN2 / 32; c += 2) {
@@ -772,14 +901,17 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         tmem_ld32(tmem_base + ((quarter * 32) << 16) + buf * BN2 + c * 32, r);
         tmem_ld_wait();
         const int col = n0 + c * 32;
-        if (col >= p.N) continue;
+        if (col >= p.N || row0 >= p.M) continue;
         const int nvalid = min(32, p.N - col);
-        float bl = 0.f;
-        if (has_bias && lane < nvalid) bl = to_f32(static_cast<const T*>(p.bias)[col + lane]);
         float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + __shfl_sync(0xffffffffu, bl, j);
-        if (row < p.M) {
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (has_bias) add_bias<T>(p, col, nvalid, v);
+        // TMA stores only for chunks wholly inside C: ragged edges are
+        // stored per thread, so no write depends on the map's bound clipping
+        if (p.staged && nvalid == 32 && row0 + 32 <= p.M) {
+          staged_chunk<T>(p, &tmC, &tmX, stg, sbuf, row0, lane, col, nvalid, v);
+        } else if (row < p.M) {
           if (p.splits > 1) store_ws_chunk(p, split, row, col, v, nvalid);
           else store_chunk<T>(p, row, col, v, nvalid);
         }
@@ -788,6 +920,8 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
       __syncwarp();
       if (lane == 0) remote_arrive(buf ? tempty_leader1 : tempty_leader0);
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   // every role of both CTAs is done before tensor memory is released and
@@ -898,7 +1032,8 @@ void bind_context() {
 
 // 2-D map over a row-major matrix [outer, inner] with row stride ld elements.
 CUtensorMap make_map(const void* ptr, int dtype, long long inner, long long outer, long long ld,
-                     int box_inner, int box_outer) {
+                     int box_inner, int box_outer,
+                     CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0)
     throw std::runtime_error("gemm operand must be 16-byte aligned");
   if ((ld * 2) % 16 != 0) throw std::runtime_error("gemm operand row stride must be 16-byte aligned");
@@ -911,7 +1046,7 @@ CUtensorMap make_map(const void* ptr, int dtype, long long inner, long long oute
   CUresult r = encode_fn()(&m, dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                            2, const_cast<void*>(ptr), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
@@ -920,12 +1055,12 @@ CUtensorMap make_map(const void* ptr, int dtype, long long inner, long long oute
 
 template <int BN>
 constexpr size_t smem_bytes() {
-  return 1024 + STAGES * (BM + BN) * BK * 2 + sizeof(Barriers);
+  return 1024 + STAGES * (BM + BN) * BK * 2 + kEpiStageBytes + sizeof(Barriers);
 }
 
 template <typename T, int BN>
-void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int grid,
-            cudaStream_t st) {
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+            const CUtensorMap& tx, const Params& p, int grid, cudaStream_t st) {
   auto kern = gemm_kernel<T, BN>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -934,7 +1069,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int g
                "gemm smem attribute");
     attr_set = true;
   }
-  kern<<<grid, kThreads, smem_bytes<BN>(), st>>>(ta, tb, p);
+  kern<<<grid, kThreads, smem_bytes<BN>(), st>>>(ta, tb, tc, tx, p);
 }
 
 template <typename T>
@@ -967,8 +1102,8 @@ int pair_capacity(const Params& p, cudaStream_t st) {
 }
 
 template <typename T>
-void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int npairs,
-                 cudaStream_t st) {
+void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                 const CUtensorMap& tx, const Params& p, int npairs, cudaStream_t st) {
   auto kern = pair::gemm2_kernel<T>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * npairs);
@@ -982,7 +1117,7 @@ void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, 
   at[0].val.clusterDim.z = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  check_cuda(cudaLaunchKernelEx(&cfg, kern, ta, tb, p), "gemm2 launch");
+  check_cuda(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, tx, p), "gemm2 launch");
 }
 
 }  // namespace tc
@@ -1086,23 +1221,31 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
                               : make_map(A, dtype, K, M, lda, 64, a_rows);
   const CUtensorMap tb = b_mn ? make_map(B, dtype, N, K, ldb, 64, 64)
                               : make_map(B, dtype, K, N, ldb, 64, b_rows);
+  // output maps for the staged epilogue: 32 x 32 boxes, 64-byte swizzle
+  // (plain and GELU/dGELU outputs; accumulation and split-K store per thread)
+  p.staged = (p.splits == 1 && !p.accumulate && p.c_vec && (mode != 1 || p.aux_vec)) ? 1 : 0;
+  const CUtensorMap tcm = p.staged ? make_map(C, dtype, N, M, ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
+                                   : ta;
+  const CUtensorMap txm = (p.staged && mode == 1)
+                              ? make_map(aux, dtype, N, M, ld_aux, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
+                              : ta;
   const int grid = std::min(p.units, kNumSMs);
   if (two_cta) {
     if (dtype == kF16) {
       const int npairs = std::min(p.units, pair_capacity<__half>(p, st));
-      launch_pair<__half>(ta, tb, p, npairs, st);
+      launch_pair<__half>(ta, tb, tcm, txm, p, npairs, st);
     } else if (dtype == kBF16) {
       const int npairs = std::min(p.units, pair_capacity<__nv_bfloat16>(p, st));
-      launch_pair<__nv_bfloat16>(ta, tb, p, npairs, st);
+      launch_pair<__nv_bfloat16>(ta, tb, tcm, txm, p, npairs, st);
     } else {
       throw std::runtime_error("tcgen05 gemm takes fp16/bf16 operands");
     }
   } else if (dtype == kF16) {
-    if (bn == 256) launch<__half, 256>(ta, tb, p, grid, st);
-    else launch<__half, 128>(ta, tb, p, grid, st);
+    if (bn == 256) launch<__half, 256>(ta, tb, tcm, txm, p, grid, st);
+    else launch<__half, 128>(ta, tb, tcm, txm, p, grid, st);
   } else if (dtype == kBF16) {
-    if (bn == 256) launch<__nv_bfloat16, 256>(ta, tb, p, grid, st);
-    else launch<__nv_bfloat16, 128>(ta, tb, p, grid, st);
+    if (bn == 256) launch<__nv_bfloat16, 256>(ta, tb, tcm, txm, p, grid, st);
+    else launch<__nv_bfloat16, 128>(ta, tb, tcm, txm, p, grid, st);
   } else {
     throw std::runtime_error("tcgen05 gemm takes fp16/bf16 operands");
   }

@@ -9,6 +9,7 @@ namespace msb {
 enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
 
 long long launch_count();
+void count_launch(int n);
 
 // ---- step pipeline (step_kernels.cu)
 int grad_stats(const void* x, int dtype, long long n, float mul, float* partials,

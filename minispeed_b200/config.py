@@ -69,12 +69,17 @@ class B200Options:
     final instead of once after backward.
     ``wait_timeout_ms``: bound on every cross-GPU spin inside fused kernels;
     past it the kernel reports an error status instead of waiting forever.
+    ``cuda_graph``: ``engine.train_batch`` replays forward + backward as one
+    captured CUDA graph (stages 0-2, CUDA) after ``graph_warmup`` eager
+    micro-steps; env ``MINISPEED_CUDA_GRAPH=1`` turns it on.
     """
 
     comm: str = "auto"
     bucket_mb: float = 64.0
     overlap: bool = True
     wait_timeout_ms: float = 10000.0
+    cuda_graph: bool = False
+    graph_warmup: int = 2
 
     @classmethod
     def parse(cls, raw: dict) -> "B200Options":
@@ -84,11 +89,16 @@ class B200Options:
             bucket_mb=float(sec.get("bucket_mb", 64.0)),
             overlap=bool(sec.get("overlap", True)),
             wait_timeout_ms=float(sec.get("wait_timeout_ms", 10000.0)),
+            cuda_graph=bool(sec.get("cuda_graph",
+                                    os.environ.get("MINISPEED_CUDA_GRAPH", "0") == "1")),
+            graph_warmup=int(sec.get("graph_warmup", 2)),
         )
         if opts.comm not in ("auto", "nccl", "fused"):
             raise ConfigError(f"b200.comm must be auto|nccl|fused, got {opts.comm!r}")
         if opts.bucket_mb <= 0:
             raise ConfigError("b200.bucket_mb must be positive")
+        if opts.graph_warmup < 1:
+            raise ConfigError("b200.graph_warmup must be at least 1")
         return opts
 
 

@@ -122,6 +122,8 @@ class DeepSpeedEngine:
         self._consumed_boundary = -1
         self.grad_norm: Optional[float] = None
         self._window_open = False
+        self._graph = None          # MicroStepGraph of train_batch (CUDA graphs)
+        self._graph_eager = 0       # eager micro-steps run for the current signature
 
     # ----------------------------------------------------------- properties
     @property
@@ -212,6 +214,93 @@ class DeepSpeedEngine:
                                                            create_graph=create_graph)
         self.micro_steps += 1
 
+    # --------------------------------------------------------- train_batch
+    def train_batch(self, *args, **kwargs) -> torch.Tensor:
+        """One micro-step: ``loss = module(*args, **kwargs)`` (the module
+        returns a scalar loss), the scaled backward, then :meth:`step` (which
+        acts only at an accumulation boundary).  Returns the loss.
+
+        With ``b200.cuda_graph`` on a CUDA device at ZeRO stage 0-2, the
+        forward + backward of a given input signature is captured once, after
+        ``b200.graph_warmup`` eager micro-steps, and replayed from then on
+        (:mod:`minispeed_b200.graphs`).  Input tensors may live on the host;
+        they are copied into the graph's static inputs.  The returned loss
+        tensor is then the graph's output, overwritten by the next call.
+        """
+        if self._graph_usable():
+            loss = self._graph_micro_step(args, kwargs)
+        else:
+            loss = self.forward(*self._to_device(args), **self._to_device(kwargs))
+            self.backward(loss)
+        self.step()
+        # detached: a caller holding the loss keeps no autograd graph alive
+        # (a live graph would pin its AccumulateGrad nodes to the stream of
+        # that step and break a later capture)
+        return loss.detach()
+
+    def _to_device(self, obj):
+        if isinstance(obj, torch.Tensor):
+            return obj.to(self.device, non_blocking=True)
+        if isinstance(obj, dict):
+            return {k: self._to_device(v) for k, v in obj.items()}
+        if isinstance(obj, (list, tuple)):
+            return type(obj)(self._to_device(v) for v in obj)
+        return obj
+
+    def _graph_usable(self) -> bool:
+        return (self.config.b200.cuda_graph and self.device.type == "cuda"
+                and self.config.zero_stage < 3 and self.module.training
+                and torch.is_grad_enabled())
+
+    def _graph_micro_step(self, args, kwargs) -> torch.Tensor:
+        from .graphs import MicroStepGraph, signature
+        sig, _ = signature(args, kwargs)
+        st = self._graph
+        if st is None or st.sig != sig or (st.graph is not None and not st.valid()):
+            if st is not None:
+                st.release()
+            self._graph = st = None
+            side = self._graph_stream()
+            cur = torch.cuda.current_stream(self.device)
+            side.wait_stream(cur)
+            if self._graph_eager < self.config.b200.graph_warmup:
+                # eager micro-steps first (GEMM autotuning, lazy library
+                # state), on the stream the capture will use
+                self._graph_eager += 1
+                with torch.cuda.stream(side):
+                    loss = self.forward(*self._to_device(args), **self._to_device(kwargs))
+                    self.backward(loss)
+                cur.wait_stream(side)
+                return loss
+            torch.cuda.empty_cache()
+            st = MicroStepGraph(self, args, kwargs)
+            st.capture(side)
+            cur.wait_stream(side)
+            self._graph = st
+        self._graph_eager = 0
+        factor = self.loss_scaler.loss_scale_factor
+        if self.gas > 1:
+            factor /= self.gas
+        st.set_seed(factor)
+        st.load_inputs(args, kwargs)
+        self._open_window()
+        with self.timers.timer("backward"):
+            loss = st.replay()
+        self.micro_steps += 1
+        return loss
+
+    def _graph_stream(self) -> torch.cuda.Stream:
+        if getattr(self, "_side_stream", None) is None:
+            self._side_stream = torch.cuda.Stream(self.device)
+        return self._side_stream
+
+    def release_graphs(self) -> None:
+        """Drop the captured micro-step graph and its memory pool."""
+        if self._graph is not None:
+            self._graph.release()
+            self._graph = None
+        self._graph_eager = 0
+
     # ---------------------------------------------------------------- step
     def step(self) -> bool:
         """Apply the optimizer at a pending accumulation boundary.
@@ -287,6 +376,7 @@ class DeepSpeedEngine:
 
     def close(self) -> None:
         """Release communication resources (peer mappings, buffers)."""
+        self.release_graphs()
         self.optimizer.close()
 
     def __repr__(self) -> str:  # pragma: no cover

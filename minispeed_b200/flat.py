@@ -85,6 +85,8 @@ class FlatParamGroup:
         self.param_arena: Optional[torch.Tensor] = None
         self.param_shard: Optional[torch.Tensor] = None
         self.grad_arena: Optional[torch.Tensor] = None
+        self._grad_views: Optional[List[torch.Tensor]] = None   # tensors bind_grads put in p.grad
+        self._grad_views_of: Optional[torch.Tensor] = None      # ... as views of this arena
         # a pinned gradient arena (peer heap) is zeroed between windows,
         # never freed, so peers can keep addressing it
         self._arena_pinned = False
@@ -128,8 +130,21 @@ class FlatParamGroup:
             return True
         base = self.param_arena.data_ptr()
         esz = self.param_arena.element_size()
+        dt = self.param_dtype
+        # Parameter.data_ptr() directly: no .data alias object per check
         for off, p in zip(self._offsets_int, self.params):
-            if p.data.data_ptr() != base + off * esz or p.data.dtype != self.param_dtype:
+            if p.data_ptr() != base + off * esz or p.dtype != dt:
+                return False
+        return True
+
+    def grads_bound(self) -> bool:
+        """True when every ``p.grad`` is still the arena view
+        :meth:`bind_grads` assigned (an identity check, no tensor calls)."""
+        views = self._grad_views
+        if views is None or self._grad_views_of is not self.grad_arena:
+            return False
+        for p, v in zip(self.params, views):
+            if p.grad is not v:
                 return False
         return True
 
@@ -248,14 +263,20 @@ class FlatParamGroup:
         if self.grad_arena is None:
             self.grad_arena = torch.zeros(self.numel_padded, dtype=self.param_dtype,
                                           device=self.device)
-        if self.param_arena is not None:
+            self._grad_views = None
+        if self.param_arena is not None and not self.grads_bound():
             self.bind_grads()
         return self.grad_arena
 
     def bind_grads(self) -> None:
         ga = self.grad_arena
+        views = []
         for off, n, shape, p in zip(self._offsets_int, self._numels, self._shapes, self.params):
-            p.grad = ga[off:off + n].view(shape)
+            v = ga[off:off + n].view(shape)
+            p.grad = v
+            views.append(p.grad)
+        self._grad_views = views
+        self._grad_views_of = ga
 
     @torch.no_grad()
     def collect_grads(self) -> torch.Tensor:
@@ -269,8 +290,11 @@ class FlatParamGroup:
         if ga is None:
             ga = self.grad_arena = torch.zeros(self.numel_padded, dtype=self.param_dtype,
                                                device=self.device)
+            self._grad_views = None
             fresh = True
         else:
+            if self.grads_bound():
+                return ga       # every gradient already accumulated in place
             fresh = False
         base = ga.data_ptr()
         esz = ga.element_size()
@@ -314,7 +338,7 @@ class FlatParamGroup:
                     p.grad = None
             else:
                 self.grad_arena.zero_()
-                if self.param_arena is not None:
+                if self.param_arena is not None and not self.grads_bound():
                     self.bind_grads()
 
     def grad_for_shard(self) -> torch.Tensor:

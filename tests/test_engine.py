@@ -193,3 +193,34 @@ def test_timers_log_format():
     assert "backward:" in text and "step:" in text
     engine.timers.reset()
     assert engine.timers("step").elapsed == 0.0
+
+
+class _LossNet(torch.nn.Module):
+    """TinyNet returning the loss, the module contract of train_batch."""
+
+    def __init__(self):
+        super().__init__()
+        self.net = make_net()
+
+    def forward(self, x, targets):
+        return mse(self.net(x), targets)
+
+
+def test_train_batch_equals_forward_backward_step():
+    x, y = make_data(STEPS, GAS, 1, MICRO)
+    torch.manual_seed(0)
+    a, b = _LossNet(), _LossNet()
+    b.load_state_dict(a.state_dict())
+    cfg = config(micro=MICRO, gas=GAS, clip=0.5)
+    ea = ms.initialize(model=a, config=cfg)
+    eb = ms.initialize(model=b, config=dict(cfg, b200={"cuda_graph": True}))  # CPU: eager
+    for s in range(STEPS):
+        for m in range(GAS):
+            la = ea(x[s, m], targets=y[s, m])
+            ea.backward(la)
+            ea.step()
+            lb = eb.train_batch(x[s, m], targets=y[s, m])
+            assert torch.equal(la.detach(), lb.detach())
+    assert ea.global_steps == eb.global_steps == STEPS
+    for pa, pb in zip(a.parameters(), b.parameters()):
+        assert torch.equal(pa, pb)
