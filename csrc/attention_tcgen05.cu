@@ -1,0 +1,1071 @@
+// Causal flash attention, forward, for sm_100a (tcgen05 + tensor memory).
+//
+//   O[b, t, h, :] = softmax_t'<=t (q_t . k_t' / sqrt(D)) v_t'     (GQA: kv head h / (H/Hkv))
+//
+// Reads Q, K and V straight out of the fused projection output: a row-major
+// [B*T, W] matrix whose row holds every head's q, k and v (column offsets
+// q_col + h*D, k_col + g*D, v_col + g*D), so no head-major copies are made.
+// Writes O as [B*T, H*D] (the layout the output projection consumes) and the
+// per-row log-sum-exp (base 2) for the backward pass.
+//
+// One CTA computes one 128-row query tile of one (batch, head):
+//   warp 0     TMA: the Q tile once, then K and V tiles of 128 keys into a
+//              two-stage ring (separate barriers, so S can start before V lands)
+//   warp 1     tensor memory owner and MMA issuer:
+//                S  = Q K^T        (M=128, N=128, K=D; A, B from shared memory)
+//                O += P V          (M=128, N=D, K=128; A = P from tensor memory,
+//                                   B = V MN-major from shared memory)
+//   warps 2-5  softmax, one thread per query row: tcgen05.ld its 128 scores,
+//              causal mask, running max, exp2, row sum; P is written back over
+//              the S columns as packed 16-bit pairs (tcgen05.st); O is
+//              rescaled in tensor memory only when the row max grew by more
+//              than 8 (log2 units) since the last rescale, so P <= 2^8 always
+//              fits the 16-bit type and most tiles skip the O round trip.
+//              After the last tile: O / l, stored to global memory.
+// Tensor memory: 128 columns S/P + D columns O (256 columns), so two CTAs
+// share an SM and one's softmax overlaps the other's MMAs.
+// Causal tile skip: query tile i visits key tiles 0..i only; the diagonal
+// tile is masked per element.  Query tiles are scheduled longest first.
+//
+// Every wait is bounded (globaltimer): past the limit the CTA records an
+// error code, raises its abort flag, waits (bounded) for copies and MMAs in
+// flight, frees its tensor memory and returns.
+#include <algorithm>
+#include <cmath>
+
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+// Phase tracing for tuning (off unless compiled with -DMSB_ATTN_TRACE): the
+// cycles each role spends per phase, summed over CTAs into g_attn_trace.
+#ifdef MSB_ATTN_TRACE
+__device__ unsigned long long g_attn_trace[32];
+#define ATTN_T0(v) const long long v = clock64()
+#define ATTN_ADD(id, v) atomicAdd(&g_attn_trace[id], (unsigned long long)(clock64() - (v)))
+#else
+#define ATTN_T0(v)
+#define ATTN_ADD(id, v)
+#endif
+
+namespace msb {
+namespace attn {
+
+using namespace ::msb::ptx;
+
+constexpr int BQ = 128;        // query rows per tile
+constexpr int BKV = 128;       // keys per tile
+constexpr int KV_MAX = 3;      // K/V ring stages: 3 for D = 64, 2 for D = 128 (shared memory)
+template <int D>
+constexpr int kv_stages() { return D == 64 ? 3 : 2; }
+constexpr int kThreads = 320;  // 10 warps
+constexpr float kRescaleLog2 = 8.f;
+
+struct Params {
+  int B, T, H, Hkv;
+  int q_col, k_col, v_col;   // column of head 0's q / k / v in the qkv row
+  void* out;
+  long long ld_out;
+  float* lse;                // [B*H, T], base-2 log-sum-exp of the scaled scores
+  float scale_log2;          // log2(e) / sqrt(D)
+  int n_qtiles, n_pairs;
+  uint32_t idesc_s, idesc_o;
+  unsigned* err;
+  unsigned long long timeout_ns;
+};
+
+template <int D>
+struct Smem {
+  static constexpr int Q_BYTES = BQ * D * 2;
+  static constexpr int KV_BYTES = BKV * D * 2;
+  static constexpr int CHUNK = BQ * 128;   // one 64-column (128-byte) slab of a tile
+};
+
+struct alignas(8) Bars {
+  uint64_t q_full;
+  uint64_t k_full[KV_MAX], k_empty[KV_MAX];
+  uint64_t v_full[KV_MAX], v_empty[KV_MAX];
+  uint64_t s_full[2];    // S of tile t in tensor memory
+  uint64_t s_free[2];    // S of tile t read into registers (4 warps arrive; separate-P layout)
+  uint64_t p_full[2];    // P of tile t written, O of tile t corrected (4 warps arrive)
+  uint64_t pv_done[2];   // O_t += P_t V retired: S_t/P_t columns free again
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int D>
+constexpr size_t smem_bytes() {
+  return 1024 + 2 * Smem<D>::Q_BYTES + kv_stages<D>() * 2 * Smem<D>::KV_BYTES + sizeof(Bars);
+}
+
+__device__ __forceinline__ bool wait_b(uint32_t bar, uint32_t parity, volatile int* abort,
+                                       const Params& p, unsigned code) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = gtime();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort) return false;
+    if (gtime() - t0 > p.timeout_ns) {
+      *abort = 1;
+      atomicCAS(p.err, 0u, code);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ bool warp_wait_f(uint32_t bar, uint32_t parity, volatile int* abort,
+                                            const Params& p, unsigned code, int lane) {
+  int w = lane == 0 ? (wait_b(bar, parity, abort, p, code) ? 1 : 0) : 0;
+  return __shfl_sync(0xffffffffu, w, 0) != 0;
+}
+
+// K-major operand (rows x D, 64-column slabs CHUNK bytes apart), k-th 16-wide step
+template <int D>
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int ks) {
+  return smem_desc(base + (ks >> 2) * Smem<D>::CHUNK + (ks & 3) * 32, 16, 1024);
+}
+// V (128 keys x D, MN-major: D contiguous), k-th 16-key step
+template <int D>
+__device__ __forceinline__ uint64_t v_desc(uint32_t base, int ks) {
+  return smem_desc(base + ks * 2048, Smem<D>::CHUNK, 1024);
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// One CTA: query tiles 2c and 2c+1 of one (batch, head).  The MMA warp
+// alternates between them (ping-pong): while warps 2-5 run the softmax of
+// tile 0's scores, the tensor core computes tile 1's, and the other way
+// round.  Each softmax thread holds its row's 128 scores in registers
+// (one batched tensor-memory load, one pass).
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
+  using S = Smem<D>;
+  constexpr int KV_STAGES = kv_stages<D>();
+  constexpr uint32_t TMEM_COLS = 512;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;                               // two tiles
+  uint8_t* sK = sQ + 2 * S::Q_BYTES;
+  uint8_t* sV = sK + KV_STAGES * S::KV_BYTES;
+  Bars* bars = reinterpret_cast<Bars*>(sV + KV_STAGES * S::KV_BYTES);
+  volatile int* abort = &bars->abort;
+
+  ATTN_T0(t_cta);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = p.n_pairs - 1 - blockIdx.x;         // longest pairs first
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int g = h / (p.H / p.Hkv);
+  const int row0 = b * p.T;
+  const int n_kv_all = (p.T + BKV - 1) / BKV;
+  const int qt0 = 2 * c, qt1 = 2 * c + 1;
+  const bool has1 = qt1 < p.n_qtiles;
+  const int nkv0 = min(n_kv_all, qt0 + 1);
+  const int nkv1 = has1 ? min(n_kv_all, qt1 + 1) : 0;
+  const int nkv = max(nkv0, nkv1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bars->q_full), 1);
+    for (int s = 0; s < KV_STAGES; ++s) {
+      mbar_init(smem_u32(&bars->k_full[s]), 1);
+      mbar_init(smem_u32(&bars->k_empty[s]), 1);
+      mbar_init(smem_u32(&bars->v_full[s]), 1);
+      mbar_init(smem_u32(&bars->v_empty[s]), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(smem_u32(&bars->s_full[t]), 1);
+      mbar_init(smem_u32(&bars->s_free[t]), 4);
+      mbar_init(smem_u32(&bars->p_full[t]), 4);
+      mbar_init(smem_u32(&bars->pv_done[t]), 1);
+    }
+    mbar_init(smem_u32(&bars->drain), 1);
+    bars->abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&bars->tmem_base), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  // Tensor memory.  D = 64: S of tile t at 128t, P at 256 + 64t, O at 384 + 64t,
+  // so the next scores of a tile can be computed while its softmax still
+  // runs.  D = 128: no room for that; P overwrites S (its next S waits for P V).
+  constexpr bool SEP_P = D == 64;
+  auto col_s = [](int t) { return (uint32_t)(128 * t); };
+  auto col_p = [](int t) { return SEP_P ? (uint32_t)(256 + 64 * t) : (uint32_t)(128 * t); };
+  auto col_o = [](int t) { return SEP_P ? (uint32_t)(384 + 64 * t) : (uint32_t)(256 + D * t); };
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ TMA
+    const uint32_t qb = smem_u32(&bars->q_full);
+    mbar_expect_tx(qb, (has1 ? 2 : 1) * S::Q_BYTES);
+#pragma unroll
+    for (int cc = 0; cc < D / 64; ++cc) {
+      tma_load_2d(smem_u32(sQ) + cc * S::CHUNK, &tm, qb, p.q_col + h * D + 64 * cc,
+                  row0 + qt0 * BQ);
+      if (has1)
+        tma_load_2d(smem_u32(sQ + S::Q_BYTES) + cc * S::CHUNK, &tm, qb,
+                    p.q_col + h * D + 64 * cc, row0 + qt1 * BQ);
+    }
+    int kpend[KV_STAGES], vpend[KV_STAGES];
+#pragma unroll
+    for (int s = 0; s < KV_STAGES; ++s) kpend[s] = vpend[s] = -1;
+    for (int j = 0; j < nkv; ++j) {
+      const int st = j % KV_STAGES;
+      const uint32_t ph = (j / KV_STAGES) & 1;
+      const int y = row0 + j * BKV;
+      if (!wait_b(smem_u32(&bars->k_empty[st]), ph ^ 1, abort, p, 21)) break;
+      const uint32_t kb = smem_u32(&bars->k_full[st]);
+      mbar_expect_tx(kb, S::KV_BYTES);
+#pragma unroll
+      for (int cc = 0; cc < D / 64; ++cc)
+        tma_load_2d(smem_u32(sK + st * S::KV_BYTES) + cc * S::CHUNK, &tm, kb,
+                    p.k_col + g * D + 64 * cc, y);
+      kpend[st] = (int)ph;
+      if (!wait_b(smem_u32(&bars->v_empty[st]), ph ^ 1, abort, p, 22)) break;
+      const uint32_t vb = smem_u32(&bars->v_full[st]);
+      mbar_expect_tx(vb, S::KV_BYTES);
+#pragma unroll
+      for (int cc = 0; cc < D / 64; ++cc)
+        tma_load_2d(smem_u32(sV + st * S::KV_BYTES) + cc * S::CHUNK, &tm, vb,
+                    p.v_col + g * D + 64 * cc, y);
+      vpend[st] = (int)ph;
+    }
+    // copies in flight land before the CTA may exit
+    const uint64_t t0 = gtime();
+    while (!mbar_try(qb, 0) && gtime() - t0 < p.timeout_ns) {
+    }
+    for (int s = 0; s < KV_STAGES; ++s) {
+      if (kpend[s] >= 0)
+        while (!mbar_try(smem_u32(&bars->k_full[s]), (uint32_t)kpend[s]) &&
+               gtime() - t0 < p.timeout_ns) {
+        }
+      if (vpend[s] >= 0)
+        while (!mbar_try(smem_u32(&bars->v_full[s]), (uint32_t)vpend[s]) &&
+               gtime() - t0 < p.timeout_ns) {
+        }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA
+    // Event loop over the two tiles: issue whichever MMA is ready (S of
+    // tile t for key tile js[t], P V of tile t for key tile jp[t]), so one
+    // tile's softmax never holds up the other's tensor-core work.
+    auto qbase = [&](int t) { return smem_u32(sQ + t * S::Q_BYTES); };
+    auto nk = [&](int t) { return t == 0 ? nkv0 : nkv1; };
+    int js[2] = {0, 0}, jp[2] = {0, 0};
+    int kfree = 0, vfree = 0;               // next key tile whose K / V slot to release
+    bool ok = wait_b(smem_u32(&bars->q_full), 0, abort, p, 23);
+    uint64_t t_idle = 0;
+    while (ok) {
+      bool progress = false, pending = false;
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        // ---- S_t(js): K landed, and tile t's S columns free (its softmax read
+        // the previous S, or, when P overwrites S, the previous P V retired)
+        const int j = t == 0 ? js[0] : js[1];
+        if (j < nk(t)) {
+          pending = true;
+          const int st = j % KV_STAGES;
+          const bool s_ok = j == 0 || (SEP_P ? mbar_test(smem_u32(&bars->s_free[t]), (j - 1) & 1)
+                                             : mbar_test(smem_u32(&bars->pv_done[t]), (j - 1) & 1));
+          if (s_ok && mbar_test(smem_u32(&bars->k_full[st]), (j / KV_STAGES) & 1)) {
+            tc_fence_after();
+            const uint32_t kb = smem_u32(sK + st * S::KV_BYTES);
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks)
+              umma_f16(tmem + col_s(t), kmajor_desc<D>(qbase(t), ks), kmajor_desc<D>(kb, ks),
+                       p.idesc_s, ks > 0 ? 1u : 0u);
+            umma_commit(smem_u32(&bars->s_full[t]));
+            if (t == 0) ++js[0]; else ++js[1];
+            progress = true;
+          }
+        }
+        // ---- P_t V(jp): P written and V landed (S of that key tile issued)
+        const int jj = t == 0 ? jp[0] : jp[1];
+        if (jj < nk(t)) {
+          pending = true;
+          const int st = jj % KV_STAGES;
+          if (jj < (t == 0 ? js[0] : js[1]) && mbar_test(smem_u32(&bars->p_full[t]), jj & 1) &&
+              mbar_test(smem_u32(&bars->v_full[st]), (jj / KV_STAGES) & 1)) {
+            tc_fence_after();
+            const uint32_t vbase = smem_u32(sV + st * S::KV_BYTES);
+#pragma unroll
+            for (int ks = 0; ks < BKV / 16; ++ks)
+              umma_f16_ts(tmem + col_o(t), tmem + col_p(t) + ks * 8, v_desc<D>(vbase, ks),
+                          p.idesc_o, (jj > 0 || ks > 0) ? 1u : 0u);
+            umma_commit(smem_u32(&bars->pv_done[t]));
+            if (t == 0) ++jp[0]; else ++jp[1];
+            progress = true;
+          }
+        }
+      }
+      // release K / V slots once every tile that reads them has issued its MMA
+      while (kfree < nkv && (kfree < js[0] || kfree >= nkv0) && (kfree < js[1] || kfree >= nkv1)) {
+        umma_commit(smem_u32(&bars->k_empty[kfree % KV_STAGES]));
+        ++kfree;
+      }
+      while (vfree < nkv && (vfree < jp[0] || vfree >= nkv0) && (vfree < jp[1] || vfree >= nkv1)) {
+        umma_commit(smem_u32(&bars->v_empty[vfree % KV_STAGES]));
+        ++vfree;
+      }
+      if (!pending) break;
+      if (progress) {
+        t_idle = 0;
+      } else {
+        if (*abort) break;
+        const uint64_t now = gtime();
+        if (t_idle == 0) {
+          t_idle = now;
+        } else if (now - t_idle > p.timeout_ns) {
+          *abort = 1;
+          atomicCAS(p.err, 0u, 26u);
+          break;
+        }
+      }
+    }
+    umma_commit(smem_u32(&bars->drain));
+    const uint64_t t0 = gtime();
+    while (!mbar_try(smem_u32(&bars->drain), 0) && gtime() - t0 < p.timeout_ns) {
+    }
+  } else if (warp >= 2) {
+    // -------------------------------------------------------- softmax
+    const int t = (warp - 2) >> 2;                    // which query tile
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;                // row of the tile = TMEM lane
+    const int qt = t == 0 ? qt0 : qt1;
+    const int nk = t == 0 ? nkv0 : nkv1;
+    const int q = qt * BQ + r;                        // query position
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+    const uint32_t cs = col_s(t), cp = col_p(t), co = col_o(t);
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nk; ++j) {
+      ATTN_T0(t_s);
+      int w = lane == 0 ? (wait_b(smem_u32(&bars->s_full[t]), j & 1, abort, p, 28) ? 1 : 0) : 0;
+      w = __shfl_sync(0xffffffffu, w, 0);
+      if (!w) { ok = false; break; }
+      if (warp == 2 && lane == 0) ATTN_ADD(0, t_s);
+      tc_fence_after();
+      ATTN_T0(t_p1);
+      // raw scores of this thread's row (scaled on use, fused into the exp's FMA)
+      uint32_t sv[BKV];
+#pragma unroll
+      for (int cc = 0; cc < BKV / 32; ++cc)
+        tmem_ld32(lane_base + cs + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(sv + cc * 32));
+      tmem_ld_wait();
+      if (SEP_P) {
+        // the scores are in registers: the tensor core may overwrite them
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&bars->s_free[t]));
+      }
+      const int kv0 = j * BKV;
+      // keys past the query (diagonal tile) or past the sequence are masked
+      const int lim = min(q, p.T - 1) - kv0;          // last visible key offset in this tile
+      if (lim < BKV - 1) {
+#pragma unroll
+        for (int e = 0; e < BKV; ++e)
+          if (e > lim) sv[e] = __float_as_uint(-INFINITY);
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < BKV; ++e) mx = fmaxf(mx, __uint_as_float(sv[e]));
+      mx *= p.scale_log2;
+      if (warp == 2 && lane == 0) ATTN_ADD(1, t_p1);
+      ATTN_T0(t_rs);
+      // lazy rescale: move the reference max only when it grew by > 2^8
+      const bool grow = mx > m_used + kRescaleLog2;
+      const float m_new = grow ? mx : m_used;
+      const float alpha = grow ? ex2(m_used - m_new) : 1.f;   // 0 on the first visible tile
+      l *= alpha;
+      m_used = m_new;
+      if (warp == 2 && lane == 0) ATTN_ADD(2, t_rs);
+      ATTN_T0(t_p2);
+      const float mref = m_used == -INFINITY ? 0.f : m_used;
+      if (SEP_P && j > 0) {
+        // P and O of this tile are free once its previous P V retired
+        if (!warp_wait_f(smem_u32(&bars->pv_done[t]), (j - 1) & 1, abort, p, 30, lane)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      // P = 2^(s - m) as packed 16-bit pairs
+#pragma unroll
+      for (int hh = 0; hh < 4; ++hh) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float a = ex2(fmaf(__uint_as_float(sv[hh * 32 + 2 * e]), p.scale_log2, -mref));
+          const float bb = ex2(fmaf(__uint_as_float(sv[hh * 32 + 2 * e + 1]), p.scale_log2, -mref));
+          l += a + bb;
+          pk[e] = pack2<T>(a, bb);
+        }
+        tmem_st16(lane_base + cp + hh * 16, pk);
+      }
+      if (__any_sync(0xffffffffu, grow && j > 0)) {
+        // O is stable: this tile's previous P V retired (waited for above, or
+        // before its S was issued), and its next P V waits for p_full
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) {
+          uint32_t v[32];
+          tmem_ld32(lane_base + co + cc * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+          tmem_st32(lane_base + co + cc * 32, v);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars->p_full[t]));
+      if (warp == 2 && lane == 0) ATTN_ADD(3, t_p2);
+    }
+    if (ok && nk > 0) {
+      int w = lane == 0 ? (wait_b(smem_u32(&bars->pv_done[t]), (nk - 1) & 1, abort, p, 29) ? 1 : 0)
+                        : 0;
+      w = __shfl_sync(0xffffffffu, w, 0);
+      if (w) {
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        T* orow = static_cast<T*>(p.out) + (long long)(row0 + q) * p.ld_out + (long long)h * D;
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) {
+          uint32_t v[32];
+          tmem_ld32(lane_base + co + cc * 32, v);
+          tmem_ld_wait();
+          if (q < p.T) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              uint4 pack;
+              uint32_t* pw = reinterpret_cast<uint32_t*>(&pack);
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                pw[e] = pack2<T>(__uint_as_float(v[u * 8 + 2 * e]) * inv,
+                                 __uint_as_float(v[u * 8 + 2 * e + 1]) * inv);
+              *reinterpret_cast<uint4*>(orow + cc * 32 + u * 8) = pack;
+            }
+          }
+        }
+        if (q < p.T) p.lse[(long long)bh * p.T + q] = m_used + __log2f(l);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+  if (threadIdx.x == 0) ATTN_ADD(8, t_cta);
+}
+
+template <typename T, int D>
+void launch_fwd(const CUtensorMap& tm, const Params& p, int B, int H, cudaStream_t st) {
+  auto kern = attn_fwd_kernel<T, D>;
+  static bool attr = false;
+  if (!attr) {
+    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)smem_bytes<D>()),
+               "attn smem attribute");
+    attr = true;
+  }
+  dim3 grid(p.n_pairs, B * H);
+  kern<<<grid, kThreads, smem_bytes<D>(), st>>>(tm, p);
+}
+
+// ======================================================================
+// Backward.  One CTA owns one 128-key tile of one (batch, kv head) and loops
+// over the query heads of its group and over the query tiles at or after
+// the diagonal.  Per (head, query tile):
+//   S^T  = K Q^T,  dP^T = V dO^T                (keys on the tensor-memory lanes)
+//   P^T  = 2^(S^T * scale*log2e - lse),  dS^T = P^T (dP^T - delta)   (warps 2-5)
+//   dV  += P^T dO,  dK += dS^T Q                (A = P^T / dS^T from tensor memory;
+//                                                accumulated across the whole loop)
+//   dQ   = dS K                                 (A = dS^T from shared memory)
+// and warps 6-9 add the dQ partial into an fp32 accumulator with TMA
+// reduce-adds (several key tiles contribute to one query tile).  delta =
+// rowsum(dO * O) and the zeroed accumulator come from attn_delta_kernel; the
+// 16-bit dQ (times the softmax scale) from attn_dq_convert_kernel.
+// Tensor memory: S^T/P^T 128, dP^T/dS^T 128, dV D, dK D, dQ D columns.
+namespace bwd {
+
+constexpr int kThreadsB = 448;   // 14 warps
+
+struct Params {
+  int B, T, H, Hkv;
+  int q_col, k_col, v_col;
+  void* dqkv;
+  long long ld_dqkv;
+  const float* lse;
+  const float* delta;
+  float scale_log2, scale;
+  int n_q;
+  uint32_t idesc_s, idesc_kv, idesc_q;
+  unsigned* err;
+  unsigned long long timeout_ns;
+};
+
+struct alignas(8) Bars {
+  uint64_t kv_full;
+  uint64_t qo_full[2], qo_empty[2];
+  uint64_t st_full;
+  uint64_t ds_ready;
+  uint64_t mma2_done;
+  uint64_t dq_full;
+  uint64_t dq_free;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int D>
+struct Layout {
+  static constexpr int TILE = 128 * D * 2;
+  static constexpr int CH = 128 * 128;
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = K_OFF + TILE;
+  static constexpr int Q_OFF = V_OFF + TILE;          // two stages
+  static constexpr int DO_OFF = Q_OFF + 2 * TILE;     // two stages
+  static constexpr int DS_OFF = DO_OFF + 2 * TILE;    // dS^T, 128 keys x 128 queries
+  static constexpr int STG_OFF = DS_OFF + 128 * 128 * 2;
+  static constexpr int STG_WARP = 32 * D * 4;         // fp32 dQ rows of one warp
+  static constexpr int LSE_OFF = STG_OFF + 4 * STG_WARP;   // per softmax warp: 64 floats
+  static constexpr int DELTA_OFF = LSE_OFF + 8 * 256;
+  static constexpr int BARS_OFF = DELTA_OFF + 8 * 256;
+  static constexpr size_t BYTES = 1024 + BARS_OFF + sizeof(Bars);
+};
+
+__device__ __forceinline__ bool wait_b(uint32_t bar, uint32_t parity, volatile int* abort,
+                                       const Params& p, unsigned code) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = gtime();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort) return false;
+    if (gtime() - t0 > p.timeout_ns) {
+      *abort = 1;
+      atomicCAS(p.err, 0u, code);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          const Params& p, unsigned code, int lane) {
+  int w = lane == 0 ? (wait_b(bar, parity, abort, p, code) ? 1 : 0) : 0;
+  return __shfl_sync(0xffffffffu, w, 0) != 0;
+}
+
+// operand whose rows (the K index of the MMA) are 128-byte swizzled rows of
+// 64 contiguous M/N elements, slabs of 64 columns CH bytes apart
+__device__ __forceinline__ uint64_t mn_desc(uint32_t base, int ks) {
+  return smem_desc(base + ks * 2048, Layout<64>::CH, 1024);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreadsB, 1)
+attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                const __grid_constant__ CUtensorMap tm_dq, const Params p) {
+  using L = Layout<D>;
+  constexpr uint32_t TMEM_COLS = 512;
+  // S^T 0-127 (dQ reuses 0-63 once every softmax warp read S^T), dP^T 128-255,
+  // packed P^T 256-319, packed dS^T 320-383, dV 384-447, dK 448-511: the
+  // softmax warps never write columns another warp still reads
+  static_assert(D == 64, "backward tensor-memory layout is for head dim 64");
+  constexpr uint32_t C_S = 0, C_DP = 128, C_P = 256, C_DS = 320, C_DV = 384, C_DK = 448,
+                     C_DQ = 0;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + L::BARS_OFF);
+  float* sLse = reinterpret_cast<float*>(smem + L::LSE_OFF);
+  float* sDelta = reinterpret_cast<float*>(smem + L::DELTA_OFF);
+  volatile int* abort = &bars->abort;
+  const uint32_t sbase = smem_u32(smem);
+
+  ATTN_T0(t_cta);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x;
+  const int b = blockIdx.y / p.Hkv, g = blockIdx.y % p.Hkv;
+  const int rep = p.H / p.Hkv;
+  const int n_i = p.n_q - j;
+  const int nit = rep * n_i;
+  const int row0 = b * p.T;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bars->kv_full), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&bars->qo_full[s]), 1);
+      mbar_init(smem_u32(&bars->qo_empty[s]), 1);
+    }
+    mbar_init(smem_u32(&bars->st_full), 1);
+    mbar_init(smem_u32(&bars->ds_ready), 8);
+    mbar_init(smem_u32(&bars->mma2_done), 1);
+    mbar_init(smem_u32(&bars->dq_full), 1);
+    mbar_init(smem_u32(&bars->dq_free), 4);
+    mbar_init(smem_u32(&bars->drain), 1);
+    bars->abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&bars->tmem_base), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ TMA
+    const uint32_t kvb = smem_u32(&bars->kv_full);
+    mbar_expect_tx(kvb, 2 * L::TILE);
+#pragma unroll
+    for (int c = 0; c < D / 64; ++c) {
+      tma_load_2d(sbase + L::K_OFF + c * L::CH, &tm_qkv, kvb, p.k_col + g * D + 64 * c,
+                  row0 + j * 128);
+      tma_load_2d(sbase + L::V_OFF + c * L::CH, &tm_qkv, kvb, p.v_col + g * D + 64 * c,
+                  row0 + j * 128);
+    }
+    int pend[2] = {-1, -1};
+    for (int it = 0; it < nit; ++it) {
+      const int st = it & 1;
+      const uint32_t ph = (it >> 1) & 1;
+      const int h = g * rep + it / n_i, i = j + it % n_i;
+      if (!wait_b(smem_u32(&bars->qo_empty[st]), ph ^ 1, abort, p, 41)) break;
+      const uint32_t fb = smem_u32(&bars->qo_full[st]);
+      mbar_expect_tx(fb, 2 * L::TILE);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_2d(sbase + L::Q_OFF + st * L::TILE + c * L::CH, &tm_qkv, fb,
+                    p.q_col + h * D + 64 * c, row0 + i * 128);
+        tma_load_2d(sbase + L::DO_OFF + st * L::TILE + c * L::CH, &tm_do, fb, h * D + 64 * c,
+                    row0 + i * 128);
+      }
+      pend[st] = (int)ph;
+    }
+    const uint64_t t0 = gtime();
+    while (!mbar_try(kvb, 0) && gtime() - t0 < p.timeout_ns) {
+    }
+    for (int s = 0; s < 2; ++s)
+      if (pend[s] >= 0)
+        while (!mbar_try(smem_u32(&bars->qo_full[s]), (uint32_t)pend[s]) &&
+               gtime() - t0 < p.timeout_ns) {
+        }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA
+    bool ok = wait_b(smem_u32(&bars->kv_full), 0, abort, p, 42);
+    const uint32_t kb = sbase + L::K_OFF, vb = sbase + L::V_OFF, dsb = sbase + L::DS_OFF;
+    for (int it = 0; it < nit && ok; ++it) {
+      const int st = it & 1;
+      const uint32_t ph = (it >> 1) & 1;
+      ATTN_T0(t_q);
+      if (!wait_b(smem_u32(&bars->qo_full[st]), ph, abort, p, 43)) break;
+      ATTN_ADD(12, t_q);
+      ATTN_T0(t_m2);
+      // S^T / dP^T columns and the dS^T tile are free once the last MMAs
+      // retired, and the S^T columns once the dQ partial there was read
+      if (it > 0 && !wait_b(smem_u32(&bars->mma2_done), (it - 1) & 1, abort, p, 44)) break;
+      ATTN_ADD(13, t_m2);
+      ATTN_T0(t_dqf);
+      if (it > 0 && !wait_b(smem_u32(&bars->dq_free), (it - 1) & 1, abort, p, 46)) break;
+      ATTN_ADD(15, t_dqf);
+      tc_fence_after();
+      const uint32_t qb = sbase + L::Q_OFF + st * L::TILE, ob = sbase + L::DO_OFF + st * L::TILE;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const uint64_t dk = kmajor_desc<D>(kb, ks), dv = kmajor_desc<D>(vb, ks);
+        umma_f16(tmem + C_S, dk, kmajor_desc<D>(qb, ks), p.idesc_s, ks > 0 ? 1u : 0u);
+        umma_f16(tmem + C_DP, dv, kmajor_desc<D>(ob, ks), p.idesc_s, ks > 0 ? 1u : 0u);
+      }
+      umma_commit(smem_u32(&bars->st_full));
+      ATTN_T0(t_ds);
+      if (!wait_b(smem_u32(&bars->ds_ready), it & 1, abort, p, 45)) break;
+      ATTN_ADD(14, t_ds);
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        umma_f16_ts(tmem + C_DV, tmem + C_P + ks * 8, mn_desc(ob, ks), p.idesc_kv,
+                    (it > 0 || ks > 0) ? 1u : 0u);
+        umma_f16_ts(tmem + C_DK, tmem + C_DS + ks * 8, mn_desc(qb, ks), p.idesc_kv,
+                    (it > 0 || ks > 0) ? 1u : 0u);
+      }
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_f16(tmem + C_DQ, mn_desc(dsb, ks), mn_desc(kb, ks), p.idesc_q, ks > 0 ? 1u : 0u);
+      umma_commit(smem_u32(&bars->qo_empty[st]));
+      umma_commit(smem_u32(&bars->mma2_done));
+      umma_commit(smem_u32(&bars->dq_full));
+    }
+    umma_commit(smem_u32(&bars->drain));
+    const uint64_t t0 = gtime();
+    while (!mbar_try(smem_u32(&bars->drain), 0) && gtime() - t0 < p.timeout_ns) {
+    }
+  } else if (warp >= 2 && warp < 10) {
+    // --------------------- P^T, dS^T (thread = key, warp = 64 of the queries)
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int r = quarter * 32 + lane;
+    const int kj = j * 128 + r;
+    const uint32_t lb = tmem + ((uint32_t)(quarter * 32) << 16);
+    uint8_t* sdS = smem + L::DS_OFF;
+    // this warp's copy of its 64 queries' lse / delta (no cross-warp barrier:
+    // every wait of these warps stays bounded)
+    float* wLse = sLse + (warp - 2) * 64;
+    float* wDelta = sDelta + (warp - 2) * 64;
+    bool ok = true;
+    for (int it = 0; it < nit; ++it) {
+      const int h = g * rep + it / n_i, i = j + it % n_i;
+      const long long lrow = (long long)(b * p.H + h) * p.T;
+      __syncwarp();
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int qi = i * 128 + half * 64 + u * 32 + lane;
+        wLse[u * 32 + lane] = qi < p.T ? p.lse[lrow + qi] : 0.f;
+        wDelta[u * 32 + lane] = qi < p.T ? p.delta[lrow + qi] : 0.f;
+      }
+      __syncwarp();
+      ATTN_T0(t_st);
+      if (!warp_wait(smem_u32(&bars->st_full), it & 1, abort, p, 47, lane)) { ok = false; break; }
+      if (warp == 2 && lane == 0) ATTN_ADD(10, t_st);
+      ATTN_T0(t_sm);
+      tc_fence_after();
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = half * 2 + cc;                  // 32-query chunk of the tile
+        uint32_t sv[32], dv[32];
+        tmem_ld32(lb + C_S + c * 32, sv);
+        tmem_ld32(lb + C_DP + c * 32, dv);
+        tmem_ld_wait();
+        uint32_t pk[16], dk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float pp[2], dd[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int col = cc * 32 + 2 * e + u;       // within this warp's 64 queries
+            const int qi = i * 128 + half * 64 + col;
+            const bool vis = qi >= kj && qi < p.T;
+            const float pr =
+                vis ? ex2(fmaf(__uint_as_float(sv[2 * e + u]), p.scale_log2, -wLse[col])) : 0.f;
+            pp[u] = pr;
+            dd[u] = pr * (__uint_as_float(dv[2 * e + u]) - wDelta[col]);
+          }
+          pk[e] = pack2<T>(pp[0], pp[1]);
+          dk[e] = pack2<T>(dd[0], dd[1]);
+        }
+        tmem_st16(lb + C_P + c * 16, pk);
+        tmem_st16(lb + C_DS + c * 16, dk);
+        // dS^T row r, queries c*32..c*32+31: 64-column slab c/2, 16-byte pieces 4*(c&1)..+3
+        uint8_t* rowp = sdS + (c >> 1) * L::CH + r * 128;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int piece = ((c & 1) * 4 + u) ^ (r & 7);
+          *reinterpret_cast<uint4*>(rowp + piece * 16) =
+              make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
+        }
+      }
+      tmem_st_wait();
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars->ds_ready));
+      if (warp == 2 && lane == 0) ATTN_ADD(11, t_sm);
+    }
+    // dK (times the softmax scale) and dV of this key tile: each warp of a
+    // quarter stores one of them
+    if (ok && nit > 0 && warp_wait(smem_u32(&bars->mma2_done), (nit - 1) & 1, abort, p, 48, lane)) {
+      tc_fence_after();
+      T* drow = static_cast<T*>(p.dqkv) + (long long)(row0 + kj) * p.ld_dqkv;
+      const int which = half;
+      const uint32_t col0 = which == 0 ? C_DK : C_DV;
+      const float f = which == 0 ? p.scale : 1.f;
+      T* dst = drow + (which == 0 ? p.k_col : p.v_col) + g * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(lb + col0 + c * 32, v);
+        tmem_ld_wait();
+        if (kj < p.T) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint4 pack;
+            uint32_t* pw = reinterpret_cast<uint32_t*>(&pack);
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              pw[e] = pack2<T>(__uint_as_float(v[u * 8 + 2 * e]) * f,
+                               __uint_as_float(v[u * 8 + 2 * e + 1]) * f);
+            *reinterpret_cast<uint4*>(dst + c * 32 + u * 8) = pack;
+          }
+        }
+      }
+    }
+  } else if (warp >= 10) {
+    // ------------------------------------- dQ partial -> fp32 accumulator
+    const int quarter = warp & 3;
+    const uint32_t lb = tmem + ((uint32_t)(quarter * 32) << 16);
+    uint8_t* stg = smem + L::STG_OFF + (warp - 10) * L::STG_WARP;
+    for (int it = 0; it < nit; ++it) {
+      const int h = g * rep + it / n_i, i = j + it % n_i;
+      ATTN_T0(t_dq);
+      if (!warp_wait(smem_u32(&bars->dq_full), it & 1, abort, p, 49, lane)) break;
+      if (warp == 10 && lane == 0) ATTN_ADD(16, t_dq);
+      ATTN_T0(t_dqe);
+      tc_fence_after();
+      uint32_t v[D];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t w[32];
+        tmem_ld32(lb + C_DQ + c * 32, w);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[c * 32 + e] = w[e];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars->dq_free));
+      if (warp == 10 && lane == 0) ATTN_ADD(17, t_dqe);
+      ATTN_T0(t_bw);
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
+      if (warp == 10 && lane == 0) ATTN_ADD(18, t_bw);
+      // 32-column boxes of 32 rows x 128 bytes, 128-byte swizzle
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint8_t* rowp = stg + c * 4096 + lane * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<uint4*>(rowp + ((u ^ (lane & 7)) << 4)) =
+              make_uint4(v[c * 32 + 4 * u], v[c * 32 + 4 * u + 1], v[c * 32 + 4 * u + 2],
+                         v[c * 32 + 4 * u + 3]);
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c)
+          tma_reduce_add_2d(&tm_dq, smem_u32(stg + c * 4096), h * D + 32 * c,
+                            row0 + i * 128 + quarter * 32);
+        bulk_commit();
+      }
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+  if (threadIdx.x == 0) ATTN_ADD(19, t_cta);
+}
+
+// delta[b, h, t] = sum_d dO * O (fp32) and a zeroed dQ accumulator row
+template <typename T, int D>
+__global__ void __launch_bounds__(256)
+attn_delta_kernel(const T* __restrict__ dout, long long ld_do, const T* __restrict__ out,
+                  long long ld_o, float* __restrict__ delta, float* __restrict__ dq_acc, int BT,
+                  int seq, int H) {
+  const long long n = (long long)BT * H;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(idx / H), h = (int)(idx % H);
+    const uint4* a = reinterpret_cast<const uint4*>(dout + (long long)row * ld_do + h * D);
+    const uint4* o = reinterpret_cast<const uint4*>(out + (long long)row * ld_o + h * D);
+    float acc = 0.f;
+#pragma unroll
+    for (int q = 0; q < D / 8; ++q) {
+      const uint4 x = a[q], y = o[q];
+      const T* xh = reinterpret_cast<const T*>(&x);
+      const T* yh = reinterpret_cast<const T*>(&y);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc += to_f32(xh[e]) * to_f32(yh[e]);
+    }
+    const int b = row / seq, t = row % seq;
+    delta[((long long)b * H + h) * seq + t] = acc;
+    float4* z = reinterpret_cast<float4*>(dq_acc + (long long)row * H * D + h * D);
+#pragma unroll
+    for (int q = 0; q < D / 4; ++q) z[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// dqkv[:, q_col + h*D + d] = dq_acc * scale
+template <typename T>
+__global__ void __launch_bounds__(256)
+attn_dq_convert_kernel(const float* __restrict__ dq_acc, int BT, int HD, T* __restrict__ dqkv,
+                       long long ld_dqkv, int q_col, float scale) {
+  const long long n = (long long)BT * HD / 8;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long e0 = idx * 8;
+    const int row = (int)(e0 / HD), col = (int)(e0 % HD);
+    const float4 x = reinterpret_cast<const float4*>(dq_acc)[idx * 2];
+    const float4 y = reinterpret_cast<const float4*>(dq_acc)[idx * 2 + 1];
+    uint4 pack;
+    uint32_t* pw = reinterpret_cast<uint32_t*>(&pack);
+    pw[0] = pack2<T>(x.x * scale, x.y * scale);
+    pw[1] = pack2<T>(x.z * scale, x.w * scale);
+    pw[2] = pack2<T>(y.x * scale, y.y * scale);
+    pw[3] = pack2<T>(y.z * scale, y.w * scale);
+    *reinterpret_cast<uint4*>(dqkv + (long long)row * ld_dqkv + q_col + col) = pack;
+  }
+}
+
+template <typename T, int D>
+void launch_bwd(const CUtensorMap& tq, const CUtensorMap& td, const CUtensorMap& tdq,
+                const Params& p, cudaStream_t st) {
+  auto kern = attn_bwd_kernel<T, D>;
+  static bool attr = false;
+  if (!attr) {
+    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)Layout<D>::BYTES),
+               "attn bwd smem attribute");
+    attr = true;
+  }
+  dim3 grid(p.n_q, p.B * p.Hkv);
+  kern<<<grid, kThreadsB, Layout<D>::BYTES, st>>>(tq, td, tdq, p);
+}
+
+}  // namespace bwd
+}  // namespace attn
+
+void attention_fwd(const void* qkv, long long ld_qkv, long long n_cols, int q_col, int k_col,
+                   int v_col, void* out, long long ld_out, float* lse, int B, int T, int H,
+                   int Hkv, int D, int dtype, float scale, unsigned* err, double timeout_s,
+                   cudaStream_t st) {
+  using namespace attn;
+  if (D != 64 && D != 128) throw std::runtime_error("attention: head dim must be 64 or 128");
+  if (H % Hkv != 0) throw std::runtime_error("attention: H must be a multiple of Hkv");
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (ld_out % 8))
+    throw std::runtime_error("attention: output must allow 16-byte row stores");
+  Params p;
+  p.B = B;
+  p.T = T;
+  p.H = H;
+  p.Hkv = Hkv;
+  p.q_col = q_col;
+  p.k_col = k_col;
+  p.v_col = v_col;
+  p.out = out;
+  p.ld_out = ld_out;
+  p.lse = lse;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.n_qtiles = (T + BQ - 1) / BQ;
+  p.n_pairs = (p.n_qtiles + 1) / 2;
+  const uint32_t fmt = dtype == kBF16 ? 1u : 0u;
+  // S = Q K^T: both K-major, N = 128, M = 128
+  p.idesc_s = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BKV >> 3) << 17) |
+              ((uint32_t)(BQ >> 4) << 24);
+  // O += P V: A (tensor memory) K-major, B = V MN-major, N = D, M = 128
+  p.idesc_o = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) | ((uint32_t)(D >> 3) << 17) |
+              ((uint32_t)(BQ >> 4) << 24);
+  p.err = err;
+  p.timeout_ns = static_cast<unsigned long long>(timeout_s * 1e9);
+  const CUtensorMap tm = make_map(qkv, dtype, n_cols, (long long)B * T, ld_qkv, 64, 128);
+  if (dtype == kF16) {
+    if (D == 64) launch_fwd<__half, 64>(tm, p, B, H, st);
+    else launch_fwd<__half, 128>(tm, p, B, H, st);
+  } else if (dtype == kBF16) {
+    if (D == 64) launch_fwd<__nv_bfloat16, 64>(tm, p, B, H, st);
+    else launch_fwd<__nv_bfloat16, 128>(tm, p, B, H, st);
+  } else {
+    throw std::runtime_error("attention takes fp16/bf16");
+  }
+  MSB_CHECK_LAUNCH("attention_fwd");
+}
+
+
+void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_col, int k_col,
+                   int v_col, const void* out, long long ld_out, const void* dout, long long ld_do,
+                   const float* lse, float* delta, float* dq_acc, void* dqkv, long long ld_dqkv,
+                   int B, int T, int H, int Hkv, int D, int dtype, float scale, unsigned* err,
+                   double timeout_s, cudaStream_t st) {
+  using namespace attn::bwd;
+  if (D != 64) throw std::runtime_error("attention backward: head dim 64 only");
+  if (H % Hkv != 0) throw std::runtime_error("attention: H must be a multiple of Hkv");
+  auto aligned = [](const void* ptr, long long ld) {
+    return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && ld % 8 == 0;
+  };
+  if (!aligned(out, ld_out) || !aligned(dout, ld_do) || !aligned(dqkv, ld_dqkv))
+    throw std::runtime_error("attention backward: operands must allow 16-byte row access");
+  const int BT = B * T;
+  const int blocks = grid_for((long long)BT * H, 256, kNumSMs * 8);
+  const int blocks_c = grid_for((long long)BT * H * D / 8, 256, kNumSMs * 8);
+  attn::bwd::Params p;
+  p.B = B;
+  p.T = T;
+  p.H = H;
+  p.Hkv = Hkv;
+  p.q_col = q_col;
+  p.k_col = k_col;
+  p.v_col = v_col;
+  p.dqkv = dqkv;
+  p.ld_dqkv = ld_dqkv;
+  p.lse = lse;
+  p.delta = delta;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.n_q = (T + 127) / 128;
+  const uint32_t fmt = dtype == kBF16 ? 1u : 0u;
+  p.idesc_s = (1u << 4) | (fmt << 7) | (fmt << 10) | (16u << 17) | (8u << 24);
+  p.idesc_kv = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) | ((uint32_t)(D >> 3) << 17) |
+               (8u << 24);
+  p.idesc_q = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 15) | (1u << 16) |
+              ((uint32_t)(D >> 3) << 17) | (8u << 24);
+  p.err = err;
+  p.timeout_ns = static_cast<unsigned long long>(timeout_s * 1e9);
+  const CUtensorMap tq = make_map(qkv, dtype, n_cols, (long long)BT, ld_qkv, 64, 128);
+  const CUtensorMap td = make_map(dout, dtype, (long long)H * D, (long long)BT, ld_do, 64, 128);
+  const CUtensorMap tdq = make_map_f32(dq_acc, (long long)H * D, (long long)BT, (long long)H * D,
+                                       32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (dtype == kF16) {
+    attn_delta_kernel<__half, 64><<<blocks, 256, 0, st>>>(
+        static_cast<const __half*>(dout), ld_do, static_cast<const __half*>(out), ld_out, delta,
+        dq_acc, BT, T, H);
+    launch_bwd<__half, 64>(tq, td, tdq, p, st);
+    attn_dq_convert_kernel<__half><<<blocks_c, 256, 0, st>>>(dq_acc, BT, H * D,
+                                                             static_cast<__half*>(dqkv), ld_dqkv,
+                                                             q_col, scale);
+  } else if (dtype == kBF16) {
+    attn_delta_kernel<__nv_bfloat16, 64><<<blocks, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(dout), ld_do, static_cast<const __nv_bfloat16*>(out),
+        ld_out, delta, dq_acc, BT, T, H);
+    launch_bwd<__nv_bfloat16, 64>(tq, td, tdq, p, st);
+    attn_dq_convert_kernel<__nv_bfloat16><<<blocks_c, 256, 0, st>>>(
+        dq_acc, BT, H * D, static_cast<__nv_bfloat16*>(dqkv), ld_dqkv, q_col, scale);
+  } else {
+    throw std::runtime_error("attention takes fp16/bf16");
+  }
+  MSB_CHECK_LAUNCH("attention_bwd");
+  count_launch(2);
+}
+
+}  // namespace msb

@@ -351,6 +351,49 @@ std::pair<int, int> tune_gemm(const at::Tensor& a, const at::Tensor& b, int a_mn
   return pick;
 }
 
+// ------------------------------------------------------------- attention
+// qkv2d: [B*T, (H + 2*Hkv)*D] rows of the fused projection (q, k, v heads);
+// out2d: [B*T, H*D]; lse: fp32 [B*H, T].
+void attention_fwd_py(const at::Tensor& qkv2d, int64_t q_col, int64_t k_col, int64_t v_col,
+                      const at::Tensor& out2d, const at::Tensor& lse, int64_t B, int64_t T,
+                      int64_t H, int64_t Hkv, int64_t D, double scale, const at::Tensor& err,
+                      double timeout_s) {
+  check_rows(qkv2d, "qkv");
+  check_rows(out2d, "attention output");
+  TORCH_CHECK(qkv2d.scalar_type() == out2d.scalar_type(), "attention dtype mismatch");
+  TORCH_CHECK(qkv2d.size(0) == B * T && out2d.size(0) == B * T && out2d.size(1) == H * D);
+  TORCH_CHECK(lse.is_cuda() && lse.scalar_type() == at::kFloat && lse.is_contiguous() &&
+              lse.numel() == B * H * T, "lse must be fp32 [B*H, T]");
+  c10::cuda::CUDAGuard g(qkv2d.device());
+  msb::attention_fwd(qkv2d.data_ptr(), qkv2d.stride(0), qkv2d.size(1), (int)q_col, (int)k_col,
+                     (int)v_col, out2d.data_ptr(), out2d.stride(0), lse.data_ptr<float>(), (int)B,
+                     (int)T, (int)H, (int)Hkv, (int)D, dtype_code(qkv2d), (float)scale,
+                     reinterpret_cast<unsigned*>(err.data_ptr<int>()), timeout_s, stream_of(qkv2d));
+}
+
+void attention_bwd_py(const at::Tensor& qkv2d, int64_t q_col, int64_t k_col, int64_t v_col,
+                      const at::Tensor& out2d, const at::Tensor& dout2d, const at::Tensor& lse,
+                      const at::Tensor& delta, const at::Tensor& dq_acc, const at::Tensor& dqkv2d,
+                      int64_t B, int64_t T, int64_t H, int64_t Hkv, int64_t D, double scale,
+                      const at::Tensor& err, double timeout_s) {
+  check_rows(qkv2d, "qkv");
+  check_rows(out2d, "attention output");
+  check_rows(dout2d, "attention output gradient");
+  check_rows(dqkv2d, "qkv gradient");
+  TORCH_CHECK(dqkv2d.sizes() == qkv2d.sizes() && dout2d.sizes() == out2d.sizes());
+  TORCH_CHECK(delta.scalar_type() == at::kFloat && delta.is_contiguous() &&
+              delta.numel() == B * H * T, "delta must be fp32 [B*H, T]");
+  TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.is_contiguous() &&
+              dq_acc.numel() == B * T * H * D, "dq accumulator must be fp32 [B*T, H*D]");
+  c10::cuda::CUDAGuard g(qkv2d.device());
+  msb::attention_bwd(qkv2d.data_ptr(), qkv2d.stride(0), qkv2d.size(1), (int)q_col, (int)k_col,
+                     (int)v_col, out2d.data_ptr(), out2d.stride(0), dout2d.data_ptr(),
+                     dout2d.stride(0), lse.data_ptr<float>(), delta.data_ptr<float>(),
+                     dq_acc.data_ptr<float>(), dqkv2d.data_ptr(), dqkv2d.stride(0), (int)B, (int)T,
+                     (int)H, (int)Hkv, (int)D, dtype_code(qkv2d), (float)scale,
+                     reinterpret_cast<unsigned*>(err.data_ptr<int>()), timeout_s, stream_of(qkv2d));
+}
+
 // C[M,N] (+)= A * B^T with A given as [M,K] (a_kmajor) or [K,M], B as [N,K]
 // (b_kmajor) or [K,N]; every matrix row-major with unit column stride.
 void gemm(const at::Tensor& a, const at::Tensor& b, bool a_kmajor, bool b_kmajor,
@@ -547,6 +590,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, mod) {
   mod.def("embedding_bwd", &embedding_bwd);
   mod.def("rope", &rope);
   mod.def("gemm", &gemm);
+  mod.def("attention_fwd", &attention_fwd_py);
+  mod.def("attention_bwd", &attention_bwd_py);
   mod.def("gemm_plan", &gemm_plan_py);
   mod.def("gemm_cached_plan", &gemm_cached_plan);
   mod.def("peer_alloc", &peer_alloc_py);

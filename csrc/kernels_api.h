@@ -58,6 +58,17 @@ void rope(void* x, const float* cos_t, const float* sin_t, long long BT, int T_l
 
 // ---- tcgen05 GEMM (gemm_tcgen05.cu)
 long long gemm_plan(int M, int N, int K, int num_sms, int* bn_out, int* splits_out);
+// ---- attention (attention_tcgen05.cu): qkv is a row-major [B*T, n_cols] matrix
+void attention_fwd(const void* qkv, long long ld_qkv, long long n_cols, int q_col, int k_col,
+                   int v_col, void* out, long long ld_out, float* lse, int B, int T, int H,
+                   int Hkv, int D, int dtype, float scale, unsigned* err, double timeout_s,
+                   cudaStream_t st);
+void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_col, int k_col,
+                   int v_col, const void* out, long long ld_out, const void* dout, long long ld_do,
+                   const float* lse, float* delta, float* dq_acc, void* dqkv, long long ld_dqkv,
+                   int B, int T, int H, int Hkv, int D, int dtype, float scale, unsigned* err,
+                   double timeout_s, cudaStream_t st);
+
 void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
                   void* C, long long ldc, const void* bias, int M, int N, int K, int dtype,
                   int accumulate, int mode, void* aux, long long ld_aux, float* ws,
