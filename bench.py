@@ -1,29 +1,36 @@
-"""Headline benchmark: GPT-2-small ZeRO-2 fp16 training throughput.
+"""Headline benchmark: training throughput of the BASELINE.json configs.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--model gpt2-small|gpt2-xl|llama3-8b]
 
-Config: GPT-2 small shape (12 layers, d_model 768,
-12 heads, MLP 3072, vocab 50257, seq 1024), fp16 with fp32 masters and dynamic
-loss scaling (initial_scale_power 16, window 1000), ZeRO stage 2, micro-batch
-16 per GPU, gas 1, AdamW, WarmupDecayLR, gradient clipping 1.0.  Synthetic
-uniform-random token ids, GPT-2 random init (std 0.02) for both arms.
+Default (the headline): GPT-2 small shape (12 layers,
+d_model 768, 12 heads, MLP 3072, vocab 50257, seq 1024), fp16 with fp32
+masters and dynamic loss scaling (initial_scale_power 16, window 1000), ZeRO
+stage 2, micro-batch 16 per GPU, gas 1, AdamW, WarmupDecayLR, gradient
+clipping 1.0.  ``--model gpt2-xl`` (config 3): 48 layers, d 1600, 25 heads,
+MLP 6400, bf16, ZeRO-1, micro-batch 4, gas 4, clipping 1.0, activation
+checkpointing on every block.  ``--model llama3-8b`` (config 4): 32 layers,
+d 4096, 32 q / 8 kv heads, SwiGLU 14336, RMSNorm, RoPE theta 500000, vocab
+128256, seq 4096, bf16, ZeRO-3, micro-batch 1, gas 8, AdamW.  Synthetic
+uniform-random token ids, random init (std 0.02) for both arms.
 
 ``--impl ours`` runs minispeed_b200 (fused sm_100a kernels) through
 ``engine.train_batch`` with ``b200.cuda_graph`` on: after two eager warm-up
 micro-steps the forward + backward is replayed as one captured CUDA graph and
-the optimizer step runs eagerly after it (one host read per step); ``--impl
-reference`` runs the unmodified reference engine installed in
-``baseline/_ref`` through its public API with a stock-PyTorch GPT-2 of the
-same architecture (nn.Linear/nn.LayerNorm/nn.GELU/SDPA, the reference
-example's model) and the reference example's fp32-upcast cross-entropy.
+the optimizer step runs eagerly after it (one host read per step; ZeRO-3
+runs eagerly).  ``--impl reference`` runs the unmodified reference engine
+installed in ``baseline/_ref`` through its public API with stock-PyTorch
+models of the same architectures (nn.Linear / nn.LayerNorm / nn.GELU / SDPA
+GPT-2 as in the reference example; a stock RMSNorm / RoPE / GQA-SDPA / SwiGLU
+Llama) and the reference example's fp32-upcast cross-entropy.
 
 Timing: W untimed warm-up steps, then K steps bracketed by barrier +
 synchronize, timed with CUDA events on the launching stream; the reported
 time is the max over ranks.  Each step streams > 2 GB (fp32 masters + Adam
-moments alone are 1.5 GB) so its inputs are larger than L2.  A second loop
-("e2e") times K more steps end to end through the public API including the
-pinned host->device copy of each step's tokens and the device->host read of
-its loss.  Prints one JSON line on rank 0.
+moments alone are 1.5 GB for GPT-2 small) so its inputs are larger than L2.
+A second loop ("e2e") times K more steps end to end through the public API
+including the pinned host->device copy of each step's tokens and the
+device->host read of its loss.  Prints one JSON line on rank 0.
 """
 
 from __future__ import annotations
@@ -44,49 +51,67 @@ import torch.nn.functional as F
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "tokens/sec whole box (max over ranks), ZeRO-2/3, 1/2/4/8 B200; exposed comm ms"
 
-VOCAB, SEQ, LAYERS, HEADS, EMBD = 50257, 1024, 12, 12, 768
-MICRO, GAS = 16, 1
+SPECS = {
+    "gpt2-small": dict(kind="gpt", vocab=50257, seq=1024, layers=12, heads=12, embd=768,
+                       mlp=3072, dtype="fp16", stage=2, micro=16, gas=1, clip=1.0, ckpt=False,
+                       label="GPT-2 small (12L, d768, 12H, MLP 3072, vocab 50257)"),
+    "gpt2-xl": dict(kind="gpt", vocab=50257, seq=1024, layers=48, heads=25, embd=1600,
+                    mlp=6400, dtype="bf16", stage=1, micro=4, gas=4, clip=1.0, ckpt=True,
+                    label="GPT-2 XL (48L, d1600, 25H, MLP 6400, vocab 50257), act-ckpt"),
+    "llama3-8b": dict(kind="llama", vocab=128256, seq=4096, layers=32, heads=32, kv_heads=8,
+                      embd=4096, mlp=14336, rope_theta=500000.0, dtype="bf16", stage=3,
+                      micro=1, gas=8, clip=None, ckpt=False,
+                      label="Llama-3-8B shape (32L, d4096, 32/8 heads, SwiGLU 14336, "
+                            "vocab 128256)"),
+}
 
 
-def ds_config(world: int, total_steps: int) -> dict:
-    return {
-        "train_micro_batch_size_per_gpu": MICRO,
-        "gradient_accumulation_steps": GAS,
-        "gradient_clipping": 1.0,
-        "fp16": {"enabled": True, "loss_scale": 0, "initial_scale_power": 16,
-                 "loss_scale_window": 1000},
+def ds_config(spec: dict, world: int, total_steps: int) -> dict:
+    cfg = {
+        "train_micro_batch_size_per_gpu": spec["micro"],
+        "gradient_accumulation_steps": spec["gas"],
+        "dtype": spec["dtype"],
         "optimizer": {"type": "AdamW", "params": {"lr": 6e-4, "betas": [0.9, 0.95],
                                                   "eps": 1e-8, "weight_decay": 0.1}},
         "scheduler": {"type": "WarmupDecayLR", "params": {
             "warmup_min_lr": 6e-5, "warmup_max_lr": 6e-4, "warmup_num_steps": 10,
             "total_num_steps": max(total_steps, 20)}},
-        "zero_optimization": {"stage": 2},
+        "zero_optimization": {"stage": spec["stage"]},
         "steps_per_print": 1000000,
     }
+    if spec["clip"]:
+        cfg["gradient_clipping"] = spec["clip"]
+    if spec["dtype"] == "fp16":
+        cfg["fp16"] = {"enabled": True, "loss_scale": 0, "initial_scale_power": 16,
+                       "loss_scale_window": 1000}
+    else:
+        cfg["bf16"] = {"enabled": True}
+    return cfg
 
 
 # ------------------------------------------------- stock PyTorch GPT-2
 class _RefAttn(nn.Module):
-    def __init__(self):
+    def __init__(self, embd, heads):
         super().__init__()
-        self.qkv = nn.Linear(EMBD, 3 * EMBD)
-        self.proj = nn.Linear(EMBD, EMBD)
+        self.heads = heads
+        self.qkv = nn.Linear(embd, 3 * embd)
+        self.proj = nn.Linear(embd, embd)
 
     def forward(self, x):
         b, t, c = x.shape
         q, k, v = self.qkv(x).chunk(3, dim=-1)
-        q, k, v = (z.view(b, t, HEADS, c // HEADS).transpose(1, 2) for z in (q, k, v))
+        q, k, v = (z.view(b, t, self.heads, c // self.heads).transpose(1, 2) for z in (q, k, v))
         y = F.scaled_dot_product_attention(q, k, v, is_causal=True)
         return self.proj(y.transpose(1, 2).contiguous().view(b, t, c))
 
 
 class _RefBlock(nn.Module):
-    def __init__(self):
+    def __init__(self, embd, heads, mlp):
         super().__init__()
-        self.ln1 = nn.LayerNorm(EMBD)
-        self.attn = _RefAttn()
-        self.ln2 = nn.LayerNorm(EMBD)
-        self.mlp = nn.Sequential(nn.Linear(EMBD, 4 * EMBD), nn.GELU(), nn.Linear(4 * EMBD, EMBD))
+        self.ln1 = nn.LayerNorm(embd)
+        self.attn = _RefAttn(embd, heads)
+        self.ln2 = nn.LayerNorm(embd)
+        self.mlp = nn.Sequential(nn.Linear(embd, mlp), nn.GELU(), nn.Linear(mlp, embd))
 
     def forward(self, x):
         x = x + self.attn(self.ln1(x))
@@ -94,23 +119,98 @@ class _RefBlock(nn.Module):
 
 
 class RefGPT(nn.Module):
-    """The reference example's TinyGPT architecture at GPT-2-small size."""
+    """The reference example's TinyGPT architecture at GPT-2 sizes."""
 
-    def __init__(self):
+    def __init__(self, spec):
         super().__init__()
-        self.wte = nn.Embedding(VOCAB, EMBD)
-        self.wpe = nn.Embedding(SEQ, EMBD)
-        self.blocks = nn.ModuleList(_RefBlock() for _ in range(LAYERS))
-        self.ln_f = nn.LayerNorm(EMBD)
-        self.head = nn.Linear(EMBD, VOCAB, bias=False)
+        self.ckpt = spec["ckpt"]
+        self.wte = nn.Embedding(spec["vocab"], spec["embd"])
+        self.wpe = nn.Embedding(spec["seq"], spec["embd"])
+        self.blocks = nn.ModuleList(_RefBlock(spec["embd"], spec["heads"], spec["mlp"])
+                                    for _ in range(spec["layers"]))
+        self.ln_f = nn.LayerNorm(spec["embd"])
+        self.head = nn.Linear(spec["embd"], spec["vocab"], bias=False)
         self.head.weight = self.wte.weight
 
     def forward(self, idx):
         t = idx.shape[1]
         x = self.wte(idx) + self.wpe(torch.arange(t, device=idx.device))
         for blk in self.blocks:
-            x = blk(x)
+            if self.ckpt and self.training:
+                x = torch.utils.checkpoint.checkpoint(blk, x, use_reentrant=False)
+            else:
+                x = blk(x)
         return self.head(self.ln_f(x))
+
+
+class _RefRMSNorm(nn.Module):
+    def __init__(self, dim, eps=1e-5):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x):
+        xf = x.float()
+        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
+        return xf.to(x.dtype) * self.weight
+
+
+def _ref_rope(x, cos, sin):
+    x1, x2 = x[..., : x.shape[-1] // 2], x[..., x.shape[-1] // 2:]
+    return x * cos + torch.cat((-x2, x1), dim=-1) * sin
+
+
+class _RefLlamaBlock(nn.Module):
+    def __init__(self, spec):
+        super().__init__()
+        d, h, hk = spec["embd"], spec["heads"], spec["kv_heads"]
+        self.h, self.hk, self.hd = h, hk, d // h
+        self.attention_norm = _RefRMSNorm(d)
+        self.wq = nn.Linear(d, d, bias=False)
+        self.wk = nn.Linear(d, hk * self.hd, bias=False)
+        self.wv = nn.Linear(d, hk * self.hd, bias=False)
+        self.wo = nn.Linear(d, d, bias=False)
+        self.ffn_norm = _RefRMSNorm(d)
+        self.w1 = nn.Linear(d, spec["mlp"], bias=False)
+        self.w3 = nn.Linear(d, spec["mlp"], bias=False)
+        self.w2 = nn.Linear(spec["mlp"], d, bias=False)
+
+    def forward(self, x, cos, sin):
+        b, t, _ = x.shape
+        hN = self.attention_norm(x)
+        q = self.wq(hN).view(b, t, self.h, self.hd).transpose(1, 2)
+        k = self.wk(hN).view(b, t, self.hk, self.hd).transpose(1, 2)
+        v = self.wv(hN).view(b, t, self.hk, self.hd).transpose(1, 2)
+        q, k = _ref_rope(q, cos, sin), _ref_rope(k, cos, sin)
+        y = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+        x = x + self.wo(y.transpose(1, 2).reshape(b, t, -1))
+        hN = self.ffn_norm(x)
+        return x + self.w2(F.silu(self.w1(hN)) * self.w3(hN))
+
+
+class RefLlama(nn.Module):
+    """A stock-PyTorch Llama-3 architecture (RMSNorm, RoPE, GQA SDPA, SwiGLU)."""
+
+    def __init__(self, spec):
+        super().__init__()
+        self.spec = spec
+        self.tok_embeddings = nn.Embedding(spec["vocab"], spec["embd"])
+        self.layers = nn.ModuleList(_RefLlamaBlock(spec) for _ in range(spec["layers"]))
+        self.norm = _RefRMSNorm(spec["embd"])
+        self.output = nn.Linear(spec["embd"], spec["vocab"], bias=False)
+
+    def forward(self, idx):
+        t = idx.shape[1]
+        hd = self.spec["embd"] // self.spec["heads"]
+        inv = 1.0 / (self.spec["rope_theta"] ** (torch.arange(0, hd, 2, device=idx.device,
+                                                              dtype=torch.float32) / hd))
+        ang = torch.outer(torch.arange(t, device=idx.device, dtype=torch.float32), inv)
+        emb = torch.cat((ang, ang), dim=-1)
+        x = self.tok_embeddings(idx)
+        cos, sin = emb.cos().to(x.dtype), emb.sin().to(x.dtype)
+        for blk in self.layers:
+            x = blk(x, cos, sin)
+        return self.output(self.norm(x))
 
 
 # ------------------------------------------------------------ clocks
@@ -172,7 +272,10 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", choices=sorted(SPECS), default="gpt2-small")
     args = ap.parse_args()
+    spec = SPECS[args.model]
+    MICRO, GAS, SEQ, VOCAB = spec["micro"], spec["gas"], spec["seq"], spec["vocab"]
     if args.warmup < 3:
         args.warmup = 3
 
@@ -197,7 +300,9 @@ def main():
         import minispeed as lib  # the unmodified reference engine
         from minispeed import comm as lcomm
         torch.manual_seed(1234)
-        model = RefGPT()
+        with torch.device(device):   # build and initialize on the GPU (8B params)
+            model = RefGPT(spec) if spec["kind"] == "gpt" else RefLlama(spec)
+            _init(model)
 
         def micro_step(eng, x, y):
             logits = eng(x)
@@ -209,18 +314,18 @@ def main():
         sys.path.insert(0, ROOT)
         import minispeed_b200 as lib
         from minispeed_b200 import comm as lcomm
-        from minispeed_b200.models import GPT, GPTConfig
+        from minispeed_b200.models import GPT, GPTConfig, Llama, LlamaConfig
         torch.manual_seed(1234)
-        model = GPT(GPTConfig(vocab_size=VOCAB, block_size=SEQ, n_layer=LAYERS, n_head=HEADS,
-                              n_embd=EMBD))
+        with torch.device(device):
+            model = _build_ours(spec, GPT, GPTConfig, Llama, LlamaConfig)
+            _init(model)
 
         def micro_step(eng, x, y):
             # forward + backward replayed as one CUDA graph, then the step
             return eng.train_batch(x, targets=y)
 
-    _init(model)
     lcomm.init_distributed()
-    cfg = ds_config(world, args.warmup + 2 * args.steps)
+    cfg = ds_config(spec, world, args.warmup + 2 * args.steps)
     if args.impl == "ours":
         cfg["b200"] = {"cuda_graph": True}
     engine, _, _, _ = lib.initialize(model=model, model_parameters=model.parameters(),
@@ -320,14 +425,17 @@ def main():
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "fp16",
-            "data": "synthetic uniform-random token ids, random-init GPT-2 weights (std 0.02)",
-            "config": {"model": "GPT-2 small (12L, d768, 12H, MLP 3072, vocab 50257)",
+            "dtype": spec["dtype"],
+            "data": "synthetic uniform-random token ids, random-init weights (std 0.02)",
+            "config": {"model": spec["label"],
                        "global_batch": world * MICRO * GAS, "micro_batch": MICRO, "gas": GAS,
-                       "seq_len": SEQ, "parallelism": f"dp{world} ZeRO-2", "zero_stage": 2,
-                       "precision": "fp16 + fp32 masters, dynamic loss scale 2^16",
-                       "optimizer": "AdamW + WarmupDecayLR, clip 1.0",
-                       "l2": "per-step working set > L2 (1.5 GB fp32 optimizer state streamed)",
+                       "seq_len": SEQ, "parallelism": f"dp{world} ZeRO-{spec['stage']}",
+                       "zero_stage": spec["stage"],
+                       "precision": ("fp16 + fp32 masters, dynamic loss scale 2^16"
+                                     if spec["dtype"] == "fp16" else "bf16 + fp32 masters"),
+                       "optimizer": "AdamW + WarmupDecayLR" + (
+                           f", clip {spec['clip']}" if spec["clip"] else ""),
+                       "l2": "per-step working set > L2 (fp32 optimizer state streamed)",
                        "collectives": getattr(engine, "collectives", "reference comm")},
             "impl": args.impl,
             "exposed_comm_ms": 0.0 if world == 1 else (
@@ -356,6 +464,18 @@ class _Null:
         return False
 
 
+def _build_ours(spec, GPT, GPTConfig, Llama, LlamaConfig):
+    if spec["kind"] == "gpt":
+        return GPT(GPTConfig(vocab_size=spec["vocab"], block_size=spec["seq"],
+                             n_layer=spec["layers"], n_head=spec["heads"], n_embd=spec["embd"],
+                             activation_checkpointing=spec["ckpt"]))
+    return Llama(LlamaConfig(vocab_size=spec["vocab"], block_size=spec["seq"],
+                             n_layer=spec["layers"], n_head=spec["heads"],
+                             n_kv_head=spec["kv_heads"], n_embd=spec["embd"],
+                             ffn_hidden=spec["mlp"], rope_theta=spec["rope_theta"],
+                             activation_checkpointing=spec["ckpt"]))
+
+
 def _init(model):
     with torch.no_grad():
         for m in model.modules():
@@ -377,4 +497,13 @@ def _max_over_ranks(v: float, distributed: bool, device) -> float:
 
 
 if __name__ == "__main__":
-    main()
+    try:
+        main()
+    except torch.cuda.OutOfMemoryError as e:
+        # a config that does not fit (e.g. the reference's full fp32 buffers
+        # for an 8B model on few GPUs) reports itself instead of a number
+        if int(os.environ.get("RANK", "0")) == 0:
+            impl = "reference" if "--impl" in sys.argv and "reference" in sys.argv else "ours"
+            print(json.dumps({"impl": impl, "unavailable": "CUDA out of memory: "
+                              + str(e).splitlines()[0][:160]}), flush=True)
+        sys.exit(0)

@@ -36,22 +36,25 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--embd", type=int, default=768)
+    ap.add_argument("--dtype", default="fp16", choices=["fp16", "bf16"])
     args = ap.parse_args()
-    T, C, V = args.tokens, 768, 50257
+    T, C, V = args.tokens, args.embd, 50257
     Vp = 50304
+    dt = torch.float16 if args.dtype == "fp16" else torch.bfloat16
     rows = []
     shapes = [("qkv", 3 * C, C), ("proj", C, C), ("fc", 4 * C, C), ("fc2", C, 4 * C), ("head", V, C)]
     for name, N, K in shapes:
-        x = torch.randn(T, K, device="cuda").half()
-        w = (torch.randn(N, K, device="cuda") * 0.02).half()
+        x = torch.randn(T, K, device="cuda").to(dt)
+        w = (torch.randn(N, K, device="cuda") * 0.02).to(dt)
         if name == "head":
-            dy = torch.randn(T, Vp, device="cuda").half()[:, :V]
+            dy = torch.randn(T, Vp, device="cuda").to(dt)[:, :V]
         else:
-            dy = torch.randn(T, N, device="cuda").half()
+            dy = torch.randn(T, N, device="cuda").to(dt)
         for kind in ("fwd", "dgrad", "wgrad"):
             if kind == "fwd" and name == "head":
                 # the model's logits buffer: rows padded to a multiple of 64
-                lg = torch.empty(T, Vp, device="cuda", dtype=torch.half)[:, :V]
+                lg = torch.empty(T, Vp, device="cuda", dtype=dt)[:, :V]
                 ours = lambda: gemm.gemm(x, w, a_kmajor=True, b_kmajor=True, out=lg)
                 lib = lambda: torch.mm(x, w.t())
             elif kind == "fwd":
@@ -71,7 +74,7 @@ def main():
                    N if kind == "fwd" else K,
                    K if kind == "fwd" else (N if kind == "dgrad" else T)]
             amn, bmn = {"fwd": (0, 0), "dgrad": (0, 1), "wgrad": (1, 1)}[kind]
-            plan = _ext.get().gemm_cached_plan(*mnk, amn, bmn, 1, 0)
+            plan = _ext.get().gemm_cached_plan(*mnk, amn, bmn, 1 if dt == torch.float16 else 2, 0)
             rows.append({"gemm": f"{name}.{kind}", "M_N_K": mnk, "plan_bn_splits": list(plan),
                          "ours_ms": round(t_o, 4), "ours_tflops": round(flops / t_o / 1e9, 1),
                          "cublas_ms": round(t_l, 4), "cublas_tflops": round(flops / t_l / 1e9, 1)})

@@ -245,9 +245,10 @@ __device__ __forceinline__ void add_bias(const Params& p, int col, int nvalid, f
 }
 
 // One 32 x 32 chunk of C, rows row0.. and columns col.. all inside C (warp-
-// uniform), through the staging buffers.  Modes as store_chunk; accumulate
-// and split-K never come here.  sbuf alternates the two buffers in modes 0
-// and 2.
+// uniform), through the staging buffers.  Modes as store_chunk; with
+// accumulate (mode 0) the TMA unit adds the chunk into C (bulk reduce-add:
+// the product is rounded to the 16-bit type, then added).  Split-K never
+// comes here.  sbuf alternates the two buffers in modes 0 and 2.
 template <typename T>
 __device__ __forceinline__ void staged_chunk(const Params& p, const CUtensorMap* tmC,
                                              const CUtensorMap* tmX, uint8_t* stg, int& sbuf,
@@ -286,7 +287,8 @@ __device__ __forceinline__ void staged_chunk(const Params& p, const CUtensorMap*
   fence_async_smem();
   __syncwarp();
   if (lane == 0) {
-    tma_store_2d(tmC, smem_u32(buf), col, row0);
+    if (p.accumulate) tma_reduce_add_2d(tmC, smem_u32(buf), col, row0);
+    else tma_store_2d(tmC, smem_u32(buf), col, row0);
     bulk_commit();
   }
   sbuf ^= 1;
@@ -1057,7 +1059,8 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
                               : make_map(B, dtype, K, N, ldb, 64, b_rows);
   // output maps for the staged epilogue: 32 x 32 boxes, 64-byte swizzle
   // (plain and GELU/dGELU outputs; accumulation and split-K store per thread)
-  p.staged = (p.splits == 1 && !p.accumulate && p.c_vec && (mode != 1 || p.aux_vec)) ? 1 : 0;
+  p.staged = (p.splits == 1 && p.c_vec && (mode != 1 || p.aux_vec) && (!p.accumulate || mode == 0))
+                 ? 1 : 0;
   const CUtensorMap tcm = p.staged ? make_map(C, dtype, N, M, ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
                                    : ta;
   const CUtensorMap txm = (p.staged && mode == 1)
