@@ -954,6 +954,351 @@ void launch_bwd(const CUtensorMap& tq, const CUtensorMap& td, const CUtensorMap&
   kern<<<grid, kThreadsB, Layout<D>::BYTES, st>>>(tq, td, tdq, p);
 }
 
+
+// ---------------------------------------------------------------- head dim 128
+// Tensor memory is full with S^T, dP^T, dV and dK (128 columns each), so P^T
+// and dS^T are packed in place over the scores they come from (one thread per
+// key row walks its row front to back and only overwrites columns it has
+// already read) and the dQ partial goes, as two 64-column halves, into the
+// columns the packing freed.  The dS^T tile in shared memory doubles as the
+// fp32 staging of the dQ reduce-adds once the dQ MMA has read it.
+// Warps: 0 TMA, 1 MMA, 2-5 P^T/dS^T (thread = key), 6-9 dQ (thread = query).
+constexpr int kThreads128 = 320;
+
+struct alignas(8) Bars128 {
+  uint64_t kv_full;
+  uint64_t qo_full[2], qo_empty[2];
+  uint64_t st_full, ds_ready, mma2_done, dq_full, dq_free, stg_free, lse_full, drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct Layout128 {
+  static constexpr int TILE = 128 * 128 * 2;
+  static constexpr int CH = 128 * 128;
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = TILE;
+  static constexpr int Q_OFF = 2 * TILE;        // two stages
+  static constexpr int DO_OFF = 4 * TILE;       // two stages
+  static constexpr int DS_OFF = 6 * TILE;       // dS^T; later the dQ staging
+  static constexpr int LSE_OFF = 7 * TILE;
+  static constexpr int DELTA_OFF = LSE_OFF + 512;
+  static constexpr int BARS_OFF = DELTA_OFF + 512;
+  static constexpr size_t BYTES = 1024 + BARS_OFF + sizeof(Bars128);
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads128, 1)
+attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
+                   const __grid_constant__ CUtensorMap tm_do,
+                   const __grid_constant__ CUtensorMap tm_dq, const Params p) {
+  constexpr int D = 128;
+  using L = Layout128;
+  constexpr uint32_t TMEM_COLS = 512;
+  constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 384;
+  constexpr uint32_t C_DQ0 = C_S + 64, C_DQ1 = C_DP + 64;   // freed by the packing
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  Bars128* bars = reinterpret_cast<Bars128*>(smem + L::BARS_OFF);
+  float* sLse = reinterpret_cast<float*>(smem + L::LSE_OFF);
+  float* sDelta = reinterpret_cast<float*>(smem + L::DELTA_OFF);
+  volatile int* abort = &bars->abort;
+  const uint32_t sbase = smem_u32(smem);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x;
+  const int b = blockIdx.y / p.Hkv, g = blockIdx.y % p.Hkv;
+  const int rep = p.H / p.Hkv;
+  const int n_i = p.n_q - j;
+  const int nit = rep * n_i;
+  const int row0 = b * p.T;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bars->kv_full), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&bars->qo_full[s]), 1);
+      mbar_init(smem_u32(&bars->qo_empty[s]), 1);
+    }
+    mbar_init(smem_u32(&bars->st_full), 1);
+    mbar_init(smem_u32(&bars->ds_ready), 4);
+    mbar_init(smem_u32(&bars->mma2_done), 1);
+    mbar_init(smem_u32(&bars->dq_full), 1);
+    mbar_init(smem_u32(&bars->dq_free), 4);
+    mbar_init(smem_u32(&bars->stg_free), 4);
+    mbar_init(smem_u32(&bars->lse_full), 4);
+    mbar_init(smem_u32(&bars->drain), 1);
+    bars->abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&bars->tmem_base), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ TMA
+    const uint32_t kvb = smem_u32(&bars->kv_full);
+    mbar_expect_tx(kvb, 2 * L::TILE);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      tma_load_2d(sbase + L::K_OFF + c * L::CH, &tm_qkv, kvb, p.k_col + g * D + 64 * c,
+                  row0 + j * 128);
+      tma_load_2d(sbase + L::V_OFF + c * L::CH, &tm_qkv, kvb, p.v_col + g * D + 64 * c,
+                  row0 + j * 128);
+    }
+    int pend[2] = {-1, -1};
+    for (int it = 0; it < nit; ++it) {
+      const int st = it & 1;
+      const uint32_t ph = (it >> 1) & 1;
+      const int h = g * rep + it / n_i, i = j + it % n_i;
+      if (!wait_b(smem_u32(&bars->qo_empty[st]), ph ^ 1, abort, p, 51)) break;
+      const uint32_t fb = smem_u32(&bars->qo_full[st]);
+      mbar_expect_tx(fb, 2 * L::TILE);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        tma_load_2d(sbase + L::Q_OFF + st * L::TILE + c * L::CH, &tm_qkv, fb,
+                    p.q_col + h * D + 64 * c, row0 + i * 128);
+        tma_load_2d(sbase + L::DO_OFF + st * L::TILE + c * L::CH, &tm_do, fb, h * D + 64 * c,
+                    row0 + i * 128);
+      }
+      pend[st] = (int)ph;
+    }
+    const uint64_t t0 = gtime();
+    while (!mbar_try(kvb, 0) && gtime() - t0 < p.timeout_ns) {
+    }
+    for (int s = 0; s < 2; ++s)
+      if (pend[s] >= 0)
+        while (!mbar_try(smem_u32(&bars->qo_full[s]), (uint32_t)pend[s]) &&
+               gtime() - t0 < p.timeout_ns) {
+        }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA
+    bool ok = wait_b(smem_u32(&bars->kv_full), 0, abort, p, 52);
+    const uint32_t kb = sbase + L::K_OFF, vb = sbase + L::V_OFF, dsb = sbase + L::DS_OFF;
+    for (int it = 0; it < nit && ok; ++it) {
+      const int st = it & 1;
+      const uint32_t ph = (it >> 1) & 1;
+      if (!wait_b(smem_u32(&bars->qo_full[st]), ph, abort, p, 53)) break;
+      // S^T / dP^T columns (and the dQ halves inside them) are free once the
+      // last MMAs retired and the dQ partial was read
+      if (it > 0 && !wait_b(smem_u32(&bars->mma2_done), (it - 1) & 1, abort, p, 54)) break;
+      if (it > 0 && !wait_b(smem_u32(&bars->dq_free), (it - 1) & 1, abort, p, 55)) break;
+      tc_fence_after();
+      const uint32_t qb = sbase + L::Q_OFF + st * L::TILE, ob = sbase + L::DO_OFF + st * L::TILE;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        umma_f16(tmem + C_S, kmajor_desc<D>(kb, ks), kmajor_desc<D>(qb, ks), p.idesc_s,
+                 ks > 0 ? 1u : 0u);
+        umma_f16(tmem + C_DP, kmajor_desc<D>(vb, ks), kmajor_desc<D>(ob, ks), p.idesc_s,
+                 ks > 0 ? 1u : 0u);
+      }
+      umma_commit(smem_u32(&bars->st_full));
+      if (!wait_b(smem_u32(&bars->ds_ready), it & 1, abort, p, 56)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        umma_f16_ts(tmem + C_DV, tmem + C_S + ks * 8, mn_desc(ob, ks), p.idesc_kv,
+                    (it > 0 || ks > 0) ? 1u : 0u);
+        umma_f16_ts(tmem + C_DK, tmem + C_DP + ks * 8, mn_desc(qb, ks), p.idesc_kv,
+                    (it > 0 || ks > 0) ? 1u : 0u);
+      }
+      // dQ = dS K in two 64-column halves (idesc_q has N = 64)
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        umma_f16(tmem + C_DQ0, mn_desc(dsb, ks), mn_desc(kb, ks), p.idesc_q, ks > 0 ? 1u : 0u);
+        umma_f16(tmem + C_DQ1, mn_desc(dsb, ks), mn_desc(kb + L::CH, ks), p.idesc_q,
+                 ks > 0 ? 1u : 0u);
+      }
+      umma_commit(smem_u32(&bars->qo_empty[st]));
+      umma_commit(smem_u32(&bars->mma2_done));
+      umma_commit(smem_u32(&bars->dq_full));
+    }
+    umma_commit(smem_u32(&bars->drain));
+    const uint64_t t0 = gtime();
+    while (!mbar_try(smem_u32(&bars->drain), 0) && gtime() - t0 < p.timeout_ns) {
+    }
+  } else if (warp >= 2 && warp < 6) {
+    // ------------------------------------------ P^T, dS^T (thread = key row)
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int kj = j * 128 + r;
+    const uint32_t lb = tmem + ((uint32_t)(quarter * 32) << 16);
+    uint8_t* sdS = smem + L::DS_OFF;
+    bool ok = true;
+    for (int it = 0; it < nit; ++it) {
+      const int h = g * rep + it / n_i, i = j + it % n_i;
+      const long long lrow = (long long)(b * p.H + h) * p.T;
+      // the shared lse / delta of the previous tile were read by every warp
+      if (it > 0 && !warp_wait(smem_u32(&bars->ds_ready), (it - 1) & 1, abort, p, 57, lane)) {
+        ok = false;
+        break;
+      }
+      {
+        const int qi = i * 128 + quarter * 32 + lane;
+        sLse[quarter * 32 + lane] = qi < p.T ? p.lse[lrow + qi] : 0.f;
+        sDelta[quarter * 32 + lane] = qi < p.T ? p.delta[lrow + qi] : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars->lse_full));
+      if (!warp_wait(smem_u32(&bars->lse_full), it & 1, abort, p, 58, lane) ||
+          !warp_wait(smem_u32(&bars->st_full), it & 1, abort, p, 59, lane) ||
+          (it > 0 && !warp_wait(smem_u32(&bars->stg_free), (it - 1) & 1, abort, p, 60, lane))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(lb + C_S + c * 32, sv);
+        tmem_ld32(lb + C_DP + c * 32, dv);
+        tmem_ld_wait();
+        uint32_t pk[16], dk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float pp[2], dd[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int col = c * 32 + 2 * e + u;
+            const int qi = i * 128 + col;
+            const bool vis = qi >= kj && qi < p.T;
+            const float pr =
+                vis ? ex2(fmaf(__uint_as_float(sv[2 * e + u]), p.scale_log2, -sLse[col])) : 0.f;
+            pp[u] = pr;
+            dd[u] = pr * (__uint_as_float(dv[2 * e + u]) - sDelta[col]);
+          }
+          pk[e] = pack2<T>(pp[0], pp[1]);
+          dk[e] = pack2<T>(dd[0], dd[1]);
+        }
+        // packed in place: columns 16c..16c+15, all read by this thread already
+        tmem_st16(lb + C_S + c * 16, pk);
+        tmem_st16(lb + C_DP + c * 16, dk);
+        uint8_t* rowp = sdS + (c >> 1) * L::CH + r * 128;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int piece = ((c & 1) * 4 + u) ^ (r & 7);
+          *reinterpret_cast<uint4*>(rowp + piece * 16) =
+              make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
+        }
+      }
+      tmem_st_wait();
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars->ds_ready));
+    }
+    // dK (times the softmax scale) and dV of this key tile
+    if (ok && nit > 0 && warp_wait(smem_u32(&bars->mma2_done), (nit - 1) & 1, abort, p, 61, lane)) {
+      tc_fence_after();
+      T* drow = static_cast<T*>(p.dqkv) + (long long)(row0 + kj) * p.ld_dqkv;
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t col0 = which == 0 ? C_DK : C_DV;
+        const float f = which == 0 ? p.scale : 1.f;
+        T* dst = drow + (which == 0 ? p.k_col : p.v_col) + g * D;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(lb + col0 + c * 32, v);
+          tmem_ld_wait();
+          if (kj < p.T) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              uint4 pack;
+              uint32_t* pw = reinterpret_cast<uint32_t*>(&pack);
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                pw[e] = pack2<T>(__uint_as_float(v[u * 8 + 2 * e]) * f,
+                                 __uint_as_float(v[u * 8 + 2 * e + 1]) * f);
+              *reinterpret_cast<uint4*>(dst + c * 32 + u * 8) = pack;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------- dQ partial -> fp32 accumulator
+    const int quarter = warp & 3;
+    const uint32_t lb = tmem + ((uint32_t)(quarter * 32) << 16);
+    // staging: this warp's 32 rows x 64 fp32 columns (two 32 x 32 boxes) in the dS^T tile
+    uint8_t* stg = smem + L::DS_OFF + (warp - 6) * 8192;
+    for (int it = 0; it < nit; ++it) {
+      const int h = g * rep + it / n_i, i = j + it % n_i;
+      if (!warp_wait(smem_u32(&bars->dq_full), it & 1, abort, p, 62, lane)) break;
+      tc_fence_after();
+      uint32_t v[128];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        tmem_ld32(lb + C_DQ0 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v + c * 32));
+        tmem_ld32(lb + C_DQ1 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v + 64 + c * 32));
+      }
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars->dq_free));
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        if (half == 1) {
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+        }
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint8_t* rowp = stg + c * 4096 + lane * 128;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int e0 = half * 64 + c * 32 + 4 * u;
+            *reinterpret_cast<uint4*>(rowp + ((u ^ (lane & 7)) << 4)) =
+                make_uint4(v[e0], v[e0 + 1], v[e0 + 2], v[e0 + 3]);
+          }
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+            tma_reduce_add_2d(&tm_dq, smem_u32(stg + c * 4096), h * D + half * 64 + 32 * c,
+                              row0 + i * 128 + quarter * 32);
+          bulk_commit();
+        }
+      }
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars->stg_free));
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+template <typename T>
+void launch_bwd128(const CUtensorMap& tq, const CUtensorMap& td, const CUtensorMap& tdq,
+                   const Params& p, cudaStream_t st) {
+  auto kern = attn_bwd128_kernel<T>;
+  static bool attr = false;
+  if (!attr) {
+    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)Layout128::BYTES),
+               "attn bwd128 smem attribute");
+    attr = true;
+  }
+  dim3 grid(p.n_q, p.B * p.Hkv);
+  kern<<<grid, kThreads128, Layout128::BYTES, st>>>(tq, td, tdq, p);
+}
+
 }  // namespace bwd
 }  // namespace attn
 
@@ -1009,7 +1354,7 @@ void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
                    int B, int T, int H, int Hkv, int D, int dtype, float scale, unsigned* err,
                    double timeout_s, cudaStream_t st) {
   using namespace attn::bwd;
-  if (D != 64) throw std::runtime_error("attention backward: head dim 64 only");
+  if (D != 64 && D != 128) throw std::runtime_error("attention backward: head dim 64 or 128");
   if (H % Hkv != 0) throw std::runtime_error("attention: H must be a multiple of Hkv");
   auto aligned = [](const void* ptr, long long ld) {
     return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && ld % 8 == 0;
@@ -1017,6 +1362,7 @@ void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
   if (!aligned(out, ld_out) || !aligned(dout, ld_do) || !aligned(dqkv, ld_dqkv))
     throw std::runtime_error("attention backward: operands must allow 16-byte row access");
   const int BT = B * T;
+  const int T_seq = T;
   const int blocks = grid_for((long long)BT * H, 256, kNumSMs * 8);
   const int blocks_c = grid_for((long long)BT * H * D / 8, 256, kNumSMs * 8);
   attn::bwd::Params p;
@@ -1038,29 +1384,35 @@ void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
   p.idesc_s = (1u << 4) | (fmt << 7) | (fmt << 10) | (16u << 17) | (8u << 24);
   p.idesc_kv = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) | ((uint32_t)(D >> 3) << 17) |
                (8u << 24);
-  p.idesc_q = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 15) | (1u << 16) |
-              ((uint32_t)(D >> 3) << 17) | (8u << 24);
+  // dQ = dS K: N = D (head dim 128: two N = 64 halves)
+  const uint32_t nq = D == 128 ? 64u : (uint32_t)D;
+  p.idesc_q = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 15) | (1u << 16) | ((nq >> 3) << 17) |
+              (8u << 24);
   p.err = err;
   p.timeout_ns = static_cast<unsigned long long>(timeout_s * 1e9);
   const CUtensorMap tq = make_map(qkv, dtype, n_cols, (long long)BT, ld_qkv, 64, 128);
   const CUtensorMap td = make_map(dout, dtype, (long long)H * D, (long long)BT, ld_do, 64, 128);
   const CUtensorMap tdq = make_map_f32(dq_acc, (long long)H * D, (long long)BT, (long long)H * D,
                                        32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  auto run = [&](auto tag) {
+    using T = decltype(tag);
+    if (D == 64)
+      attn_delta_kernel<T, 64><<<blocks, 256, 0, st>>>(static_cast<const T*>(dout), ld_do,
+                                                       static_cast<const T*>(out), ld_out, delta,
+                                                       dq_acc, BT, T_seq, H);
+    else
+      attn_delta_kernel<T, 128><<<blocks, 256, 0, st>>>(static_cast<const T*>(dout), ld_do,
+                                                        static_cast<const T*>(out), ld_out, delta,
+                                                        dq_acc, BT, T_seq, H);
+    if (D == 64) launch_bwd<T, 64>(tq, td, tdq, p, st);
+    else launch_bwd128<T>(tq, td, tdq, p, st);
+    attn_dq_convert_kernel<T><<<blocks_c, 256, 0, st>>>(dq_acc, BT, H * D, static_cast<T*>(dqkv),
+                                                        ld_dqkv, q_col, scale);
+  };
   if (dtype == kF16) {
-    attn_delta_kernel<__half, 64><<<blocks, 256, 0, st>>>(
-        static_cast<const __half*>(dout), ld_do, static_cast<const __half*>(out), ld_out, delta,
-        dq_acc, BT, T, H);
-    launch_bwd<__half, 64>(tq, td, tdq, p, st);
-    attn_dq_convert_kernel<__half><<<blocks_c, 256, 0, st>>>(dq_acc, BT, H * D,
-                                                             static_cast<__half*>(dqkv), ld_dqkv,
-                                                             q_col, scale);
+    run(__half());
   } else if (dtype == kBF16) {
-    attn_delta_kernel<__nv_bfloat16, 64><<<blocks, 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(dout), ld_do, static_cast<const __nv_bfloat16*>(out),
-        ld_out, delta, dq_acc, BT, T, H);
-    launch_bwd<__nv_bfloat16, 64>(tq, td, tdq, p, st);
-    attn_dq_convert_kernel<__nv_bfloat16><<<blocks_c, 256, 0, st>>>(
-        dq_acc, BT, H * D, static_cast<__nv_bfloat16*>(dqkv), ld_dqkv, q_col, scale);
+    run(__nv_bfloat16());
   } else {
     throw std::runtime_error("attention takes fp16/bf16");
   }

@@ -10,10 +10,8 @@ kernels (``csrc/attention_tcgen05.cu``): they read q, k and v straight out of
 the projection output (no head-major copies), keep the scores in tensor
 memory, skip the key tiles above the causal diagonal, and write the
 gradient of the whole projection output (dq, dk, dv) in one buffer.  Head
-dim 64 runs forward and backward natively; head dim 128 runs the native
-forward, and its backward (not written yet) goes through PyTorch's
-scaled_dot_product_attention recomputation.  ``MSB_ATTN=sdpa`` selects
-PyTorch's SDPA for every shape (comparison runs).
+dims 64 and 128 (GPT-2, Llama-3).  ``MSB_ATTN=sdpa`` selects PyTorch's SDPA
+for every shape (comparison runs).
 
 Reference: the example model's ``F.scaled_dot_product_attention(q, k, v,
 is_causal=True)`` (``examples/train_lm.py:76``).
@@ -69,8 +67,6 @@ class _Flash(torch.autograd.Function):
     def backward(ctx, dout):
         q2, out, lse = ctx.saved_tensors
         B, T, H, Hkv, D, scale = ctx.dims
-        if D != 64:
-            return _sdpa_backward(ctx, q2, dout), None, None, None
         d2 = dout.reshape(B * T, H * D)
         if d2.stride(-1) != 1 or d2.stride(0) % 8:
             d2 = d2.contiguous()
@@ -81,16 +77,6 @@ class _Flash(torch.autograd.Function):
                                  delta, dq_acc, dqkv, B, T, H, Hkv, D, scale,
                                  gemm.error_word(q2.device), gemm.TIMEOUT_S)
         return dqkv.view(ctx.qkv_shape), None, None, None
-
-
-def _sdpa_backward(ctx, q2, dout):
-    """Head dims without a native backward: recompute through SDPA's autograd."""
-    B, T, H, Hkv, D, _ = ctx.dims
-    x = q2.view(B, T, H + 2 * Hkv, D).detach().requires_grad_()
-    with torch.enable_grad():
-        o = _sdpa(x[:, :, :H], x[:, :, H:H + Hkv], x[:, :, H + Hkv:]).reshape(B, T, H * D)
-    (g,) = torch.autograd.grad(o, (x,), dout)
-    return g.view(ctx.qkv_shape)
 
 
 def _use_native(qkv: torch.Tensor, D: int) -> bool:

@@ -56,7 +56,7 @@ def test_lse_matches_reference(B, T, H, Hkv, D):
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("B,T,H,Hkv,D", SHAPES[:4])
+@pytest.mark.parametrize("B,T,H,Hkv,D", SHAPES + [(1, 384, 4, 1, 128)])
 def test_backward_matches_reference(B, T, H, Hkv, D, dtype):
     torch.manual_seed(2)
     qkv = torch.randn(B, T, H + 2 * Hkv, D, device="cuda").to(dtype).requires_grad_()
