@@ -327,7 +327,7 @@ def main():
     lcomm.init_distributed()
     cfg = ds_config(spec, world, args.warmup + 2 * args.steps)
     if args.impl == "ours":
-        cfg["b200"] = {"cuda_graph": True}
+        cfg["b200"] = {"cuda_graph": os.environ.get("MINISPEED_CUDA_GRAPH", "1") == "1"}
     engine, _, _, _ = lib.initialize(model=model, model_parameters=model.parameters(),
                                      config=cfg)
     dist = torch.distributed

@@ -70,7 +70,7 @@ def main():
 
             def fn():
                 st.reset()
-                C.rs_stats(heaps, 0, 1, 0, out, 1, 1.0, -1, st.partials, st.flags, 0, 1184, True)
+                C.rs_stats(heaps, 0, 1, 0, out, 1, 1.0, None, -1, st.partials, st.flags, 0, 1184, True, 256)
             timed(fn, a.iters, n * (2 + 4), "rs_stats")
         finally:
             torch.cuda.synchronize()

@@ -508,34 +508,45 @@ at::Tensor tensor_from_ptr(int64_t ptr, int64_t numel, int64_t dtype, int64_t de
   return at::from_blob(reinterpret_cast<void*>(ptr), {numel}, opts);
 }
 
+unsigned* epoch_counter(const at::Tensor& ctr) {
+  TORCH_CHECK(ctr.is_cuda() && ctr.scalar_type() == at::kInt && ctr.numel() >= 1,
+              "epoch counter must be a CUDA int32 tensor");
+  return reinterpret_cast<unsigned*>(ctr.data_ptr<int>());
+}
+
 void peer_barrier_py(const at::Tensor& heaps, int64_t sync_off, int64_t rank, int64_t world,
-                     int64_t epoch, double timeout_s, const at::Tensor& status) {
+                     const at::Tensor& ctr, double timeout_s, const at::Tensor& status) {
   c10::cuda::CUDAGuard g(heaps.device());
-  msb::peer_barrier(heap_table(heaps), sync_off, (int)rank, (int)world, (unsigned)epoch,
+  msb::peer_barrier(heap_table(heaps), sync_off, (int)rank, (int)world, epoch_counter(ctr),
                     timeout_s, reinterpret_cast<unsigned*>(status.data_ptr<int>()),
                     stream_of(heaps));
 }
 
 int64_t rs_stats_py(const at::Tensor& heaps, int64_t grad_off, int64_t dtype, int64_t s0,
-                    const at::Tensor& out, int64_t world, double mul, int64_t fanout_off,
-                    const at::Tensor& partials, const at::Tensor& flags, int64_t slot,
-                    int64_t max_blocks, bool aligned16) {
+                    const at::Tensor& out, int64_t world, double mul, const OptT& mul_dev,
+                    int64_t fanout_off, const at::Tensor& partials, const at::Tensor& flags,
+                    int64_t slot, int64_t max_blocks, bool aligned16, int64_t threads) {
   check_cuda_contig(out, "out");
   TORCH_CHECK(out.scalar_type() == at::kFloat);
   TORCH_CHECK(slot >= 0 && slot + max_blocks <= partials.numel(), "stats scratch overflow");
+  const float* md = nullptr;
+  if (mul_dev.has_value() && mul_dev->defined()) {
+    TORCH_CHECK(mul_dev->is_cuda() && mul_dev->scalar_type() == at::kFloat, "mul_dev: fp32 CUDA");
+    md = mul_dev->data_ptr<float>();
+  }
   c10::cuda::CUDAGuard g(heaps.device());
   return msb::rs_stats(heap_table(heaps), grad_off, (int)dtype, s0, out.numel(), (int)world,
-                       (float)mul, out.data_ptr<float>(), fanout_off,
+                       (float)mul, md, out.data_ptr<float>(), fanout_off,
                        partials.data_ptr<float>() + slot,
                        reinterpret_cast<unsigned*>(flags.data_ptr<int>()) + slot, (int)max_blocks,
-                       aligned16, stream_of(heaps));
+                       aligned16, stream_of(heaps), (int)threads);
 }
 
 void stats_exchange_py(const at::Tensor& heaps, int64_t sync_off, int64_t rank, int64_t world,
-                       int64_t epoch, const at::Tensor& out, double max_norm, double timeout_s,
-                       const at::Tensor& status) {
+                       const at::Tensor& ctr, const at::Tensor& out, double max_norm,
+                       double timeout_s, const at::Tensor& status) {
   c10::cuda::CUDAGuard g(heaps.device());
-  msb::stats_exchange(heap_table(heaps), sync_off, (int)rank, (int)world, (unsigned)epoch,
+  msb::stats_exchange(heap_table(heaps), sync_off, (int)rank, (int)world, epoch_counter(ctr),
                       out.data_ptr<float>(), max_norm, timeout_s,
                       reinterpret_cast<unsigned*>(status.data_ptr<int>()), stream_of(heaps));
 }

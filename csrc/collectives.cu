@@ -63,13 +63,21 @@ __device__ __forceinline__ Board* board_of(char* heap, long long sync_off) {
   return reinterpret_cast<Board*>(heap + sync_off + kMaxRanks * sizeof(unsigned) * 4);
 }
 
+// Epochs come from a per-rank device counter that every barrier-type kernel
+// advances by one: all ranks run the same sequence of barriers, so the
+// counters agree, and a kernel replayed from a CUDA graph uses the next epoch
+// rather than the one current at capture time.
 __global__ void peer_barrier_kernel(char* const* heaps, long long sync_off, int rank, int world,
-                                    unsigned epoch, unsigned long long timeout_ns,
+                                    unsigned* ctr, unsigned long long timeout_ns,
                                     unsigned* status) {
   // make this device's earlier writes (local and peer stores of preceding
   // kernels) visible system-wide before announcing the epoch
   __threadfence_system();
+  __shared__ unsigned s_epoch;
   const int t = threadIdx.x;
+  if (t == 0) s_epoch = *ctr + 1u;
+  __syncthreads();
+  const unsigned epoch = s_epoch;
   if (t < world) st_release_sys(flags_of(heaps[t], sync_off) + rank, epoch);
   __syncthreads();
   if (t < world) {
@@ -83,14 +91,19 @@ __global__ void peer_barrier_kernel(char* const* heaps, long long sync_off, int 
     }
   }
   __syncthreads();
+  if (t == 0) *ctr = epoch;
   __threadfence_system();
 }
 
 template <typename T, int VEC>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 2)
 rs_stats_kernel(char* const* heaps, long long grad_off, long long s0, long long n, int world,
-                float mul, float* __restrict__ out, long long fanout_off,
-                float* __restrict__ partials, unsigned* __restrict__ pflags) {
+                float mul_host, const float* __restrict__ mul_dev, float* __restrict__ out,
+                long long fanout_off, float* __restrict__ partials,
+                unsigned* __restrict__ pflags) {
+  // the multiplier (1 / (loss scale * world)) may live on the device, so a
+  // launch replayed from a CUDA graph follows the current loss scale
+  const float mul = mul_dev != nullptr ? mul_host * *mul_dev : mul_host;
   float ss = 0.f;
   unsigned bad = 0u;
   const long long nvec = n / VEC;
@@ -159,8 +172,9 @@ rs_stats_kernel(char* const* heaps, long long grad_off, long long s0, long long 
   }
   __syncthreads();
   if (warp == 0) {
-    ss = lane < 8 ? s_ss[lane] : 0.f;
-    bad = lane < 8 ? s_bad[lane] : 0u;
+    const int nw = blockDim.x >> 5;
+    ss = lane < nw ? s_ss[lane] : 0.f;
+    bad = lane < nw ? s_bad[lane] : 0u;
     ss = warp_sum(ss);
     bad = warp_or(bad);
     if (lane == 0) {
@@ -171,9 +185,11 @@ rs_stats_kernel(char* const* heaps, long long grad_off, long long s0, long long 
 }
 
 __global__ void stats_exchange_kernel(char* const* heaps, long long sync_off, int rank, int world,
-                                      unsigned epoch, float* out, double max_norm,
+                                      unsigned* ctr, float* out, double max_norm,
                                       unsigned long long timeout_ns, unsigned* status) {
   if (threadIdx.x == 0) {
+    const unsigned epoch = *ctr + 1u;
+    *ctr = epoch;
     const float flag = out[0], sumsq = out[1];
     for (int q = 0; q < world; ++q) {
       Board* b = board_of(heaps[q], sync_off) + rank;
@@ -307,38 +323,42 @@ gather_pull_kernel(char* const* heaps, long long shard_off, long long shard, int
 }  // namespace
 
 // ------------------------------------------------------------- host API
-void peer_barrier(char* const* heaps, long long sync_off, int rank, int world, unsigned epoch,
+void peer_barrier(char* const* heaps, long long sync_off, int rank, int world, unsigned* ctr,
                   double timeout_s, unsigned* status, cudaStream_t st) {
-  peer_barrier_kernel<<<1, 32, 0, st>>>(heaps, sync_off, rank, world, epoch,
+  peer_barrier_kernel<<<1, 32, 0, st>>>(heaps, sync_off, rank, world, ctr,
                                         (unsigned long long)(timeout_s * 1e9), status);
   MSB_CHECK_LAUNCH("peer_barrier");
 }
 
+// threads: 256, or 128 for reductions that run beside other kernels (a
+// 128 x 32-register block fits next to any of this library's large CTAs)
 int rs_stats(char* const* heaps, long long grad_off, int dtype, long long s0, long long n,
-             int world, float mul, float* out, long long fanout_off, float* partials,
-             unsigned* pflags, int max_blocks, bool aligned16, cudaStream_t st) {
+             int world, float mul, const float* mul_dev, float* out, long long fanout_off,
+             float* partials, unsigned* pflags, int max_blocks, bool aligned16, cudaStream_t st,
+             int threads) {
   int blocks = 1;
+  if (threads != 128) threads = 256;
   MSB_DISPATCH_FLOAT(dtype, T, {
     constexpr int V = 16 / sizeof(T);
     // vector loads need 16-byte aligned sources, vector stores an aligned out
     if (aligned16 && V == 8 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
-      blocks = grid_for(n / V, 256, max_blocks);
-      rs_stats_kernel<T, 8><<<blocks, 256, 0, st>>>(heaps, grad_off, s0, n, world, mul, out,
-                                                    fanout_off, partials, pflags);
+      blocks = grid_for(n / V, threads, max_blocks);
+      rs_stats_kernel<T, 8><<<blocks, threads, 0, st>>>(heaps, grad_off, s0, n, world, mul,
+                                                        mul_dev, out, fanout_off, partials, pflags);
     } else {
-      blocks = grid_for(n, 256, max_blocks);
-      rs_stats_kernel<T, 1><<<blocks, 256, 0, st>>>(heaps, grad_off, s0, n, world, mul, out,
-                                                    fanout_off, partials, pflags);
+      blocks = grid_for(n, threads, max_blocks);
+      rs_stats_kernel<T, 1><<<blocks, threads, 0, st>>>(heaps, grad_off, s0, n, world, mul,
+                                                        mul_dev, out, fanout_off, partials, pflags);
     }
   });
   MSB_CHECK_LAUNCH("rs_stats");
   return blocks;
 }
 
-void stats_exchange(char* const* heaps, long long sync_off, int rank, int world, unsigned epoch,
+void stats_exchange(char* const* heaps, long long sync_off, int rank, int world, unsigned* ctr,
                     float* out, double max_norm, double timeout_s, unsigned* status,
                     cudaStream_t st) {
-  stats_exchange_kernel<<<1, 32, 0, st>>>(heaps, sync_off, rank, world, epoch, out, max_norm,
+  stats_exchange_kernel<<<1, 32, 0, st>>>(heaps, sync_off, rank, world, ctr, out, max_norm,
                                           (unsigned long long)(timeout_s * 1e9), status);
   MSB_CHECK_LAUNCH("stats_exchange");
 }

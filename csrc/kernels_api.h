@@ -76,12 +76,14 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
                   int force_bn = 0, int force_splits = 0);
 
 // ---- NVLink peer heap + fused collectives (collectives.cu)
-void peer_barrier(char* const* heaps, long long sync_off, int rank, int world, unsigned epoch,
+// barrier-type kernels take this rank's device epoch counter (advanced by one each)
+void peer_barrier(char* const* heaps, long long sync_off, int rank, int world, unsigned* ctr,
                   double timeout_s, unsigned* status, cudaStream_t st);
 int rs_stats(char* const* heaps, long long grad_off, int dtype, long long s0, long long n,
-             int world, float mul, float* out, long long fanout_off, float* partials,
-             unsigned* pflags, int max_blocks, bool aligned16, cudaStream_t st);
-void stats_exchange(char* const* heaps, long long sync_off, int rank, int world, unsigned epoch,
+             int world, float mul, const float* mul_dev, float* out, long long fanout_off,
+             float* partials, unsigned* pflags, int max_blocks, bool aligned16, cudaStream_t st,
+             int threads = 256);
+void stats_exchange(char* const* heaps, long long sync_off, int rank, int world, unsigned* ctr,
                     float* out, double max_norm, double timeout_s, unsigned* status,
                     cudaStream_t st);
 void adamw_fanout(float* master, float* m, float* v, const float* grad, char* const* heaps,

@@ -124,6 +124,8 @@ class DeepSpeedEngine:
         self._window_open = False
         self._graph = None          # MicroStepGraph of train_batch (CUDA graphs)
         self._graph_eager = 0       # eager micro-steps run for the current signature
+        self._overlap_now = False   # this micro-step's backward reduces buckets
+        self._bucket_hooks = self._setup_overlap()
 
     # ----------------------------------------------------------- properties
     @property
@@ -179,11 +181,54 @@ class DeepSpeedEngine:
                 g.ensure_grad_arena()
         self._window_open = True
 
+    # ---------------------------------------------- overlapped reductions
+    def _bucket_modules(self) -> List[nn.Module]:
+        fn = getattr(self.module, "bucket_modules", None)
+        if callable(fn):
+            return list(fn())
+        for name in ("blocks", "layers", "h"):
+            mods = getattr(self.module, name, None)
+            if isinstance(mods, nn.ModuleList) and len(mods) > 0:
+                return list(mods)
+        return []
+
+    def _setup_overlap(self) -> list:
+        """Reduce each block's gradients while backward continues with the
+        blocks before it (fused collectives, ``b200.overlap``).  A marker
+        wraps the block's input; its backward runs once the block's whole
+        backward has written the block's gradients."""
+        if not (self.config.b200.overlap and self.world_size > 1 and self.device.type == "cuda"):
+            return []
+        mods = self._bucket_modules()
+        if not mods or not self.optimizer.plan_overlap([list(m.parameters()) for m in mods]):
+            return []
+        hooks = []
+        for k, m in enumerate(mods):
+            hooks.append(m.register_forward_pre_hook(self._bucket_hook(k)))
+        return hooks
+
+    def _bucket_hook(self, k: int):
+        def hook(module, args):
+            if (not self._overlap_now or not torch.is_grad_enabled() or not args
+                    or not isinstance(args[0], torch.Tensor) or not args[0].requires_grad):
+                return None
+            return (_BucketMark.apply(args[0], self.optimizer, k),) + tuple(args[1:])
+        return hook
+
+    def _begin_micro_step(self) -> None:
+        """Decided at forward time: the micro-step that closes an accumulation
+        window reduces its buckets during backward."""
+        self._overlap_now = bool(self._bucket_hooks) and self.module.training and \
+            (self.micro_steps + 1) % self.gas == 0
+        if self._overlap_now:
+            self.optimizer.set_loss_scale(self.loss_scaler.loss_scale_factor)
+
     def forward(self, *args, **kwargs):
         if not self.optimizer.params_gathered:
             with self.timers.timer("gather"):
                 self.optimizer.gather_parameters()
         self._open_window()
+        self._begin_micro_step()
         return self.module(*self._cast_inputs(args), **self._cast_inputs(kwargs))
 
     def __call__(self, *args, **kwargs):
@@ -254,7 +299,9 @@ class DeepSpeedEngine:
 
     def _graph_micro_step(self, args, kwargs) -> torch.Tensor:
         from .graphs import MicroStepGraph, signature
+        self._begin_micro_step()
         sig, _ = signature(args, kwargs)
+        sig = (sig, self._overlap_now)
         st = self._graph
         if st is None or st.sig != sig or (st.graph is not None and not st.valid()):
             if st is not None:
@@ -274,6 +321,7 @@ class DeepSpeedEngine:
                 return loss
             torch.cuda.empty_cache()
             st = MicroStepGraph(self, args, kwargs)
+            st.sig = sig            # inputs and whether the bucket reductions are captured
             st.capture(side)
             cur.wait_stream(side)
             self._graph = st
@@ -286,6 +334,8 @@ class DeepSpeedEngine:
         self._open_window()
         with self.timers.timer("backward"):
             loss = st.replay()
+        if st.overlap:
+            self.optimizer._overlap_ran = True   # the replay ran the bucket reductions
         self.micro_steps += 1
         return loss
 
@@ -377,11 +427,30 @@ class DeepSpeedEngine:
     def close(self) -> None:
         """Release communication resources (peer mappings, buffers)."""
         self.release_graphs()
+        for h in self._bucket_hooks:
+            h.remove()
+        self._bucket_hooks = []
         self.optimizer.close()
 
     def __repr__(self) -> str:  # pragma: no cover
         return (f"DeepSpeedEngine({self.config!r}, global_steps={self.global_steps}, "
                 f"micro_steps={self.micro_steps})")
+
+
+class _BucketMark(torch.autograd.Function):
+    """Identity on a block's input; its backward launches the reduction of
+    the block's gradient bucket."""
+
+    @staticmethod
+    def forward(ctx, x, optimizer, k):
+        ctx.optimizer = optimizer
+        ctx.k = k
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, grad):
+        ctx.optimizer.launch_bucket(ctx.k)
+        return grad, None, None
 
 
 def initialize(model: Optional[nn.Module] = None, model_parameters=None, config=None,

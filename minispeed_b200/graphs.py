@@ -85,6 +85,7 @@ class MicroStepGraph:
         self._seed_value = 1.0
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.loss: Optional[torch.Tensor] = None
+        self.overlap = engine._overlap_now   # captured with the bucket reductions
         self.kernels = 0          # this library's kernels per replay
         self.replays = 0
         self._ptrs: Tuple[int, ...] = ()
@@ -122,6 +123,10 @@ class MicroStepGraph:
             if not isinstance(loss, torch.Tensor) or loss.dim() != 0:
                 raise RuntimeError("train_batch: the module must return a scalar loss")
             torch.autograd.backward(loss, self.seed.to(loss.dtype))
+            if self.overlap:
+                eng.optimizer.join_comm()   # the bucket reductions rejoin the graph
+        if self.overlap:
+            eng.optimizer._overlap_ran = False   # captured, not run
         self.kernels = _ext.launch_count() - n0
         self.graph = g
         self.loss = loss.detach()    # the graph's output buffer, no autograd refs

@@ -80,8 +80,10 @@ class FusedCollectives:
         self.heap: Optional[PeerHeap] = None
         self.groups: List[FlatParamGroup] = []
         self.stage = 0
-        self.epoch = 0
         self.status = torch.zeros(4, dtype=torch.int32, device=self.device)
+        # epochs of the barrier-type kernels: a device counter each of them
+        # advances, so launches replayed from a CUDA graph stay in step
+        self.epoch_dev = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._shard32 = {}
         self._step_open = False
 
@@ -124,13 +126,81 @@ class FusedCollectives:
         torch.cuda.synchronize(self.device)
         self.barrier()
 
-    def _next_epoch(self) -> int:
-        self.epoch += 1
-        return self.epoch
-
     def barrier(self) -> None:
         _ext.get().peer_barrier(self.heap.heaps, self.heap.sync_off, self.rank,
-                                self.world_size, self._next_epoch(), self.timeout_s, self.status)
+                                self.world_size, self.epoch_dev, self.timeout_s, self.status)
+
+    # ---------------------------------------------- bucketed overlap
+    BUCKET_SLOTS = 64   # statistics slots (thread blocks) reserved per bucket
+    # thread blocks per bucket reduction: it shares the GPU with the backward
+    # kernels still running, so it gets a small grid
+    BUCKET_BLOCKS = int(os.environ.get("MINISPEED_BUCKET_BLOCKS", "48"))
+
+    def _shard_range(self, g: FlatParamGroup) -> Tuple[int, int]:
+        if self.stage == 0:
+            return self.rank * g.shard_size, (self.rank + 1) * g.shard_size
+        return g.shard_start, g.shard_end
+
+    def plan_buckets(self, buckets: List[List[Tuple[int, int, int]]]) -> int:
+        """Fix the reduction of gradient buckets that become final during
+        backward.  ``buckets[k]`` lists ``(group, lo, hi)`` arena ranges.  Each
+        rank reduces ``[lo, hi)`` cut to its shard and to 8-element (16-byte)
+        boundaries; what the buckets leave (other parameters, unaligned
+        edges) is reduced at the step.  Returns the statistics slots the
+        buckets occupy (bucket k writes slots ``[k*64, (k+1)*64)``)."""
+        self.bucket_plan = []
+        covered = {i: [] for i in range(len(self.groups))}
+        for ranges in buckets:
+            segs = []
+            for (i, lo, hi) in ranges:
+                a, b = self._shard_range(self.groups[i])
+                s0, e0 = max(lo, a), min(hi, b)
+                s0, e0 = (s0 + 7) // 8 * 8, e0 // 8 * 8
+                if e0 > s0:
+                    segs.append((i, s0, e0))
+                    covered[i].append((s0, e0))
+            self.bucket_plan.append(segs)
+        self.remaining = {}
+        for i, g in enumerate(self.groups):
+            a, b = self._shard_range(g)
+            rest, cur = [], a
+            for s0, e0 in sorted(covered[i]):
+                if s0 > cur:
+                    rest.append((cur, s0))
+                cur = max(cur, e0)
+            if cur < b:
+                rest.append((cur, b))
+            self.remaining[i] = rest
+        return len(buckets) * self.BUCKET_SLOTS
+
+    def _out_slice(self, i: int, g: FlatParamGroup, s0: int, e0: int) -> torch.Tensor:
+        if self.stage == 0:
+            return g._grad[s0:e0]
+        a = g.shard_start
+        return self._shard_out(i, g)[s0 - a:e0 - a]
+
+    def _reduce_segment(self, i: int, s0: int, e0: int, mul: float, mul_dev, stats,
+                        slot: int, max_blocks: int, threads: int = 256) -> int:
+        g = self.groups[i]
+        out = self._out_slice(i, g, s0, e0)
+        esz = g.grad_arena.element_size()
+        aligned = (s0 * esz) % 16 == 0 and (self.heap.offsets[f"grad{i}"] % 16) == 0
+        fan = self.heap.offsets[f"grad32_{i}"] if self.stage == 0 else -1
+        return int(_ext.get().rs_stats(self.heap.heaps, self.heap.offsets[f"grad{i}"],
+                                       DTYPE_CODE[g.grad_arena.dtype], s0, out, self.world_size,
+                                       mul, mul_dev, fan, stats.partials, stats.flags, slot,
+                                       max_blocks, aligned, threads))
+
+    def launch_bucket(self, k: int, mul_dev: torch.Tensor, stats) -> None:
+        """Barrier (every rank has this bucket's gradients), then the
+        reduction of this rank's part of bucket k, on the current stream.
+        The multiplier 1 / loss scale is read from ``mul_dev``."""
+        self.barrier()
+        slot = k * self.BUCKET_SLOTS
+        end = slot + self.BUCKET_SLOTS
+        for (i, s0, e0) in self.bucket_plan[k]:
+            slot += self._reduce_segment(i, s0, e0, 1.0 / self.world_size, mul_dev, stats, slot,
+                                         max(1, min(self.BUCKET_BLOCKS, end - slot)), threads=128)
 
     # ------------------------------------------------------------- step
     def _shard_out(self, i: int, g: FlatParamGroup) -> torch.Tensor:
@@ -142,13 +212,23 @@ class FusedCollectives:
                                                  device=self.device)
         return buf
 
-    def reduce_grads(self, g: FlatParamGroup, arena: torch.Tensor, inv_scale: float, stats=None):
+    def reduce_grads(self, g: FlatParamGroup, arena: torch.Tensor, inv_scale: float, stats=None,
+                     overlapped: bool = False):
         i = self.groups.index(g)
         if not self._step_open:
             self.barrier()          # every rank's gradient arena is final
             self._step_open = True
         if g.grad_arena is not arena:
             raise RuntimeError("gradient arena left the peer heap")
+        if overlapped:
+            # the buckets were reduced during backward: only the rest remains
+            for s0, e0 in self.remaining[i]:
+                left = stats.partials.numel() - stats.used
+                stats.used += self._reduce_segment(i, s0, e0, inv_scale / self.world_size, None,
+                                                   stats, stats.used, min(left, 148 * 8))
+            if self.stage == 0:
+                return g._grad, 1.0, True
+            return self._shard_out(i, g), 1.0, True
         if self.stage == 0:
             # two-shot all-reduce: reduce slice `rank`, store it to every peer
             s0 = self.rank * g.shard_size
@@ -162,8 +242,8 @@ class FusedCollectives:
         left = stats.partials.numel() - stats.used
         nb = _ext.get().rs_stats(self.heap.heaps, self.heap.offsets[f"grad{i}"],
                                  DTYPE_CODE[arena.dtype], s0, out, self.world_size,
-                                 inv_scale / self.world_size, fan, stats.partials, stats.flags,
-                                 stats.used, min(left, 148 * 8), aligned)
+                                 inv_scale / self.world_size, None, fan, stats.partials,
+                                 stats.flags, stats.used, min(left, 148 * 8), aligned, 256)
         stats.used += int(nb)
         if self.stage == 0:
             return g._grad, 1.0, True
@@ -174,7 +254,7 @@ class FusedCollectives:
 
     def all_reduce_stats(self, out: torch.Tensor, max_norm: Optional[float] = None) -> None:
         _ext.get().stats_exchange(self.heap.heaps, self.heap.sync_off, self.rank,
-                                  self.world_size, self._next_epoch(), out,
+                                  self.world_size, self.epoch_dev, out,
                                   float(max_norm) if max_norm else 0.0, self.timeout_s,
                                   self.status)
 

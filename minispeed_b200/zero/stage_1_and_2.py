@@ -84,6 +84,12 @@ class ZeROOptimizer:
         # optional CUDA-event timing of the communication phases of each step
         # (list of (reduce_ms, gather_ms)); enabled by the engine
         self.phase_log = None
+        # bucketed reduction overlapped with backward (fused collectives)
+        self.overlap_slots = 0
+        self._overlap_ran = False
+        self.comm_stream = None
+        self.inv_scale_dev = None
+        self._inv_scale_host = None
 
     # ------------------------------------------------------ torch surface
     @property
@@ -97,6 +103,58 @@ class ZeROOptimizer:
     def zero_grad(self) -> None:
         for g in self.flat_groups:
             g.zero_grad()
+
+    # ------------------------------------------- overlap with backward
+    def plan_overlap(self, buckets: List[List[torch.nn.Parameter]]) -> bool:
+        """Set up the reduction of each parameter bucket as soon as backward
+        has produced it (``launch_bucket``).  A bucket's parameters must fill
+        one contiguous arena range per group.  Returns False (no overlap) when
+        the collectives cannot run buckets or a bucket does not qualify."""
+        if not hasattr(self.coll, "plan_buckets") or self.stats.device.type != "cuda":
+            return False
+        where = {}
+        for gi, g in enumerate(self.flat_groups):
+            for p, off, n in zip(g.params, g._offsets_int, g._numels):
+                where[id(p)] = (gi, off, n)
+        seen, plan = set(), []
+        for params in buckets:
+            spans = {}
+            for p in params:
+                if id(p) not in where or id(p) in seen:
+                    return False
+                seen.add(id(p))
+                gi, off, n = where[id(p)]
+                lo, hi, tot = spans.get(gi, (off, off + n, 0))
+                spans[gi] = (min(lo, off), max(hi, off + n), tot + n)
+            if any(hi - lo != tot for lo, hi, tot in spans.values()):
+                return False        # not one contiguous range
+            plan.append([(gi, lo, hi) for gi, (lo, hi, _) in sorted(spans.items())])
+        if not plan:
+            return False
+        self.overlap_slots = self.coll.plan_buckets(plan)
+        self.comm_stream = torch.cuda.Stream(self.stats.device)
+        self.inv_scale_dev = torch.ones(1, dtype=torch.float32, device=self.stats.device)
+        return True
+
+    def set_loss_scale(self, scale: float) -> None:
+        """The multiplier the overlapped reductions read (1 / loss scale)."""
+        if self.inv_scale_dev is not None and scale != self._inv_scale_host:
+            self.inv_scale_dev.fill_(1.0 / float(scale))
+            self._inv_scale_host = scale
+
+    def launch_bucket(self, k: int) -> None:
+        """Reduce bucket k on the communication stream, after the work the
+        current (backward) stream has queued so far."""
+        cur = torch.cuda.current_stream(self.stats.device)
+        self.comm_stream.wait_stream(cur)
+        with torch.cuda.stream(self.comm_stream):
+            self.coll.launch_bucket(k, self.inv_scale_dev, self.stats)
+        self._overlap_ran = True
+
+    def join_comm(self) -> None:
+        """Make the current stream wait for the overlapped reductions."""
+        if self.comm_stream is not None:
+            torch.cuda.current_stream(self.stats.device).wait_stream(self.comm_stream)
 
     # ---------------------------------------------- parameter lifecycle
     @property
@@ -139,6 +197,11 @@ class ZeROOptimizer:
         inv = 1.0 / float(loss_scale)
         st = self.stats
         st.reset()
+        overlapped = self._overlap_ran
+        self._overlap_ran = False
+        if overlapped:
+            self.join_comm()
+            st.used = self.overlap_slots
         ev = None
         if self.phase_log is not None and st.device.type == "cuda":
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
@@ -146,7 +209,10 @@ class ZeROOptimizer:
         grads, mul = [], 1.0
         for g in self.flat_groups:
             arena = g.collect_grads()
-            red, mul, stats_done = self.coll.reduce_grads(g, arena, inv, st)
+            if overlapped:
+                red, mul, stats_done = self.coll.reduce_grads(g, arena, inv, st, overlapped=True)
+            else:
+                red, mul, stats_done = self.coll.reduce_grads(g, arena, inv, st)
             if not stats_done:
                 st.accumulate(red, mul)
             grads.append(red)

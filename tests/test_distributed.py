@@ -112,3 +112,31 @@ def test_bf16_two_ranks_stage2(tmp_path):
                                rtol=3e-2, atol=3e-3)
     for k in r0["params"]:
         torch.testing.assert_close(r0["params"][k], r1["params"][k], rtol=0, atol=0)
+
+
+def test_bucket_plan_covers_each_shard_exactly():
+    """Overlapped buckets + the step's remainder reduce every element of the
+    rank's shard once, on 16-byte boundaries."""
+    import types
+
+    from minispeed_b200.parallel.fused import FusedCollectives
+
+    for stage in (0, 2):
+        for rank in range(3):
+            fc = FusedCollectives.__new__(FusedCollectives)
+            fc.rank, fc.world_size, fc.stage = rank, 3, stage
+            g = types.SimpleNamespace(shard_size=1000, shard_start=1000 * rank,
+                                      shard_end=1000 * (rank + 1))
+            fc.groups = [g]
+            buckets = [[(0, 5, 733)], [(0, 733, 1501)], [(0, 1501, 2999)]]
+            slots = fc.plan_buckets(buckets)
+            assert slots == 3 * FusedCollectives.BUCKET_SLOTS
+            a, b = fc._shard_range(g)
+            segs = [(s, e) for bk in fc.bucket_plan for (_, s, e) in bk] + fc.remaining[0]
+            segs.sort()
+            assert segs[0][0] == a and segs[-1][1] == b
+            for (s0, e0), (s1, _) in zip(segs, segs[1:]):
+                assert e0 == s1            # disjoint and gap-free
+            for bk in fc.bucket_plan:
+                for (_, s, e) in bk:
+                    assert s % 8 == 0 and e % 8 == 0 and e > s

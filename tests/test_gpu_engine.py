@@ -120,7 +120,8 @@ def test_peer_barrier_wait_times_out_with_status():
         heaps = torch.tensor([a, b], dtype=torch.int64, device="cuda")
         status = torch.zeros(4, dtype=torch.int32, device="cuda")
         t0 = time.time()
-        C.peer_barrier(heaps, 0, 0, 2, 1, 0.3, status)
+        ctr = torch.zeros(1, dtype=torch.int32, device="cuda")   # epoch counter
+        C.peer_barrier(heaps, 0, 0, 2, ctr, 0.3, status)
         torch.cuda.synchronize()
         assert 0.2 < time.time() - t0 < 30
         assert int(status[0]) == 0x101          # waited on rank 1
@@ -142,7 +143,8 @@ def test_stats_exchange_times_out_and_blocks_the_update():
         heaps = torch.tensor([a, b], dtype=torch.int64, device="cuda")
         status = torch.zeros(4, dtype=torch.int32, device="cuda")
         out = torch.tensor([0.0, 4.0, 0, 0, 0, 0, 0, 0], device="cuda")
-        C.stats_exchange(heaps, 0, 0, 2, 7, out, 1.0, 0.2, status)
+        ctr = torch.zeros(1, dtype=torch.int32, device="cuda")
+        C.stats_exchange(heaps, 0, 0, 2, ctr, out, 1.0, 0.2, status)
         torch.cuda.synchronize()
         assert int(status[0]) == 0x201
         assert float(out[0]) == 1.0   # a timed-out step is flagged, never applied

@@ -100,3 +100,15 @@ def test_graph_overflow_skips_and_recovers():
         assert torch.isfinite(loss)
     assert eng.global_steps == steps + 3
     eng.close()
+
+
+def test_graph_is_captured_once():
+    eng, _ = _engine(2, 1, True)
+    data = [t.cuda() for t in _batches(8)]
+    first = None
+    for i, t in enumerate(data):
+        eng.train_batch(t[:, :-1], targets=t[:, 1:])
+        if i == 2:
+            first = eng._graph
+    assert eng._graph is first and first.replays == len(data) - 2
+    eng.close()

@@ -75,3 +75,55 @@ def test_fused_matches_nccl_path(dtype, tmp_path):
     for k in fused[0]["params"]:
         torch.testing.assert_close(fused[0]["params"][k], nccl[0]["params"][k], rtol=tol,
                                    atol=tol)
+
+
+def _gpt_worker(rank, stage, overlap, graph, port, out_dir):
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port),
+                       "RANK": str(rank), "WORLD_SIZE": str(WORLD), "LOCAL_RANK": str(rank),
+                       "LOCAL_WORLD_SIZE": str(WORLD), "MINISPEED_DEVICE": f"cuda:{rank}",
+                       "MINISPEED_PG_TIMEOUT_S": "120", "NCCL_NVLS_ENABLE": "0"})
+    os.environ.pop("MINISPEED_BACKEND", None)
+    torch.cuda.set_device(rank)
+    from minispeed_b200.models import GPT, GPTConfig, init_gpt2_
+    torch.manual_seed(0)
+    model = GPT(GPTConfig(vocab_size=512, block_size=64, n_layer=3, n_head=4, n_embd=128))
+    init_gpt2_(model)
+    cfg = {"train_micro_batch_size_per_gpu": 4, "gradient_accumulation_steps": 2,
+           "gradient_clipping": 1.0, "dtype": "fp16",
+           "fp16": {"enabled": True, "initial_scale_power": 10, "loss_scale_window": 3},
+           "optimizer": {"type": "AdamW", "params": {"lr": 1e-3, "weight_decay": 0.1}},
+           "zero_optimization": {"stage": stage},
+           "b200": {"comm": "fused", "overlap": overlap, "cuda_graph": graph,
+                    "wait_timeout_ms": 20000}}
+    engine = ms.initialize(model=model, config=cfg)
+    g = torch.Generator().manual_seed(11)
+    data = [torch.randint(0, 512, (WORLD * 4, 65), generator=g) for _ in range(12)]
+    losses = []
+    for t in data:
+        t = t[rank * 4:(rank + 1) * 4].cuda()
+        losses.append(float(engine.train_batch(t[:, :-1], targets=t[:, 1:])))
+    params = {k: v.detach().float().cpu() for k, v in engine.state_dict().items()}
+    torch.save({"losses": torch.tensor(losses), "params": params,
+                "slots": engine.optimizer.overlap_slots, "steps": engine.global_steps,
+                "scale": engine.get_loss_scale()}, os.path.join(out_dir, f"r{rank}.pt"))
+    engine.close()
+    ms.comm.destroy()
+
+
+@pytest.mark.parametrize("stage", [0, 2])
+@pytest.mark.parametrize("graph", [False, True])
+def test_overlapped_bucket_reduction_matches_step_reduction(stage, graph, tmp_path):
+    runs = {}
+    for overlap in (False, True):
+        d = tmp_path / f"o{int(overlap)}"
+        d.mkdir()
+        mp.spawn(_gpt_worker, args=(stage, overlap, graph, free_port(), str(d)), nprocs=WORLD,
+                 join=True)
+        runs[overlap] = [torch.load(d / f"r{r}.pt", weights_only=False) for r in range(WORLD)]
+    off, on = runs[False], runs[True]
+    assert off[0]["slots"] == 0 and on[0]["slots"] > 0       # the buckets were planned
+    assert on[0]["steps"] == off[0]["steps"] == 6 and on[0]["scale"] == off[0]["scale"]
+    torch.testing.assert_close(on[0]["losses"], off[0]["losses"], rtol=2e-3, atol=2e-3)
+    for k in off[0]["params"]:
+        torch.testing.assert_close(on[0]["params"][k], on[1]["params"][k], rtol=0, atol=0)
+        torch.testing.assert_close(on[0]["params"][k], off[0]["params"][k], rtol=2e-3, atol=2e-4)
