@@ -565,13 +565,29 @@ void adamw_fanout_py(const at::Tensor& master, const at::Tensor& m, const at::Te
                     wd, bc1, bc2, grad_mul, stream_of(master));
 }
 
+bool base_aligned(const at::Tensor& heaps, int64_t shard_off, const at::Tensor& dst) {
+  // heap bases are cudaMalloc'd (256-byte aligned); the region offset and the
+  // destination decide the 16-byte path
+  return (shard_off % 16) == 0 && (reinterpret_cast<uintptr_t>(dst.data_ptr()) & 15) == 0;
+}
+
 void gather_pull_py(const at::Tensor& heaps, int64_t shard_off, int64_t shard, int64_t world,
                     const at::Tensor& dst) {
   check_cuda_contig(dst, "dst");
   TORCH_CHECK(dst.numel() >= shard * world);
   c10::cuda::CUDAGuard g(dst.device());
   msb::gather_pull(heap_table(heaps), shard_off, shard, (int)world, dst.data_ptr(),
-                   dtype_code(dst), stream_of(dst));
+                   dtype_code(dst), base_aligned(heaps, shard_off, dst), stream_of(dst));
+}
+
+// dst (the full flat arena) [lo, hi) <- the owners' shards
+void gather_range_py(const at::Tensor& heaps, int64_t shard_off, int64_t shard, int64_t lo,
+                     int64_t hi, const at::Tensor& dst) {
+  check_cuda_contig(dst, "dst");
+  TORCH_CHECK(0 <= lo && lo <= hi && hi <= dst.numel(), "gather range out of bounds");
+  c10::cuda::CUDAGuard g(dst.device());
+  msb::gather_range(heap_table(heaps), shard_off, shard, lo, hi, dst.data_ptr(), dtype_code(dst),
+                    base_aligned(heaps, shard_off, dst), stream_of(dst));
 }
 
 }  // namespace
@@ -616,4 +632,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, mod) {
   mod.def("stats_exchange", &stats_exchange_py);
   mod.def("adamw_fanout", &adamw_fanout_py);
   mod.def("gather_pull", &gather_pull_py);
+  mod.def("gather_range", &gather_range_py);
 }

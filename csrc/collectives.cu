@@ -21,8 +21,8 @@
 //   adamw_fanout      AdamW on this rank's shard whose fp16/bf16 cast is
 //                     stored into the parameter arena of EVERY rank (the
 //                     parameter all-gather fused into the update)
-//   gather_pull       stage-3 parameter gather: local arena <- every peer's
-//                     model-dtype shard
+//   gather_range      stage-3 parameter gather: a range of the local arena <-
+//                     the owning peers' model-dtype shards (gather_pull: all)
 //
 // Waits use %globaltimer bounds; on expiry a kernel records an error code in
 // a local status word and returns, leaving the context usable.
@@ -307,16 +307,26 @@ adamw_fanout_kernel(float* __restrict__ master, float* __restrict__ m, float* __
   __threadfence_system();
 }
 
-template <typename T>
+// dst[i] = owner(i)'s shard element, for flat indices i in [lo, hi); owner
+// q holds [q*shard, (q+1)*shard).  VEC elements (16 bytes) per access when the
+// shard size, lo and both bases are 16-byte aligned (a vector then never
+// crosses two owners).
+template <typename T, int VEC>
 __global__ void __launch_bounds__(256)
-gather_pull_kernel(char* const* heaps, long long shard_off, long long shard, int world,
-                   T* __restrict__ dst) {
-  const long long total = shard * world;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
+gather_range_kernel(char* const* heaps, long long shard_off, long long shard, long long lo,
+                    long long hi, T* __restrict__ dst) {
+  const long long nv = (hi - lo) / VEC;
+  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < nv;
+       v += (long long)gridDim.x * blockDim.x) {
+    const long long i = lo + v * VEC;
     const int q = (int)(i / shard);
     const long long j = i - (long long)q * shard;
-    dst[i] = reinterpret_cast<const T*>(heaps[q] + shard_off)[j];
+    const T* src = reinterpret_cast<const T*>(heaps[q] + shard_off) + j;
+    if (VEC == 8) {
+      *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<const uint4*>(src);
+    } else {
+      dst[i] = *src;
+    }
   }
 }
 
@@ -399,14 +409,27 @@ void adamw_fanout(float* master, float* m, float* v, const float* grad, char* co
   MSB_CHECK_LAUNCH("adamw_fanout");
 }
 
-void gather_pull(char* const* heaps, long long shard_off, long long shard, int world, void* dst,
-                 int dtype, cudaStream_t st) {
-  const int blocks = grid_for(shard * world, 256, kNumSMs * 16);
+void gather_range(char* const* heaps, long long shard_off, long long shard, long long lo,
+                  long long hi, void* dst, int dtype, bool aligned16, cudaStream_t st) {
+  if (hi <= lo) return;
   MSB_DISPATCH_FLOAT(dtype, T, {
-    gather_pull_kernel<T><<<blocks, 256, 0, st>>>(heaps, shard_off, shard, world,
-                                                  static_cast<T*>(dst));
+    constexpr int V = 16 / sizeof(T);
+    if (aligned16 && V == 8 && shard % V == 0 && lo % V == 0 && hi % V == 0) {
+      const int blocks = grid_for((hi - lo) / V, 256, kNumSMs * 8);
+      gather_range_kernel<T, 8><<<blocks, 256, 0, st>>>(heaps, shard_off, shard, lo, hi,
+                                                        static_cast<T*>(dst));
+    } else {
+      const int blocks = grid_for(hi - lo, 256, kNumSMs * 16);
+      gather_range_kernel<T, 1><<<blocks, 256, 0, st>>>(heaps, shard_off, shard, lo, hi,
+                                                        static_cast<T*>(dst));
+    }
   });
-  MSB_CHECK_LAUNCH("gather_pull");
+  MSB_CHECK_LAUNCH("gather_range");
+}
+
+void gather_pull(char* const* heaps, long long shard_off, long long shard, int world, void* dst,
+                 int dtype, bool aligned16, cudaStream_t st) {
+  gather_range(heaps, shard_off, shard, 0, shard * world, dst, dtype, aligned16, st);
 }
 
 // --------------------------------------------------------- peer heap

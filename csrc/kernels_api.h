@@ -91,7 +91,9 @@ void adamw_fanout(float* master, float* m, float* v, const float* grad, char* co
                   const float* stats, double lr, double beta1, double beta2, double eps,
                   double wd, double bc1, double bc2, double grad_mul, cudaStream_t st);
 void gather_pull(char* const* heaps, long long shard_off, long long shard, int world, void* dst,
-                 int dtype, cudaStream_t st);
+                 int dtype, bool aligned16, cudaStream_t st);
+void gather_range(char* const* heaps, long long shard_off, long long shard, long long lo,
+                  long long hi, void* dst, int dtype, bool aligned16, cudaStream_t st);
 void* peer_alloc(size_t bytes);
 void peer_free(void* p);
 void peer_handle(void* p, char out[64]);

@@ -125,7 +125,7 @@ class DeepSpeedEngine:
         self._graph = None          # MicroStepGraph of train_batch (CUDA graphs)
         self._graph_eager = 0       # eager micro-steps run for the current signature
         self._overlap_now = False   # this micro-step's backward reduces buckets
-        self._bucket_hooks = self._setup_overlap()
+        self._bucket_hooks = self._setup_overlap() + self._setup_layer_gather()
 
     # ----------------------------------------------------------- properties
     @property
@@ -207,6 +207,21 @@ class DeepSpeedEngine:
             hooks.append(m.register_forward_pre_hook(self._bucket_hook(k)))
         return hooks
 
+    def _setup_layer_gather(self) -> list:
+        """Stage 3 with fused collectives: gather each block's parameters one
+        block ahead of its forward (``ZeROStage3Optimizer.layer_ready``)."""
+        plan = getattr(self.optimizer, "plan_layer_gather", None)
+        if plan is None or self.world_size <= 1 or self.device.type != "cuda":
+            return []
+        mods = self._bucket_modules()
+        if not mods or not plan([list(m.parameters()) for m in mods]):
+            return []
+        hooks = []
+        for k, m in enumerate(mods):
+            hooks.append(m.register_forward_pre_hook(
+                lambda module, args, k=k: self.optimizer.layer_ready(k)))
+        return hooks
+
     def _bucket_hook(self, k: int):
         def hook(module, args):
             if (not self._overlap_now or not torch.is_grad_enabled() or not args
@@ -226,7 +241,10 @@ class DeepSpeedEngine:
     def forward(self, *args, **kwargs):
         if not self.optimizer.params_gathered:
             with self.timers.timer("gather"):
-                self.optimizer.gather_parameters()
+                if getattr(self.optimizer, "plan_layer_gather", None) is not None:
+                    self.optimizer.gather_parameters(layerwise=True)
+                else:
+                    self.optimizer.gather_parameters()
         self._open_window()
         self._begin_micro_step()
         return self.module(*self._cast_inputs(args), **self._cast_inputs(kwargs))

@@ -278,6 +278,13 @@ class FusedCollectives:
         _ext.get().gather_pull(self.heap.heaps, self.heap.offsets[f"pshard{i}"], g.shard_size,
                                self.world_size, g.param_arena)
 
+    def gather_range(self, g: FlatParamGroup, lo: int, hi: int) -> None:
+        """Stage 3: arena elements [lo, hi) from their owners' shards (peer
+        loads over NVLink), on the current stream."""
+        i = self.groups.index(g)
+        _ext.get().gather_range(self.heap.heaps, self.heap.offsets[f"pshard{i}"], g.shard_size,
+                                lo, hi, g.param_arena)
+
     def gather_masters(self, g: FlatParamGroup) -> None:
         if g._partitioned:
             return
