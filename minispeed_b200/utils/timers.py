@@ -11,15 +11,22 @@ with CUDA events recorded on the current stream; ``elapsed_ms()`` syncs
 once and sums every completed interval.  ``max_over_ranks`` reduces a value
 with MAX across the process group, which is how multi-GPU times are
 reported.
+
+With ``MINISPEED_NVTX=1`` every named section is also an NVTX range
+(``torch.cuda.nvtx``), so the engine's gather / backward / step / reduce
+phases show up in a timeline profiler.
 """
 
 from __future__ import annotations
 
+import os
 import time
 from contextlib import contextmanager
 from typing import Dict, Iterator, List
 
 import torch
+
+_NVTX = os.environ.get("MINISPEED_NVTX", "0") == "1"
 
 
 class Timer:
@@ -60,8 +67,15 @@ class Timers:
 
     @contextmanager
     def timer(self, name: str) -> Iterator[None]:
-        with self(name).section():
-            yield
+        nvtx = _NVTX and torch.cuda.is_available()
+        if nvtx:
+            torch.cuda.nvtx.range_push(name)
+        try:
+            with self(name).section():
+                yield
+        finally:
+            if nvtx:
+                torch.cuda.nvtx.range_pop()
 
     def names(self) -> List[str]:
         return list(self._timers)

@@ -13,7 +13,7 @@ import torch
 import torch.multiprocessing as mp
 
 import minispeed_b200 as ms
-from tests.helpers import config, free_port, make_data, make_net, rank_slice, run, set_rank_env
+from tests.helpers import config, free_port, make_data, make_net, mse, rank_slice, run, set_rank_env
 
 WORLD, STEPS, GAS, MICRO = 2, 5, 2, 4
 
@@ -140,3 +140,48 @@ def test_bucket_plan_covers_each_shard_exactly():
             for bk in fc.bucket_plan:
                 for (_, s, e) in bk:
                     assert s % 8 == 0 and e % 8 == 0 and e > s
+
+
+def _leaving_worker(rank, port, out_dir):
+    import time
+
+    set_rank_env(rank, WORLD, port, "gloo", "cpu")
+    os.environ["MINISPEED_PG_TIMEOUT_S"] = "20"
+    engine = ms.initialize(model=make_net(), config=config(micro=MICRO, gas=1, stage=2))
+    x, y = make_data(2, 1, WORLD, MICRO)
+    xs, ys = rank_slice(x, rank, MICRO), rank_slice(y, rank, MICRO)
+    engine.backward(mse(engine(xs[0, 0]), ys[0, 0]))
+    engine.step()
+    if rank == 1:
+        os._exit(0)          # leaves between steps, nothing of its own in flight
+    t0 = time.time()
+    try:
+        engine.backward(mse(engine(xs[1, 0]), ys[1, 0]))
+        engine.step()
+        result = "no error"
+    except Exception as e:   # the step's reduce-scatter finds the peer gone
+        result = type(e).__name__
+    torch.save({"result": result, "seconds": time.time() - t0},
+               os.path.join(out_dir, "r0.pt"))
+    os._exit(0)
+
+
+@pytest.mark.timeout(180)
+def test_surviving_rank_fails_cleanly_when_a_peer_leaves(tmp_path):
+    """A rank that leaves mid-run makes the others' next collective raise
+    (bounded by the process-group timeout) instead of hanging."""
+    ctx = mp.get_context("spawn")
+    port = free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, port, str(tmp_path)))
+             for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=150)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank hung after its peer left")
+    out = torch.load(tmp_path / "r0.pt", weights_only=False)
+    assert out["result"] != "no error"
+    assert out["seconds"] < 60
