@@ -194,6 +194,86 @@ norm_dx_kernel(const T* __restrict__ dy, const T* __restrict__ s, const T* __res
   }
 }
 
+// Same computation with every load of a row issued before the row
+// reductions: the raw 16-byte packs of s, dy and the residual gradient stay in
+// registers (4 registers per 8 values) and x-hat / g are recomputed in the
+// second pass.  Used when the activation rows are 16-byte aligned and a row
+// is at most 2048 wide (NV <= 8).
+template <typename T>
+__device__ __forceinline__ void unpack8(const Pack8<T>& r, float (&f)[8]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) f[k] = to_f32(r.v[k]);
+}
+
+template <typename T, int NV, bool RMS>
+__global__ void __launch_bounds__(256)
+norm_dx_prefetch_kernel(const T* __restrict__ dy, const T* __restrict__ s,
+                        const T* __restrict__ w, const float* __restrict__ mean_in,
+                        const float* __restrict__ rstd_in, const T* __restrict__ dres,
+                        T* __restrict__ dx, int M, int C) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nvec = C >> 3;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+    const size_t base = (size_t)row * C;
+    Pack8<T> sp[NV], dp[NV], rp[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (lane + i * 32) << 3;
+      if ((lane + i * 32) < nvec) {
+        sp[i] = *reinterpret_cast<const Pack8<T>*>(s + base + c);
+        dp[i] = *reinterpret_cast<const Pack8<T>*>(dy + base + c);
+        if (dres != nullptr) rp[i] = *reinterpret_cast<const Pack8<T>*>(dres + base + c);
+      }
+    }
+    const float mean = RMS ? 0.f : mean_in[row];
+    const float rstd = rstd_in[row];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (lane + i * 32) << 3;
+      if ((lane + i * 32) < nvec) {
+        float sv[8], dyv[8], wv[8];
+        unpack8(sp[i], sv);
+        unpack8(dp[i], dyv);
+        load8(w + c, wv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float xh = (sv[k] - mean) * rstd;
+          const float g = dyv[k] * wv[k];
+          s1 += g;
+          s2 += g * xh;
+        }
+      }
+    }
+    s1 = warp_sum(s1) / (float)C;
+    s2 = warp_sum(s2) / (float)C;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (lane + i * 32) << 3;
+      if ((lane + i * 32) < nvec) {
+        float sv[8], dyv[8], wv[8], o[8];
+        unpack8(sp[i], sv);
+        unpack8(dp[i], dyv);
+        load8(w + c, wv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float xh = (sv[k] - mean) * rstd;
+          const float g = dyv[k] * wv[k];
+          o[k] = RMS ? rstd * (g - xh * s2) : rstd * (g - s1 - xh * s2);
+        }
+        if (dres != nullptr) {
+          float r[8];
+          unpack8(rp[i], r);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) o[k] += r[k];
+        }
+        store8(dx + base + c, o);
+      }
+    }
+  }
+}
+
 // Column partials of dw = sum_rows dy * xhat and db = sum_rows dy, tiled like
 // colsum_partial_kernel: block (256-column slab, row chunk).
 template <typename T, bool RMS>
@@ -652,6 +732,18 @@ static void launch_norm_dx(const void* dy, const void* s, const void* w, const f
                            const float* rstd, const void* dres, void* dx, int M, int C, bool rms,
                            cudaStream_t st) {
   const int blocks = grid_for((M + 7) / 8, 1, kNumSMs * 16);
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if constexpr (NVV <= 8) {
+    if (C % 8 == 0 && al(dy) && al(s) && al(dx) && (dres == nullptr || al(dres))) {
+      if (rms)
+        norm_dx_prefetch_kernel<T, NVV, true><<<blocks, 256, 0, st>>>(
+            (const T*)dy, (const T*)s, (const T*)w, mean, rstd, (const T*)dres, (T*)dx, M, C);
+      else
+        norm_dx_prefetch_kernel<T, NVV, false><<<blocks, 256, 0, st>>>(
+            (const T*)dy, (const T*)s, (const T*)w, mean, rstd, (const T*)dres, (T*)dx, M, C);
+      return;
+    }
+  }
   if (rms)
     norm_dx_kernel<T, NVV, true><<<blocks, 256, 0, st>>>((const T*)dy, (const T*)s, (const T*)w,
                                                           mean, rstd, (const T*)dres, (T*)dx, M, C);

@@ -349,7 +349,12 @@ class DeepSpeedEngine:
             factor /= self.gas
         st.set_seed(factor)
         st.load_inputs(args, kwargs)
-        self._open_window()
+        if not self._window_open:
+            # the graph checked the arena addresses; only the p.grad views
+            # (which the step reads) need to be in place
+            for g in self.flat_groups:
+                g.ensure_grad_arena()
+            self._window_open = True
         with self.timers.timer("backward"):
             loss = st.replay()
         if st.overlap:
