@@ -515,8 +515,6 @@ void launch_fwd(const CUtensorMap& tm, const Params& p, int B, int H, cudaStream
 // Tensor memory: S^T/P^T 128, dP^T/dS^T 128, dV D, dK D, dQ D columns.
 namespace bwd {
 
-constexpr int kThreadsB = 448;   // 14 warps
-
 struct Params {
   int B, T, H, Hkv;
   int q_col, k_col, v_col;
@@ -531,33 +529,61 @@ struct Params {
   unsigned long long timeout_ns;
 };
 
+// operand whose rows (the K index of the MMA) are 128-byte swizzled rows of
+// 64 contiguous M/N elements, slabs of 64 columns 16 KB apart
+__device__ __forceinline__ uint64_t mn_desc(uint32_t base, int ks) {
+  return smem_desc(base + ks * 2048, 128 * 128, 1024);
+}
+// K-major operand: rows of 64 contiguous K elements (128-byte swizzle), k-th 16-wide step
+__device__ __forceinline__ uint64_t k_desc(uint32_t base, int ks) {
+  return smem_desc(base + ks * 32, 16, 1024);
+}
+
+// ---------------------------------------------------------------- head dim 64
+// One CTA: one 128-key block j of one (batch, kv head); it walks the 64-row
+// query tiles from the diagonal down, for every query head that shares the kv
+// head.  Per query tile t (score buffer b = t & 1):
+//   S^T = K Q_t^T, dP^T = V dO_t^T       M = 128 keys, N = 64 queries -> buffer b
+//   softmax warps: P^T = exp2(S^T * scale_log2 - lse), dS^T = P^T (dP^T - delta);
+//                  P^T -> tensor memory (packed 16-bit), dS^T -> shared memory
+//   dV += P^T dO_t (A from tensor memory), dK += dS^T Q_t (A from shared memory)
+//   every second tile: dQ = dS K over the pair's 128 queries (M = 128), read
+//                  out by the dQ warps and reduce-added into an fp32 buffer
+// The MMA warp issues tile t+1's scores before tile t's gradient MMAs, so the
+// tensor core works on one tile while the softmax warps work on the other.
+// Tensor memory (512 columns): S^T 0/128, dP^T 64/192 (buffer 0/1), P^T
+// 256/288, dV 320, dK 384, dQ 448.
+// Warps: 0 TMA, 1 MMA, 2-9 softmax (thread = key row, warp = 32 queries),
+// 10-13 dQ read-out (thread = query row).
+constexpr int kThreadsB = 448;
+constexpr int kStages64 = 4;   // Q / dO tiles in flight
+
 struct alignas(8) Bars {
   uint64_t kv_full;
-  uint64_t qo_full[2], qo_empty[2];
-  uint64_t st_full;
-  uint64_t ds_ready;
-  uint64_t mma2_done;
-  uint64_t dq_full;
-  uint64_t dq_free;
+  uint64_t qo_full[kStages64], qo_empty[kStages64];
+  uint64_t st_full[2];   // scores of a tile in buffer b
+  uint64_t ds_ready[2];  // softmax of a tile done: P^T / dS^T written, buffer b read (8 warps)
+  uint64_t p_free[2];    // gradient MMAs of a tile retired (and every MMA before them)
+  uint64_t dq_full;      // dQ of a tile pair in tensor memory
+  uint64_t dq_free;      // dQ read out (4 warps)
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
 };
 
-template <int D>
-struct Layout {
-  static constexpr int TILE = 128 * D * 2;
-  static constexpr int CH = 128 * 128;
+struct Layout64 {
+  static constexpr int KV = 128 * 128;   // 128 rows x 128 bytes
+  static constexpr int QT = 64 * 128;    // 64 rows x 128 bytes
   static constexpr int K_OFF = 0;
-  static constexpr int V_OFF = K_OFF + TILE;
-  static constexpr int Q_OFF = V_OFF + TILE;          // two stages
-  static constexpr int DO_OFF = Q_OFF + 2 * TILE;     // two stages
-  static constexpr int DS_OFF = DO_OFF + 2 * TILE;    // dS^T, 128 keys x 128 queries
-  static constexpr int STG_OFF = DS_OFF + 128 * 128 * 2;
-  static constexpr int STG_WARP = 32 * D * 4;         // fp32 dQ rows of one warp
-  static constexpr int LSE_OFF = STG_OFF + 4 * STG_WARP;   // per softmax warp: 64 floats
-  static constexpr int DELTA_OFF = LSE_OFF + 8 * 256;
-  static constexpr int BARS_OFF = DELTA_OFF + 8 * 256;
+  static constexpr int V_OFF = KV;
+  static constexpr int Q_OFF = 2 * KV;
+  static constexpr int DO_OFF = Q_OFF + kStages64 * QT;
+  static constexpr int DS_OFF = DO_OFF + kStages64 * QT;   // 2 pair slots x 2 tiles x [128 keys][64 q]
+  static constexpr int STG_OFF = DS_OFF + 4 * KV;          // dQ staging: 4 warps x 32 rows x 64 fp32
+  static constexpr int STG_WARP = 32 * 64 * 4;
+  static constexpr int LSE_OFF = STG_OFF + 4 * STG_WARP;   // 8 softmax warps x 32 floats
+  static constexpr int DELTA_OFF = LSE_OFF + 8 * 128;
+  static constexpr int BARS_OFF = DELTA_OFF + 8 * 128;
   static constexpr size_t BYTES = 1024 + BARS_OFF + sizeof(Bars);
 };
 
@@ -581,24 +607,48 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
   return __shfl_sync(0xffffffffu, w, 0) != 0;
 }
 
-// operand whose rows (the K index of the MMA) are 128-byte swizzled rows of
-// 64 contiguous M/N elements, slabs of 64 columns CH bytes apart
-__device__ __forceinline__ uint64_t mn_desc(uint32_t base, int ks) {
-  return smem_desc(base + ks * 2048, Layout<64>::CH, 1024);
+// P^T and dS^T of 32 queries (one row of keys) from their scores and dP^T.
+// MASK: causal / sequence-end mask (diagonal and last tiles only).
+template <typename T, bool MASK>
+__device__ __forceinline__ void softmax_bwd_row(const uint32_t (&sv)[32], const uint32_t (&dv)[32],
+                                                const float* wl, const float* wd, float scale_log2,
+                                                int qbase, int kj, int seq, uint32_t (&pk)[16],
+                                                uint32_t (&dk)[16]) {
+  const float4* l4 = reinterpret_cast<const float4*>(wl);
+  const float4* d4 = reinterpret_cast<const float4*>(wd);
+#pragma unroll
+  for (int e4 = 0; e4 < 8; ++e4) {
+    const float4 lv = l4[e4], dl = d4[e4];
+    const float la[4] = {lv.x, lv.y, lv.z, lv.w};
+    const float da[4] = {dl.x, dl.y, dl.z, dl.w};
+    float pp[4], dd[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int c = 4 * e4 + u;
+      float pr = ex2(fmaf(__uint_as_float(sv[c]), scale_log2, -la[u]));
+      if (MASK) {
+        const int qi = qbase + c;
+        pr = (qi >= kj && qi < seq) ? pr : 0.f;
+      }
+      pp[u] = pr;
+      dd[u] = pr * (__uint_as_float(dv[c]) - da[u]);
+    }
+    pk[2 * e4] = pack2<T>(pp[0], pp[1]);
+    pk[2 * e4 + 1] = pack2<T>(pp[2], pp[3]);
+    dk[2 * e4] = pack2<T>(dd[0], dd[1]);
+    dk[2 * e4 + 1] = pack2<T>(dd[2], dd[3]);
+  }
 }
 
-template <typename T, int D>
+template <typename T>
 __global__ void __launch_bounds__(kThreadsB, 1)
-attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                const __grid_constant__ CUtensorMap tm_dq, const Params p) {
-  using L = Layout<D>;
+attn_bwd64_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
+                  const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_dq,
+                  const Params p) {
+  using L = Layout64;
+  constexpr int D = 64;
   constexpr uint32_t TMEM_COLS = 512;
-  // S^T 0-127 (dQ reuses 0-63 once every softmax warp read S^T), dP^T 128-255,
-  // packed P^T 256-319, packed dS^T 320-383, dV 384-447, dK 448-511: the
-  // softmax warps never write columns another warp still reads
-  static_assert(D == 64, "backward tensor-memory layout is for head dim 64");
-  constexpr uint32_t C_S = 0, C_DP = 128, C_P = 256, C_DS = 320, C_DV = 384, C_DK = 448,
-                     C_DQ = 0;
+  constexpr uint32_t C_P = 256, C_DV = 320, C_DK = 384, C_DQ = 448;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -610,22 +660,26 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constan
 
   ATTN_T0(t_cta);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int j = blockIdx.x;
-  const int b = blockIdx.y / p.Hkv, g = blockIdx.y % p.Hkv;
+  // all key blocks j = 0 (the most query tiles) first, then j = 1, ...
+  const int nbh = p.B * p.Hkv;
+  const int j = blockIdx.x / nbh, bh = blockIdx.x % nbh;
+  const int b = bh / p.Hkv, g = bh % p.Hkv;
   const int rep = p.H / p.Hkv;
-  const int n_i = p.n_q - j;
+  const int n_i = 2 * (p.n_q - j);   // 64-row query tiles from the diagonal on (even)
   const int nit = rep * n_i;
   const int row0 = b * p.T;
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&bars->kv_full), 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kStages64; ++s) {
       mbar_init(smem_u32(&bars->qo_full[s]), 1);
       mbar_init(smem_u32(&bars->qo_empty[s]), 1);
     }
-    mbar_init(smem_u32(&bars->st_full), 1);
-    mbar_init(smem_u32(&bars->ds_ready), 8);
-    mbar_init(smem_u32(&bars->mma2_done), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&bars->st_full[s]), 1);
+      mbar_init(smem_u32(&bars->ds_ready[s]), 8);
+      mbar_init(smem_u32(&bars->p_free[s]), 1);
+    }
     mbar_init(smem_u32(&bars->dq_full), 1);
     mbar_init(smem_u32(&bars->dq_free), 4);
     mbar_init(smem_u32(&bars->drain), 1);
@@ -645,168 +699,177 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constan
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ TMA
     const uint32_t kvb = smem_u32(&bars->kv_full);
-    mbar_expect_tx(kvb, 2 * L::TILE);
-#pragma unroll
-    for (int c = 0; c < D / 64; ++c) {
-      tma_load_2d(sbase + L::K_OFF + c * L::CH, &tm_qkv, kvb, p.k_col + g * D + 64 * c,
-                  row0 + j * 128);
-      tma_load_2d(sbase + L::V_OFF + c * L::CH, &tm_qkv, kvb, p.v_col + g * D + 64 * c,
-                  row0 + j * 128);
-    }
-    int pend[2] = {-1, -1};
-    for (int it = 0; it < nit; ++it) {
-      const int st = it & 1;
-      const uint32_t ph = (it >> 1) & 1;
-      const int h = g * rep + it / n_i, i = j + it % n_i;
-      if (!wait_b(smem_u32(&bars->qo_empty[st]), ph ^ 1, abort, p, 41)) break;
-      const uint32_t fb = smem_u32(&bars->qo_full[st]);
-      mbar_expect_tx(fb, 2 * L::TILE);
-#pragma unroll
-      for (int c = 0; c < D / 64; ++c) {
-        tma_load_2d(sbase + L::Q_OFF + st * L::TILE + c * L::CH, &tm_qkv, fb,
-                    p.q_col + h * D + 64 * c, row0 + i * 128);
-        tma_load_2d(sbase + L::DO_OFF + st * L::TILE + c * L::CH, &tm_do, fb, h * D + 64 * c,
-                    row0 + i * 128);
-      }
-      pend[st] = (int)ph;
+    mbar_expect_tx(kvb, 2 * L::KV);
+    tma_load_2d(sbase + L::K_OFF, &tm_kv, kvb, p.k_col + g * D, row0 + j * 128);
+    tma_load_2d(sbase + L::V_OFF, &tm_kv, kvb, p.v_col + g * D, row0 + j * 128);
+    uint32_t used = 0, phases = 0;   // stages loaded, and the phase of each one's last load
+    for (int t = 0; t < nit; ++t) {
+      const int s = t % kStages64;
+      const uint32_t ph = (t / kStages64) & 1;
+      const int h = g * rep + t / n_i, q0 = j * 128 + (t % n_i) * 64;
+      if (!wait_b(smem_u32(&bars->qo_empty[s]), ph ^ 1, abort, p, 41)) break;
+      const uint32_t fb = smem_u32(&bars->qo_full[s]);
+      mbar_expect_tx(fb, 2 * L::QT);
+      tma_load_2d(sbase + L::Q_OFF + s * L::QT, &tm_q, fb, p.q_col + h * D, row0 + q0);
+      tma_load_2d(sbase + L::DO_OFF + s * L::QT, &tm_do, fb, h * D, row0 + q0);
+      used |= 1u << s;
+      phases = (phases & ~(1u << s)) | (ph << s);
     }
     const uint64_t t0 = gtime();
     while (!mbar_try(kvb, 0) && gtime() - t0 < p.timeout_ns) {
     }
-    for (int s = 0; s < 2; ++s)
-      if (pend[s] >= 0)
-        while (!mbar_try(smem_u32(&bars->qo_full[s]), (uint32_t)pend[s]) &&
+    for (int s = 0; s < kStages64; ++s)
+      if (used >> s & 1)
+        while (!mbar_try(smem_u32(&bars->qo_full[s]), (phases >> s) & 1) &&
                gtime() - t0 < p.timeout_ns) {
         }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA
     bool ok = wait_b(smem_u32(&bars->kv_full), 0, abort, p, 42);
-    const uint32_t kb = sbase + L::K_OFF, vb = sbase + L::V_OFF, dsb = sbase + L::DS_OFF;
-    for (int it = 0; it < nit && ok; ++it) {
-      const int st = it & 1;
-      const uint32_t ph = (it >> 1) & 1;
-      ATTN_T0(t_q);
-      if (!wait_b(smem_u32(&bars->qo_full[st]), ph, abort, p, 43)) break;
-      ATTN_ADD(12, t_q);
-      ATTN_T0(t_m2);
-      // S^T / dP^T columns and the dS^T tile are free once the last MMAs
-      // retired, and the S^T columns once the dQ partial there was read
-      if (it > 0 && !wait_b(smem_u32(&bars->mma2_done), (it - 1) & 1, abort, p, 44)) break;
-      ATTN_ADD(13, t_m2);
-      ATTN_T0(t_dqf);
-      if (it > 0 && !wait_b(smem_u32(&bars->dq_free), (it - 1) & 1, abort, p, 46)) break;
-      ATTN_ADD(15, t_dqf);
-      tc_fence_after();
-      const uint32_t qb = sbase + L::Q_OFF + st * L::TILE, ob = sbase + L::DO_OFF + st * L::TILE;
+    const uint32_t kb = sbase + L::K_OFF, vb = sbase + L::V_OFF;
+    // gradient MMAs of tile u, whose softmax is done (and, after a pair's
+    // second tile, the pair's dQ)
+    auto grads = [&](int u) -> bool {
+      const int bu = u & 1, su = u % kStages64;
+      const uint32_t qb = sbase + L::Q_OFF + su * L::QT, ob = sbase + L::DO_OFF + su * L::QT;
+      const uint32_t dsb = sbase + L::DS_OFF + ((u >> 1) & 1) * 2 * L::KV + (u & 1) * L::KV;
 #pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) {
-        const uint64_t dk = kmajor_desc<D>(kb, ks), dv = kmajor_desc<D>(vb, ks);
-        umma_f16(tmem + C_S, dk, kmajor_desc<D>(qb, ks), p.idesc_s, ks > 0 ? 1u : 0u);
-        umma_f16(tmem + C_DP, dv, kmajor_desc<D>(ob, ks), p.idesc_s, ks > 0 ? 1u : 0u);
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint32_t acc = (u > 0 || ks > 0) ? 1u : 0u;
+        umma_f16_ts(tmem + C_DV, tmem + C_P + bu * 32 + ks * 8, mn_desc(ob, ks), p.idesc_kv, acc);
+        umma_f16(tmem + C_DK, k_desc(dsb, ks), mn_desc(qb, ks), p.idesc_kv, acc);
       }
-      umma_commit(smem_u32(&bars->st_full));
-      ATTN_T0(t_ds);
-      if (!wait_b(smem_u32(&bars->ds_ready), it & 1, abort, p, 45)) break;
-      ATTN_ADD(14, t_ds);
-      tc_fence_after();
+      umma_commit(smem_u32(&bars->qo_empty[su]));
+      umma_commit(smem_u32(&bars->p_free[bu]));
+      if (u & 1) {
+        const int pr = u >> 1;
+        ATTN_T0(t_dqf);
+        if (pr > 0 && !wait_b(smem_u32(&bars->dq_free), (pr - 1) & 1, abort, p, 46)) return false;
+        ATTN_ADD(15, t_dqf);
+        tc_fence_after();
+        const uint32_t slot = sbase + L::DS_OFF + (pr & 1) * 2 * L::KV;
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        umma_f16_ts(tmem + C_DV, tmem + C_P + ks * 8, mn_desc(ob, ks), p.idesc_kv,
-                    (it > 0 || ks > 0) ? 1u : 0u);
-        umma_f16_ts(tmem + C_DK, tmem + C_DS + ks * 8, mn_desc(qb, ks), p.idesc_kv,
-                    (it > 0 || ks > 0) ? 1u : 0u);
+        for (int ks = 0; ks < 8; ++ks)
+          umma_f16(tmem + C_DQ, mn_desc(slot, ks), mn_desc(kb, ks), p.idesc_q, ks > 0 ? 1u : 0u);
+        umma_commit(smem_u32(&bars->dq_full));
       }
+      return true;
+    };
+    // step u: once the softmax of tile u-2 is done, its score buffer takes
+    // tile u (issued first, so the softmax warps get their next scores as
+    // early as possible), then tile u-2's gradient MMAs
+    for (int u = 0; u < nit + 2 && ok; ++u) {
+      if (u >= 2) {
+        ATTN_T0(t_ds);
+        if (!wait_b(smem_u32(&bars->ds_ready[u & 1]), ((u - 2) >> 1) & 1, abort, p, 45)) {
+          ok = false;
+          break;
+        }
+        ATTN_ADD(14, t_ds);
+        tc_fence_after();
+      }
+      if (u < nit) {
+        const int bt = u & 1, st = u % kStages64;
+        ATTN_T0(t_q);
+        if (!wait_b(smem_u32(&bars->qo_full[st]), (u / kStages64) & 1, abort, p, 43)) {
+          ok = false;
+          break;
+        }
+        ATTN_ADD(12, t_q);
+        tc_fence_after();
+        const uint32_t qb = sbase + L::Q_OFF + st * L::QT, ob = sbase + L::DO_OFF + st * L::QT;
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks)
-        umma_f16(tmem + C_DQ, mn_desc(dsb, ks), mn_desc(kb, ks), p.idesc_q, ks > 0 ? 1u : 0u);
-      umma_commit(smem_u32(&bars->qo_empty[st]));
-      umma_commit(smem_u32(&bars->mma2_done));
-      umma_commit(smem_u32(&bars->dq_full));
+        for (int ks = 0; ks < 4; ++ks) {
+          umma_f16(tmem + bt * 128, k_desc(kb, ks), k_desc(qb, ks), p.idesc_s, ks > 0 ? 1u : 0u);
+          umma_f16(tmem + bt * 128 + 64, k_desc(vb, ks), k_desc(ob, ks), p.idesc_s,
+                   ks > 0 ? 1u : 0u);
+        }
+        umma_commit(smem_u32(&bars->st_full[bt]));
+      }
+      if (u >= 2 && !grads(u - 2)) ok = false;
     }
     umma_commit(smem_u32(&bars->drain));
     const uint64_t t0 = gtime();
     while (!mbar_try(smem_u32(&bars->drain), 0) && gtime() - t0 < p.timeout_ns) {
     }
   } else if (warp >= 2 && warp < 10) {
-    // --------------------- P^T, dS^T (thread = key, warp = 64 of the queries)
+    // ------------------- P^T, dS^T (thread = key, warp = 32 of the 64 queries)
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const int kj = j * 128 + r;
     const uint32_t lb = tmem + ((uint32_t)(quarter * 32) << 16);
     uint8_t* sdS = smem + L::DS_OFF;
-    // this warp's copy of its 64 queries' lse / delta (no cross-warp barrier:
-    // every wait of these warps stays bounded)
-    float* wLse = sLse + (warp - 2) * 64;
-    float* wDelta = sDelta + (warp - 2) * 64;
-    bool ok = true;
-    for (int it = 0; it < nit; ++it) {
-      const int h = g * rep + it / n_i, i = j + it % n_i;
+    // this warp's copy of its 32 queries' lse / delta, loaded one tile ahead
+    float* wLse = sLse + (warp - 2) * 32;
+    float* wDelta = sDelta + (warp - 2) * 32;
+    auto gload = [&](int t, float& l, float& d) {
+      const int h = g * rep + t / n_i, qi = j * 128 + (t % n_i) * 64 + half * 32 + lane;
       const long long lrow = (long long)(b * p.H + h) * p.T;
+      l = qi < p.T ? p.lse[lrow + qi] : 0.f;
+      d = qi < p.T ? p.delta[lrow + qi] : 0.f;
+    };
+    float gl = 0.f, gd = 0.f;
+    if (nit > 0) gload(0, gl, gd);
+    bool ok = true;
+    for (int t = 0; t < nit; ++t) {
+      const int bt = t & 1, ti = t % n_i;
+      const int qbase = j * 128 + ti * 64 + half * 32;
       __syncwarp();
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int qi = i * 128 + half * 64 + u * 32 + lane;
-        wLse[u * 32 + lane] = qi < p.T ? p.lse[lrow + qi] : 0.f;
-        wDelta[u * 32 + lane] = qi < p.T ? p.delta[lrow + qi] : 0.f;
-      }
+      wLse[lane] = gl;
+      wDelta[lane] = gd;
       __syncwarp();
+      if (t + 1 < nit) gload(t + 1, gl, gd);
       ATTN_T0(t_st);
-      if (!warp_wait(smem_u32(&bars->st_full), it & 1, abort, p, 47, lane)) { ok = false; break; }
+      if (!warp_wait(smem_u32(&bars->st_full[bt]), (t >> 1) & 1, abort, p, 47, lane)) {
+        ok = false;
+        break;
+      }
       if (warp == 2 && lane == 0) ATTN_ADD(10, t_st);
       ATTN_T0(t_sm);
       tc_fence_after();
+      uint32_t sv[32], dv[32];
+      tmem_ld32(lb + bt * 128 + half * 32, sv);
+      tmem_ld32(lb + bt * 128 + 64 + half * 32, dv);
+      tmem_ld_wait();
+      uint32_t pk[16], dk[16];
+      if (ti < 2 || qbase - half * 32 + 64 > p.T)
+        softmax_bwd_row<T, true>(sv, dv, wLse, wDelta, p.scale_log2, qbase, kj, p.T, pk, dk);
+      else
+        softmax_bwd_row<T, false>(sv, dv, wLse, wDelta, p.scale_log2, qbase, kj, p.T, pk, dk);
+      // P^T columns of buffer bt and the dS^T slab of tile t are free once the
+      // gradient MMAs of tile t-2 retired (and with them the dQ MMA of the
+      // pair that last used the slab)
+      if (t >= 2 && !warp_wait(smem_u32(&bars->p_free[bt]), ((t - 2) >> 1) & 1, abort, p, 50,
+                               lane)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      tmem_st16(lb + C_P + bt * 32 + half * 16, pk);
+      // dS^T row r, queries half*32 .. +31 of the tile: 16-byte pieces 4*half .. 4*half+3
+      uint8_t* rowp = sdS + (((t >> 1) & 1) * 2 + (t & 1)) * L::KV + r * 128;
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c = half * 2 + cc;                  // 32-query chunk of the tile
-        uint32_t sv[32], dv[32];
-        tmem_ld32(lb + C_S + c * 32, sv);
-        tmem_ld32(lb + C_DP + c * 32, dv);
-        tmem_ld_wait();
-        uint32_t pk[16], dk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float pp[2], dd[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int col = cc * 32 + 2 * e + u;       // within this warp's 64 queries
-            const int qi = i * 128 + half * 64 + col;
-            const bool vis = qi >= kj && qi < p.T;
-            const float pr =
-                vis ? ex2(fmaf(__uint_as_float(sv[2 * e + u]), p.scale_log2, -wLse[col])) : 0.f;
-            pp[u] = pr;
-            dd[u] = pr * (__uint_as_float(dv[2 * e + u]) - wDelta[col]);
-          }
-          pk[e] = pack2<T>(pp[0], pp[1]);
-          dk[e] = pack2<T>(dd[0], dd[1]);
-        }
-        tmem_st16(lb + C_P + c * 16, pk);
-        tmem_st16(lb + C_DS + c * 16, dk);
-        // dS^T row r, queries c*32..c*32+31: 64-column slab c/2, 16-byte pieces 4*(c&1)..+3
-        uint8_t* rowp = sdS + (c >> 1) * L::CH + r * 128;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int piece = ((c & 1) * 4 + u) ^ (r & 7);
-          *reinterpret_cast<uint4*>(rowp + piece * 16) =
-              make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
-        }
+      for (int u = 0; u < 4; ++u) {
+        const int piece = (half * 4 + u) ^ (r & 7);
+        *reinterpret_cast<uint4*>(rowp + piece * 16) =
+            make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
       }
       tmem_st_wait();
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&bars->ds_ready));
+      if (lane == 0) mbar_arrive(smem_u32(&bars->ds_ready[bt]));
       if (warp == 2 && lane == 0) ATTN_ADD(11, t_sm);
     }
-    // dK (times the softmax scale) and dV of this key tile: each warp of a
-    // quarter stores one of them
-    if (ok && nit > 0 && warp_wait(smem_u32(&bars->mma2_done), (nit - 1) & 1, abort, p, 48, lane)) {
+    // dK (times the softmax scale) and dV of this key block: the warps of
+    // half 0 store dK, those of half 1 dV
+    if (ok && nit > 0 && warp_wait(smem_u32(&bars->drain), 0, abort, p, 48, lane)) {
       tc_fence_after();
       T* drow = static_cast<T*>(p.dqkv) + (long long)(row0 + kj) * p.ld_dqkv;
-      const int which = half;
-      const uint32_t col0 = which == 0 ? C_DK : C_DV;
-      const float f = which == 0 ? p.scale : 1.f;
-      T* dst = drow + (which == 0 ? p.k_col : p.v_col) + g * D;
+      const uint32_t col0 = half == 0 ? C_DK : C_DV;
+      const float f = half == 0 ? p.scale : 1.f;
+      T* dst = drow + (half == 0 ? p.k_col : p.v_col) + g * D;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t v[32];
@@ -827,14 +890,15 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constan
       }
     }
   } else if (warp >= 10) {
-    // ------------------------------------- dQ partial -> fp32 accumulator
+    // ------------------------------------- dQ of a tile pair -> fp32 accumulator
     const int quarter = warp & 3;
     const uint32_t lb = tmem + ((uint32_t)(quarter * 32) << 16);
     uint8_t* stg = smem + L::STG_OFF + (warp - 10) * L::STG_WARP;
-    for (int it = 0; it < nit; ++it) {
-      const int h = g * rep + it / n_i, i = j + it % n_i;
+    for (int pr = 0; pr < nit / 2; ++pr) {
+      const int t = 2 * pr;
+      const int h = g * rep + t / n_i, q0 = j * 128 + (t % n_i) * 64;
       ATTN_T0(t_dq);
-      if (!warp_wait(smem_u32(&bars->dq_full), it & 1, abort, p, 49, lane)) break;
+      if (!warp_wait(smem_u32(&bars->dq_full), pr & 1, abort, p, 49, lane)) break;
       if (warp == 10 && lane == 0) ATTN_ADD(16, t_dq);
       ATTN_T0(t_dqe);
       tc_fence_after();
@@ -871,7 +935,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constan
 #pragma unroll
         for (int c = 0; c < D / 32; ++c)
           tma_reduce_add_2d(&tm_dq, smem_u32(stg + c * 4096), h * D + 32 * c,
-                            row0 + i * 128 + quarter * 32);
+                            row0 + q0 + quarter * 32);
         bulk_commit();
       }
     }
@@ -939,19 +1003,18 @@ attn_dq_convert_kernel(const float* __restrict__ dq_acc, int BT, int HD, T* __re
   }
 }
 
-template <typename T, int D>
-void launch_bwd(const CUtensorMap& tq, const CUtensorMap& td, const CUtensorMap& tdq,
-                const Params& p, cudaStream_t st) {
-  auto kern = attn_bwd_kernel<T, D>;
+template <typename T>
+void launch_bwd64(const CUtensorMap& tkv, const CUtensorMap& tq, const CUtensorMap& td,
+                  const CUtensorMap& tdq, const Params& p, cudaStream_t st) {
+  auto kern = attn_bwd64_kernel<T>;
   static bool attr = false;
   if (!attr) {
     check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)Layout<D>::BYTES),
+                                    (int)Layout64::BYTES),
                "attn bwd smem attribute");
     attr = true;
   }
-  dim3 grid(p.n_q, p.B * p.Hkv);
-  kern<<<grid, kThreadsB, Layout<D>::BYTES, st>>>(tq, td, tdq, p);
+  kern<<<p.n_q * p.B * p.Hkv, kThreadsB, Layout64::BYTES, st>>>(tkv, tq, td, tdq, p);
 }
 
 
@@ -1381,7 +1444,8 @@ void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
   p.scale_log2 = scale * 1.4426950408889634f;
   p.n_q = (T + 127) / 128;
   const uint32_t fmt = dtype == kBF16 ? 1u : 0u;
-  p.idesc_s = (1u << 4) | (fmt << 7) | (fmt << 10) | (16u << 17) | (8u << 24);
+  // S^T = K Q^T, dP^T = V dO^T: N = 128 queries (head dim 128), 64 (head dim 64)
+  p.idesc_s = (1u << 4) | (fmt << 7) | (fmt << 10) | ((D == 128 ? 16u : 8u) << 17) | (8u << 24);
   p.idesc_kv = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) | ((uint32_t)(D >> 3) << 17) |
                (8u << 24);
   // dQ = dS K: N = D (head dim 128: two N = 64 halves)
@@ -1392,6 +1456,8 @@ void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
   p.timeout_ns = static_cast<unsigned long long>(timeout_s * 1e9);
   const CUtensorMap tq = make_map(qkv, dtype, n_cols, (long long)BT, ld_qkv, 64, 128);
   const CUtensorMap td = make_map(dout, dtype, (long long)H * D, (long long)BT, ld_do, 64, 128);
+  const CUtensorMap tq64 = make_map(qkv, dtype, n_cols, (long long)BT, ld_qkv, 64, 64);
+  const CUtensorMap td64 = make_map(dout, dtype, (long long)H * D, (long long)BT, ld_do, 64, 64);
   const CUtensorMap tdq = make_map_f32(dq_acc, (long long)H * D, (long long)BT, (long long)H * D,
                                        32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
   auto run = [&](auto tag) {
@@ -1404,7 +1470,7 @@ void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
       attn_delta_kernel<T, 128><<<blocks, 256, 0, st>>>(static_cast<const T*>(dout), ld_do,
                                                         static_cast<const T*>(out), ld_out, delta,
                                                         dq_acc, BT, T_seq, H);
-    if (D == 64) launch_bwd<T, 64>(tq, td, tdq, p, st);
+    if (D == 64) launch_bwd64<T>(tq, tq64, td64, tdq, p, st);
     else launch_bwd128<T>(tq, td, tdq, p, st);
     attn_dq_convert_kernel<T><<<blocks_c, 256, 0, st>>>(dq_acc, BT, H * D, static_cast<T*>(dqkv),
                                                         ld_dqkv, q_col, scale);
