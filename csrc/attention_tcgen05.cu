@@ -103,7 +103,7 @@ __device__ __forceinline__ bool wait_b(uint32_t bar, uint32_t parity, volatile i
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = gtime();
   while (true) {
-    if (mbar_try(bar, parity)) return true;
+    if (mbar_try_for(bar, parity, 1000000u)) return true;
     if (*abort) return false;
     if (gtime() - t0 > p.timeout_ns) {
       *abort = 1;
@@ -147,6 +147,45 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// explicit shared-memory accesses (a pointer that went through the CTA's
+// alignment round-up is generic to the compiler, and generic accesses wait
+// on the long scoreboard)
+__device__ __forceinline__ float4 lds_f4(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void sts_u4(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+__device__ __forceinline__ void sts_f(uint32_t a, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+
+#ifndef MSB_EXP2_POLY
+#define MSB_EXP2_POLY 0   // of every 4 backward exponentials, how many use exp2_poly
+#endif
+
+// 2^x on the FMA and integer pipes (the special-function unit that ex2 uses
+// is the softmax's bottleneck).  Range reduction x = n + f, n = rint(x),
+// f in [-1/2, 1/2]: adding 1.5 * 2^23 leaves rint(x) in the low mantissa
+// bits.  2^f is a degree-3 polynomial whose coefficients minimise the maximum
+// relative error on [-1/2, 1/2] (a linear program over 4001 points):
+// 7.5e-5, below half an fp16 ulp.  n is added to the exponent field; x is
+// clamped at -125 so the result stays a normal number.
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  float q = fmaf(0.05517222f, f, 0.24261115f);
+  q = fmaf(q, f, 0.69326085f);
+  q = fmaf(q, f, 0.99992806f);
+  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
 }
 
 // One CTA: query tiles 2c and 2c+1 of one (batch, head).  The MMA warp
@@ -524,6 +563,7 @@ struct Params {
   const float* delta;
   float scale_log2, scale;
   int n_q;
+  int rep, nbh;          // H / Hkv, B * Hkv
   uint32_t idesc_s, idesc_kv, idesc_q;
   unsigned* err;
   unsigned long long timeout_ns;
@@ -540,32 +580,40 @@ __device__ __forceinline__ uint64_t k_desc(uint32_t base, int ks) {
 }
 
 // ---------------------------------------------------------------- head dim 64
-// One CTA: one 128-key block j of one (batch, kv head); it walks the 64-row
-// query tiles from the diagonal down, for every query head that shares the kv
-// head.  Per query tile t (score buffer b = t & 1):
-//   S^T = K Q_t^T, dP^T = V dO_t^T       M = 128 keys, N = 64 queries -> buffer b
+// Persistent: one CTA per SM walks work items w = blockIdx.x, + gridDim.x, ...
+// An item is one 128-key block j of one (batch, kv head); items are ordered
+// by key block, so the ones with the most query tiles come first.  Per item
+// the CTA walks the 64-row query tiles from the diagonal down, for every
+// query head that shares the kv head.  Per query tile t (score buffer t & 1):
+//   S^T = K Q_t^T, dP^T = V dO_t^T       M = 128 keys, N = 64 queries -> buffer
 //   softmax warps: P^T = exp2(S^T * scale_log2 - lse), dS^T = P^T (dP^T - delta);
 //                  P^T -> tensor memory (packed 16-bit), dS^T -> shared memory
 //   dV += P^T dO_t (A from tensor memory), dK += dS^T Q_t (A from shared memory)
 //   every second tile: dQ = dS K over the pair's 128 queries (M = 128), read
 //                  out by the dQ warps and reduce-added into an fp32 buffer
-// The MMA warp issues tile t+1's scores before tile t's gradient MMAs, so the
-// tensor core works on one tile while the softmax warps work on the other.
+// The MMA warp issues tile t+2's scores as soon as the softmax of tile t is
+// done, then tile t's gradient MMAs, so the tensor core works on one tile
+// while the softmax warps work on the other.  Tiles are numbered across the
+// CTA's items, so the next item's K/V loads and first scores overlap the end
+// of the current one; K/V are double-buffered, dK/dV are read out of tensor
+// memory by the softmax warps after an item's last tile.
 // Tensor memory (512 columns): S^T 0/128, dP^T 64/192 (buffer 0/1), P^T
 // 256/288, dV 320, dK 384, dQ 448.
 // Warps: 0 TMA, 1 MMA, 2-9 softmax (thread = key row, warp = 32 queries),
 // 10-13 dQ read-out (thread = query row).
 constexpr int kThreadsB = 448;
-constexpr int kStages64 = 4;   // Q / dO tiles in flight
+constexpr int kStages64 = 5;   // Q / dO tiles in flight
 
 struct alignas(8) Bars {
-  uint64_t kv_full;
+  uint64_t kv_full[2], kv_empty[2];
   uint64_t qo_full[kStages64], qo_empty[kStages64];
   uint64_t st_full[2];   // scores of a tile in buffer b
   uint64_t ds_ready[2];  // softmax of a tile done: P^T / dS^T written, buffer b read (8 warps)
   uint64_t p_free[2];    // gradient MMAs of a tile retired (and every MMA before them)
   uint64_t dq_full;      // dQ of a tile pair in tensor memory
   uint64_t dq_free;      // dQ read out (4 warps)
+  uint64_t acc_full;     // dK / dV of an item complete
+  uint64_t acc_free;     // dK / dV read out (8 warps)
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -574,17 +622,17 @@ struct alignas(8) Bars {
 struct Layout64 {
   static constexpr int KV = 128 * 128;   // 128 rows x 128 bytes
   static constexpr int QT = 64 * 128;    // 64 rows x 128 bytes
-  static constexpr int K_OFF = 0;
-  static constexpr int V_OFF = KV;
-  static constexpr int Q_OFF = 2 * KV;
+  static constexpr int KV_OFF = 0;                          // 2 buffers x (K, V)
+  static constexpr int Q_OFF = 4 * KV;
   static constexpr int DO_OFF = Q_OFF + kStages64 * QT;
   static constexpr int DS_OFF = DO_OFF + kStages64 * QT;   // 2 pair slots x 2 tiles x [128 keys][64 q]
-  static constexpr int STG_OFF = DS_OFF + 4 * KV;          // dQ staging: 4 warps x 32 rows x 64 fp32
-  static constexpr int STG_WARP = 32 * 64 * 4;
+  static constexpr int STG_OFF = DS_OFF + 4 * KV;          // dQ staging: 4 warps x 32 rows x 16 fp32
+  static constexpr int STG_WARP = 32 * 16 * 4;
   static constexpr int LSE_OFF = STG_OFF + 4 * STG_WARP;   // 8 softmax warps x 32 floats
   static constexpr int DELTA_OFF = LSE_OFF + 8 * 128;
   static constexpr int BARS_OFF = DELTA_OFF + 8 * 128;
   static constexpr size_t BYTES = 1024 + BARS_OFF + sizeof(Bars);
+  static_assert(BYTES <= 227 * 1024, "shared memory");
 };
 
 __device__ __forceinline__ bool wait_b(uint32_t bar, uint32_t parity, volatile int* abort,
@@ -592,7 +640,7 @@ __device__ __forceinline__ bool wait_b(uint32_t bar, uint32_t parity, volatile i
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = gtime();
   while (true) {
-    if (mbar_try(bar, parity)) return true;
+    if (mbar_try_for(bar, parity, 1000000u)) return true;
     if (*abort) return false;
     if (gtime() - t0 > p.timeout_ns) {
       *abort = 1;
@@ -607,25 +655,90 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
   return __shfl_sync(0xffffffffu, w, 0) != 0;
 }
 
+// A CTA's position in its sequence of work items and their query tiles
+// (counters only: no divisions per tile).
+struct Cursor {
+  int k;      // item ordinal within the CTA
+  int j, b, g;
+  int n_i;    // 64-row query tiles per query head (even)
+  int nit;    // query tiles of the item (all heads of the group)
+  int t;      // tile within the item
+  int ti, hh; // t = hh * n_i + ti
+  bool valid;
+  __device__ __forceinline__ void load(const Params& p) {
+    const int w = blockIdx.x + k * gridDim.x;
+    valid = w < p.n_q * p.nbh;
+    t = ti = hh = 0;
+    if (!valid) return;
+    j = w / p.nbh;
+    const int bh = w - j * p.nbh;
+    b = bh / p.Hkv;
+    g = bh - b * p.Hkv;
+    n_i = 2 * (p.n_q - j);
+    nit = p.rep * n_i;
+  }
+  __device__ __forceinline__ void start(const Params& p) {
+    k = 0;
+    load(p);
+  }
+  __device__ __forceinline__ void next(const Params& p) {
+    ++t;
+    if (++ti == n_i) {
+      ti = 0;
+      ++hh;
+    }
+    if (t == nit) {
+      ++k;
+      load(p);
+    }
+  }
+  __device__ __forceinline__ int head(const Params& p) const { return g * p.rep + hh; }
+  __device__ __forceinline__ int q0() const { return j * 128 + ti * 64; }
+};
+
+// slot and phase of a kStages64-deep ring
+struct Ring {
+  int s = 0;
+  uint32_t ph = 0;
+  __device__ __forceinline__ void next() {
+    if (++s == kStages64) {
+      s = 0;
+      ph ^= 1;
+    }
+  }
+};
+
+__device__ __forceinline__ int cta_tiles(const Params& p) {
+  Cursor c;
+  c.start(p);
+  int n = 0;
+  while (c.valid) {
+    n += c.nit;
+    ++c.k;
+    c.load(p);
+  }
+  return n;
+}
+
 // P^T and dS^T of 32 queries (one row of keys) from their scores and dP^T.
 // MASK: causal / sequence-end mask (diagonal and last tiles only).
 template <typename T, bool MASK>
 __device__ __forceinline__ void softmax_bwd_row(const uint32_t (&sv)[32], const uint32_t (&dv)[32],
-                                                const float* wl, const float* wd, float scale_log2,
+                                                uint32_t wl, uint32_t wd, float scale_log2,
                                                 int qbase, int kj, int seq, uint32_t (&pk)[16],
                                                 uint32_t (&dk)[16]) {
-  const float4* l4 = reinterpret_cast<const float4*>(wl);
-  const float4* d4 = reinterpret_cast<const float4*>(wd);
 #pragma unroll
   for (int e4 = 0; e4 < 8; ++e4) {
-    const float4 lv = l4[e4], dl = d4[e4];
+    const float4 lv = lds_f4(wl + e4 * 16), dl = lds_f4(wd + e4 * 16);
     const float la[4] = {lv.x, lv.y, lv.z, lv.w};
     const float da[4] = {dl.x, dl.y, dl.z, dl.w};
     float pp[4], dd[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int c = 4 * e4 + u;
-      float pr = ex2(fmaf(__uint_as_float(sv[c]), scale_log2, -la[u]));
+      // half of the exponentials on the special-function unit, half on the FMA pipe
+      const float x = fmaf(__uint_as_float(sv[c]), scale_log2, -la[u]);
+      float pr = u < 4 - MSB_EXP2_POLY ? ex2(x) : exp2_poly(x);
       if (MASK) {
         const int qi = qbase + c;
         pr = (qi >= kj && qi < seq) ? pr : 0.f;
@@ -660,28 +773,24 @@ attn_bwd64_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_consta
 
   ATTN_T0(t_cta);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // all key blocks j = 0 (the most query tiles) first, then j = 1, ...
-  const int nbh = p.B * p.Hkv;
-  const int j = blockIdx.x / nbh, bh = blockIdx.x % nbh;
-  const int b = bh / p.Hkv, g = bh % p.Hkv;
-  const int rep = p.H / p.Hkv;
-  const int n_i = 2 * (p.n_q - j);   // 64-row query tiles from the diagonal on (even)
-  const int nit = rep * n_i;
-  const int row0 = b * p.T;
+  const int total = cta_tiles(p);   // query tiles over all of this CTA's items (even)
 
   if (threadIdx.x == 0) {
-    mbar_init(smem_u32(&bars->kv_full), 1);
-    for (int s = 0; s < kStages64; ++s) {
-      mbar_init(smem_u32(&bars->qo_full[s]), 1);
-      mbar_init(smem_u32(&bars->qo_empty[s]), 1);
-    }
     for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&bars->kv_full[s]), 1);
+      mbar_init(smem_u32(&bars->kv_empty[s]), 1);
       mbar_init(smem_u32(&bars->st_full[s]), 1);
       mbar_init(smem_u32(&bars->ds_ready[s]), 8);
       mbar_init(smem_u32(&bars->p_free[s]), 1);
     }
+    for (int s = 0; s < kStages64; ++s) {
+      mbar_init(smem_u32(&bars->qo_full[s]), 1);
+      mbar_init(smem_u32(&bars->qo_empty[s]), 1);
+    }
     mbar_init(smem_u32(&bars->dq_full), 1);
     mbar_init(smem_u32(&bars->dq_free), 4);
+    mbar_init(smem_u32(&bars->acc_full), 1);
+    mbar_init(smem_u32(&bars->acc_free), 8);
     mbar_init(smem_u32(&bars->drain), 1);
     bars->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -698,97 +807,198 @@ attn_bwd64_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_consta
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ TMA
-    const uint32_t kvb = smem_u32(&bars->kv_full);
-    mbar_expect_tx(kvb, 2 * L::KV);
-    tma_load_2d(sbase + L::K_OFF, &tm_kv, kvb, p.k_col + g * D, row0 + j * 128);
-    tma_load_2d(sbase + L::V_OFF, &tm_kv, kvb, p.v_col + g * D, row0 + j * 128);
-    uint32_t used = 0, phases = 0;   // stages loaded, and the phase of each one's last load
-    for (int t = 0; t < nit; ++t) {
-      const int s = t % kStages64;
-      const uint32_t ph = (t / kStages64) & 1;
-      const int h = g * rep + t / n_i, q0 = j * 128 + (t % n_i) * 64;
-      if (!wait_b(smem_u32(&bars->qo_empty[s]), ph ^ 1, abort, p, 41)) break;
-      const uint32_t fb = smem_u32(&bars->qo_full[s]);
-      mbar_expect_tx(fb, 2 * L::QT);
-      tma_load_2d(sbase + L::Q_OFF + s * L::QT, &tm_q, fb, p.q_col + h * D, row0 + q0);
-      tma_load_2d(sbase + L::DO_OFF + s * L::QT, &tm_do, fb, h * D, row0 + q0);
-      used |= 1u << s;
-      phases = (phases & ~(1u << s)) | (ph << s);
-    }
-    const uint64_t t0 = gtime();
-    while (!mbar_try(kvb, 0) && gtime() - t0 < p.timeout_ns) {
-    }
-    for (int s = 0; s < kStages64; ++s)
-      if (used >> s & 1)
-        while (!mbar_try(smem_u32(&bars->qo_full[s]), (phases >> s) & 1) &&
-               gtime() - t0 < p.timeout_ns) {
+    Cursor c, kc;   // next tile to load; next item whose K / V to load
+    c.start(p);
+    kc.start(p);
+    uint32_t used = 0, phases = 0;   // buffers loaded, and the phase of each one's last load
+    Ring ring;
+    // K and V of item kc into buffer kc.k & 1 once the item two back is done
+    // with it (wait: block until then; otherwise return if it is still busy)
+    auto load_kv = [&](bool wait) -> bool {
+      const int kb = kc.k & 1;
+      const uint32_t eb = smem_u32(&bars->kv_empty[kb]), par = ((kc.k - 2) >> 1) & 1;
+      if (kc.k >= 2) {
+        if (wait) {
+          if (!wait_b(eb, par, abort, p, 40)) return false;
+        } else if (!mbar_test(eb, par)) {
+          return true;
         }
-  } else if (warp == 1 && lane == 0) {
-    // ------------------------------------------------------------ MMA
-    bool ok = wait_b(smem_u32(&bars->kv_full), 0, abort, p, 42);
-    const uint32_t kb = sbase + L::K_OFF, vb = sbase + L::V_OFF;
-    // gradient MMAs of tile u, whose softmax is done (and, after a pair's
-    // second tile, the pair's dQ)
-    auto grads = [&](int u) -> bool {
-      const int bu = u & 1, su = u % kStages64;
-      const uint32_t qb = sbase + L::Q_OFF + su * L::QT, ob = sbase + L::DO_OFF + su * L::QT;
-      const uint32_t dsb = sbase + L::DS_OFF + ((u >> 1) & 1) * 2 * L::KV + (u & 1) * L::KV;
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const uint32_t acc = (u > 0 || ks > 0) ? 1u : 0u;
-        umma_f16_ts(tmem + C_DV, tmem + C_P + bu * 32 + ks * 8, mn_desc(ob, ks), p.idesc_kv, acc);
-        umma_f16(tmem + C_DK, k_desc(dsb, ks), mn_desc(qb, ks), p.idesc_kv, acc);
       }
-      umma_commit(smem_u32(&bars->qo_empty[su]));
-      umma_commit(smem_u32(&bars->p_free[bu]));
-      if (u & 1) {
-        const int pr = u >> 1;
-        ATTN_T0(t_dqf);
-        if (pr > 0 && !wait_b(smem_u32(&bars->dq_free), (pr - 1) & 1, abort, p, 46)) return false;
-        ATTN_ADD(15, t_dqf);
-        tc_fence_after();
-        const uint32_t slot = sbase + L::DS_OFF + (pr & 1) * 2 * L::KV;
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          umma_f16(tmem + C_DQ, mn_desc(slot, ks), mn_desc(kb, ks), p.idesc_q, ks > 0 ? 1u : 0u);
-        umma_commit(smem_u32(&bars->dq_full));
-      }
+      const uint32_t fb = smem_u32(&bars->kv_full[kb]);
+      const int row = kc.b * p.T + kc.j * 128;
+      mbar_expect_tx(fb, 2 * L::KV);
+      tma_load_2d(sbase + L::KV_OFF + kb * 2 * L::KV, &tm_kv, fb, p.k_col + kc.g * D, row);
+      tma_load_2d(sbase + L::KV_OFF + kb * 2 * L::KV + L::KV, &tm_kv, fb, p.v_col + kc.g * D, row);
+      used |= 1u << (kStages64 + kb);
+      phases = (phases & ~(1u << (kStages64 + kb))) | ((uint32_t)((kc.k >> 1) & 1) << (kStages64 + kb));
+      ++kc.k;
+      kc.load(p);
       return true;
     };
+    bool ok = true;
+    for (int t = 0; t < total && ok; ++t, c.next(p)) {
+      if (kc.valid && kc.k <= c.k && !load_kv(true)) break;   // this item's K / V
+      const int s = ring.s;
+      const uint32_t ph = ring.ph;
+      ring.next();
+      const uint32_t eb = smem_u32(&bars->qo_empty[s]);
+      // while the ring slot is busy, load the next item's K / V if its buffer frees
+      const uint64_t t0 = gtime();
+      while (!mbar_try_for(eb, ph ^ 1, 2000u)) {
+        if (kc.valid && kc.k == c.k + 1 && !load_kv(false)) ok = false;
+        if (!ok || *abort) {
+          ok = false;
+          break;
+        }
+        if (gtime() - t0 > p.timeout_ns) {
+          *abort = 1;
+          atomicCAS(p.err, 0u, 41u);
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) break;
+      const uint32_t fb = smem_u32(&bars->qo_full[s]);
+      const int row = c.b * p.T + c.q0(), h = c.head(p);
+      mbar_expect_tx(fb, 2 * L::QT);
+      tma_load_2d(sbase + L::Q_OFF + s * L::QT, &tm_q, fb, p.q_col + h * D, row);
+      tma_load_2d(sbase + L::DO_OFF + s * L::QT, &tm_do, fb, h * D, row);
+      used |= 1u << s;
+      phases = (phases & ~(1u << s)) | (ph << s);
+      if (kc.valid && kc.k == c.k + 1) load_kv(false);
+    }
+    // let every load this warp issued land before the CTA exits
+    const uint64_t t0 = gtime();
+    for (int s = 0; s < kStages64 + 2; ++s) {
+      if (!(used >> s & 1)) continue;
+      const uint32_t bar = s < kStages64 ? smem_u32(&bars->qo_full[s])
+                                         : smem_u32(&bars->kv_full[s - kStages64]);
+      while (!mbar_try(bar, (phases >> s) & 1) && gtime() - t0 < p.timeout_ns) {
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA
+    // The whole warp runs this loop (waits, descriptors, cursors) and issues
+    // through the warp-wide umma_*_w forms (one elected lane issues).
+    const bool issuer = lane == 0;
+    bool ok = true;
+    Cursor sc, gc;   // the tile whose scores are issued next; whose gradients are issued next
+    Ring rs, rg;     // their Q / dO ring slots
+    // operand descriptors built once: a buffer or k-step offset adds to the
+    // start-address field (16-byte units: a 128 x 128-byte tile is 1024, a
+    // K-major k-step 2, an MN-major k-step 128)
+    const uint64_t kd_kv = k_desc(sbase + L::KV_OFF, 0), md_kv = mn_desc(sbase + L::KV_OFF, 0);
+    const uint64_t kd_q = k_desc(sbase + L::Q_OFF, 0), md_q = mn_desc(sbase + L::Q_OFF, 0);
+    const uint64_t kd_o = k_desc(sbase + L::DO_OFF, 0), md_o = mn_desc(sbase + L::DO_OFF, 0);
+    const uint64_t kd_s = k_desc(sbase + L::DS_OFF, 0), md_s = mn_desc(sbase + L::DS_OFF, 0);
+    constexpr uint32_t U_KV = L::KV / 16, U_QT = L::QT / 16;
+    sc.start(p);
+    gc.start(p);
+    // gradient MMAs of global tile v (cursor gc), whose softmax is done (and,
+    // after a pair's second tile, the pair's dQ; after an item's last tile,
+    // its dK / dV and K / V buffers are released)
+    auto grads = [&](int v) -> bool {
+      const int bv = v & 1, sv = rg.s, kvb = gc.k & 1;
+      rg.next();
+      if (gc.t == 0 && gc.k > 0 &&
+          !warp_wait(smem_u32(&bars->acc_free), (gc.k - 1) & 1, abort, p, 44, lane))
+        return false;
+      tc_fence_after();
+      ATTN_T0(t_g1);
+      const uint64_t b_o = md_o + sv * U_QT, b_q = md_q + sv * U_QT;
+      const uint64_t a_ds = kd_s + (((v >> 1) & 1) * 2 + (v & 1)) * U_KV;
+      const uint32_t first = gc.t == 0 ? 0u : 1u;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint32_t acc = ks > 0 ? 1u : first;
+        umma_f16_ts_w(tmem + C_DV, tmem + C_P + bv * 32 + ks * 8, b_o + 128 * ks, p.idesc_kv, acc);
+        umma_f16_w(tmem + C_DK, a_ds + 2 * ks, b_q + 128 * ks, p.idesc_kv, acc);
+      }
+      umma_commit_w(smem_u32(&bars->qo_empty[sv]));
+      umma_commit_w(smem_u32(&bars->p_free[bv]));
+      if (issuer) ATTN_ADD(25, t_g1);
+      if (v & 1) {
+        const int pr = v >> 1;
+        ATTN_T0(t_dqf);
+        if (pr > 0 && !warp_wait(smem_u32(&bars->dq_free), (pr - 1) & 1, abort, p, 46, lane))
+          return false;
+        if (issuer) ATTN_ADD(15, t_dqf);
+        tc_fence_after();
+        ATTN_T0(t_g2);
+        const uint64_t a_s = md_s + (pr & 1) * 2 * U_KV, b_k = md_kv + kvb * 2 * U_KV;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma_f16_w(tmem + C_DQ, a_s + 128 * ks, b_k + 128 * ks, p.idesc_q, ks > 0 ? 1u : 0u);
+        umma_commit_w(smem_u32(&bars->dq_full));
+        if (issuer) ATTN_ADD(26, t_g2);
+      }
+      if (gc.t == gc.nit - 1) {
+        umma_commit_w(smem_u32(&bars->acc_full));
+        umma_commit_w(smem_u32(&bars->kv_empty[kvb]));
+      }
+      gc.next(p);
+      return true;
+    };
+    // S^T and dP^T of global tile u (cursor sc) into buffer u & 1
+    auto issue_s = [&](int u) {
+      ATTN_T0(t_is);
+      const int bt = u & 1, st = rs.s, kvb = sc.k & 1;
+      rs.next();
+      const uint64_t a_k = kd_kv + kvb * 2 * U_KV, a_v = a_k + U_KV;
+      const uint64_t b_q = kd_q + st * U_QT, b_o = kd_o + st * U_QT;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        umma_f16_w(tmem + bt * 128, a_k + 2 * ks, b_q + 2 * ks, p.idesc_s, ks > 0 ? 1u : 0u);
+        umma_f16_w(tmem + bt * 128 + 64, a_v + 2 * ks, b_o + 2 * ks, p.idesc_s, ks > 0 ? 1u : 0u);
+      }
+      umma_commit_w(smem_u32(&bars->st_full[bt]));
+      if (issuer) ATTN_ADD(24, t_is);
+      sc.next(p);
+    };
+    // non-blocking probe, the same answer in every lane
+    auto ready = [&](uint32_t bar, uint32_t parity) -> bool {
+      const int r = issuer ? (mbar_test(bar, parity) ? 1 : 0) : 0;
+      return __shfl_sync(0xffffffffu, r, 0) != 0;
+    };
     // step u: once the softmax of tile u-2 is done, its score buffer takes
-    // tile u (issued first, so the softmax warps get their next scores as
-    // early as possible), then tile u-2's gradient MMAs
-    for (int u = 0; u < nit + 2 && ok; ++u) {
+    // tile u, and tile u-2's gradient MMAs are issued
+    for (int u = 0; u < total + 2 && ok; ++u) {
       if (u >= 2) {
         ATTN_T0(t_ds);
-        if (!wait_b(smem_u32(&bars->ds_ready[u & 1]), ((u - 2) >> 1) & 1, abort, p, 45)) {
+        if (!warp_wait(smem_u32(&bars->ds_ready[u & 1]), ((u - 2) >> 1) & 1, abort, p, 45, lane)) {
           ok = false;
           break;
         }
-        ATTN_ADD(14, t_ds);
+        if (issuer) ATTN_ADD(14, t_ds);
         tc_fence_after();
       }
-      if (u < nit) {
-        const int bt = u & 1, st = u % kStages64;
+      // tile u's scores go first when its K / V and Q / dO are in; otherwise
+      // tile u-2's gradient MMAs go first and the scores follow
+      bool pend = u < total;
+      if (pend && (sc.t > 0 || ready(smem_u32(&bars->kv_full[sc.k & 1]), (sc.k >> 1) & 1)) &&
+          ready(smem_u32(&bars->qo_full[rs.s]), rs.ph)) {
+        tc_fence_after();
+        issue_s(u);
+        pend = false;
+      }
+      if (u >= 2 && !grads(u - 2)) {
+        ok = false;
+        break;
+      }
+      if (pend) {
         ATTN_T0(t_q);
-        if (!wait_b(smem_u32(&bars->qo_full[st]), (u / kStages64) & 1, abort, p, 43)) {
+        if ((sc.t == 0 && !warp_wait(smem_u32(&bars->kv_full[sc.k & 1]), (sc.k >> 1) & 1, abort,
+                                     p, 42, lane)) ||
+            !warp_wait(smem_u32(&bars->qo_full[rs.s]), rs.ph, abort, p, 43, lane)) {
           ok = false;
           break;
         }
-        ATTN_ADD(12, t_q);
+        if (issuer) ATTN_ADD(12, t_q);
         tc_fence_after();
-        const uint32_t qb = sbase + L::Q_OFF + st * L::QT, ob = sbase + L::DO_OFF + st * L::QT;
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          umma_f16(tmem + bt * 128, k_desc(kb, ks), k_desc(qb, ks), p.idesc_s, ks > 0 ? 1u : 0u);
-          umma_f16(tmem + bt * 128 + 64, k_desc(vb, ks), k_desc(ob, ks), p.idesc_s,
-                   ks > 0 ? 1u : 0u);
-        }
-        umma_commit(smem_u32(&bars->st_full[bt]));
+        issue_s(u);
       }
-      if (u >= 2 && !grads(u - 2)) ok = false;
     }
-    umma_commit(smem_u32(&bars->drain));
+    umma_commit_w(smem_u32(&bars->drain));
     const uint64_t t0 = gtime();
     while (!mbar_try(smem_u32(&bars->drain), 0) && gtime() - t0 < p.timeout_ns) {
     }
@@ -797,29 +1007,68 @@ attn_bwd64_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_consta
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
-    const int kj = j * 128 + r;
     const uint32_t lb = tmem + ((uint32_t)(quarter * 32) << 16);
-    uint8_t* sdS = smem + L::DS_OFF;
+    const uint32_t sdS = sbase + L::DS_OFF;
     // this warp's copy of its 32 queries' lse / delta, loaded one tile ahead
-    float* wLse = sLse + (warp - 2) * 32;
-    float* wDelta = sDelta + (warp - 2) * 32;
-    auto gload = [&](int t, float& l, float& d) {
-      const int h = g * rep + t / n_i, qi = j * 128 + (t % n_i) * 64 + half * 32 + lane;
-      const long long lrow = (long long)(b * p.H + h) * p.T;
+    const uint32_t wLse = smem_u32(sLse + (warp - 2) * 32);
+    const uint32_t wDelta = smem_u32(sDelta + (warp - 2) * 32);
+    auto gload = [&](const Cursor& c, float& l, float& d) {
+      const int qi = c.q0() + half * 32 + lane;
+      const long long lrow = (long long)(c.b * p.H + c.head(p)) * p.T;
       l = qi < p.T ? p.lse[lrow + qi] : 0.f;
       d = qi < p.T ? p.delta[lrow + qi] : 0.f;
     };
+    // dK (times the softmax scale) and dV of item ep_k: the warps of half 0
+    // store dK, those of half 1 dV
+    int ep_k = -1, ep_b = 0, ep_j = 0, ep_g = 0;
+    auto epilogue = [&]() -> bool {
+      ATTN_T0(t_ep);
+      if (!warp_wait(smem_u32(&bars->acc_full), ep_k & 1, abort, p, 48, lane)) return false;
+      tc_fence_after();
+      const uint32_t col0 = half == 0 ? C_DK : C_DV;
+      uint32_t v[64];
+      tmem_ld32(lb + col0, *reinterpret_cast<uint32_t(*)[32]>(v));
+      tmem_ld32(lb + col0 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars->acc_free));
+      const int kj = ep_j * 128 + r;
+      if (kj < p.T) {
+        const float f = half == 0 ? p.scale : 1.f;
+        T* dst = static_cast<T*>(p.dqkv) + (long long)(ep_b * p.T + kj) * p.ld_dqkv +
+                 (half == 0 ? p.k_col : p.v_col) + ep_g * D;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          uint4 pack;
+          uint32_t* pw = reinterpret_cast<uint32_t*>(&pack);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            pw[e] = pack2<T>(__uint_as_float(v[u * 8 + 2 * e]) * f,
+                             __uint_as_float(v[u * 8 + 2 * e + 1]) * f);
+          *reinterpret_cast<uint4*>(dst + u * 8) = pack;
+        }
+      }
+      ep_k = -1;
+      if (warp == 2 && lane == 0) ATTN_ADD(13, t_ep);
+      return true;
+    };
+    Cursor c, nc;
+    c.start(p);
+    nc = c;
     float gl = 0.f, gd = 0.f;
-    if (nit > 0) gload(0, gl, gd);
+    if (total > 0) gload(c, gl, gd);
     bool ok = true;
-    for (int t = 0; t < nit; ++t) {
-      const int bt = t & 1, ti = t % n_i;
-      const int qbase = j * 128 + ti * 64 + half * 32;
+    for (int t = 0; t < total; ++t, c.next(p)) {
+      const int bt = t & 1, ti = c.ti;
+      const int kj = c.j * 128 + r;
+      const int qbase = c.q0() + half * 32;
       __syncwarp();
-      wLse[lane] = gl;
-      wDelta[lane] = gd;
+      sts_f(wLse + lane * 4, gl);
+      sts_f(wDelta + lane * 4, gd);
       __syncwarp();
-      if (t + 1 < nit) gload(t + 1, gl, gd);
+      nc.next(p);
+      if (t + 1 < total) gload(nc, gl, gd);
       ATTN_T0(t_st);
       if (!warp_wait(smem_u32(&bars->st_full[bt]), (t >> 1) & 1, abort, p, 47, lane)) {
         ok = false;
@@ -832,11 +1081,18 @@ attn_bwd64_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_consta
       tmem_ld32(lb + bt * 128 + half * 32, sv);
       tmem_ld32(lb + bt * 128 + 64 + half * 32, dv);
       tmem_ld_wait();
+      if (warp == 2 && lane == 0) ATTN_ADD(20, t_sm);
+      ATTN_T0(t_c1);
       uint32_t pk[16], dk[16];
       if (ti < 2 || qbase - half * 32 + 64 > p.T)
         softmax_bwd_row<T, true>(sv, dv, wLse, wDelta, p.scale_log2, qbase, kj, p.T, pk, dk);
       else
         softmax_bwd_row<T, false>(sv, dv, wLse, wDelta, p.scale_log2, qbase, kj, p.T, pk, dk);
+#ifdef MSB_ATTN_TRACE
+      __syncwarp();
+      if (warp == 2 && lane == 0) ATTN_ADD(21, t_c1);
+#endif
+      ATTN_T0(t_c2);
       // P^T columns of buffer bt and the dS^T slab of tile t are free once the
       // gradient MMAs of tile t-2 retired (and with them the dQ MMA of the
       // pair that last used the slab)
@@ -845,15 +1101,16 @@ attn_bwd64_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_consta
         ok = false;
         break;
       }
+      if (warp == 2 && lane == 0) ATTN_ADD(22, t_c2);
+      ATTN_T0(t_c3);
       tc_fence_after();
       tmem_st16(lb + C_P + bt * 32 + half * 16, pk);
       // dS^T row r, queries half*32 .. +31 of the tile: 16-byte pieces 4*half .. 4*half+3
-      uint8_t* rowp = sdS + (((t >> 1) & 1) * 2 + (t & 1)) * L::KV + r * 128;
+      const uint32_t rowp = sdS + (((t >> 1) & 1) * 2 + (t & 1)) * L::KV + r * 128;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int piece = (half * 4 + u) ^ (r & 7);
-        *reinterpret_cast<uint4*>(rowp + piece * 16) =
-            make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
+        sts_u4(rowp + piece * 16, dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
       }
       tmem_st_wait();
       fence_async_smem();
@@ -861,82 +1118,62 @@ attn_bwd64_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bars->ds_ready[bt]));
       if (warp == 2 && lane == 0) ATTN_ADD(11, t_sm);
-    }
-    // dK (times the softmax scale) and dV of this key block: the warps of
-    // half 0 store dK, those of half 1 dV
-    if (ok && nit > 0 && warp_wait(smem_u32(&bars->drain), 0, abort, p, 48, lane)) {
-      tc_fence_after();
-      T* drow = static_cast<T*>(p.dqkv) + (long long)(row0 + kj) * p.ld_dqkv;
-      const uint32_t col0 = half == 0 ? C_DK : C_DV;
-      const float f = half == 0 ? p.scale : 1.f;
-      T* dst = drow + (half == 0 ? p.k_col : p.v_col) + g * D;
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(lb + col0 + c * 32, v);
-        tmem_ld_wait();
-        if (kj < p.T) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            uint4 pack;
-            uint32_t* pw = reinterpret_cast<uint32_t*>(&pack);
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              pw[e] = pack2<T>(__uint_as_float(v[u * 8 + 2 * e]) * f,
-                               __uint_as_float(v[u * 8 + 2 * e + 1]) * f);
-            *reinterpret_cast<uint4*>(dst + c * 32 + u * 8) = pack;
-          }
-        }
+      if (warp == 2 && lane == 0) ATTN_ADD(23, t_c3);
+      // the previous item's dK / dV once this tile's softmax is out (its last
+      // gradient MMAs ran meanwhile)
+      if (ep_k >= 0 && !epilogue()) {
+        ok = false;
+        break;
+      }
+      if (c.t == c.nit - 1) {
+        ep_k = c.k;
+        ep_b = c.b;
+        ep_j = c.j;
+        ep_g = c.g;
       }
     }
+    if (ok && ep_k >= 0) epilogue();
   } else if (warp >= 10) {
     // ------------------------------------- dQ of a tile pair -> fp32 accumulator
     const int quarter = warp & 3;
     const uint32_t lb = tmem + ((uint32_t)(quarter * 32) << 16);
     uint8_t* stg = smem + L::STG_OFF + (warp - 10) * L::STG_WARP;
-    for (int pr = 0; pr < nit / 2; ++pr) {
-      const int t = 2 * pr;
-      const int h = g * rep + t / n_i, q0 = j * 128 + (t % n_i) * 64;
+    Cursor c;
+    c.start(p);
+    for (int pr = 0; pr < total / 2; ++pr, c.next(p), c.next(p)) {
+      const int h = c.head(p), row = c.b * p.T + c.q0() + quarter * 32;
       ATTN_T0(t_dq);
       if (!warp_wait(smem_u32(&bars->dq_full), pr & 1, abort, p, 49, lane)) break;
       if (warp == 10 && lane == 0) ATTN_ADD(16, t_dq);
       ATTN_T0(t_dqe);
       tc_fence_after();
       uint32_t v[D];
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t w[32];
-        tmem_ld32(lb + C_DQ + c * 32, w);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) v[c * 32 + e] = w[e];
-      }
+      tmem_ld32(lb + C_DQ, *reinterpret_cast<uint32_t(*)[32]>(v));
+      tmem_ld32(lb + C_DQ + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+      tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bars->dq_free));
       if (warp == 10 && lane == 0) ATTN_ADD(17, t_dqe);
-      ATTN_T0(t_bw);
-      if (lane == 0) bulk_wait_read<0>();
-      __syncwarp();
-      if (warp == 10 && lane == 0) ATTN_ADD(18, t_bw);
-      // 32-column boxes of 32 rows x 128 bytes, 128-byte swizzle
+      // four 16-column boxes of 32 rows x 64 bytes (64-byte swizzle) through
+      // one staging buffer
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint8_t* rowp = stg + c * 4096 + lane * 128;
+      for (int cc = 0; cc < D / 16; ++cc) {
+        ATTN_T0(t_bw);
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+        if (warp == 10 && lane == 0) ATTN_ADD(18, t_bw);
+        const uint32_t rowp = smem_u32(stg) + lane * 64;
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-          *reinterpret_cast<uint4*>(rowp + ((u ^ (lane & 7)) << 4)) =
-              make_uint4(v[c * 32 + 4 * u], v[c * 32 + 4 * u + 1], v[c * 32 + 4 * u + 2],
-                         v[c * 32 + 4 * u + 3]);
-      }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c)
-          tma_reduce_add_2d(&tm_dq, smem_u32(stg + c * 4096), h * D + 32 * c,
-                            row0 + q0 + quarter * 32);
-        bulk_commit();
+        for (int u = 0; u < 4; ++u)
+          sts_u4(rowp + ((u ^ ((lane >> 1) & 3)) << 4), v[cc * 16 + 4 * u], v[cc * 16 + 4 * u + 1],
+                 v[cc * 16 + 4 * u + 2], v[cc * 16 + 4 * u + 3]);
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_2d(&tm_dq, smem_u32(stg), h * D + 16 * cc, row);
+          bulk_commit();
+        }
       }
     }
     if (lane == 0) bulk_wait_all();
@@ -1014,7 +1251,8 @@ void launch_bwd64(const CUtensorMap& tkv, const CUtensorMap& tq, const CUtensorM
                "attn bwd smem attribute");
     attr = true;
   }
-  kern<<<p.n_q * p.B * p.Hkv, kThreadsB, Layout64::BYTES, st>>>(tkv, tq, td, tdq, p);
+  const int items = p.n_q * p.B * p.Hkv;
+  kern<<<std::min(items, kNumSMs), kThreadsB, Layout64::BYTES, st>>>(tkv, tq, td, tdq, p);
 }
 
 
@@ -1443,6 +1681,8 @@ void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.n_q = (T + 127) / 128;
+  p.rep = H / Hkv;
+  p.nbh = B * Hkv;
   const uint32_t fmt = dtype == kBF16 ? 1u : 0u;
   // S^T = K Q^T, dP^T = V dO^T: N = 128 queries (head dim 128), 64 (head dim 64)
   p.idesc_s = (1u << 4) | (fmt << 7) | (fmt << 10) | ((D == 128 ? 16u : 8u) << 17) | (8u << 24);
@@ -1460,6 +1700,8 @@ void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
   const CUtensorMap td64 = make_map(dout, dtype, (long long)H * D, (long long)BT, ld_do, 64, 64);
   const CUtensorMap tdq = make_map_f32(dq_acc, (long long)H * D, (long long)BT, (long long)H * D,
                                        32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tdq16 = make_map_f32(dq_acc, (long long)H * D, (long long)BT, (long long)H * D,
+                                         16, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   auto run = [&](auto tag) {
     using T = decltype(tag);
     if (D == 64)
@@ -1470,7 +1712,7 @@ void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
       attn_delta_kernel<T, 128><<<blocks, 256, 0, st>>>(static_cast<const T*>(dout), ld_do,
                                                         static_cast<const T*>(out), ld_out, delta,
                                                         dq_acc, BT, T_seq, H);
-    if (D == 64) launch_bwd64<T>(tq, tq64, td64, tdq, p, st);
+    if (D == 64) launch_bwd64<T>(tq, tq64, td64, tdq16, p, st);
     else launch_bwd128<T>(tq, td, tdq, p, st);
     attn_dq_convert_kernel<T><<<blocks_c, 256, 0, st>>>(dq_acc, BT, H * D, static_cast<T*>(dqkv),
                                                         ld_dqkv, q_col, scale);

@@ -84,6 +84,8 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int mn_major, in
   if (mn_major) return smem_desc(base + kstep * 2048, BK * 128, 1024);
   return smem_desc(base + kstep * 32, 16, 1024);
 }
+// the k-th step's descriptor is the 0-th's plus k times this (start address, 16-byte units)
+__device__ __forceinline__ uint32_t operand_step(int mn_major) { return mn_major ? 128u : 2u; }
 
 struct alignas(8) Barriers {
   uint64_t full[STAGES];
@@ -109,6 +111,12 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile
       return false;
     }
   }
+}
+// the same for a whole warp: lane 0 waits, every lane gets its answer
+__device__ __forceinline__ bool wait_bar_w(uint32_t bar, uint32_t parity, volatile int* abort,
+                                           const Params& p, unsigned code, int lane) {
+  const int r = lane == 0 ? (wait_bar(bar, parity, abort, p, code) ? 1 : 0) : 0;
+  return __shfl_sync(0xffffffffu, r, 0) != 0;
 }
 
 template <int BN, int TM = BM>
@@ -398,43 +406,43 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
              gtime() - t0 < p.timeout_ns) {
       }
     }
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer
+    // the whole warp runs the loop; one elected lane issues (umma_*_w)
     int stage = 0;
     uint32_t phase = 0;
     int it = 0;
     bool ok = true;
+    const uint32_t a_step = operand_step(p.a_mn), b_step = operand_step(p.b_mn);
     for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++it) {
       int m0, n0, kb0, kb1, split;
       unit_coords<BN>(p, u, m0, n0, kb0, kb1, split);
       const int buf = it & 1;
       const uint32_t tphase = (it >> 1) & 1;
-      if (!wait_bar(smem_u32(&bars->tempty[buf]), tphase ^ 1, abort, p, 2)) break;
+      if (!wait_bar_w(smem_u32(&bars->tempty[buf]), tphase ^ 1, abort, p, 2, lane)) break;
       tc_fence_after();
       const uint32_t d = tmem_base + buf * BN;
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!wait_bar(smem_u32(&bars->full[stage]), phase, abort, p, 3)) {
+        if (!wait_bar_w(smem_u32(&bars->full[stage]), phase, abort, p, 3, lane)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
-        const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
+        const uint64_t ad = operand_desc(smem_u32(sA + stage * A_BYTES), p.a_mn, 0);
+        const uint64_t bd = operand_desc(smem_u32(sB + stage * B_BYTES), p.b_mn, 0);
 #pragma unroll
-        for (int ks = 0; ks < BK / 16; ++ks) {
-          umma_f16(d, operand_desc(a_base, p.a_mn, ks), operand_desc(b_base, p.b_mn, ks), p.idesc,
-                   (kb > kb0 || ks > 0) ? 1u : 0u);
-        }
-        umma_commit(smem_u32(&bars->empty[stage]));
+        for (int ks = 0; ks < BK / 16; ++ks)
+          umma_f16_w(d, ad + ks * a_step, bd + ks * b_step, p.idesc, (kb > kb0 || ks > 0) ? 1u : 0u);
+        umma_commit_w(smem_u32(&bars->empty[stage]));
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1;
         }
       }
-      if (ok) umma_commit(smem_u32(&bars->tfull[buf]));
+      if (ok) umma_commit_w(smem_u32(&bars->tfull[buf]));
     }
-    // every MMA issued by this thread retires before tensor memory is freed
-    umma_commit(smem_u32(&bars->drain));
+    // every MMA issued by this warp retires before tensor memory is freed
+    umma_commit_w(smem_u32(&bars->drain));
     const uint64_t t0 = gtime();
     while (!mbar_try(smem_u32(&bars->drain), 0) && gtime() - t0 < p.timeout_ns) {
     }
@@ -603,10 +611,27 @@ __device__ __forceinline__ void commit2_both(uint32_t bar) {
   commit2_to(bar);
   commit2_to(mapa(bar, 1));
 }
-__device__ __forceinline__ void commit2_local(uint32_t bar) {
+// warp-wide forms (one elected lane issues; see umma_f16_w)
+__device__ __forceinline__ void mma2_w(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                       uint32_t accumulate) {
   asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void commit2_to_w(uint32_t cluster_bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          cluster_bar)
       : "memory");
+}
+__device__ __forceinline__ void commit2_both_w(uint32_t bar) {
+  commit2_to_w(bar);
+  commit2_to_w(mapa(bar, 1));
 }
 
 struct alignas(8) Bars2 {
@@ -721,41 +746,46 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         }
       }
     }
-  } else if (warp == 1 && lane == 0 && leader) {
+  } else if (warp == 1 && leader) {
     // ------------------------------------------------------- MMA issuer
+    // the whole warp runs the loop; one elected lane issues (mma2_w)
     int stage = 0;
     uint32_t phase = 0;
     int it = 0;
     bool ok = true;
+    const uint32_t a_step = operand_step(p.a_mn), b_step = operand_step(p.b_mn);
+    auto wait2_w = [&](uint32_t bar, uint32_t parity, unsigned code) -> bool {
+      const int r = lane == 0 ? (wait2(bar, parity, abort, p, code) ? 1 : 0) : 0;
+      return __shfl_sync(0xffffffffu, r, 0) != 0;
+    };
     for (int u = pair_id; u < p.units && ok; u += npairs, ++it) {
       int m0, n0, kb0, kb1, split;
       unit_coords<BN2, TM>(p, u, m0, n0, kb0, kb1, split);
       const int buf = it & 1;
       const uint32_t tphase = (it >> 1) & 1;
-      if (!wait2(smem_u32(&bars->tempty[buf]), tphase ^ 1, abort, p, 12)) break;
+      if (!wait2_w(smem_u32(&bars->tempty[buf]), tphase ^ 1, 12)) break;
       tc_fence_after();
       const uint32_t d = tmem_base + buf * BN2;
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!wait2(smem_u32(&bars->full[stage]), phase, abort, p, 13)) {
+        if (!wait2_w(smem_u32(&bars->full[stage]), phase, 13)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t a_base = smem_u32(sA + stage * A2_BYTES);
-        const uint32_t b_base = smem_u32(sB + stage * B2_BYTES);
+        const uint64_t ad = operand_desc(smem_u32(sA + stage * A2_BYTES), p.a_mn, 0);
+        const uint64_t bd = operand_desc(smem_u32(sB + stage * B2_BYTES), p.b_mn, 0);
 #pragma unroll
         for (int ks = 0; ks < BK / 16; ++ks)
-          mma2(d, operand_desc(a_base, p.a_mn, ks), operand_desc(b_base, p.b_mn, ks), p.idesc,
-               (kb > kb0 || ks > 0) ? 1u : 0u);
-        commit2_both(smem_u32(&bars->empty[stage]));
+          mma2_w(d, ad + ks * a_step, bd + ks * b_step, p.idesc, (kb > kb0 || ks > 0) ? 1u : 0u);
+        commit2_both_w(smem_u32(&bars->empty[stage]));
         if (++stage == STAGES2) {
           stage = 0;
           phase ^= 1;
         }
       }
-      if (ok) commit2_both(smem_u32(&bars->tfull[buf]));
+      if (ok) commit2_both_w(smem_u32(&bars->tfull[buf]));
     }
-    commit2_local(smem_u32(&bars->drain));
+    commit2_to_w(smem_u32(&bars->drain));   // this CTA's own barrier (the elected lane issued)
     const uint64_t t0 = gtime();
     while (!mbar_try(smem_u32(&bars->drain), 0) && gtime() - t0 < p.timeout_ns) {
     }

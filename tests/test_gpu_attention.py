@@ -56,7 +56,10 @@ def test_lse_matches_reference(B, T, H, Hkv, D):
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("B,T,H,Hkv,D", SHAPES + [(1, 384, 4, 1, 128)])
+# the last two launch more key blocks than the GPU has SMs, so the persistent
+# backward kernel walks several work items per CTA (GQA and a ragged length)
+@pytest.mark.parametrize("B,T,H,Hkv,D", SHAPES + [(1, 384, 4, 1, 128), (4, 1024, 12, 6, 64),
+                                                  (20, 200, 8, 8, 64)])
 def test_backward_matches_reference(B, T, H, Hkv, D, dtype):
     torch.manual_seed(2)
     qkv = torch.randn(B, T, H + 2 * Hkv, D, device="cuda").to(dtype).requires_grad_()
