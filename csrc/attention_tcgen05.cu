@@ -307,16 +307,22 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
                gtime() - t0 < p.timeout_ns) {
         }
     }
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1) {
     // ------------------------------------------------------------ MMA
     // Event loop over the two tiles: issue whichever MMA is ready (S of
     // tile t for key tile js[t], P V of tile t for key tile jp[t]), so one
-    // tile's softmax never holds up the other's tensor-core work.
+    // tile's softmax never holds up the other's tensor-core work.  The whole
+    // warp runs it (lane 0 probes the barriers, every lane gets the answer)
+    // and issues through the warp-wide umma_*_w forms.
+    auto ready = [&](uint32_t bar, uint32_t parity) -> bool {
+      const int r = lane == 0 ? (mbar_test(bar, parity) ? 1 : 0) : 0;
+      return __shfl_sync(0xffffffffu, r, 0) != 0;
+    };
     auto qbase = [&](int t) { return smem_u32(sQ + t * S::Q_BYTES); };
     auto nk = [&](int t) { return t == 0 ? nkv0 : nkv1; };
     int js[2] = {0, 0}, jp[2] = {0, 0};
     int kfree = 0, vfree = 0;               // next key tile whose K / V slot to release
-    bool ok = wait_b(smem_u32(&bars->q_full), 0, abort, p, 23);
+    bool ok = warp_wait_f(smem_u32(&bars->q_full), 0, abort, p, 23, lane);
     uint64_t t_idle = 0;
     while (ok) {
       bool progress = false, pending = false;
@@ -328,16 +334,16 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
         if (j < nk(t)) {
           pending = true;
           const int st = j % KV_STAGES;
-          const bool s_ok = j == 0 || (SEP_P ? mbar_test(smem_u32(&bars->s_free[t]), (j - 1) & 1)
-                                             : mbar_test(smem_u32(&bars->pv_done[t]), (j - 1) & 1));
-          if (s_ok && mbar_test(smem_u32(&bars->k_full[st]), (j / KV_STAGES) & 1)) {
+          const bool s_ok = j == 0 || (SEP_P ? ready(smem_u32(&bars->s_free[t]), (j - 1) & 1)
+                                             : ready(smem_u32(&bars->pv_done[t]), (j - 1) & 1));
+          if (s_ok && ready(smem_u32(&bars->k_full[st]), (j / KV_STAGES) & 1)) {
             tc_fence_after();
             const uint32_t kb = smem_u32(sK + st * S::KV_BYTES);
 #pragma unroll
             for (int ks = 0; ks < D / 16; ++ks)
-              umma_f16(tmem + col_s(t), kmajor_desc<D>(qbase(t), ks), kmajor_desc<D>(kb, ks),
-                       p.idesc_s, ks > 0 ? 1u : 0u);
-            umma_commit(smem_u32(&bars->s_full[t]));
+              umma_f16_w(tmem + col_s(t), kmajor_desc<D>(qbase(t), ks), kmajor_desc<D>(kb, ks),
+                         p.idesc_s, ks > 0 ? 1u : 0u);
+            umma_commit_w(smem_u32(&bars->s_full[t]));
             if (t == 0) ++js[0]; else ++js[1];
             progress = true;
           }
@@ -347,15 +353,15 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
         if (jj < nk(t)) {
           pending = true;
           const int st = jj % KV_STAGES;
-          if (jj < (t == 0 ? js[0] : js[1]) && mbar_test(smem_u32(&bars->p_full[t]), jj & 1) &&
-              mbar_test(smem_u32(&bars->v_full[st]), (jj / KV_STAGES) & 1)) {
+          if (jj < (t == 0 ? js[0] : js[1]) && ready(smem_u32(&bars->p_full[t]), jj & 1) &&
+              ready(smem_u32(&bars->v_full[st]), (jj / KV_STAGES) & 1)) {
             tc_fence_after();
             const uint32_t vbase = smem_u32(sV + st * S::KV_BYTES);
 #pragma unroll
             for (int ks = 0; ks < BKV / 16; ++ks)
-              umma_f16_ts(tmem + col_o(t), tmem + col_p(t) + ks * 8, v_desc<D>(vbase, ks),
-                          p.idesc_o, (jj > 0 || ks > 0) ? 1u : 0u);
-            umma_commit(smem_u32(&bars->pv_done[t]));
+              umma_f16_ts_w(tmem + col_o(t), tmem + col_p(t) + ks * 8, v_desc<D>(vbase, ks),
+                            p.idesc_o, (jj > 0 || ks > 0) ? 1u : 0u);
+            umma_commit_w(smem_u32(&bars->pv_done[t]));
             if (t == 0) ++jp[0]; else ++jp[1];
             progress = true;
           }
@@ -363,29 +369,35 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
       }
       // release K / V slots once every tile that reads them has issued its MMA
       while (kfree < nkv && (kfree < js[0] || kfree >= nkv0) && (kfree < js[1] || kfree >= nkv1)) {
-        umma_commit(smem_u32(&bars->k_empty[kfree % KV_STAGES]));
+        umma_commit_w(smem_u32(&bars->k_empty[kfree % KV_STAGES]));
         ++kfree;
       }
       while (vfree < nkv && (vfree < jp[0] || vfree >= nkv0) && (vfree < jp[1] || vfree >= nkv1)) {
-        umma_commit(smem_u32(&bars->v_empty[vfree % KV_STAGES]));
+        umma_commit_w(smem_u32(&bars->v_empty[vfree % KV_STAGES]));
         ++vfree;
       }
       if (!pending) break;
       if (progress) {
         t_idle = 0;
       } else {
-        if (*abort) break;
-        const uint64_t now = gtime();
-        if (t_idle == 0) {
-          t_idle = now;
-        } else if (now - t_idle > p.timeout_ns) {
-          *abort = 1;
-          atomicCAS(p.err, 0u, 26u);
-          break;
+        // lane 0 decides, so the warp leaves together
+        int stop = 0;
+        if (lane == 0) {
+          const uint64_t now = gtime();
+          if (*abort) {
+            stop = 1;
+          } else if (t_idle == 0) {
+            t_idle = now;
+          } else if (now - t_idle > p.timeout_ns) {
+            *abort = 1;
+            atomicCAS(p.err, 0u, 26u);
+            stop = 1;
+          }
         }
+        if (__shfl_sync(0xffffffffu, stop, 0)) break;
       }
     }
-    umma_commit(smem_u32(&bars->drain));
+    umma_commit_w(smem_u32(&bars->drain));
     const uint64_t t0 = gtime();
     while (!mbar_try(smem_u32(&bars->drain), 0) && gtime() - t0 < p.timeout_ns) {
     }
@@ -1378,49 +1390,50 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
         while (!mbar_try(smem_u32(&bars->qo_full[s]), (uint32_t)pend[s]) &&
                gtime() - t0 < p.timeout_ns) {
         }
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1) {
     // ------------------------------------------------------------ MMA
-    bool ok = wait_b(smem_u32(&bars->kv_full), 0, abort, p, 52);
+    // (the whole warp; lane 0 waits, umma_*_w issue from one elected lane)
+    bool ok = warp_wait(smem_u32(&bars->kv_full), 0, abort, p, 52, lane);
     const uint32_t kb = sbase + L::K_OFF, vb = sbase + L::V_OFF, dsb = sbase + L::DS_OFF;
     for (int it = 0; it < nit && ok; ++it) {
       const int st = it & 1;
       const uint32_t ph = (it >> 1) & 1;
-      if (!wait_b(smem_u32(&bars->qo_full[st]), ph, abort, p, 53)) break;
+      if (!warp_wait(smem_u32(&bars->qo_full[st]), ph, abort, p, 53, lane)) break;
       // S^T / dP^T columns (and the dQ halves inside them) are free once the
       // last MMAs retired and the dQ partial was read
-      if (it > 0 && !wait_b(smem_u32(&bars->mma2_done), (it - 1) & 1, abort, p, 54)) break;
-      if (it > 0 && !wait_b(smem_u32(&bars->dq_free), (it - 1) & 1, abort, p, 55)) break;
+      if (it > 0 && !warp_wait(smem_u32(&bars->mma2_done), (it - 1) & 1, abort, p, 54, lane)) break;
+      if (it > 0 && !warp_wait(smem_u32(&bars->dq_free), (it - 1) & 1, abort, p, 55, lane)) break;
       tc_fence_after();
       const uint32_t qb = sbase + L::Q_OFF + st * L::TILE, ob = sbase + L::DO_OFF + st * L::TILE;
 #pragma unroll
       for (int ks = 0; ks < D / 16; ++ks) {
-        umma_f16(tmem + C_S, kmajor_desc<D>(kb, ks), kmajor_desc<D>(qb, ks), p.idesc_s,
+        umma_f16_w(tmem + C_S, kmajor_desc<D>(kb, ks), kmajor_desc<D>(qb, ks), p.idesc_s,
                  ks > 0 ? 1u : 0u);
-        umma_f16(tmem + C_DP, kmajor_desc<D>(vb, ks), kmajor_desc<D>(ob, ks), p.idesc_s,
+        umma_f16_w(tmem + C_DP, kmajor_desc<D>(vb, ks), kmajor_desc<D>(ob, ks), p.idesc_s,
                  ks > 0 ? 1u : 0u);
       }
-      umma_commit(smem_u32(&bars->st_full));
-      if (!wait_b(smem_u32(&bars->ds_ready), it & 1, abort, p, 56)) break;
+      umma_commit_w(smem_u32(&bars->st_full));
+      if (!warp_wait(smem_u32(&bars->ds_ready), it & 1, abort, p, 56, lane)) break;
       tc_fence_after();
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
-        umma_f16_ts(tmem + C_DV, tmem + C_S + ks * 8, mn_desc(ob, ks), p.idesc_kv,
+        umma_f16_ts_w(tmem + C_DV, tmem + C_S + ks * 8, mn_desc(ob, ks), p.idesc_kv,
                     (it > 0 || ks > 0) ? 1u : 0u);
-        umma_f16_ts(tmem + C_DK, tmem + C_DP + ks * 8, mn_desc(qb, ks), p.idesc_kv,
+        umma_f16_ts_w(tmem + C_DK, tmem + C_DP + ks * 8, mn_desc(qb, ks), p.idesc_kv,
                     (it > 0 || ks > 0) ? 1u : 0u);
       }
       // dQ = dS K in two 64-column halves (idesc_q has N = 64)
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
-        umma_f16(tmem + C_DQ0, mn_desc(dsb, ks), mn_desc(kb, ks), p.idesc_q, ks > 0 ? 1u : 0u);
-        umma_f16(tmem + C_DQ1, mn_desc(dsb, ks), mn_desc(kb + L::CH, ks), p.idesc_q,
+        umma_f16_w(tmem + C_DQ0, mn_desc(dsb, ks), mn_desc(kb, ks), p.idesc_q, ks > 0 ? 1u : 0u);
+        umma_f16_w(tmem + C_DQ1, mn_desc(dsb, ks), mn_desc(kb + L::CH, ks), p.idesc_q,
                  ks > 0 ? 1u : 0u);
       }
-      umma_commit(smem_u32(&bars->qo_empty[st]));
-      umma_commit(smem_u32(&bars->mma2_done));
-      umma_commit(smem_u32(&bars->dq_full));
+      umma_commit_w(smem_u32(&bars->qo_empty[st]));
+      umma_commit_w(smem_u32(&bars->mma2_done));
+      umma_commit_w(smem_u32(&bars->dq_full));
     }
-    umma_commit(smem_u32(&bars->drain));
+    umma_commit_w(smem_u32(&bars->drain));
     const uint64_t t0 = gtime();
     while (!mbar_try(smem_u32(&bars->drain), 0) && gtime() - t0 < p.timeout_ns) {
     }
