@@ -1201,32 +1201,45 @@ attn_bwd64_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_consta
   if (threadIdx.x == 0) ATTN_ADD(19, t_cta);
 }
 
-// delta[b, h, t] = sum_d dO * O (fp32) and a zeroed dQ accumulator row
+// delta[b, h, t] = sum_d dO * O (fp32) and a zeroed dQ accumulator row.
+// Eight lanes per (row, head), each on its own 16-byte pieces, so a warp's
+// loads and stores cover whole contiguous segments.
 template <typename T, int D>
 __global__ void __launch_bounds__(256)
 attn_delta_kernel(const T* __restrict__ dout, long long ld_do, const T* __restrict__ out,
                   long long ld_o, float* __restrict__ delta, float* __restrict__ dq_acc, int BT,
                   int seq, int H) {
+  constexpr int V = D / 64;   // 16-byte pieces of a head row per lane
   const long long n = (long long)BT * H;
-  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const int row = (int)(idx / H), h = (int)(idx % H);
+  const int sub = threadIdx.x & 7;
+  // a warp takes four consecutive (row, head) items per pass; the loop bound
+  // is the warp's, so every lane reaches the shuffles
+  const long long step = ((long long)gridDim.x * blockDim.x) >> 3;
+  for (long long w0 = (((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 4; w0 < n;
+       w0 += step) {
+    const long long idx = w0 + ((threadIdx.x & 31) >> 3);
+    const bool valid = idx < n;
+    const int row = valid ? (int)(idx / H) : 0, h = valid ? (int)(idx % H) : 0;
     const uint4* a = reinterpret_cast<const uint4*>(dout + (long long)row * ld_do + h * D);
     const uint4* o = reinterpret_cast<const uint4*>(out + (long long)row * ld_o + h * D);
     float acc = 0.f;
 #pragma unroll
-    for (int q = 0; q < D / 8; ++q) {
-      const uint4 x = a[q], y = o[q];
+    for (int q = 0; q < V && valid; ++q) {
+      const uint4 x = a[sub + 8 * q], y = o[sub + 8 * q];
       const T* xh = reinterpret_cast<const T*>(&x);
       const T* yh = reinterpret_cast<const T*>(&y);
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc += to_f32(xh[e]) * to_f32(yh[e]);
     }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    if (!valid) continue;
     const int b = row / seq, t = row % seq;
-    delta[((long long)b * H + h) * seq + t] = acc;
+    if (sub == 0) delta[((long long)b * H + h) * seq + t] = acc;
     float4* z = reinterpret_cast<float4*>(dq_acc + (long long)row * H * D + h * D);
 #pragma unroll
-    for (int q = 0; q < D / 4; ++q) z[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < D / 32; ++q) z[sub + 8 * q] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
 
@@ -1677,7 +1690,7 @@ void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
     throw std::runtime_error("attention backward: operands must allow 16-byte row access");
   const int BT = B * T;
   const int T_seq = T;
-  const int blocks = grid_for((long long)BT * H, 256, kNumSMs * 8);
+  const int blocks = grid_for((long long)BT * H * 8, 256, kNumSMs * 8);
   const int blocks_c = grid_for((long long)BT * H * D / 8, 256, kNumSMs * 8);
   attn::bwd::Params p;
   p.B = B;

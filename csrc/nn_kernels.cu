@@ -287,18 +287,32 @@ norm_dwdb_partial_kernel(const T* __restrict__ dy, const T* __restrict__ s,
   const int r0 = blockIdx.y * rows_per_block;
   const int r1 = min(M, r0 + rows_per_block);
   float aw[8] = {0, 0, 0, 0, 0, 0, 0, 0}, ab[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  auto row = [&](const float (&d)[8], const float (&x)[8], int r) {
+    const float mean = RMS ? 0.f : mean_in[r];
+    const float rstd = rstd_in[r];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      aw[k] += d[k] * ((x[k] - mean) * rstd);
+      ab[k] += d[k];
+    }
+  };
   if (c0 < C) {
-    for (int r = r0 + warp; r < r1; r += 8) {
+    int r = r0 + warp;
+    // two rows per step: four 16-byte loads in flight per lane
+    for (; r + 8 < r1; r += 16) {
+      float d0[8], x0[8], d1[8], x1[8];
+      load8(dy + (size_t)r * C + c0, d0);
+      load8(s + (size_t)r * C + c0, x0);
+      load8(dy + (size_t)(r + 8) * C + c0, d1);
+      load8(s + (size_t)(r + 8) * C + c0, x1);
+      row(d0, x0, r);
+      row(d1, x1, r + 8);
+    }
+    for (; r < r1; r += 8) {
       float d[8], x[8];
       load8(dy + (size_t)r * C + c0, d);
       load8(s + (size_t)r * C + c0, x);
-      const float mean = RMS ? 0.f : mean_in[r];
-      const float rstd = rstd_in[r];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        aw[k] += d[k] * ((x[k] - mean) * rstd);
-        ab[k] += d[k];
-      }
+      row(d, x, r);
     }
   }
   __shared__ float red[8][256 + 8];
@@ -331,7 +345,27 @@ colsum_partial_kernel(const T* __restrict__ a, float* __restrict__ part, int M, 
   const int r0 = blockIdx.y * rows_per_block;
   const int r1 = min(M, r0 + rows_per_block);
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  if (c0 < N) {
+  const bool vec = c0 + 8 <= N &&
+                   ((reinterpret_cast<uintptr_t>(a) | (uintptr_t)(ld * (long long)sizeof(T))) & 15) == 0;
+  if (vec) {
+    // four rows per step: four independent 16-byte loads in flight per lane
+    int r = r0 + warp;
+    for (; r + 24 < r1; r += 32) {
+      Pack8<T> v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        v[u] = *reinterpret_cast<const Pack8<T>*>(a + (long long)(r + 8 * u) * ld + c0);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] += to_f32(v[u].v[k]);
+    }
+    for (; r < r1; r += 8) {
+      const Pack8<T> v = *reinterpret_cast<const Pack8<T>*>(a + (long long)r * ld + c0);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] += to_f32(v.v[k]);
+    }
+  } else if (c0 < N) {
     for (int r = r0 + warp; r < r1; r += 8) {
       float f[8];
       const T* p = a + (long long)r * ld + c0;
