@@ -210,8 +210,10 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
 
   ATTN_T0(t_cta);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = p.n_pairs - 1 - blockIdx.x;         // longest pairs first
-  const int bh = blockIdx.y;
+  // blocks are dispatched x-fastest: every head's last pair (the most key
+  // tiles) first, then the next-to-last, ...
+  const int c = p.n_pairs - 1 - blockIdx.y;
+  const int bh = blockIdx.x;
   const int b = bh / p.H, h = bh % p.H;
   const int g = h / (p.H / p.Hkv);
   const int row0 = b * p.T;
@@ -546,7 +548,7 @@ void launch_fwd(const CUtensorMap& tm, const Params& p, int B, int H, cudaStream
                "attn smem attribute");
     attr = true;
   }
-  dim3 grid(p.n_pairs, B * H);
+  dim3 grid(B * H, p.n_pairs);
   kern<<<grid, kThreads, smem_bytes<D>(), st>>>(tm, p);
 }
 
@@ -1333,8 +1335,10 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
   const uint32_t sbase = smem_u32(smem);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int j = blockIdx.x;
-  const int b = blockIdx.y / p.Hkv, g = blockIdx.y % p.Hkv;
+  // blocks are dispatched x-fastest: every kv head's key block 0 (the most
+  // query tiles) first, then key block 1, ...
+  const int j = blockIdx.y;
+  const int b = blockIdx.x / p.Hkv, g = blockIdx.x % p.Hkv;
   const int rep = p.H / p.Hkv;
   const int n_i = p.n_q - j;
   const int nit = rep * n_i;
@@ -1457,6 +1461,7 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
     const int kj = j * 128 + r;
     const uint32_t lb = tmem + ((uint32_t)(quarter * 32) << 16);
     uint8_t* sdS = smem + L::DS_OFF;
+    const uint32_t lse_s = smem_u32(sLse), delta_s = smem_u32(sDelta);
     bool ok = true;
     for (int it = 0; it < nit; ++it) {
       const int h = g * rep + it / n_i, i = j + it % n_i;
@@ -1487,31 +1492,21 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
         tmem_ld32(lb + C_DP + c * 32, dv);
         tmem_ld_wait();
         uint32_t pk[16], dk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float pp[2], dd[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int col = c * 32 + 2 * e + u;
-            const int qi = i * 128 + col;
-            const bool vis = qi >= kj && qi < p.T;
-            const float pr =
-                vis ? ex2(fmaf(__uint_as_float(sv[2 * e + u]), p.scale_log2, -sLse[col])) : 0.f;
-            pp[u] = pr;
-            dd[u] = pr * (__uint_as_float(dv[2 * e + u]) - sDelta[col]);
-          }
-          pk[e] = pack2<T>(pp[0], pp[1]);
-          dk[e] = pack2<T>(dd[0], dd[1]);
-        }
+        // the causal / sequence-end mask only on the diagonal and last tiles
+        if (i == j || i * 128 + 128 > p.T)
+          softmax_bwd_row<T, true>(sv, dv, lse_s + c * 128, delta_s + c * 128, p.scale_log2,
+                                   i * 128 + c * 32, kj, p.T, pk, dk);
+        else
+          softmax_bwd_row<T, false>(sv, dv, lse_s + c * 128, delta_s + c * 128, p.scale_log2,
+                                    i * 128 + c * 32, kj, p.T, pk, dk);
         // packed in place: columns 16c..16c+15, all read by this thread already
         tmem_st16(lb + C_S + c * 16, pk);
         tmem_st16(lb + C_DP + c * 16, dk);
-        uint8_t* rowp = sdS + (c >> 1) * L::CH + r * 128;
+        const uint32_t rowp = smem_u32(sdS) + (c >> 1) * L::CH + r * 128;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int piece = ((c & 1) * 4 + u) ^ (r & 7);
-          *reinterpret_cast<uint4*>(rowp + piece * 16) =
-              make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
+          sts_u4(rowp + piece * 16, dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
         }
       }
       tmem_st_wait();
@@ -1622,7 +1617,7 @@ void launch_bwd128(const CUtensorMap& tq, const CUtensorMap& td, const CUtensorM
                "attn bwd128 smem attribute");
     attr = true;
   }
-  dim3 grid(p.n_q, p.B * p.Hkv);
+  dim3 grid(p.B * p.Hkv, p.n_q);
   kern<<<grid, kThreads128, Layout128::BYTES, st>>>(tq, td, tdq, p);
 }
 
