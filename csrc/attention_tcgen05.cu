@@ -39,7 +39,7 @@
 // Phase tracing for tuning (off unless compiled with -DMSB_ATTN_TRACE): the
 // cycles each role spends per phase, summed over CTAs into g_attn_trace.
 #ifdef MSB_ATTN_TRACE
-__device__ unsigned long long g_attn_trace[32];
+__device__ unsigned long long g_attn_trace[64];
 #define ATTN_T0(v) const long long v = clock64()
 #define ATTN_ADD(id, v) atomicAdd(&g_attn_trace[id], (unsigned long long)(clock64() - (v)))
 #else
@@ -1415,11 +1415,16 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
     for (int it = 0; it < nit && ok; ++it) {
       const int st = it & 1;
       const uint32_t ph = (it >> 1) & 1;
+      ATTN_T0(t_a);
       if (!warp_wait(smem_u32(&bars->qo_full[st]), ph, abort, p, 53, lane)) break;
+      if (lane == 0) ATTN_ADD(27, t_a);
+      ATTN_T0(t_b);
       // S^T / dP^T columns (and the dQ halves inside them) are free once the
       // last MMAs retired and the dQ partial was read
       if (it > 0 && !warp_wait(smem_u32(&bars->mma2_done), (it - 1) & 1, abort, p, 54, lane)) break;
       if (it > 0 && !warp_wait(smem_u32(&bars->dq_free), (it - 1) & 1, abort, p, 55, lane)) break;
+      if (lane == 0) ATTN_ADD(28, t_b);
+      ATTN_T0(t_c);
       tc_fence_after();
       const uint32_t qb = sbase + L::Q_OFF + st * L::TILE, ob = sbase + L::DO_OFF + st * L::TILE;
 #pragma unroll
@@ -1430,7 +1435,11 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
                  ks > 0 ? 1u : 0u);
       }
       umma_commit_w(smem_u32(&bars->st_full));
+      if (lane == 0) ATTN_ADD(30, t_c);
+      ATTN_T0(t_d);
       if (!warp_wait(smem_u32(&bars->ds_ready), it & 1, abort, p, 56, lane)) break;
+      if (lane == 0) ATTN_ADD(31, t_d);
+      ATTN_T0(t_e);
       tc_fence_after();
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
@@ -1439,6 +1448,8 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
         umma_f16_ts_w(tmem + C_DK, tmem + C_DP + ks * 8, mn_desc(qb, ks), p.idesc_kv,
                     (it > 0 || ks > 0) ? 1u : 0u);
       }
+      if (lane == 0) ATTN_ADD(29, t_e);
+      ATTN_T0(t_e2);
       // dQ = dS K in two 64-column halves (idesc_q has N = 64)
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
@@ -1449,6 +1460,7 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
       umma_commit_w(smem_u32(&bars->qo_empty[st]));
       umma_commit_w(smem_u32(&bars->mma2_done));
       umma_commit_w(smem_u32(&bars->dq_full));
+      if (lane == 0) ATTN_ADD(32, t_e2);
     }
     umma_commit_w(smem_u32(&bars->drain));
     const uint64_t t0 = gtime();
@@ -1467,6 +1479,7 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
       const int h = g * rep + it / n_i, i = j + it % n_i;
       const long long lrow = (long long)(b * p.H + h) * p.T;
       // the shared lse / delta of the previous tile were read by every warp
+      ATTN_T0(t_f);
       if (it > 0 && !warp_wait(smem_u32(&bars->ds_ready), (it - 1) & 1, abort, p, 57, lane)) {
         ok = false;
         break;
@@ -1484,6 +1497,8 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
         ok = false;
         break;
       }
+      if (warp == 2 && lane == 0) ATTN_ADD(33, t_f);
+      ATTN_T0(t_g);
       tc_fence_after();
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
@@ -1514,6 +1529,7 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bars->ds_ready));
+      if (warp == 2 && lane == 0) ATTN_ADD(34, t_g);
     }
     // dK (times the softmax scale) and dV of this key tile
     if (ok && nit > 0 && warp_wait(smem_u32(&bars->mma2_done), (nit - 1) & 1, abort, p, 61, lane)) {
@@ -1552,7 +1568,10 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
     uint8_t* stg = smem + L::DS_OFF + (warp - 6) * 8192;
     for (int it = 0; it < nit; ++it) {
       const int h = g * rep + it / n_i, i = j + it % n_i;
+      ATTN_T0(t_h);
       if (!warp_wait(smem_u32(&bars->dq_full), it & 1, abort, p, 62, lane)) break;
+      if (warp == 6 && lane == 0) ATTN_ADD(35, t_h);
+      ATTN_T0(t_i);
       tc_fence_after();
       uint32_t v[128];
 #pragma unroll
@@ -1593,6 +1612,7 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
       if (lane == 0) bulk_wait_read<0>();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bars->stg_free));
+      if (warp == 6 && lane == 0) ATTN_ADD(36, t_i);
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
