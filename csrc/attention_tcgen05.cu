@@ -115,8 +115,7 @@ __device__ __forceinline__ bool wait_b(uint32_t bar, uint32_t parity, volatile i
 
 __device__ __forceinline__ bool warp_wait_f(uint32_t bar, uint32_t parity, volatile int* abort,
                                             const Params& p, unsigned code, int lane) {
-  int w = lane == 0 ? (wait_b(bar, parity, abort, p, code) ? 1 : 0) : 0;
-  return __shfl_sync(0xffffffffu, w, 0) != 0;
+  return warp_wait_all(bar, parity, abort, p.err, code, p.timeout_ns, lane);
 }
 
 // K-major operand (rows x D, 64-column slabs CHUNK bytes apart), k-th 16-wide step
@@ -314,12 +313,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
     // Event loop over the two tiles: issue whichever MMA is ready (S of
     // tile t for key tile js[t], P V of tile t for key tile jp[t]), so one
     // tile's softmax never holds up the other's tensor-core work.  The whole
-    // warp runs it (lane 0 probes the barriers, every lane gets the answer)
-    // and issues through the warp-wide umma_*_w forms.
-    auto ready = [&](uint32_t bar, uint32_t parity) -> bool {
-      const int r = lane == 0 ? (mbar_test(bar, parity) ? 1 : 0) : 0;
-      return __shfl_sync(0xffffffffu, r, 0) != 0;
-    };
+    // warp runs it (every lane probes the barriers, a vote keeps it
+    // converged) and issues through the warp-wide umma_*_w forms.
+    auto ready = [&](uint32_t bar, uint32_t parity) -> bool { return warp_test(bar, parity); };
     auto qbase = [&](int t) { return smem_u32(sQ + t * S::Q_BYTES); };
     auto nk = [&](int t) { return t == 0 ? nkv0 : nkv1; };
     int js[2] = {0, 0}, jp[2] = {0, 0};
@@ -665,8 +661,7 @@ __device__ __forceinline__ bool wait_b(uint32_t bar, uint32_t parity, volatile i
 }
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort,
                                           const Params& p, unsigned code, int lane) {
-  int w = lane == 0 ? (wait_b(bar, parity, abort, p, code) ? 1 : 0) : 0;
-  return __shfl_sync(0xffffffffu, w, 0) != 0;
+  return warp_wait_all(bar, parity, abort, p.err, code, p.timeout_ns, lane);
 }
 
 // A CTA's position in its sequence of work items and their query tiles
@@ -970,10 +965,7 @@ attn_bwd64_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_consta
       sc.next(p);
     };
     // non-blocking probe, the same answer in every lane
-    auto ready = [&](uint32_t bar, uint32_t parity) -> bool {
-      const int r = issuer ? (mbar_test(bar, parity) ? 1 : 0) : 0;
-      return __shfl_sync(0xffffffffu, r, 0) != 0;
-    };
+    auto ready = [&](uint32_t bar, uint32_t parity) -> bool { return warp_test(bar, parity); };
     // step u: once the softmax of tile u-2 is done, its score buffer takes
     // tile u, and tile u-2's gradient MMAs are issued
     for (int u = 0; u < total + 2 && ok; ++u) {

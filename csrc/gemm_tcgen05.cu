@@ -112,11 +112,10 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile
     }
   }
 }
-// the same for a whole warp: lane 0 waits, every lane gets its answer
+// the same for a whole converged warp (see warp_wait_all)
 __device__ __forceinline__ bool wait_bar_w(uint32_t bar, uint32_t parity, volatile int* abort,
                                            const Params& p, unsigned code, int lane) {
-  const int r = lane == 0 ? (wait_bar(bar, parity, abort, p, code) ? 1 : 0) : 0;
-  return __shfl_sync(0xffffffffu, r, 0) != 0;
+  return warp_wait_all(bar, parity, abort, p.err, code, p.timeout_ns, lane);
 }
 
 template <int BN, int TM = BM>
@@ -754,9 +753,24 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     int it = 0;
     bool ok = true;
     const uint32_t a_step = operand_step(p.a_mn), b_step = operand_step(p.b_mn);
+    // every lane polls, a vote keeps the warp converged (see warp_wait_all)
     auto wait2_w = [&](uint32_t bar, uint32_t parity, unsigned code) -> bool {
-      const int r = lane == 0 ? (wait2(bar, parity, abort, p, code) ? 1 : 0) : 0;
-      return __shfl_sync(0xffffffffu, r, 0) != 0;
+      if (__all_sync(0xffffffffu, try_cluster(bar, parity))) return true;
+      const uint64_t t0 = gtime();
+      while (true) {
+        if (__all_sync(0xffffffffu, try_cluster(bar, parity))) return true;
+        int stop = 0;
+        if (lane == 0) {
+          if (*abort) {
+            stop = 1;
+          } else if (gtime() - t0 > p.timeout_ns) {
+            *abort = 1;
+            atomicCAS(p.err, 0u, code);
+            stop = 1;
+          }
+        }
+        if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+      }
     };
     for (int u = pair_id; u < p.units && ok; u += npairs, ++it) {
       int m0, n0, kb0, kb1, split;
