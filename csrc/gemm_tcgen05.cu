@@ -356,8 +356,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
 
-  if (warp == 0 && lane == 0) {
+  if (warp == 0) {
     // ------------------------------------------------------ TMA producer
+    // the whole warp runs the loop; one elected lane issues (tma_load_2d_w)
     int stage = 0;
     uint32_t phase = 0;
     int pending[STAGES];
@@ -368,26 +369,26 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       int m0, n0, kb0, kb1, split;
       unit_coords<BN>(p, u, m0, n0, kb0, kb1, split);
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!wait_bar(smem_u32(&bars->empty[stage]), phase ^ 1, abort, p, 1)) {
+        if (!wait_bar_w(smem_u32(&bars->empty[stage]), phase ^ 1, abort, p, 1, lane)) {
           ok = false;
           break;
         }
         const uint32_t full = smem_u32(&bars->full[stage]);
-        mbar_expect_tx(full, A_BYTES + B_BYTES);
+        mbar_expect_tx_w(full, A_BYTES + B_BYTES);
         const uint32_t a_dst = smem_u32(sA + stage * A_BYTES);
         const uint32_t b_dst = smem_u32(sB + stage * B_BYTES);
         const int k0 = kb * BK;
         if (p.a_mn) {
 #pragma unroll
-          for (int j = 0; j < BM / 64; ++j) tma_load_2d(a_dst + j * 8192, &tmA, full, m0 + 64 * j, k0);
+          for (int j = 0; j < BM / 64; ++j) tma_load_2d_w(a_dst + j * 8192, &tmA, full, m0 + 64 * j, k0);
         } else {
-          tma_load_2d(a_dst, &tmA, full, k0, m0);
+          tma_load_2d_w(a_dst, &tmA, full, k0, m0);
         }
         if (p.b_mn) {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, full, n0 + 64 * j, k0);
+          for (int j = 0; j < BN / 64; ++j) tma_load_2d_w(b_dst + j * 8192, &tmB, full, n0 + 64 * j, k0);
         } else {
-          tma_load_2d(b_dst, &tmB, full, k0, n0);
+          tma_load_2d_w(b_dst, &tmB, full, k0, n0);
         }
         pending[stage] = static_cast<int>(phase);
         if (++stage == STAGES) {
@@ -460,9 +461,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       const int buf = it & 1;
       const uint32_t tphase = (it >> 1) & 1;
       // one lane polls; the warp follows it as a unit (tcgen05.ld is .sync.aligned)
-      int ok = lane == 0 ? (wait_bar(smem_u32(&bars->tfull[buf]), tphase, abort, p, 4) ? 1 : 0) : 0;
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
+      if (!wait_bar_w(smem_u32(&bars->tfull[buf]), tphase, abort, p, 4, lane)) break;
       tc_fence_after();
       const int row0 = m0 + quarter * 32;
       const int row = m0 + row_in_tile;
@@ -568,11 +567,33 @@ __device__ __forceinline__ bool wait2(uint32_t bar, uint32_t parity, volatile in
     }
   }
 }
-__device__ __forceinline__ void tma_load_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                              int x, int y) {
+// the same for a whole converged warp: every lane polls and votes (see warp_wait_all)
+__device__ __forceinline__ bool wait2_w(uint32_t bar, uint32_t parity, volatile int* abort,
+                                        const Params& p, unsigned code, int lane) {
+  if (__all_sync(0xffffffffu, try_cluster(bar, parity))) return true;
+  const uint64_t t0 = gtime();
+  while (true) {
+    if (__all_sync(0xffffffffu, try_cluster(bar, parity))) return true;
+    int stop = 0;
+    if (lane == 0) {
+      if (*abort) {
+        stop = 1;
+      } else if (gtime() - t0 > p.timeout_ns) {
+        *abort = 1;
+        atomicCAS(p.err, 0u, code);
+        stop = 1;
+      }
+    }
+    if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+  }
+}
+__device__ __forceinline__ void tma_load_pair_w(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                                int x, int y) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.cta_group::2"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.cta_group::2"
+      " [%0], [%1, {%2, %3}], [%4];\n\t}" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
       : "memory");
 }
@@ -693,7 +714,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
 
-  if (warp == 0 && lane == 0) {
+  if (warp == 0) {
     // ------------------------------------------------------ TMA producer
     int stage = 0;
     uint32_t phase = 0;
@@ -706,27 +727,27 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
       unit_coords<BN2, TM>(p, u, m0, n0, kb0, kb1, split);
       const int am = m0 + HALF * rank, bn = n0 + HALF * rank;
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!wait2(smem_u32(&bars->empty[stage]), phase ^ 1, abort, p, 11)) {
+        if (!wait2_w(smem_u32(&bars->empty[stage]), phase ^ 1, abort, p, 11, lane)) {
           ok = false;
           break;
         }
         const uint32_t full_local = smem_u32(&bars->full[stage]);
         const uint32_t full_leader = mapa(full_local, 0);
-        if (leader) mbar_expect_tx(full_local, 2 * (A2_BYTES + B2_BYTES));
+        if (leader) mbar_expect_tx_w(full_local, 2 * (A2_BYTES + B2_BYTES));
         const uint32_t a_dst = smem_u32(sA + stage * A2_BYTES);
         const uint32_t b_dst = smem_u32(sB + stage * B2_BYTES);
         const int k0 = kb * BK;
         if (p.a_mn) {
-          tma_load_pair(a_dst, &tmA, full_leader, am, k0);
-          tma_load_pair(a_dst + 8192, &tmA, full_leader, am + 64, k0);
+          tma_load_pair_w(a_dst, &tmA, full_leader, am, k0);
+          tma_load_pair_w(a_dst + 8192, &tmA, full_leader, am + 64, k0);
         } else {
-          tma_load_pair(a_dst, &tmA, full_leader, k0, am);
+          tma_load_pair_w(a_dst, &tmA, full_leader, k0, am);
         }
         if (p.b_mn) {
-          tma_load_pair(b_dst, &tmB, full_leader, bn, k0);
-          tma_load_pair(b_dst + 8192, &tmB, full_leader, bn + 64, k0);
+          tma_load_pair_w(b_dst, &tmB, full_leader, bn, k0);
+          tma_load_pair_w(b_dst + 8192, &tmB, full_leader, bn + 64, k0);
         } else {
-          tma_load_pair(b_dst, &tmB, full_leader, k0, bn);
+          tma_load_pair_w(b_dst, &tmB, full_leader, k0, bn);
         }
         pending[stage] = static_cast<int>(phase);
         if (++stage == STAGES2) {
@@ -753,35 +774,16 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     int it = 0;
     bool ok = true;
     const uint32_t a_step = operand_step(p.a_mn), b_step = operand_step(p.b_mn);
-    // every lane polls, a vote keeps the warp converged (see warp_wait_all)
-    auto wait2_w = [&](uint32_t bar, uint32_t parity, unsigned code) -> bool {
-      if (__all_sync(0xffffffffu, try_cluster(bar, parity))) return true;
-      const uint64_t t0 = gtime();
-      while (true) {
-        if (__all_sync(0xffffffffu, try_cluster(bar, parity))) return true;
-        int stop = 0;
-        if (lane == 0) {
-          if (*abort) {
-            stop = 1;
-          } else if (gtime() - t0 > p.timeout_ns) {
-            *abort = 1;
-            atomicCAS(p.err, 0u, code);
-            stop = 1;
-          }
-        }
-        if (__shfl_sync(0xffffffffu, stop, 0)) return false;
-      }
-    };
     for (int u = pair_id; u < p.units && ok; u += npairs, ++it) {
       int m0, n0, kb0, kb1, split;
       unit_coords<BN2, TM>(p, u, m0, n0, kb0, kb1, split);
       const int buf = it & 1;
       const uint32_t tphase = (it >> 1) & 1;
-      if (!wait2_w(smem_u32(&bars->tempty[buf]), tphase ^ 1, 12)) break;
+      if (!wait2_w(smem_u32(&bars->tempty[buf]), tphase ^ 1, abort, p, 12, lane)) break;
       tc_fence_after();
       const uint32_t d = tmem_base + buf * BN2;
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!wait2_w(smem_u32(&bars->full[stage]), phase, 13)) {
+        if (!wait2_w(smem_u32(&bars->full[stage]), phase, abort, p, 13, lane)) {
           ok = false;
           break;
         }
@@ -819,9 +821,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
       unit_coords<BN2, TM>(p, u, m0, n0, kb0, kb1, split);
       const int buf = it & 1;
       const uint32_t tphase = (it >> 1) & 1;
-      int ok = lane == 0 ? (wait2(smem_u32(&bars->tfull[buf]), tphase, abort, p, 14) ? 1 : 0) : 0;
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
+      if (!wait2_w(smem_u32(&bars->tfull[buf]), tphase, abort, p, 14, lane)) break;
       tc_fence_after();
       const int row0 = m0 + HALF * rank + quarter * 32;
       const int row = m0 + row_in_tile;
