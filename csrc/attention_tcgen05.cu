@@ -258,16 +258,17 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
   auto col_p = [](int t) { return SEP_P ? (uint32_t)(256 + 64 * t) : (uint32_t)(128 * t); };
   auto col_o = [](int t) { return SEP_P ? (uint32_t)(384 + 64 * t) : (uint32_t)(256 + D * t); };
 
-  if (warp == 0 && lane == 0) {
+  if (warp == 0) {
     // ------------------------------------------------------------ TMA
+    // (the whole warp; one elected lane issues the copies)
     const uint32_t qb = smem_u32(&bars->q_full);
-    mbar_expect_tx(qb, (has1 ? 2 : 1) * S::Q_BYTES);
+    mbar_expect_tx_w(qb, (has1 ? 2 : 1) * S::Q_BYTES);
 #pragma unroll
     for (int cc = 0; cc < D / 64; ++cc) {
-      tma_load_2d(smem_u32(sQ) + cc * S::CHUNK, &tm, qb, p.q_col + h * D + 64 * cc,
+      tma_load_2d_w(smem_u32(sQ) + cc * S::CHUNK, &tm, qb, p.q_col + h * D + 64 * cc,
                   row0 + qt0 * BQ);
       if (has1)
-        tma_load_2d(smem_u32(sQ + S::Q_BYTES) + cc * S::CHUNK, &tm, qb,
+        tma_load_2d_w(smem_u32(sQ + S::Q_BYTES) + cc * S::CHUNK, &tm, qb,
                     p.q_col + h * D + 64 * cc, row0 + qt1 * BQ);
     }
     int kpend[KV_STAGES], vpend[KV_STAGES];
@@ -277,20 +278,20 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
       const int st = j % KV_STAGES;
       const uint32_t ph = (j / KV_STAGES) & 1;
       const int y = row0 + j * BKV;
-      if (!wait_b(smem_u32(&bars->k_empty[st]), ph ^ 1, abort, p, 21)) break;
+      if (!warp_wait_f(smem_u32(&bars->k_empty[st]), ph ^ 1, abort, p, 21, lane)) break;
       const uint32_t kb = smem_u32(&bars->k_full[st]);
-      mbar_expect_tx(kb, S::KV_BYTES);
+      mbar_expect_tx_w(kb, S::KV_BYTES);
 #pragma unroll
       for (int cc = 0; cc < D / 64; ++cc)
-        tma_load_2d(smem_u32(sK + st * S::KV_BYTES) + cc * S::CHUNK, &tm, kb,
+        tma_load_2d_w(smem_u32(sK + st * S::KV_BYTES) + cc * S::CHUNK, &tm, kb,
                     p.k_col + g * D + 64 * cc, y);
       kpend[st] = (int)ph;
-      if (!wait_b(smem_u32(&bars->v_empty[st]), ph ^ 1, abort, p, 22)) break;
+      if (!warp_wait_f(smem_u32(&bars->v_empty[st]), ph ^ 1, abort, p, 22, lane)) break;
       const uint32_t vb = smem_u32(&bars->v_full[st]);
-      mbar_expect_tx(vb, S::KV_BYTES);
+      mbar_expect_tx_w(vb, S::KV_BYTES);
 #pragma unroll
       for (int cc = 0; cc < D / 64; ++cc)
-        tma_load_2d(smem_u32(sV + st * S::KV_BYTES) + cc * S::CHUNK, &tm, vb,
+        tma_load_2d_w(smem_u32(sV + st * S::KV_BYTES) + cc * S::CHUNK, &tm, vb,
                     p.v_col + g * D + 64 * cc, y);
       vpend[st] = (int)ph;
     }
@@ -814,8 +815,9 @@ attn_bwd64_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_consta
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == 0 && lane == 0) {
+  if (warp == 0) {
     // ------------------------------------------------------------ TMA
+    // (the whole warp; one elected lane issues the copies)
     Cursor c, kc;   // next tile to load; next item whose K / V to load
     c.start(p);
     kc.start(p);
@@ -828,16 +830,16 @@ attn_bwd64_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_consta
       const uint32_t eb = smem_u32(&bars->kv_empty[kb]), par = ((kc.k - 2) >> 1) & 1;
       if (kc.k >= 2) {
         if (wait) {
-          if (!wait_b(eb, par, abort, p, 40)) return false;
-        } else if (!mbar_test(eb, par)) {
+          if (!warp_wait(eb, par, abort, p, 40, lane)) return false;
+        } else if (!warp_test(eb, par)) {
           return true;
         }
       }
       const uint32_t fb = smem_u32(&bars->kv_full[kb]);
       const int row = kc.b * p.T + kc.j * 128;
-      mbar_expect_tx(fb, 2 * L::KV);
-      tma_load_2d(sbase + L::KV_OFF + kb * 2 * L::KV, &tm_kv, fb, p.k_col + kc.g * D, row);
-      tma_load_2d(sbase + L::KV_OFF + kb * 2 * L::KV + L::KV, &tm_kv, fb, p.v_col + kc.g * D, row);
+      mbar_expect_tx_w(fb, 2 * L::KV);
+      tma_load_2d_w(sbase + L::KV_OFF + kb * 2 * L::KV, &tm_kv, fb, p.k_col + kc.g * D, row);
+      tma_load_2d_w(sbase + L::KV_OFF + kb * 2 * L::KV + L::KV, &tm_kv, fb, p.v_col + kc.g * D, row);
       used |= 1u << (kStages64 + kb);
       phases = (phases & ~(1u << (kStages64 + kb))) | ((uint32_t)((kc.k >> 1) & 1) << (kStages64 + kb));
       ++kc.k;
@@ -853,15 +855,19 @@ attn_bwd64_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_consta
       const uint32_t eb = smem_u32(&bars->qo_empty[s]);
       // while the ring slot is busy, load the next item's K / V if its buffer frees
       const uint64_t t0 = gtime();
-      while (!mbar_try_for(eb, ph ^ 1, 2000u)) {
+      while (!__all_sync(0xffffffffu, mbar_try_for(eb, ph ^ 1, 2000u))) {
         if (kc.valid && kc.k == c.k + 1 && !load_kv(false)) ok = false;
-        if (!ok || *abort) {
-          ok = false;
-          break;
+        int stop = 0;
+        if (lane == 0) {
+          if (!ok || *abort) {
+            stop = 1;
+          } else if (gtime() - t0 > p.timeout_ns) {
+            *abort = 1;
+            atomicCAS(p.err, 0u, 41u);
+            stop = 1;
+          }
         }
-        if (gtime() - t0 > p.timeout_ns) {
-          *abort = 1;
-          atomicCAS(p.err, 0u, 41u);
+        if (__shfl_sync(0xffffffffu, stop, 0)) {
           ok = false;
           break;
         }
@@ -869,9 +875,9 @@ attn_bwd64_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_consta
       if (!ok) break;
       const uint32_t fb = smem_u32(&bars->qo_full[s]);
       const int row = c.b * p.T + c.q0(), h = c.head(p);
-      mbar_expect_tx(fb, 2 * L::QT);
-      tma_load_2d(sbase + L::Q_OFF + s * L::QT, &tm_q, fb, p.q_col + h * D, row);
-      tma_load_2d(sbase + L::DO_OFF + s * L::QT, &tm_do, fb, h * D, row);
+      mbar_expect_tx_w(fb, 2 * L::QT);
+      tma_load_2d_w(sbase + L::Q_OFF + s * L::QT, &tm_q, fb, p.q_col + h * D, row);
+      tma_load_2d_w(sbase + L::DO_OFF + s * L::QT, &tm_do, fb, h * D, row);
       used |= 1u << s;
       phases = (phases & ~(1u << s)) | (ph << s);
       if (kc.valid && kc.k == c.k + 1) load_kv(false);
@@ -1363,15 +1369,16 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == 0 && lane == 0) {
+  if (warp == 0) {
     // ------------------------------------------------------------ TMA
+    // (the whole warp; one elected lane issues the copies)
     const uint32_t kvb = smem_u32(&bars->kv_full);
-    mbar_expect_tx(kvb, 2 * L::TILE);
+    mbar_expect_tx_w(kvb, 2 * L::TILE);
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
-      tma_load_2d(sbase + L::K_OFF + c * L::CH, &tm_qkv, kvb, p.k_col + g * D + 64 * c,
+      tma_load_2d_w(sbase + L::K_OFF + c * L::CH, &tm_qkv, kvb, p.k_col + g * D + 64 * c,
                   row0 + j * 128);
-      tma_load_2d(sbase + L::V_OFF + c * L::CH, &tm_qkv, kvb, p.v_col + g * D + 64 * c,
+      tma_load_2d_w(sbase + L::V_OFF + c * L::CH, &tm_qkv, kvb, p.v_col + g * D + 64 * c,
                   row0 + j * 128);
     }
     int pend[2] = {-1, -1};
@@ -1379,14 +1386,14 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
       const int st = it & 1;
       const uint32_t ph = (it >> 1) & 1;
       const int h = g * rep + it / n_i, i = j + it % n_i;
-      if (!wait_b(smem_u32(&bars->qo_empty[st]), ph ^ 1, abort, p, 51)) break;
+      if (!warp_wait(smem_u32(&bars->qo_empty[st]), ph ^ 1, abort, p, 51, lane)) break;
       const uint32_t fb = smem_u32(&bars->qo_full[st]);
-      mbar_expect_tx(fb, 2 * L::TILE);
+      mbar_expect_tx_w(fb, 2 * L::TILE);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        tma_load_2d(sbase + L::Q_OFF + st * L::TILE + c * L::CH, &tm_qkv, fb,
+        tma_load_2d_w(sbase + L::Q_OFF + st * L::TILE + c * L::CH, &tm_qkv, fb,
                     p.q_col + h * D + 64 * c, row0 + i * 128);
-        tma_load_2d(sbase + L::DO_OFF + st * L::TILE + c * L::CH, &tm_do, fb, h * D + 64 * c,
+        tma_load_2d_w(sbase + L::DO_OFF + st * L::TILE + c * L::CH, &tm_do, fb, h * D + 64 * c,
                     row0 + i * 128);
       }
       pend[st] = (int)ph;
