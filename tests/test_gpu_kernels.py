@@ -179,18 +179,24 @@ def test_swiglu(dtype):
 
 
 @pytest.mark.parametrize("dtype", DT)
-@pytest.mark.parametrize("V", [50257, 1000])
-def test_cross_entropy(dtype, V):
+@pytest.mark.parametrize("V,ld", [(50257, 50257), (1000, 1000), (50257, 50304), (1003, 1008)])
+def test_cross_entropy(dtype, V, ld):
+    """ld > V: rows padded to a multiple of 8 (the vectorized forward path)."""
     torch.manual_seed(3)
     M = 129
-    logits = (torch.randn(M, V, device="cuda") * 3).to(dtype)
+    logits = (torch.randn(M, ld, device="cuda") * 3).to(dtype)[:, :V]
     tgt = torch.randint(0, V, (M,), device="cuda")
     tgt[5] = -100
     ref_l = logits.detach().float().requires_grad_()
     ref = F.cross_entropy(ref_l, tgt)
     (ref * 7).backward()
-    lg = logits.clone().requires_grad_()
-    loss = ops.cross_entropy(lg * 1, tgt)  # autograd path (non-leaf logits)
+    if ld == V:
+        lg = logits.clone().requires_grad_()
+        loss = ops.cross_entropy(lg * 1, tgt)  # autograd path (non-leaf logits)
+    else:
+        # the padded view itself (rows ld apart); its storage becomes the gradient
+        lg = logits.requires_grad_()
+        loss = ops.cross_entropy(lg, tgt)
     (loss * 7).backward()
     assert float(loss) == pytest.approx(float(ref), rel=1e-5, abs=1e-5)
     rt, at = _tol(dtype)
