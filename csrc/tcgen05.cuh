@@ -58,14 +58,24 @@ __device__ __forceinline__ bool mbar_try_for(uint32_t bar, uint32_t parity, uint
       : "memory");
   return ok != 0;
 }
+// non-blocking probe of a phase (no suspension)
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Warp-wide bounded wait: every lane polls, and the vote keeps the warp
 // converged through the wait.  A warp that waited on lane 0 alone (the other
 // lanes parked at a shuffle) issued its next tcgen05.mma ops about five
 // times slower on B200 in the attention backward (measured, head dim 128:
 // 1.39 vs 0.83 ms).  Returns 1 when the phase completed, 0 when *abort was
 // raised or timeout_ns passed (then lane 0 raises *abort and records code).
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity);
-__device__ __forceinline__ uint64_t gtime();
 __device__ __forceinline__ bool warp_wait_all(uint32_t bar, uint32_t parity, volatile int* abort,
                                               unsigned* err, unsigned code,
                                               unsigned long long timeout_ns, int lane) {
@@ -87,21 +97,8 @@ __device__ __forceinline__ bool warp_wait_all(uint32_t bar, uint32_t parity, vol
   }
 }
 // non-blocking probe, the same answer in every lane of a converged warp
-__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity);
 __device__ __forceinline__ bool warp_test(uint32_t bar, uint32_t parity) {
   return __all_sync(0xffffffffu, mbar_test(bar, parity));
-}
-// non-blocking probe of a phase (no suspension)
-__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int x, int y) {

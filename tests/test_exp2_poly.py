@@ -1,5 +1,6 @@
-"""The FMA-pipe exp2 used by the attention backward (``exp2_poly`` in
-``csrc/attention_tcgen05.cu``), evaluated step by step in float32 with numpy:
+"""The FMA-pipe exp2 the attention backward can use for part of its
+exponentials (``exp2_poly`` in ``csrc/attention_tcgen05.cu``, selected at
+build time with ``-DMSB_EXP2_POLY=n``), evaluated step by step in float32:
 range reduction through the 1.5 * 2^23 rounding constant, degree-3 minimax
 polynomial, exponent-field add.  Checks the relative error bound the kernel
 comment states and the clamp at -125."""
