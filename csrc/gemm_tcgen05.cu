@@ -97,22 +97,8 @@ struct alignas(8) Barriers {
   int abort;
 };
 
-// Bounded wait: returns false when the CTA aborted or the limit passed.
-__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort,
-                                         const Params& p, unsigned code) {
-  if (mbar_try(bar, parity)) return true;
-  const uint64_t t0 = gtime();
-  while (true) {
-    if (mbar_try(bar, parity)) return true;
-    if (*abort) return false;
-    if (gtime() - t0 > p.timeout_ns) {
-      *abort = 1;
-      atomicCAS(p.err, 0u, code);
-      return false;
-    }
-  }
-}
-// the same for a whole converged warp (see warp_wait_all)
+// Bounded wait of a whole converged warp (see warp_wait_all): false when the
+// CTA aborted or the limit passed.
 __device__ __forceinline__ bool wait_bar_w(uint32_t bar, uint32_t parity, volatile int* abort,
                                            const Params& p, unsigned code, int lane) {
   return warp_wait_all(bar, parity, abort, p.err, code, p.timeout_ns, lane);
@@ -553,21 +539,8 @@ __device__ __forceinline__ bool try_cluster(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ bool wait2(uint32_t bar, uint32_t parity, volatile int* abort,
-                                      const Params& p, unsigned code) {
-  if (try_cluster(bar, parity)) return true;
-  const uint64_t t0 = gtime();
-  while (true) {
-    if (try_cluster(bar, parity)) return true;
-    if (*abort) return false;
-    if (gtime() - t0 > p.timeout_ns) {
-      *abort = 1;
-      atomicCAS(p.err, 0u, code);
-      return false;
-    }
-  }
-}
-// the same for a whole converged warp: every lane polls and votes (see warp_wait_all)
+// Bounded cluster-scope wait of a whole converged warp: every lane polls and
+// votes (see warp_wait_all); false when the CTA aborted or the limit passed.
 __device__ __forceinline__ bool wait2_w(uint32_t bar, uint32_t parity, volatile int* abort,
                                         const Params& p, unsigned code, int lane) {
   if (__all_sync(0xffffffffu, try_cluster(bar, parity))) return true;
@@ -609,28 +582,9 @@ __device__ __forceinline__ void dealloc2(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
                : "memory");
 }
-__device__ __forceinline__ void mma2(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
-                                     uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 // arrive (when the issued MMAs retire) on the barrier at this offset in
 // both CTAs of the pair: one commit per barrier, the peer's addressed
 // through its shared::cluster window
-__device__ __forceinline__ void commit2_to(uint32_t cluster_bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          cluster_bar)
-      : "memory");
-}
-__device__ __forceinline__ void commit2_both(uint32_t bar) {
-  commit2_to(bar);
-  commit2_to(mapa(bar, 1));
-}
 // warp-wide forms (one elected lane issues; see umma_f16_w)
 __device__ __forceinline__ void mma2_w(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
                                        uint32_t accumulate) {
