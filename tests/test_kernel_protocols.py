@@ -1,5 +1,6 @@
-"""Barrier protocol of the persistent head-dim-64 attention backward
-(``attn_bwd64_kernel`` in ``csrc/attention_tcgen05.cu``), checked on the CPU.
+"""Barrier protocols of the persistent head-dim-64 attention backward
+(``attn_bwd64_kernel`` in ``csrc/attention_tcgen05.cu``) and of the tcgen05
+GEMM (``gemm_kernel`` in ``csrc/gemm_tcgen05.cu``), checked on the CPU.
 
 The kernel's roles (TMA warp, MMA warp, softmax warps, dQ warps) synchronise
 only through mbarriers whose waits name a phase parity.  A wrong parity is a
@@ -168,10 +169,12 @@ def barriers():
     return bars
 
 
-def run(items, seed):
+def run(items, seed, progs=None, bars=None):
+    """Random interleavings of the roles; a wait whose intended completion
+    index is None only has to pass (no index check)."""
     rng = random.Random(seed)
-    progs = roles(items)
-    bars = barriers()
+    if progs is None:
+        progs, bars = roles(items), barriers()
     pc = {r: 0 for r in progs}
     tma_async, mma_fifo = [], []
     readers = {}          # resource -> number of warps reading it (generic proxy)
@@ -191,6 +194,10 @@ def run(items, seed):
             if op[0] == "wait":
                 _, b, parity, k = op
                 bar = bars[b]
+                if k is None:
+                    if bar.passes(parity):
+                        choices.append(("run", r))
+                    continue
                 # no barrier may run two phases ahead of a waiter
                 assert bar.completed <= k + 1, (r, op, bar.completed)
                 if bar.passes(parity):
@@ -297,3 +304,58 @@ def test_work_items_cover_every_tile_once():
                         seen.add(key)
                 k += 1
         assert len(seen) == nbh * rep * sum(2 * (n_q - j) for j in range(n_q))
+
+
+# ---------------------------------------------------------------- GEMM
+def gemm_roles(units_kb, stages=4):
+    """The persistent tcgen05 GEMM (``gemm_kernel`` in ``csrc/gemm_tcgen05.cu``)
+    for one CTA: a TMA producer over a `stages`-deep operand ring, the MMA
+    warp with two tensor-memory accumulators, the epilogue warps (one role
+    here; the barrier counts them as one arrival per phase).  `units_kb`
+    lists the k-blocks of each tile the CTA owns."""
+    tma, mma, epi = [], [], []
+    g = 0                                  # k-blocks so far: slot g % stages, use g // stages
+    stage, phase = 0, 0
+    for kbs in units_kb:
+        for _ in range(kbs):
+            tma.append(("wait", f"empty{stage}", phase ^ 1, g // stages - 1))
+            tma.append(("async", "tma", f"full{stage}"))
+            stage, phase = (0, phase ^ 1) if stage + 1 == stages else (stage + 1, phase)
+            g += 1
+    g = 0
+    stage, phase = 0, 0
+    for u, kbs in enumerate(units_kb):
+        buf, tphase = u & 1, (u >> 1) & 1
+        mma.append(("wait", f"tempty{buf}", tphase ^ 1, (u >> 1) - 1))
+        for _ in range(kbs):
+            mma.append(("wait", f"full{stage}", phase, g // stages))
+            g += 1
+            mma.append(("mma_op", (f"ring{stage}",), (f"ACC{buf}",)))
+            mma.append(("async", "mma", f"empty{stage}"))
+            stage, phase = (0, phase ^ 1) if stage + 1 == stages else (stage + 1, phase)
+        mma.append(("async", "mma", f"tfull{buf}"))
+        epi.append(("wait", f"tfull{buf}", tphase, u >> 1))
+        epi.append(("read_begin", f"ACC{buf}"))
+        epi.append(("read_end", f"ACC{buf}"))
+        epi.append(("arrive", f"tempty{buf}"))
+    mma.append(("async", "mma", "drain"))
+    mma.append(("wait", "drain", 0, 0))
+    return {"tma": tma, "mma": mma, "epilogue": epi}
+
+
+def gemm_barriers(stages=4):
+    bars = {}
+    for s in range(stages):
+        bars[f"full{s}"] = Barrier(f"full{s}", 1)
+        bars[f"empty{s}"] = Barrier(f"empty{s}", 1)
+    for b in range(2):
+        bars[f"tfull{b}"] = Barrier(f"tfull{b}", 1)
+        bars[f"tempty{b}"] = Barrier(f"tempty{b}", 1)
+    bars["drain"] = Barrier("drain", 1)
+    return bars
+
+
+@pytest.mark.parametrize("units_kb", [[12] * 8, [3, 1, 7, 2, 5], [1] * 9, [256, 256, 1]])
+def test_gemm_barrier_protocol(units_kb):
+    for seed in range(10):
+        run(None, seed, progs=gemm_roles(units_kb), bars=gemm_barriers())
