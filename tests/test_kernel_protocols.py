@@ -359,3 +359,69 @@ def gemm_barriers(stages=4):
 def test_gemm_barrier_protocol(units_kb):
     for seed in range(10):
         run(None, seed, progs=gemm_roles(units_kb), bars=gemm_barriers())
+
+
+def gemm2_roles(units_kb, stages=4):
+    """The 2-CTA GEMM (``gemm2_kernel``): both CTAs' TMA warps load into
+    their own operand rings and signal the leader's stage barrier (the
+    leader's expect_tx is the one arrival, each CTA's loads complete the
+    transaction bytes); the leader's MMA warp issues for the pair and its
+    commits arrive on both CTAs' barriers; both epilogues release the
+    leader's accumulator barrier."""
+    progs = {"tma0": [], "tma1": [], "mma": [], "epi0": [], "epi1": []}
+    for c in (0, 1):
+        tma = progs[f"tma{c}"]
+        g, stage, phase = 0, 0, 0
+        for kbs in units_kb:
+            for _ in range(kbs):
+                tma.append(("wait", f"c{c}.empty{stage}", phase ^ 1, g // stages - 1))
+                if c == 0:
+                    tma.append(("arrive", f"c0.full{stage}"))     # expect_tx
+                tma.append(("write", f"c{c}.ring{stage}"))
+                tma.append(("async", "tma", f"c0.full{stage}"))   # complete_tx
+                stage, phase = (0, phase ^ 1) if stage + 1 == stages else (stage + 1, phase)
+                g += 1
+    mma = progs["mma"]
+    g, stage, phase = 0, 0, 0
+    for u, kbs in enumerate(units_kb):
+        buf, tphase = u & 1, (u >> 1) & 1
+        mma.append(("wait", f"c0.tempty{buf}", tphase ^ 1, (u >> 1) - 1))
+        for _ in range(kbs):
+            mma.append(("wait", f"c0.full{stage}", phase, g // stages))
+            mma.append(("mma_op", (f"c0.ring{stage}", f"c1.ring{stage}"), (f"c0.ACC{buf}", f"c1.ACC{buf}")))
+            mma.append(("async", "mma", f"c0.empty{stage}"))
+            mma.append(("async", "mma", f"c1.empty{stage}"))
+            stage, phase = (0, phase ^ 1) if stage + 1 == stages else (stage + 1, phase)
+            g += 1
+        mma.append(("async", "mma", f"c0.tfull{buf}"))
+        mma.append(("async", "mma", f"c1.tfull{buf}"))
+        for c in (0, 1):
+            epi = progs[f"epi{c}"]
+            epi.append(("wait", f"c{c}.tfull{buf}", tphase, u >> 1))
+            epi.append(("read_begin", f"c{c}.ACC{buf}"))
+            epi.append(("read_end", f"c{c}.ACC{buf}"))
+            epi.append(("arrive", f"c0.tempty{buf}"))
+    mma.append(("async", "mma", "c0.drain"))
+    mma.append(("wait", "c0.drain", 0, 0))
+    return progs
+
+
+def gemm2_barriers(stages=4):
+    bars = {}
+    for c in (0, 1):
+        for s in range(stages):
+            bars[f"c{c}.empty{s}"] = Barrier(f"c{c}.empty{s}", 1)
+        for b in range(2):
+            bars[f"c{c}.tfull{b}"] = Barrier(f"c{c}.tfull{b}", 1)
+    for s in range(stages):
+        bars[f"c0.full{s}"] = Barrier(f"c0.full{s}", 3)        # expect_tx + both CTAs' bytes
+    for b in range(2):
+        bars[f"c0.tempty{b}"] = Barrier(f"c0.tempty{b}", 2)    # both CTAs' epilogues
+    bars["c0.drain"] = Barrier("c0.drain", 1)
+    return bars
+
+
+@pytest.mark.parametrize("units_kb", [[12] * 8, [3, 1, 7, 2, 5], [1] * 9])
+def test_gemm2_barrier_protocol(units_kb):
+    for seed in range(10):
+        run(None, seed, progs=gemm2_roles(units_kb, stages=6), bars=gemm2_barriers(stages=6))
