@@ -1,6 +1,8 @@
-"""Barrier protocols of the persistent head-dim-64 attention backward
-(``attn_bwd64_kernel`` in ``csrc/attention_tcgen05.cu``) and of the tcgen05
-GEMM (``gemm_kernel`` in ``csrc/gemm_tcgen05.cu``), checked on the CPU.
+"""Barrier protocols of the tcgen05 kernels, checked on the CPU: the
+persistent head-dim-64 attention backward (``attn_bwd64_kernel``), the
+attention forward's event loop (``attn_fwd_kernel``), both in
+``csrc/attention_tcgen05.cu``, and the 1-CTA and 2-CTA GEMMs
+(``csrc/gemm_tcgen05.cu``).
 
 The kernel's roles (TMA warp, MMA warp, softmax warps, dQ warps) synchronise
 only through mbarriers whose waits name a phase parity.  A wrong parity is a
@@ -425,3 +427,163 @@ def gemm2_barriers(stages=4):
 def test_gemm2_barrier_protocol(units_kb):
     for seed in range(10):
         run(None, seed, progs=gemm2_roles(units_kb, stages=6), bars=gemm2_barriers(stages=6))
+
+
+# ------------------------------------------------------- attention forward
+def run_forward(nkv0, nkv1, sep_p, kv_stages, seed):
+    """The attention forward (``attn_fwd_kernel``) for one CTA with query
+    tiles needing nkv0 and nkv1 key tiles: the TMA warp's K / V ring, the MMA
+    warp's event loop (issue S of a tile when its key tile landed and its
+    score columns are free; issue P V when P is written and V landed; release
+    ring slots once every tile that reads them has issued), and the two
+    softmax groups.  Checks waits, parities and tensor-memory reuse as run()
+    does, with the MMA warp's non-blocking probes taken from the live state."""
+    rng = random.Random(seed)
+    nk = [nkv0, nkv1]
+    nkv = max(nkv0, nkv1)
+    bars = {n: Barrier(n, 1) for n in ["q_full", "drain"]}
+    for s in range(kv_stages):
+        for n in ("k_full", "k_empty", "v_full", "v_empty"):
+            bars[f"{n}{s}"] = Barrier(f"{n}{s}", 1)
+    for t in range(2):
+        for n in ("s_full", "s_free", "p_full", "pv_done"):
+            bars[f"{n}{t}"] = Barrier(f"{n}{t}", 1)
+
+    tma = [("async", "tma", "q_full")]
+    for j in range(nkv):
+        st, ph = j % kv_stages, (j // kv_stages) & 1
+        tma += [("wait", f"k_empty{st}", ph ^ 1, j // kv_stages - 1),
+                ("write", f"K{st}"), ("async", "tma", f"k_full{st}"),
+                ("wait", f"v_empty{st}", ph ^ 1, j // kv_stages - 1),
+                ("write", f"V{st}"), ("async", "tma", f"v_full{st}")]
+    softmax = {}
+    for t in range(2):
+        ops = []
+        for j in range(nk[t]):
+            ops += [("wait", f"s_full{t}", j & 1, j), ("read_begin", f"S{t}")]
+            if sep_p:
+                ops += [("read_end", f"S{t}"), ("arrive", f"s_free{t}")]
+                if j > 0:
+                    ops.append(("wait", f"pv_done{t}", (j - 1) & 1, j - 1))
+            ops += [("write", f"P{t}"), ("write", f"O{t}")]     # P, and O rescaled in place
+            if not sep_p:
+                ops.append(("read_end", f"S{t}"))
+            ops.append(("arrive", f"p_full{t}"))
+        if nk[t] > 0:
+            ops += [("wait", f"pv_done{t}", (nk[t] - 1) & 1, nk[t] - 1), ("read_begin", f"O{t}"),
+                    ("read_end", f"O{t}")]
+        softmax[f"softmax{t}"] = ops
+    progs = {"tma": tma, **softmax}
+    pc = {r: 0 for r in progs}
+    js, jp = [0, 0], [0, 0]
+    kfree = vfree = 0
+    q_ok = False
+    mma_done = False
+    tma_async, mma_fifo, retire_mark, inflight = [], [], [], []
+    readers = {}
+
+    def mma_issue(reads, writes, commits):
+        for res in writes:
+            assert readers.get(res, 0) == 0, ("tensor core overwrites a buffer still read", res)
+        inflight.extend([(r, "r") for r in reads] + [(w, "w") for w in writes])
+        for c in commits:
+            mma_fifo.append(c)
+            retire_mark.append(len(inflight))
+
+    def mma_pass():
+        """One pass of the event loop; returns True if it issued anything."""
+        nonlocal kfree, vfree, q_ok
+        if not q_ok:
+            q_ok = bars["q_full"].passes(0)
+            return q_ok
+        progress = False
+        for t in range(2):
+            j = js[t]
+            if j < nk[t]:
+                st = j % kv_stages
+                free = j == 0 or (bars[f"s_free{t}"].passes((j - 1) & 1) if sep_p
+                                  else bars[f"pv_done{t}"].passes((j - 1) & 1))
+                if free and bars[f"k_full{st}"].passes((j // kv_stages) & 1):
+                    mma_issue((f"Q{t}", f"K{st}"), (f"S{t}",), [f"s_full{t}"])
+                    js[t] += 1
+                    progress = True
+            jj = jp[t]
+            if jj < nk[t]:
+                st = jj % kv_stages
+                if (jj < js[t] and bars[f"p_full{t}"].passes(jj & 1)
+                        and bars[f"v_full{st}"].passes((jj // kv_stages) & 1)):
+                    mma_issue((f"P{t}", f"V{st}"), (f"O{t}",), [f"pv_done{t}"])
+                    jp[t] += 1
+                    progress = True
+        while kfree < nkv and (kfree < js[0] or kfree >= nk[0]) and (kfree < js[1] or kfree >= nk[1]):
+            mma_issue((), (), [f"k_empty{kfree % kv_stages}"])
+            kfree += 1
+        while vfree < nkv and (vfree < jp[0] or vfree >= nk[0]) and (vfree < jp[1] or vfree >= nk[1]):
+            mma_issue((), (), [f"v_empty{vfree % kv_stages}"])
+            vfree += 1
+        return progress
+
+    steps = 0
+    while True:
+        steps += 1
+        assert steps < 2_000_000
+        choices = []
+        for r, ops in progs.items():
+            if pc[r] >= len(ops):
+                continue
+            op = ops[pc[r]]
+            if op[0] == "wait":
+                _, b, parity, k = op
+                bar = bars[b]
+                assert bar.completed <= k + 1, (r, op, bar.completed)
+                if bar.passes(parity):
+                    assert bar.completed == k + 1, (r, op, bar.completed)
+                    choices.append(("run", r))
+            else:
+                choices.append(("run", r))
+        pending_mma = js[0] < nk[0] or js[1] < nk[1] or jp[0] < nk[0] or jp[1] < nk[1] or not q_ok
+        if pending_mma:
+            choices.append(("mma", None))
+        if tma_async:
+            choices.append(("tma_done", None))
+        if mma_fifo:
+            choices.append(("mma_done", None))
+        if not choices:
+            unfinished = [r for r in progs if pc[r] < len(progs[r])]
+            assert not unfinished and not pending_mma, ("deadlock", unfinished, js, jp)
+            return
+        kind, r = rng.choice(choices)
+        if kind == "mma":
+            if not mma_pass() and not tma_async and not mma_fifo:
+                # the event loop can only make progress after another role acts
+                others = [c for c in choices if c[0] == "run"]
+                assert others, ("MMA event loop stuck", js, jp, {k: pc[k] for k in pc})
+            continue
+        if kind == "tma_done":
+            bars[tma_async.pop(rng.randrange(len(tma_async)))].arrive()
+            continue
+        if kind == "mma_done":
+            bars[mma_fifo.pop(0)].arrive()
+            n = retire_mark.pop(0)
+            del inflight[:n]
+            retire_mark[:] = [m - n for m in retire_mark]
+            continue
+        op = progs[r][pc[r]]
+        pc[r] += 1
+        if op[0] == "arrive":
+            bars[op[1]].arrive()
+        elif op[0] == "async":
+            tma_async.append(op[2])
+        elif op[0] == "read_begin":
+            readers[op[1]] = readers.get(op[1], 0) + 1
+        elif op[0] == "read_end":
+            readers[op[1]] -= 1
+        elif op[0] == "write":
+            assert all(res != op[1] for res, _ in inflight), ("write while an MMA uses it", op[1])
+
+
+@pytest.mark.parametrize("sep_p,kv_stages", [(True, 3), (False, 2)])
+@pytest.mark.parametrize("nkv0,nkv1", [(1, 2), (3, 4), (7, 8), (5, 0), (8, 8)])
+def test_attention_forward_protocol(sep_p, kv_stages, nkv0, nkv1):
+    for seed in range(15):
+        run_forward(nkv0, nkv1, sep_p, kv_stages, seed)
