@@ -1,8 +1,8 @@
 """Barrier protocols of the tcgen05 kernels, checked on the CPU: the
 persistent head-dim-64 attention backward (``attn_bwd64_kernel``), the
-attention forward's event loop (``attn_fwd_kernel``), both in
-``csrc/attention_tcgen05.cu``, and the 1-CTA and 2-CTA GEMMs
-(``csrc/gemm_tcgen05.cu``).
+head-dim-128 backward (``attn_bwd128_kernel``) and the attention forward's
+event loop (``attn_fwd_kernel``), all in ``csrc/attention_tcgen05.cu``, and
+the 1-CTA and 2-CTA GEMMs (``csrc/gemm_tcgen05.cu``).
 
 The kernel's roles (TMA warp, MMA warp, softmax warps, dQ warps) synchronise
 only through mbarriers whose waits name a phase parity.  A wrong parity is a
@@ -240,14 +240,15 @@ def run(items, seed, progs=None, bars=None):
         elif op[0] == "mma_op":
             reads, writes = op[1], op[2]
             for res in writes:
-                assert readers.get(res, 0) == 0, ("tensor core overwrites a buffer still read", res)
+                assert not readers.get(res), ("tensor core overwrites a buffer still read", res)
             inflight.extend([(res, "r") for res in reads] + [(res, "w") for res in writes])
         elif op[0] == "read_begin":
-            readers[op[1]] = readers.get(op[1], 0) + 1
+            readers.setdefault(op[1], set()).add(r)
         elif op[0] == "read_end":
-            readers[op[1]] -= 1
+            readers[op[1]].discard(r)
         elif op[0] == "write":
             assert all(res != op[1] for res, _ in inflight), ("write while an MMA uses it", op[1])
+            assert not (readers.get(op[1], set()) - {r}), ("write while another role reads", op[1])
         elif op[0] == "poll_kv":
             k = op[1]
             if k in kv_loaded:
@@ -484,7 +485,7 @@ def run_forward(nkv0, nkv1, sep_p, kv_stages, seed):
 
     def mma_issue(reads, writes, commits):
         for res in writes:
-            assert readers.get(res, 0) == 0, ("tensor core overwrites a buffer still read", res)
+            assert not readers.get(res), ("tensor core overwrites a buffer still read", res)
         inflight.extend([(r, "r") for r in reads] + [(w, "w") for w in writes])
         for c in commits:
             mma_fifo.append(c)
@@ -575,11 +576,12 @@ def run_forward(nkv0, nkv1, sep_p, kv_stages, seed):
         elif op[0] == "async":
             tma_async.append(op[2])
         elif op[0] == "read_begin":
-            readers[op[1]] = readers.get(op[1], 0) + 1
+            readers.setdefault(op[1], set()).add(r)
         elif op[0] == "read_end":
-            readers[op[1]] -= 1
+            readers[op[1]].discard(r)
         elif op[0] == "write":
             assert all(res != op[1] for res, _ in inflight), ("write while an MMA uses it", op[1])
+            assert not (readers.get(op[1], set()) - {r}), ("write while another role reads", op[1])
 
 
 @pytest.mark.parametrize("sep_p,kv_stages", [(True, 3), (False, 2)])
@@ -587,3 +589,63 @@ def run_forward(nkv0, nkv1, sep_p, kv_stages, seed):
 def test_attention_forward_protocol(sep_p, kv_stages, nkv0, nkv1):
     for seed in range(15):
         run_forward(nkv0, nkv1, sep_p, kv_stages, seed)
+
+
+# ------------------------------------------- attention backward, head dim 128
+def bwd128_roles(nit):
+    """``attn_bwd128_kernel`` for one CTA walking `nit` 128-row query tiles:
+    one score buffer in tensor memory (P^T and dS^T packed in place, the dQ
+    halves in the freed columns), the dS^T tile in shared memory doubling as
+    the dQ staging of the reduce-adds.  The four softmax warps and the four
+    dQ warps are one role each (one arrival per phase)."""
+    tma = [("write", "K"), ("async", "tma", "kv_full")]
+    for it in range(nit):
+        st, ph = it & 1, (it >> 1) & 1
+        if it >= 2:
+            tma.append(("wait", f"qo_empty{st}", ph ^ 1, (it >> 1) - 1))
+        tma += [("write", f"Q{st}"), ("async", "tma", f"qo_full{st}")]
+    mma = [("wait", "kv_full", 0, 0)]
+    for it in range(nit):
+        st, ph = it & 1, (it >> 1) & 1
+        mma.append(("wait", f"qo_full{st}", ph, it >> 1))
+        if it > 0:
+            mma += [("wait", "mma2_done", (it - 1) & 1, it - 1),
+                    ("wait", "dq_free", (it - 1) & 1, it - 1)]
+        mma += [("mma_op", ("K", f"Q{st}"), ("S", "DQ")), ("async", "mma", "st_full"),
+                ("wait", "ds_ready", it & 1, it),
+                ("mma_op", ("S", f"Q{st}", "DSB", "K"), ("ACC", "DQ")),
+                ("async", "mma", f"qo_empty{st}"), ("async", "mma", "mma2_done"),
+                ("async", "mma", "dq_full")]
+    mma += [("async", "mma", "drain"), ("wait", "drain", 0, 0)]
+    sm = []
+    for it in range(nit):
+        if it > 0:
+            sm.append(("wait", "ds_ready", (it - 1) & 1, it - 1))
+        sm += [("arrive", "lse_full"), ("wait", "lse_full", it & 1, it),
+               ("wait", "st_full", it & 1, it)]
+        if it > 0:
+            sm.append(("wait", "stg_free", (it - 1) & 1, it - 1))
+        sm += [("read_begin", "S"), ("write", "S"), ("write", "DSB"), ("read_end", "S"),
+               ("arrive", "ds_ready")]
+    if nit:
+        sm += [("wait", "mma2_done", (nit - 1) & 1, nit - 1), ("read_begin", "ACC"),
+               ("read_end", "ACC")]
+    dq = []
+    for it in range(nit):
+        dq += [("wait", "dq_full", it & 1, it), ("read_begin", "DQ"), ("read_end", "DQ"),
+               ("arrive", "dq_free"), ("write", "DSB"), ("read_begin", "DSB"),
+               ("read_end", "DSB"), ("arrive", "stg_free")]
+    progs = {"tma": tma, "mma": mma, "softmax": sm, "dq": dq}
+    bars = {n: Barrier(n, 1) for n in ("kv_full", "st_full", "ds_ready", "mma2_done", "dq_full",
+                                        "dq_free", "stg_free", "lse_full", "drain")}
+    for s in range(2):
+        bars[f"qo_full{s}"] = Barrier(f"qo_full{s}", 1)
+        bars[f"qo_empty{s}"] = Barrier(f"qo_empty{s}", 1)
+    return progs, bars
+
+
+@pytest.mark.parametrize("nit", [1, 2, 5, 32])
+def test_attention_backward128_protocol(nit):
+    for seed in range(12):
+        progs, bars = bwd128_roles(nit)
+        run(None, seed, progs=progs, bars=bars)
