@@ -1,8 +1,9 @@
 """Barrier protocols of the tcgen05 kernels, checked on the CPU: the
 persistent head-dim-64 attention backward (``attn_bwd64_kernel``), the
 head-dim-128 backward (``attn_bwd128_kernel``) and the attention forward's
-event loop (``attn_fwd_kernel``), all in ``csrc/attention_tcgen05.cu``, and
-the 1-CTA and 2-CTA GEMMs (``csrc/gemm_tcgen05.cu``).
+event loop (``attn_fwd_kernel``), all in ``csrc/attention_tcgen05.cu``,
+the 1-CTA and 2-CTA GEMMs (``csrc/gemm_tcgen05.cu``), and the cross-GPU
+epoch protocol of the fused NVLink step (``csrc/collectives.cu``).
 
 The kernel's roles (TMA warp, MMA warp, softmax warps, dQ warps) synchronise
 only through mbarriers whose waits name a phase parity.  A wrong parity is a
@@ -649,3 +650,114 @@ def test_attention_backward128_protocol(nit):
     for seed in range(12):
         progs, bars = bwd128_roles(nit)
         run(None, seed, progs=progs, bars=bars)
+
+
+# ------------------------------------------------- fused NVLink step pipeline
+def run_fused_step(world, steps, seed, barrier_after=True):
+    """The fused collective step (``minispeed_b200/parallel/fused.py``,
+    ``csrc/collectives.cu``) across `world` ranks: backward writes the rank's
+    gradient arena; ``peer_barrier``; ``rs_stats`` reads every peer's arena;
+    ``stats_exchange`` posts (flag, sum of squares, epoch) on every peer's
+    board and waits for every board slot to carry this epoch; ``adamw_fanout``
+    stores into every peer's parameter arena; ``peer_barrier``.  Both barrier
+    kinds take their epoch from the rank's one device counter.  Checks that
+    no rank reads a peer's gradients while that peer writes them, that no
+    parameter store lands while the owner computes with its parameters, that
+    every exchange reads the values of its own epoch, and that nothing hangs."""
+    rng = random.Random(seed)
+    flags = [[0] * world for _ in range(world)]        # flags[owner][writer]
+    board = [[(0, None) for _ in range(world)] for _ in range(world)]   # (epoch, value)
+    busy = {}                                           # resource -> set of ranks using it
+    progs = []
+    for r in range(world):
+        ops, e = [], 0
+        for s in range(steps):
+            ops += [("use", f"P{r}", f"G{r}", "begin"), ("use", f"P{r}", f"G{r}", "end")]
+            e += 1
+            ops += [("flag_post", e), ("flag_wait", e)]
+            ops += [("read_peers", "G", "begin"), ("read_peers", "G", "end")]
+            e += 1
+            ops += [("board_post", e, (s, r)), ("board_wait", e, s)]
+            ops += [("write_peers", "P", "begin"), ("write_peers", "P", "end")]
+            if barrier_after:
+                e += 1
+                ops += [("flag_post", e), ("flag_wait", e)]
+        progs.append(ops)
+    pc = [0] * world
+    n = 0
+    while True:
+        n += 1
+        assert n < 2_000_000
+        runnable = []
+        for r in range(world):
+            if pc[r] >= len(progs[r]):
+                continue
+            op = progs[r][pc[r]]
+            if op[0] == "flag_wait":
+                # signed difference, as the kernel compares epochs
+                if all(flags[r][q] - op[1] >= 0 for q in range(world)):
+                    runnable.append(r)
+            elif op[0] == "board_wait":
+                eps = [board[r][q][0] for q in range(world)]
+                assert all(x <= op[1] for x in eps), ("a peer posted a later epoch", r, eps, op)
+                if all(x == op[1] for x in eps):
+                    runnable.append(r)
+            else:
+                runnable.append(r)
+        if not runnable:
+            assert all(pc[r] >= len(progs[r]) for r in range(world)), ("hang", pc)
+            return
+        r = rng.choice(runnable)
+        op = progs[r][pc[r]]
+        pc[r] += 1
+        kind = op[0]
+        if kind == "use":        # forward + backward: reads own params, writes own gradients
+            _, p, g, phase = op
+            if phase == "begin":
+                assert not busy.get(p) and not busy.get(g), ("peers use this rank's arenas", r, busy)
+                busy.setdefault(f"own{p}", set()).add(r)
+                busy.setdefault(f"own{g}", set()).add(r)
+            else:
+                busy[f"own{p}"].discard(r)
+                busy[f"own{g}"].discard(r)
+        elif kind == "flag_post":
+            for q in range(world):
+                flags[q][r] = op[1]
+        elif kind == "board_post":
+            for q in range(world):
+                board[q][r] = (op[1], op[2])
+        elif kind == "board_wait":
+            vals = [board[r][q][1] for q in range(world)]
+            assert all(v == (op[2], q) for q, v in enumerate(vals)), ("stale board", r, vals)
+        elif kind == "read_peers":
+            for q in range(world):
+                if op[2] == "begin":
+                    assert not busy.get(f"ownG{q}"), ("reads gradients a peer is writing", r, q)
+                    busy.setdefault(f"G{q}", set()).add(r)
+                else:
+                    busy[f"G{q}"].discard(r)
+        elif kind == "write_peers":
+            for q in range(world):
+                if op[2] == "begin":
+                    assert not busy.get(f"ownP{q}"), ("stores into parameters in use", r, q)
+                    busy.setdefault(f"P{q}", set()).add(r)
+                else:
+                    busy[f"P{q}"].discard(r)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_step_protocol(world):
+    for seed in range(20):
+        run_fused_step(world, steps=4, seed=seed)
+
+
+def test_fused_step_needs_the_closing_barrier():
+    """Without the barrier after the parameter stores, some interleaving lets
+    a rank start its next backward while a peer still stores into it."""
+    failures = 0
+    for seed in range(200):
+        try:
+            run_fused_step(2, steps=3, seed=seed, barrier_after=False)
+        except AssertionError:
+            failures += 1
+    assert failures > 0
