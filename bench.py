@@ -216,7 +216,7 @@ class RefLlama(nn.Module):
 # ------------------------------------------------------------ clocks
 class ClockSampler:
     """Samples nvidia-smi clocks/throttle reasons in a thread, one query every
-    50 ms after the previous one returns (the timed region of the headline
+    100 ms after the previous one returns (the timed region of the headline
     run lasts well under a second)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -240,7 +240,7 @@ class ClockSampler:
                     self.rows.append([c.strip() for c in line.split(",")])
             except Exception:
                 pass
-            self._stop.wait(0.05)
+            self._stop.wait(0.1)
 
     def __enter__(self):
         self._t = threading.Thread(target=self._run, daemon=True)
