@@ -1,0 +1,85 @@
+"""Per-kernel device time of one training step (torch.profiler, CUDA activity).
+
+    python benchmarks/step_profile.py [--model gpt2-small|gpt2-xl|llama3-8b] [--impl ours|reference]
+
+Builds the same model and config as ``bench.py`` (synthetic tokens, random
+weights), runs three warm-up steps, profiles one step and prints the step's
+span, the summed kernel time and the kernels sorted by total time.  Profiler
+timings are for shares, not for the headline number (``bench.py`` times
+without a profiler).
+"""
+
+import argparse
+import collections
+import os
+import sys
+
+import torch
+import torch.nn.functional as F
+from torch.profiler import ProfilerActivity, profile
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+import bench  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", choices=sorted(bench.SPECS), default="gpt2-small")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--top", type=int, default=25)
+    a = ap.parse_args()
+    spec = bench.SPECS[a.model]
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    os.environ.setdefault("MINISPEED_DEVICE", "cuda:0")
+    if a.impl == "ours":
+        import minispeed_b200 as lib
+        from minispeed_b200.models import GPT, GPTConfig, Llama, LlamaConfig
+        with torch.device(dev):
+            model = bench._build_ours(spec, GPT, GPTConfig, Llama, LlamaConfig)
+            bench._init(model)
+        cfg = bench.ds_config(spec, 1, 100)
+        cfg["b200"] = {"cuda_graph": True}
+        eng = lib.initialize(model=model, config=cfg)
+
+        def micro(x, y):
+            eng.train_batch(x, targets=y)
+    else:
+        sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+        import minispeed as lib
+        with torch.device(dev):
+            model = bench.RefGPT(spec) if spec["kind"] == "gpt" else bench.RefLlama(spec)
+            bench._init(model)
+        eng = lib.initialize(model=model, config=bench.ds_config(spec, 1, 100))
+
+        def micro(x, y):
+            loss = F.cross_entropy(eng(x).reshape(-1, spec["vocab"]).float(), y.reshape(-1))
+            eng.backward(loss)
+            eng.step()
+    t = torch.randint(0, spec["vocab"], (spec["micro"], spec["seq"] + 1), device=dev)
+
+    def step():
+        for _ in range(spec["gas"]):
+            micro(t[:, :-1], t[:, 1:])
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize()
+    evs = [e for e in prof.events()
+           if e.device_type == torch.autograd.DeviceType.CUDA and e.time_range.elapsed_us() > 0]
+    evs.sort(key=lambda e: e.time_range.start)
+    span = evs[-1].time_range.end - evs[0].time_range.start
+    tot, cnt = collections.defaultdict(float), collections.Counter()
+    for e in evs:
+        tot[e.name[:90]] += e.time_range.elapsed_us()
+        cnt[e.name[:90]] += 1
+    print(f"{a.model} {a.impl}: span {span / 1000:.2f} ms, kernel sum {sum(tot.values()) / 1000:.2f} ms")
+    for k, v in sorted(tot.items(), key=lambda kv: -kv[1])[:a.top]:
+        print(f"{v / 1000:9.3f} ms  {cnt[k]:5d}  {k}")
+
+
+if __name__ == "__main__":
+    main()
