@@ -607,11 +607,14 @@ __device__ __forceinline__ uint64_t k_desc(uint32_t base, int ks) {
 // while the softmax warps work on the other.  Tiles are numbered across the
 // CTA's items, so the next item's K/V loads and first scores overlap the end
 // of the current one; K/V are double-buffered, dK/dV are read out of tensor
-// memory by the softmax warps after an item's last tile.
+// memory by the softmax warps after the next item's first tile.
 // Tensor memory (512 columns): S^T 0/128, dP^T 64/192 (buffer 0/1), P^T
 // 256/288, dV 320, dK 384, dQ 448.
 // Warps: 0 TMA, 1 MMA, 2-9 softmax (thread = key row, warp = 32 queries),
-// 10-13 dQ read-out (thread = query row).
+// 10-13 dQ read-out (thread = query row).  The TMA and MMA warps run their
+// loops as whole warps (every lane polls the barriers, one elected lane
+// issues), which keeps the MMA issue rate at the tensor core's.  The
+// barrier protocol is modelled on the CPU in tests/test_kernel_protocols.py.
 constexpr int kThreadsB = 448;
 constexpr int kStages64 = 5;   // Q / dO tiles in flight
 
