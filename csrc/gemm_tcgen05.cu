@@ -11,9 +11,12 @@
 //   warp 0     TMA producer: 64-deep K slices of A and B into a 4-stage
 //              shared-memory ring (128-byte swizzle), one mbarrier per stage
 //   warp 1     owns the tensor memory (allocates 2 x BN fp32 columns) and
-//              issues tcgen05.mma (M=128, N=BN, K=16) from one thread;
+//              issues tcgen05.mma (M=128, N=BN, K=16);
 //              tcgen05.commit frees a ring stage once its MMAs retire and
 //              signals "accumulator full" after a tile's last K slice
+//   Warps 0 and 1 run their loops as whole warps: every lane polls the
+//   barriers and votes, one elected lane issues (a lone issuing thread in a
+//   diverged warp measured up to a third slower per MMA).
 //   warps 2-9  epilogue: tcgen05.ld 32 columns at a time (one TMEM lane =
 //              one output row per thread), bias, activation, cast; each
 //              32 x 32 chunk is staged in shared memory and written by a TMA
