@@ -13,6 +13,11 @@ Drop-in API of lzwjava/minispeed::
 PyTorch is the framework layer; the optimizer step, the collectives fused
 with it and the model hot ops run as hand-written sm_100a kernels
 (``minispeed_b200._C``).
+
+Reference: the package exports of ``minispeed/__init__.py:23-42``
+(``initialize``, ``DeepSpeedEngine``, ``DeepSpeedConfig``, ``ConfigError``,
+``ZeROOptimizer``, ``DynamicLossScaler``, ``WarmupLR``, ``WarmupDecayLR``,
+``Timers``, ``set_seed``, ``comm``).
 """
 
 from . import comm

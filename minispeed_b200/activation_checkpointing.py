@@ -1,6 +1,6 @@
 """Activation checkpointing (recompute in backward).
 
-Same API as the reference helper (``minispeed/activation_checkpointing.py``):
+Same API as the reference helper (``minispeed/activation_checkpointing.py:17-30``):
 ``checkpoint(fn, *args)`` and ``checkpoint_sequential(functions, segments,
 input)``, non-reentrant by default.  The model blocks of
 :mod:`minispeed_b200.models` call :func:`checkpoint` per block when built

@@ -7,6 +7,10 @@ for the GEMM kernels: ``attn.qkv`` is [(H + 2*Hkv) * D, C] (q heads, then k,
 then v) and ``mlp.gate_up`` is [2F, C] (gate rows, then up rows).  As in the
 GPT model, every residual add is fused into the following RMSNorm kernel.
 
+There is no reference counterpart: the reference trains only the example
+GPT of ``examples/train_lm.py:97-115``.  The Llama-3-8B shape is the
+largest model configuration of the benchmark set this library is measured on.
+
 :func:`llama3_8b` is the Llama-3-8B shape (32 layers, d_model 4096, 32/8
 heads, FFN 14336, vocab 128256).
 """

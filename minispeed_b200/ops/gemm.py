@@ -15,6 +15,10 @@ at an odd arena offset) is copied into an aligned buffer first.
 ``MSB_GEMM=torch`` selects the library product instead (comparison baseline
 in the GEMM tests and benchmarks).
 
+Reference: the ``nn.Linear`` layers of the example model
+(``examples/train_lm.py:67-68``, ``:88``, ``:106``), whose products PyTorch
+runs through cuBLAS there.
+
 Each launch carries a device error word; kernels whose bounded waits time
 out set it and return.  :func:`check` reads it (one host sync) and raises.
 """

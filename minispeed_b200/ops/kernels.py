@@ -3,6 +3,13 @@
 CUDA tensors run the sm_100a kernels of ``minispeed_b200._C``; CPU tensors
 run the PyTorch statements that define what each kernel computes (they are
 also the fp32 oracle of the GPU numerics tests).
+
+Reference: AdamW on the flat fp32 shard (``minispeed/optim/adam.py:60-93``),
+the overflow check and its all-reduce (``minispeed/precision.py:79-92``),
+gradient flattening, unscaling and the shard's sum of squares
+(``minispeed/flat.py:197-257``), and the fp32 -> model-dtype copy back into the
+parameters (``minispeed/flat.py:134-156``).  Here each of those is one fused
+kernel over the flat arenas.
 """
 
 from __future__ import annotations

@@ -14,6 +14,12 @@ Ops:
   ``cross_entropy``   fused softmax cross-entropy on model-dtype logits
   ``embedding``       token (+ learned position) embedding
   ``rope_``           rotary embedding on q/k views
+
+Reference: the layers of the example model (``examples/train_lm.py:62-115``:
+``nn.Linear`` projections, ``nn.LayerNorm`` at ``:84``, ``:86`` and ``:105``,
+``nn.GELU`` MLP at ``:88``, token + position embeddings) and its loss
+(``F.cross_entropy`` at ``:246``).  ``swiglu``, RMSNorm and ``rope_`` serve the
+Llama family, which the reference has no model for.
 """
 
 from __future__ import annotations

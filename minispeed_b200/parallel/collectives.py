@@ -19,6 +19,11 @@ Strategies:
   (``zero/stage_1_and_2.py:87-102``), model-dtype parameter all-gather.
 * :class:`minispeed_b200.parallel.fused.FusedCollectives` - in-kernel NVLink
   peer loads/stores (one rank per GPU of one node).
+
+Reference: the collectives of ``minispeed/comm.py:94-141`` (``barrier``,
+``all_reduce``, ``all_reduce_flag``, ``reduce_scatter``, ``all_gather_flat``,
+``broadcast``) as used by ``zero/stage_1_and_2.py:80-131`` (sync, reduce,
+clip, step) and ``zero/stage_3.py:68-100`` (gather / free parameters).
 """
 
 from __future__ import annotations

@@ -25,6 +25,11 @@ Bytes over NVLink per rank and step: (W-1)/W * N * 2 for the gradient
 the parameters, against (W-1)/W * N * 4 each for the reference's fp32 NCCL
 reduce-scatter and all-gather.
 
+Reference: the same step semantics as ``minispeed/engine.py:269-322``
+(``_take_optimizer_step``) over ``zero/stage_1_and_2.py:87-145`` (fp32
+reduce-scatter, overflow all-reduce, global norm, clip, AdamW on the shard,
+all-gather), with the NCCL calls replaced by peer memory accesses.
+
 Every wait in these kernels is bounded (``b200.wait_timeout_ms``); a
 timeout is recorded in a status word that :meth:`check` turns into
 :class:`CommTimeoutError` on the host.

@@ -7,6 +7,10 @@ over NVLink).  Kernels receive ``heaps``: a device table of every rank's
 heap base in this process's address space, so ``heaps[q] + offset`` is rank
 q's copy of a region.  Regions are 256-byte aligned; the last region is the
 synchronization area (barrier flags and the step-statistics board).
+
+There is no reference counterpart: the reference moves every byte through
+NCCL (``minispeed/comm.py:99-141``).  The heap is what lets this library's
+kernels read and write peer memory directly over NVLink.
 """
 
 from __future__ import annotations
