@@ -10,6 +10,7 @@ example, ``examples/train_lm.py``).
     python examples/train_lm.py --dtype fp16 --zero 2
     torchrun --nproc-per-node 2 --master-addr 127.0.0.1 examples/train_lm.py --zero 3
     python examples/train_lm.py --resume out            # continue from out/latest
+    python examples/train_lm.py --resume out/global_step150   # a given tag
     python examples/train_lm.py --config examples/ds_config_tiny.json --steps 50
 """
 
@@ -81,6 +82,17 @@ def make_config(a) -> dict:
     return cfg
 
 
+def resume(engine, path: str) -> None:
+    """``path`` is a save dir (follow its ``latest`` file), a ``dir/tag``
+    checkpoint directory, or the ``dir/latest`` file itself."""
+    path = os.path.normpath(path)
+    if os.path.isfile(os.path.join(path, "latest")):
+        engine.load_checkpoint(path)
+        return
+    parent, tag = os.path.split(path)
+    engine.load_checkpoint(parent, tag=None if tag == "latest" else tag)
+
+
 def main():
     p = argparse.ArgumentParser(description="minispeed_b200 character LM example")
     p.add_argument("--steps", type=int, default=300)
@@ -111,10 +123,7 @@ def main():
     engine, _, _, sched = ms.initialize(model=model, model_parameters=model.parameters(),
                                         config=make_config(a))
     if a.resume:
-        if os.path.isdir(a.resume):
-            engine.load_checkpoint(a.resume)
-        else:
-            engine.load_checkpoint(os.path.dirname(a.resume), tag=os.path.basename(a.resume))
+        resume(engine, a.resume)
         if rank == 0:
             print(f"resumed {a.resume} at step {engine.global_steps}")
     if rank == 0:
@@ -150,10 +159,13 @@ def main():
             engine.save_checkpoint(a.ckpt_dir)
     engine.save_checkpoint(a.ckpt_dir)
 
+    # the sample reads whole parameters; at ZeRO-3 gathering them is a
+    # collective, so every rank takes part before rank 0 samples alone
+    engine.eval()
+    engine.optimizer.gather_parameters()
     if rank == 0:
         print(f"done: loss {float(loss.detach()):.4f}, skipped {engine.skipped_steps}, "
               f"checkpoint in {a.ckpt_dir}")
-        engine.eval()
         ctx = torch.tensor([[stoi[c] for c in "the "]], device=device)
         with torch.no_grad():
             for _ in range(60):
