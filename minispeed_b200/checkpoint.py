@@ -26,6 +26,7 @@ Two robustness changes that keep the format:
 from __future__ import annotations
 
 import os
+import pickle
 from typing import Optional, Tuple
 
 import torch
@@ -99,21 +100,15 @@ def save_checkpoint(engine, save_dir: str, tag: Optional[str] = None) -> str:
     return ckpt_dir
 
 
-@torch.no_grad()
-def load_checkpoint(engine, load_dir: str, tag: Optional[str] = None) -> Tuple[str, dict]:
-    tag = tag or _read_latest(load_dir)
-    ckpt_dir = os.path.join(load_dir, tag)
-
-    was_gathered = engine.optimizer.params_gathered
-    engine.optimizer.gather_parameters()
-
-    model_state = torch.load(os.path.join(ckpt_dir, MODEL_STATES), map_location="cpu",
-                             weights_only=True)
-    engine.module.load_state_dict(model_state["module"])
-
+def _read_and_check(engine, ckpt_dir: str) -> Tuple[dict, dict]:
+    """This rank's two files, checked against the engine before anything is
+    changed: shard present, same world size, same groups and master sizes,
+    same module keys and shapes."""
     optim_path = os.path.join(ckpt_dir, optim_states_name(engine.rank))
     if not os.path.exists(optim_path):
         raise FileNotFoundError(f"Missing optimizer shard for rank {engine.rank}: {optim_path}")
+    model_state = torch.load(os.path.join(ckpt_dir, MODEL_STATES), map_location="cpu",
+                             weights_only=True)
     state = torch.load(optim_path, map_location="cpu", weights_only=True)
     saved_world = int(state.get("world_size", engine.world_size))
     if saved_world != engine.world_size:
@@ -128,6 +123,49 @@ def load_checkpoint(engine, load_dir: str, tag: Optional[str] = None) -> Tuple[s
         if buf.numel() != g.data.numel():
             raise RuntimeError(f"fp32 master size mismatch: checkpoint {buf.numel()} vs "
                                f"engine {g.data.numel()}")
+    live = engine.module.state_dict()
+    saved = model_state["module"]
+    if set(saved) != set(live):
+        missing, extra = sorted(set(live) - set(saved)), sorted(set(saved) - set(live))
+        raise RuntimeError(f"module keys differ: missing {missing[:5]}, unexpected {extra[:5]}")
+    for k, v in saved.items():
+        if tuple(v.shape) != tuple(live[k].shape):
+            raise RuntimeError(f"module tensor {k}: checkpoint shape {tuple(v.shape)} vs "
+                               f"engine {tuple(live[k].shape)}")
+    return model_state, state
+
+
+@torch.no_grad()
+def load_checkpoint(engine, load_dir: str, tag: Optional[str] = None) -> Tuple[str, dict]:
+    """Restore a checkpoint on every rank, or on none.
+
+    Each rank reads and checks its files first; the ranks then agree (one
+    flag all-reduce) before any state changes.  A rank whose files are bad
+    raises its own error (``FileNotFoundError`` for a missing shard), the
+    others a ``RuntimeError``, and no rank has changed anything, so no rank
+    is left waiting in a collective the failed one never joins."""
+    tag = tag or _read_latest(load_dir)
+    ckpt_dir = os.path.join(load_dir, tag)
+
+    was_gathered = engine.optimizer.params_gathered
+    engine.optimizer.gather_parameters()     # stage 3: full-shaped params to check and load
+
+    err: Optional[BaseException] = None
+    try:
+        model_state, state = _read_and_check(engine, ckpt_dir)
+    except (OSError, RuntimeError, KeyError, ValueError, EOFError,
+            pickle.UnpicklingError) as e:
+        err = e
+    if comm.all_reduce_flag(err is not None):
+        if not was_gathered:
+            engine.optimizer.free_parameters()
+        if err is not None:
+            raise err
+        raise RuntimeError(f"checkpoint {ckpt_dir} failed to load on another rank; "
+                           "nothing was changed")
+
+    engine.module.load_state_dict(model_state["module"])
+    for g, buf in zip(engine.flat_groups, state["fp32_groups"]):
         g.data.copy_(buf)
         g.copy_flat_to_model()
     engine.optimizer._masters_stale = False
