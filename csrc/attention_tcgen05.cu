@@ -1646,6 +1646,24 @@ void launch_bwd128(const CUtensorMap& tq, const CUtensorMap& td, const CUtensorM
 }  // namespace bwd
 }  // namespace attn
 
+// The q, k and v heads are read with TMA at column q_col + h*D (k_col, v_col
+// alike).  A TMA copy's innermost coordinate must be a multiple of 16 bytes
+// (8 16-bit elements): an unaligned one is an illegal instruction, not an
+// error the kernel can report, so it is refused here.  Each head range must
+// also lie inside the row.
+static void check_head_columns(const char* what, long long n_cols, int q_col, int k_col,
+                               int v_col, int H, int Hkv, int D) {
+  const long long cols[3] = {q_col, k_col, v_col};
+  const long long widths[3] = {(long long)H * D, (long long)Hkv * D, (long long)Hkv * D};
+  for (int i = 0; i < 3; ++i) {
+    if (cols[i] < 0 || cols[i] % 8 != 0)
+      throw std::runtime_error(std::string(what) +
+                               ": q/k/v column offsets must be non-negative multiples of 8");
+    if (cols[i] + widths[i] > n_cols)
+      throw std::runtime_error(std::string(what) + ": q/k/v heads extend past the row");
+  }
+}
+
 void attention_fwd(const void* qkv, long long ld_qkv, long long n_cols, int q_col, int k_col,
                    int v_col, void* out, long long ld_out, float* lse, int B, int T, int H,
                    int Hkv, int D, int dtype, float scale, unsigned* err, double timeout_s,
@@ -1653,6 +1671,7 @@ void attention_fwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
   using namespace attn;
   if (D != 64 && D != 128) throw std::runtime_error("attention: head dim must be 64 or 128");
   if (H % Hkv != 0) throw std::runtime_error("attention: H must be a multiple of Hkv");
+  check_head_columns("attention", n_cols, q_col, k_col, v_col, H, Hkv, D);
   if ((reinterpret_cast<uintptr_t>(out) & 15) || (ld_out % 8))
     throw std::runtime_error("attention: output must allow 16-byte row stores");
   Params p;
@@ -1700,6 +1719,7 @@ void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
   using namespace attn::bwd;
   if (D != 64 && D != 128) throw std::runtime_error("attention backward: head dim 64 or 128");
   if (H % Hkv != 0) throw std::runtime_error("attention: H must be a multiple of Hkv");
+  check_head_columns("attention backward", n_cols, q_col, k_col, v_col, H, Hkv, D);
   auto aligned = [](const void* ptr, long long ld) {
     return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && ld % 8 == 0;
   };
