@@ -12,6 +12,7 @@ example, ``examples/train_lm.py``).
     python examples/train_lm.py --resume out            # continue from out/latest
     python examples/train_lm.py --resume out/global_step150   # a given tag
     python examples/train_lm.py --config examples/ds_config_tiny.json --steps 50
+    python examples/train_lm.py --arch llama --zero 3     # Llama-3 family block
 """
 
 from __future__ import annotations
@@ -28,7 +29,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 import minispeed_b200 as ms  # noqa: E402
 from minispeed_b200 import comm  # noqa: E402
-from minispeed_b200.models import GPT, GPTConfig  # noqa: E402
+from minispeed_b200.models import GPT, GPTConfig, Llama, LlamaConfig  # noqa: E402
 
 TEXT = """
 a flat buffer holds every weight of a group in one piece, so one kernel can
@@ -106,6 +107,9 @@ def main():
     p.add_argument("--n-embd", type=int, default=128)
     p.add_argument("--n-layer", type=int, default=2)
     p.add_argument("--n-head", type=int, default=4)
+    p.add_argument("--arch", default="gpt", choices=["gpt", "llama"],
+                   help="gpt: the reference example's TinyGPT; llama: RMSNorm, RoPE, GQA, SwiGLU")
+    p.add_argument("--n-kv-head", type=int, default=2, help="llama: key/value heads")
     p.add_argument("--log-every", type=int, default=25)
     p.add_argument("--ckpt-dir", default="out")
     p.add_argument("--save-every", type=int, default=150)
@@ -118,8 +122,13 @@ def main():
     device = comm.resolve_device()
     ms.set_seed(1337)
     ids, vocab, stoi = encode()
-    model = GPT(GPTConfig(vocab_size=len(vocab), block_size=a.block_size, n_layer=a.n_layer,
-                          n_head=a.n_head, n_embd=a.n_embd))
+    if a.arch == "llama":
+        model = Llama(LlamaConfig(vocab_size=len(vocab), block_size=a.block_size,
+                                  n_layer=a.n_layer, n_head=a.n_head, n_kv_head=a.n_kv_head,
+                                  n_embd=a.n_embd, ffn_hidden=4 * a.n_embd, rope_theta=10000.0))
+    else:
+        model = GPT(GPTConfig(vocab_size=len(vocab), block_size=a.block_size, n_layer=a.n_layer,
+                              n_head=a.n_head, n_embd=a.n_embd))
     engine, _, _, sched = ms.initialize(model=model, model_parameters=model.parameters(),
                                         config=make_config(a))
     if a.resume:

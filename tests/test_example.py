@@ -85,3 +85,11 @@ def test_two_ranks_under_torchrun(zero, tmp_path):
     assert names == ["mp_rank_00_model_states.pt",
                      "zero_pp_rank0_mp_rank_00_optim_states.pt",
                      "zero_pp_rank1_mp_rank_00_optim_states.pt"]
+
+
+def test_llama_arch(tmp_path):
+    log = _run([sys.executable, SCRIPT, "--arch", "llama", "--dtype", "fp32", "--zero", "3",
+                "--n-layer", "1", "--n-embd", "32", "--n-head", "4", "--n-kv-head", "2",
+                "--block-size", "16", "--batch-size", "4", "--gas", "1", "--steps", "3",
+                "--log-every", "1", "--save-every", "0", "--ckpt-dir", str(tmp_path / "l")])
+    assert "step     3/3" in log and "sample:" in log
