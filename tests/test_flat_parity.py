@@ -81,3 +81,41 @@ def test_layout_and_masters_match_reference(ref_flat, shapes, world, stage, data
     b.copy_flat_to_model()
     for p, q in zip(pa, pb):
         assert p.data.shape == q.data.shape and torch.equal(p.data, q.data)
+
+
+@settings(max_examples=100, deadline=None,
+          suppress_health_check=[HealthCheck.function_scoped_fixture])
+@given(shapes=shapes, world=st.integers(1, 4), stage=st.integers(0, 2), steps=st.integers(1, 4),
+       lr=st.sampled_from([1e-3, 0.05]), wd=st.sampled_from([0.0, 0.1]),
+       betas=st.sampled_from([(0.9, 0.999), (0.8, 0.95)]), data=st.data())
+def test_adamw_shard_update_matches_reference(ref_flat, shapes, world, stage, steps, lr, wd,
+                                               betas, data):
+    """The AdamW update of a rank's shard (``minispeed/optim/adam.py:60-93``):
+    same masters, moments and step counts after several steps."""
+    from minispeed_b200.optim.adam import FlatAdam
+    sys.path.insert(0, REF)
+    try:
+        ref_adam = importlib.import_module("minispeed.optim.adam")
+    finally:
+        sys.path.remove(REF)
+    rank = data.draw(st.integers(0, world - 1))
+    opts = [{"lr": lr, "betas": betas, "eps": 1e-8, "weight_decay": wd}]
+    a = FlatParamGroup(_params(shapes, 2), rank=rank, world_size=world, zero_stage=stage,
+                       device=CPU)
+    b = ref_flat.FlatParamGroup(_params(shapes, 2), rank=rank, world_size=world,
+                                zero_stage=stage, device=CPU)
+    for fg in (a, b):
+        fg.copy_model_to_flat()
+    oa, ob = FlatAdam([a], opts, zero_stage=stage), ref_adam.FlatAdam([b], opts, zero_stage=stage)
+    g = torch.Generator().manual_seed(9)
+    for _ in range(steps):
+        grad = torch.randn(a.numel_shard(), generator=g)
+        for fg in (a, b):
+            fg.grad_for_shard().copy_(grad)
+        oa.step()
+        ob.step()
+    assert torch.equal(a.data, b.data)
+    for sa, sb in zip(oa.state, ob.state):
+        assert sa["step"] == sb["step"]
+        assert torch.equal(sa["exp_avg"], sb["exp_avg"])
+        assert torch.equal(sa["exp_avg_sq"], sb["exp_avg_sq"])
