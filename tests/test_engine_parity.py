@@ -66,3 +66,39 @@ def test_engine_matches_reference(ref, stage, micro, gas, clip, dtype, sched, wa
         assert na == pytest.approx(nb, rel=max(rtol, 1e-4))
     for k in pa:
         torch.testing.assert_close(pa[k], pb[k], rtol=rtol, atol=atol)
+
+
+@settings(max_examples=30, deadline=None,
+          suppress_health_check=[HealthCheck.function_scoped_fixture])
+@given(stage=st.integers(0, 3), gas=st.integers(1, 2), window=st.integers(1, 3),
+       inject=st.lists(st.booleans(), min_size=1, max_size=6))
+def test_overflow_handling_matches_reference(ref, stage, gas, window, inject):
+    """fp16 with inf written into a gradient before chosen boundaries: the
+    same steps are skipped, and scale, counters and weights agree."""
+    micro, steps = 4, len(inject)
+    cfg = config(micro=micro, gas=gas, stage=stage, dtype="fp16", window=window, lr=1e-2)
+    x, y = make_data(steps, gas, 1, micro)
+    out = []
+    for lib in (ours, ref):
+        eng = lib.initialize(model=make_net(), config=cfg)
+        scales, applied = [], []
+        for s in range(steps):
+            for m in range(gas):
+                loss = ((eng(x[s, m]).float() - y[s, m]) ** 2).mean()
+                eng.backward(loss)
+                if m == gas - 1 and inject[s]:
+                    p = next(eng.module.parameters())
+                    if p.grad is None:      # stage 3 between gathers: inject into a live grad
+                        p = [q for q in eng.module.parameters() if q.grad is not None][0]
+                    p.grad.view(-1)[0] = float("inf")
+                r = eng.step()
+                if m == gas - 1:
+                    applied.append(bool(r))
+            scales.append(eng.get_loss_scale())
+        out.append((applied, scales, eng.global_steps, eng.skipped_steps,
+                    {k: v.float().clone() for k, v in eng.state_dict().items()}))
+    (aa, sa, ga, ka, pa), (ab, sb, gb, kb, pb) = out
+    assert aa == ab == [not i for i in inject]
+    assert sa == sb and (ga, ka) == (gb, kb)
+    for k in pa:
+        torch.testing.assert_close(pa[k], pb[k], rtol=5e-3, atol=5e-4)
