@@ -26,7 +26,6 @@ Two robustness changes that keep the format:
 from __future__ import annotations
 
 import os
-import pickle
 from typing import Optional, Tuple
 
 import torch
@@ -129,7 +128,8 @@ def _read_and_check(engine, ckpt_dir: str) -> Tuple[dict, dict]:
         missing, extra = sorted(set(live) - set(saved)), sorted(set(saved) - set(live))
         raise RuntimeError(f"module keys differ: missing {missing[:5]}, unexpected {extra[:5]}")
     for k, v in saved.items():
-        if tuple(v.shape) != tuple(live[k].shape):
+        if torch.is_tensor(v) and torch.is_tensor(live[k]) and \
+                tuple(v.shape) != tuple(live[k].shape):
             raise RuntimeError(f"module tensor {k}: checkpoint shape {tuple(v.shape)} vs "
                                f"engine {tuple(live[k].shape)}")
     return model_state, state
@@ -153,8 +153,7 @@ def load_checkpoint(engine, load_dir: str, tag: Optional[str] = None) -> Tuple[s
     err: Optional[BaseException] = None
     try:
         model_state, state = _read_and_check(engine, ckpt_dir)
-    except (OSError, RuntimeError, KeyError, ValueError, EOFError,
-            pickle.UnpicklingError) as e:
+    except Exception as e:  # re-raised below, after every rank has reported
         err = e
     if comm.all_reduce_flag(err is not None):
         if not was_gathered:
