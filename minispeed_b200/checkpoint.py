@@ -144,22 +144,28 @@ def load_checkpoint(engine, load_dir: str, tag: Optional[str] = None) -> Tuple[s
     raises its own error (``FileNotFoundError`` for a missing shard), the
     others a ``RuntimeError``, and no rank has changed anything, so no rank
     is left waiting in a collective the failed one never joins."""
-    tag = tag or _read_latest(load_dir)
-    ckpt_dir = os.path.join(load_dir, tag)
-
     was_gathered = engine.optimizer.params_gathered
     engine.optimizer.gather_parameters()     # stage 3: full-shaped params to check and load
 
     err: Optional[BaseException] = None
+    ckpt_dir = None
     try:
+        tag = tag or _read_latest(load_dir)
+        ckpt_dir = os.path.join(load_dir, tag)
         model_state, state = _read_and_check(engine, ckpt_dir)
     except Exception as e:  # re-raised below, after every rank has reported
         err = e
-    if comm.all_reduce_flag(err is not None):
+    # one collective: every rank's outcome and tag (a save directory that is
+    # not shared can show the ranks different ``latest`` files)
+    reports = comm.all_gather_object((err is not None, tag))
+    if any(failed for failed, _ in reports) or len({t for _, t in reports}) > 1:
         if not was_gathered:
             engine.optimizer.free_parameters()
         if err is not None:
             raise err
+        if len({t for _, t in reports}) > 1:
+            raise RuntimeError(f"ranks would load different checkpoints: "
+                               f"{[t for _, t in reports]}; nothing was changed")
         raise RuntimeError(f"checkpoint {ckpt_dir} failed to load on another rank; "
                            "nothing was changed")
 

@@ -168,3 +168,30 @@ def test_one_rank_missing_shard_fails_both_and_keeps_lockstep(tmp_path):
     assert r0["outcome"] == "other rank" and r1["outcome"] == "missing"
     for k in r0["params"]:
         torch.testing.assert_close(r0["params"][k], r1["params"][k], rtol=0, atol=0)
+
+
+def _diverging_tags_worker(rank, port, out_dir):
+    set_rank_env(rank, WORLD, port, "gloo", "cpu")
+    x, y = make_data(2, GAS, WORLD, MICRO)
+    x, y = rank_slice(x, rank, MICRO), rank_slice(y, rank, MICRO)
+    cfg = config(micro=MICRO, gas=GAS, stage=1)
+    eng = ms.initialize(model=make_net(), config=cfg)
+    run(eng, x, y, 1, GAS)
+    eng.save_checkpoint(out_dir, tag="t1")
+    run(eng, x[1:], y[1:], 1, GAS)
+    eng.save_checkpoint(out_dir, tag="t2")
+    fresh = ms.initialize(model=make_net(seed=5), config=cfg)
+    snap = _snapshot(fresh)
+    try:      # as if each rank saw a different ``latest`` file
+        fresh.load_checkpoint(out_dir, tag="t1" if rank == 0 else "t2")
+        outcome = "loaded"
+    except RuntimeError as e:
+        outcome = "refused" if "different checkpoints" in str(e) else repr(e)
+    _assert_unchanged(fresh, snap)
+    torch.save(outcome, os.path.join(out_dir, f"o{rank}.pt"))
+    ms.comm.destroy()
+
+
+def test_ranks_refuse_to_load_different_tags(tmp_path):
+    mp.spawn(_diverging_tags_worker, args=(free_port(), str(tmp_path)), nprocs=WORLD, join=True)
+    assert [torch.load(tmp_path / f"o{r}.pt") for r in range(WORLD)] == ["refused", "refused"]
