@@ -15,9 +15,13 @@ reference and vice versa.
 Two robustness changes that keep the format:
 
 * every file is written to ``<name>.tmp`` and renamed into place, and rank 0
-  writes ``latest`` only after a barrier that follows every rank's shard, so
-  a crash never leaves ``latest`` naming an incomplete tag (the reference
-  writes ``latest`` before the shards, ``checkpoint.py:52-68``);
+  writes ``latest`` only after every rank has reported its shard written
+  (one flag all-reduce), so a crash or a failed write never leaves
+  ``latest`` naming an incomplete tag, and a rank whose write failed makes
+  every rank raise at once instead of leaving them in a barrier (the
+  reference writes ``latest`` before the shards, ``checkpoint.py:52-68``);
+* a load reads and checks every rank's files, and the ranks agree on the
+  outcome and the tag, before any state changes;
 * the saved module tensors are detached copies, one per distinct storage
   (tied weights stay tied), so the file has the same structure as the
   reference's even though the live params are views into one arena.
@@ -72,22 +76,34 @@ def save_checkpoint(engine, save_dir: str, tag: Optional[str] = None) -> str:
     engine.optimizer.gather_parameters()
     engine.optimizer.sync_master_weights()
 
-    if engine.rank == 0:
-        _atomic_save({"module": _standalone_state_dict(engine.module), "tag": tag},
-                     os.path.join(ckpt_dir, MODEL_STATES))
-    state = {
-        "optimizer": engine.optimizer.state_dict(),
-        "fp32_groups": [g.data.clone() for g in engine.flat_groups],
-        "lr_scheduler": engine.lr_scheduler.state_dict(),
-        "loss_scaler": engine.loss_scaler.state_dict(),
-        "global_steps": engine.global_steps,
-        "micro_steps": engine.micro_steps,
-        "grad_norm": engine.grad_norm,
-        "rank": engine.rank,
-        "world_size": engine.world_size,
-    }
-    _atomic_save(state, os.path.join(ckpt_dir, optim_states_name(engine.rank)))
-    comm.barrier()
+    err: Optional[BaseException] = None
+    try:
+        if engine.rank == 0:
+            _atomic_save({"module": _standalone_state_dict(engine.module), "tag": tag},
+                         os.path.join(ckpt_dir, MODEL_STATES))
+        state = {
+            "optimizer": engine.optimizer.state_dict(),
+            "fp32_groups": [g.data.clone() for g in engine.flat_groups],
+            "lr_scheduler": engine.lr_scheduler.state_dict(),
+            "loss_scaler": engine.loss_scaler.state_dict(),
+            "global_steps": engine.global_steps,
+            "micro_steps": engine.micro_steps,
+            "grad_norm": engine.grad_norm,
+            "rank": engine.rank,
+            "world_size": engine.world_size,
+        }
+        _atomic_save(state, os.path.join(ckpt_dir, optim_states_name(engine.rank)))
+    except Exception as e:  # e.g. a full disk: reported to every rank below
+        err = e
+    # every rank's files are written (or one failed) before ``latest`` moves
+    failed = comm.all_reduce_flag(err is not None)
+    if failed:
+        if not was_gathered:
+            engine.optimizer.free_parameters()
+        if err is not None:
+            raise err
+        raise RuntimeError(f"checkpoint {ckpt_dir}: another rank failed to write its files; "
+                           "latest still names the previous checkpoint")
     if engine.rank == 0:
         latest = os.path.join(save_dir, LATEST)
         with open(latest + ".tmp", "w", encoding="utf-8") as fh:

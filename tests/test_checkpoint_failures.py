@@ -2,9 +2,10 @@
 
 Host-side fault injection only: a missing or truncated shard, a shard from
 another world size, a checkpoint of another model, a save that dies before
-``latest`` is written, and a two-rank load where only one rank's shard is
-missing (both ranks must fail promptly, change nothing, and stay in
-lockstep for the collectives that follow).
+``latest`` is written, and two-rank cases where only one rank fails (a
+missing shard, a full disk while saving, ranks that would load different
+tags): every rank must fail promptly, change nothing, keep ``latest``, and
+stay in lockstep for the collectives that follow.
 """
 
 import os
@@ -118,7 +119,7 @@ def test_save_that_dies_before_latest_keeps_the_old_tag(tmp_path, monkeypatch):
     def dead(*a, **k):
         raise RuntimeError("rank died")
 
-    monkeypatch.setattr(ckpt.comm, "barrier", dead)
+    monkeypatch.setattr(ckpt.comm, "all_reduce_flag", dead)
     with pytest.raises(RuntimeError, match="rank died"):
         eng.save_checkpoint(str(tmp_path), tag="partial")
     monkeypatch.undo()
@@ -195,3 +196,34 @@ def _diverging_tags_worker(rank, port, out_dir):
 def test_ranks_refuse_to_load_different_tags(tmp_path):
     mp.spawn(_diverging_tags_worker, args=(free_port(), str(tmp_path)), nprocs=WORLD, join=True)
     assert [torch.load(tmp_path / f"o{r}.pt") for r in range(WORLD)] == ["refused", "refused"]
+
+
+def _failed_write_worker(rank, port, out_dir):
+    set_rank_env(rank, WORLD, port, "gloo", "cpu")
+    x, y = make_data(2, GAS, WORLD, MICRO)
+    x, y = rank_slice(x, rank, MICRO), rank_slice(y, rank, MICRO)
+    eng = ms.initialize(model=make_net(), config=config(micro=MICRO, gas=GAS, stage=2))
+    run(eng, x, y, 1, GAS)
+    eng.save_checkpoint(out_dir, tag="good")
+    if rank == 1:
+        def full_disk(*a, **k):
+            raise OSError(28, "No space left on device")
+        ckpt.torch.save = full_disk
+    try:
+        eng.save_checkpoint(out_dir, tag="bad")
+        outcome = "saved"
+    except OSError:
+        outcome = "own error"
+    except RuntimeError as e:
+        outcome = "other rank" if "another rank" in str(e) else repr(e)
+    ms.comm.barrier()      # still in lockstep
+    with open(os.path.join(out_dir, f"w{rank}.txt"), "w") as fh:   # torch.save is patched
+        fh.write(outcome)
+    ms.comm.destroy()
+
+
+def test_failed_write_on_one_rank_fails_all_and_keeps_latest(tmp_path):
+    mp.spawn(_failed_write_worker, args=(free_port(), str(tmp_path)), nprocs=WORLD, join=True)
+    assert (tmp_path / "w0.txt").read_text() == "other rank"
+    assert (tmp_path / "w1.txt").read_text() == "own error"
+    assert (tmp_path / "latest").read_text() == "good"
