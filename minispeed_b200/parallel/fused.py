@@ -38,6 +38,7 @@ timeout is recorded in a status word that :meth:`check` turns into
 from __future__ import annotations
 
 import os
+import socket
 from typing import List, Optional, Tuple
 
 import torch
@@ -52,6 +53,18 @@ class CommTimeoutError(RuntimeError):
     """A peer did not arrive at a device-side barrier within the limit."""
 
 
+def _device_identity(device: torch.device) -> str:
+    props = torch.cuda.get_device_properties(device)
+    uuid = getattr(props, "uuid", None)
+    return f"{socket.gethostname()}/{uuid if uuid is not None else device.index}"
+
+
+def shared_gpu(identities) -> bool:
+    """True when two ranks reported the same GPU."""
+    ids = list(identities)
+    return len(set(ids)) != len(ids)
+
+
 def supported(device: torch.device) -> Tuple[bool, str]:
     if device.type != "cuda":
         return False, "fused collectives need CUDA devices"
@@ -63,6 +76,11 @@ def supported(device: torch.device) -> Tuple[bool, str]:
         return False, "ranks span more than one node"
     if torch.distributed.get_backend() != "nccl":
         return False, "ranks share a GPU (gloo backend)"
+    # every rank takes part here, before any rank-dependent return: the
+    # fused kernels wait on their peers, and two such waiting kernels from
+    # two processes on one GPU are not guaranteed to run at the same time
+    if shared_gpu(comm.all_gather_object(_device_identity(device))):
+        return False, "two ranks use the same GPU"
     if not _ext.available():
         return False, "minispeed_b200._C not built"
     n = torch.cuda.device_count()
