@@ -83,6 +83,12 @@ def make_config(a) -> dict:
     return cfg
 
 
+def gpu_times(engine) -> str:
+    """GPU time per phase when ``"b200": {"device_timers": true}`` is set."""
+    ms_ = engine.device_time_ms()
+    return "".join(f" | gpu {k}: {v:.1f}ms" for k, v in ms_.items())
+
+
 def resume(engine, path: str) -> None:
     """``path`` is a save dir (follow its ``latest`` file), a ``dir/tag``
     checkpoint directory, or the ``dir/latest`` file itself."""
@@ -161,8 +167,9 @@ def main():
             print(f"step {step:5d}/{a.steps} | loss {lv:.4f} | ppl {math.exp(min(lv, 20)):8.2f}"
                   f" | lr {sched.get_last_lr():.2e} | norm {engine.grad_norm:.3f}"
                   f" | scale {engine.get_loss_scale():.0f} | tok/s {n * tokens / dt:,.0f}"
-                  f" | {engine.timers.log()}", flush=True)
+                  f" | {engine.timers.log()}{gpu_times(engine)}", flush=True)
             engine.timers.reset()
+            engine.device_timers.reset()
             t0 = time.time()
         if a.save_every and step % a.save_every == 0:
             engine.save_checkpoint(a.ckpt_dir)

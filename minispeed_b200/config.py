@@ -75,6 +75,8 @@ class B200Options:
     ``cuda_graph``: ``engine.train_batch`` replays forward + backward as one
     captured CUDA graph (stages 0-2, CUDA) after ``graph_warmup`` eager
     micro-steps; env ``MINISPEED_CUDA_GRAPH=1`` turns it on.
+    ``device_timers``: also time the engine's phases on the GPU with CUDA
+    events (``engine.device_time_ms()``); env ``MINISPEED_DEVICE_TIMERS=1``.
     """
 
     comm: str = "auto"
@@ -83,6 +85,7 @@ class B200Options:
     wait_timeout_ms: float = 10000.0
     cuda_graph: bool = False
     graph_warmup: int = 2
+    device_timers: bool = False
 
     @classmethod
     def parse(cls, raw: dict) -> "B200Options":
@@ -95,6 +98,8 @@ class B200Options:
             cuda_graph=bool(sec.get("cuda_graph",
                                     os.environ.get("MINISPEED_CUDA_GRAPH", "0") == "1")),
             graph_warmup=int(sec.get("graph_warmup", 2)),
+            device_timers=bool(sec.get("device_timers",
+                                       os.environ.get("MINISPEED_DEVICE_TIMERS", "0") == "1")),
         )
         if opts.comm not in ("auto", "nccl", "fused"):
             raise ConfigError(f"b200.comm must be auto|nccl|fused, got {opts.comm!r}")

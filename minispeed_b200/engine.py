@@ -26,6 +26,7 @@ work).  Device-side phase timers (CUDA events) complement the wall-clock
 from __future__ import annotations
 
 import logging
+from contextlib import contextmanager, nullcontext
 from typing import Iterator, List, Optional
 
 import torch
@@ -37,7 +38,7 @@ from .config import DeepSpeedConfig, load_config
 from .flat import FlatParamGroup, build_flat_groups
 from .optim import build_scheduler
 from .precision import DynamicLossScaler
-from .utils import Timers
+from .utils import DeviceTimers, Timers
 from .zero import build_zero_optimizer, make_collectives
 
 logger = logging.getLogger("minispeed_b200")
@@ -83,6 +84,9 @@ class DeepSpeedEngine:
         if self.device.type == "cuda":
             torch.cuda.set_device(self.device)
         self.timers = Timers()
+        # CUDA-event times of the same phases plus "forward" (b200.device_timers)
+        self.device_timers = DeviceTimers()
+        self._device_timing = self.config.b200.device_timers and self.device.type == "cuda"
         self.module = model.to(self.device)
         self._broadcast_model()
 
@@ -240,14 +244,32 @@ class DeepSpeedEngine:
 
     def forward(self, *args, **kwargs):
         if not self.optimizer.params_gathered:
-            with self.timers.timer("gather"):
+            with self._phase("gather"):
                 if getattr(self.optimizer, "plan_layer_gather", None) is not None:
                     self.optimizer.gather_parameters(layerwise=True)
                 else:
                     self.optimizer.gather_parameters()
         self._open_window()
         self._begin_micro_step()
-        return self.module(*self._cast_inputs(args), **self._cast_inputs(kwargs))
+        with self._device_phase("forward"):
+            return self.module(*self._cast_inputs(args), **self._cast_inputs(kwargs))
+
+    @contextmanager
+    def _phase(self, name: str):
+        """Wall-clock section of ``engine.timers`` (and of ``device_timers``
+        when ``b200.device_timers`` is on)."""
+        with self.timers.timer(name), self._device_phase(name):
+            yield
+
+    def _device_phase(self, name: str):
+        return self.device_timers.timer(name) if self._device_timing else nullcontext()
+
+    def device_time_ms(self) -> dict:
+        """Milliseconds of GPU time per phase (``forward``, ``backward``,
+        ``step``, ``reduce``, ``gather``) since the last reset, from CUDA
+        events on the launching stream; empty unless ``b200.device_timers``
+        is on.  Synchronizes the GPU."""
+        return self.device_timers.elapsed_ms() if self._device_timing else {}
 
     def __call__(self, *args, **kwargs):
         return self.forward(*args, **kwargs)
@@ -272,7 +294,7 @@ class DeepSpeedEngine:
 
     def backward(self, loss: torch.Tensor, scale_wrt_gas: bool = True,
                  retain_graph: bool = False, create_graph: bool = False) -> None:
-        with self.timers.timer("backward"):
+        with self._phase("backward"):
             self._scale_loss(loss, scale_wrt_gas).backward(retain_graph=retain_graph,
                                                            create_graph=create_graph)
         self.micro_steps += 1
@@ -355,7 +377,7 @@ class DeepSpeedEngine:
             for g in self.flat_groups:
                 g.ensure_grad_arena()
             self._window_open = True
-        with self.timers.timer("backward"):
+        with self._phase("backward"):
             loss = st.replay()
         if st.overlap:
             self.optimizer._overlap_ran = True   # the replay ran the bucket reductions
@@ -382,13 +404,13 @@ class DeepSpeedEngine:
         if not self._boundary_pending:
             return False
         self._consumed_boundary = self.micro_steps
-        with self.timers.timer("step"):
+        with self._phase("step"):
             return self._take_optimizer_step()
 
     @torch.no_grad()
     def _take_optimizer_step(self) -> bool:
         scale = self.loss_scaler.loss_scale_factor
-        with self.timers.timer("reduce"):
+        with self._phase("reduce"):
             applied, norm = self.optimizer.boundary_step(scale, self.config.gradient_clipping)
         self.optimizer.after_step(applied)
         self._window_open = False

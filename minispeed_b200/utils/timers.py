@@ -93,11 +93,25 @@ class Timers:
 
 
 class DeviceTimers:
-    """CUDA-event section timers (no-ops on CPU)."""
+    """CUDA-event section timers (no-ops on CPU).
 
-    def __init__(self) -> None:
+    Intervals whose end event has completed are folded into the totals
+    without a sync once more than ``fold_after`` are pending, so a long run
+    that never reads the timers holds a bounded number of events."""
+
+    def __init__(self, fold_after: int = 256) -> None:
         self._pending: Dict[str, list] = {}
         self._done: Dict[str, float] = {}
+        self._fold_after = fold_after
+
+    def _fold_completed(self, name: str) -> None:
+        keep = []
+        for a, b in self._pending.get(name, []):
+            if b.query():
+                self._done[name] = self._done.get(name, 0.0) + a.elapsed_time(b)
+            else:
+                keep.append((a, b))
+        self._pending[name] = keep
 
     @contextmanager
     def timer(self, name: str) -> Iterator[None]:
@@ -111,7 +125,10 @@ class DeviceTimers:
             yield
         finally:
             b.record()
-            self._pending.setdefault(name, []).append((a, b))
+            pend = self._pending.setdefault(name, [])
+            pend.append((a, b))
+            if len(pend) > self._fold_after:
+                self._fold_completed(name)
 
     def elapsed_ms(self) -> Dict[str, float]:
         if self._pending:

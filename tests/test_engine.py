@@ -224,3 +224,15 @@ def test_train_batch_equals_forward_backward_step():
     assert ea.global_steps == eb.global_steps == STEPS
     for pa, pb in zip(a.parameters(), b.parameters()):
         assert torch.equal(pa, pb)
+
+
+def test_device_timers_option():
+    """``b200.device_timers`` parses (config or env) and is a no-op off CUDA."""
+    from minispeed_b200.config import DeepSpeedConfig
+    assert DeepSpeedConfig({"b200": {"device_timers": True}}).b200.device_timers
+    assert not DeepSpeedConfig({}).b200.device_timers
+    engine = ms.initialize(model=make_net(), config=config(b200={"device_timers": True}))
+    x, y = make_data(1, 2, 1, 4)
+    run(engine, x, y, 1, 2)
+    assert engine.device_time_ms() == {}
+    assert "backward" in engine.timers.names() and "step" in engine.timers.names()
