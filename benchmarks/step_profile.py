@@ -4,7 +4,9 @@
 
 Builds the same model and config as ``bench.py`` (synthetic tokens, random
 weights), runs three warm-up steps, profiles one step and prints the step's
-span, the summed kernel time and the kernels sorted by total time.  Profiler
+span, the summed kernel time, the kernels sorted by total time, and the
+device's idle gaps between them (count and time by length, the longest with
+their neighbours).  Profiler
 timings are for shares, not for the headline number (``bench.py`` times
 without a profiler).
 """
@@ -21,6 +23,35 @@ from torch.profiler import ProfilerActivity, profile
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
 import bench  # noqa: E402
+
+
+def idle_gaps(intervals):
+    """Idle stretches of the device between ``(start, end, name)`` intervals
+    (any order, possibly overlapping across streams): a gap opens when every
+    activity seen so far has ended.  Returns ``[(length, after_name,
+    before_name)]``."""
+    gaps, busy_until, last = [], None, None
+    for start, end, name in sorted(intervals):
+        if busy_until is not None and start > busy_until:
+            gaps.append((start - busy_until, last, name))
+        if busy_until is None or end > busy_until:
+            busy_until, last = end, name
+    return gaps
+
+
+def gap_report(gaps, top=5):
+    """Total idle time, a histogram by gap length and the longest gaps."""
+    bins = [(2, "< 2 us"), (10, "2-10 us"), (100, "10-100 us"), (float("inf"), ">= 100 us")]
+    hist = collections.OrderedDict((label, [0, 0.0]) for _, label in bins)
+    for g, _, _ in gaps:
+        label = next(lb for lim, lb in bins if g < lim)
+        hist[label][0] += 1
+        hist[label][1] += g
+    lines = [f"idle {sum(g for g, _, _ in gaps) / 1000:.3f} ms in {len(gaps)} gaps: " +
+             ", ".join(f"{lb} {n} ({t / 1000:.3f} ms)" for lb, (n, t) in hist.items())]
+    for g, after, before in sorted(gaps, reverse=True)[:top]:
+        lines.append(f"  {g:9.1f} us  after {after[:50]}  before {before[:50]}")
+    return "\n".join(lines)
 
 
 def main():
@@ -79,6 +110,7 @@ def main():
     print(f"{a.model} {a.impl}: span {span / 1000:.2f} ms, kernel sum {sum(tot.values()) / 1000:.2f} ms")
     for k, v in sorted(tot.items(), key=lambda kv: -kv[1])[:a.top]:
         print(f"{v / 1000:9.3f} ms  {cnt[k]:5d}  {k}")
+    print(gap_report(idle_gaps([(e.time_range.start, e.time_range.end, e.name) for e in evs])))
 
 
 if __name__ == "__main__":
