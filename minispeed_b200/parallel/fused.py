@@ -54,9 +54,15 @@ class CommTimeoutError(RuntimeError):
 
 
 def _device_identity(device: torch.device) -> str:
-    props = torch.cuda.get_device_properties(device)
-    uuid = getattr(props, "uuid", None)
-    return f"{socket.gethostname()}/{uuid if uuid is not None else device.index}"
+    """Host name and the GPU's UUID (its raw bytes, so that no formatting of
+    the UUID object can make two GPUs look alike); the device index when the
+    UUID is not available."""
+    raw = getattr(getattr(torch.cuda.get_device_properties(device), "uuid", None), "bytes", None)
+    try:
+        key = bytes(raw).hex() if raw is not None else None
+    except (TypeError, ValueError):
+        key = None
+    return f"{socket.gethostname()}/{key if key else 'index%d' % device.index}"
 
 
 def shared_gpu(identities) -> bool:

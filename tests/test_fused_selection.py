@@ -48,3 +48,22 @@ def test_ranks_across_nodes_are_refused(monkeypatch):
     monkeypatch.setenv("LOCAL_WORLD_SIZE", "1")
     ok, why = fused.supported(torch.device("cuda", 0))
     assert not ok and "node" in why
+
+
+def test_device_identity_uses_uuid_bytes(monkeypatch):
+    class Uuid:
+        bytes = list(range(16))
+
+    class Props:
+        uuid = Uuid()
+
+    monkeypatch.setattr(torch.cuda, "get_device_properties", lambda d: Props())
+    a = fused._device_identity(torch.device("cuda", 0))
+    b = fused._device_identity(torch.device("cuda", 5))
+    assert a == b and a.endswith("/000102030405060708090a0b0c0d0e0f")   # same GPU, any index
+
+    class NoUuid:
+        pass
+
+    monkeypatch.setattr(torch.cuda, "get_device_properties", lambda d: NoUuid())
+    assert fused._device_identity(torch.device("cuda", 5)).endswith("/index5")
