@@ -25,6 +25,7 @@ SUBMODULES = (
 
 
 def install() -> None:
+    """Register ``minispeed`` and its submodules as names of this package."""
     pkg = importlib.import_module("minispeed_b200")
     current = sys.modules.get("minispeed")
     if current is not None and current is not pkg:

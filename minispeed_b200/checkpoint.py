@@ -68,6 +68,8 @@ def _standalone_state_dict(module: torch.nn.Module) -> dict:
 
 @torch.no_grad()
 def save_checkpoint(engine, save_dir: str, tag: Optional[str] = None) -> str:
+    """Write ``save_dir/<tag>/`` (rank 0: the module states; every rank: its optimizer
+    shard) and then ``save_dir/latest``.  Collective: every rank calls it."""
     tag = tag or f"global_step{engine.global_steps}"
     ckpt_dir = os.path.join(save_dir, tag)
     os.makedirs(ckpt_dir, exist_ok=True)

@@ -41,6 +41,8 @@ def _env_int(name: str, default: int) -> int:
 
 
 def resolve_backend() -> str:
+    """``MINISPEED_BACKEND`` if set, else NCCL when every rank can have its own
+    visible GPU, else gloo."""
     forced = os.environ.get("MINISPEED_BACKEND")
     if forced:
         return forced
@@ -54,6 +56,8 @@ def get_local_rank() -> int:
 
 
 def resolve_device() -> torch.device:
+    """``MINISPEED_DEVICE`` if set, else ``cuda:LOCAL_RANK`` (clamped to the visible
+    GPUs), else the CPU."""
     forced = os.environ.get("MINISPEED_DEVICE")
     if forced:
         return torch.device(forced)
@@ -175,6 +179,7 @@ def broadcast_tensors(tensors: Iterable[torch.Tensor], src: int = 0) -> None:
 
 
 def all_gather_object(obj) -> List:
+    """Every rank's picklable ``obj``, in rank order (``[obj]`` in one process)."""
     if not is_distributed():
         return [obj]
     out: List = [None] * dist.get_world_size()

@@ -243,6 +243,8 @@ class DeepSpeedEngine:
             self.optimizer.set_loss_scale(self.loss_scaler.loss_scale_factor)
 
     def forward(self, *args, **kwargs):
+        """Run the module on inputs cast to the training dtype (stage 3: gathering
+        the parameters first) and open the micro-step's gradient window."""
         if not self.optimizer.params_gathered:
             with self._phase("gather"):
                 if getattr(self.optimizer, "plan_layer_gather", None) is not None:

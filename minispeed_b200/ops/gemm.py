@@ -42,6 +42,8 @@ class KernelTimeoutError(RuntimeError):
 
 
 def error_word(device: torch.device) -> torch.Tensor:
+    """The device status word that this device's GEMM and attention kernels set
+    when a bounded wait gives up (allocated once per device)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     t = _ERR.get(idx)
     if t is None:

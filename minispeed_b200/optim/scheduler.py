@@ -84,6 +84,8 @@ class ConstantLR(WarmupLR):
 
 
 def build_scheduler(optimizer, scheduler_type: str, params: dict):
+    """The scheduler named by the config (``WarmupLR`` and its aliases, or
+    ``WarmupDecayLR``) over ``optimizer.param_groups``."""
     kwargs = dict(warmup_min_lr=params.get("warmup_min_lr", 0.0),
                   warmup_max_lr=params.get("warmup_max_lr"),
                   warmup_num_steps=params.get("warmup_num_steps", 0),

@@ -72,6 +72,8 @@ def shared_gpu(identities) -> bool:
 
 
 def supported(device: torch.device) -> Tuple[bool, str]:
+    """Whether the fused NVLink collectives can serve this process group, and
+    why not.  Collective when the group uses NCCL: every rank must call it."""
     if device.type != "cuda":
         return False, "fused collectives need CUDA devices"
     if not comm.is_distributed():

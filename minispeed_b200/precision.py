@@ -45,6 +45,8 @@ class DynamicLossScaler:
         return self.scale if self.enabled else 1.0
 
     def update(self, overflow: bool) -> None:
+        """Advance the scaler after a step: halve on overflow (and count the skip),
+        double after ``scale_window`` consecutive good steps."""
         if not self.enabled:
             return
         if overflow:

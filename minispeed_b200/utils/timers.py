@@ -144,6 +144,8 @@ class DeviceTimers:
 
 
 def max_over_ranks(value: float) -> float:
+    """The largest ``value`` over the process group (device times are reported
+    as the slowest rank's)."""
     from .. import comm
 
     if not comm.is_distributed():
