@@ -20,7 +20,7 @@ def plain_torch(x, y, lr, wd, clip):
     for s in range(STEPS):
         for m in range(GAS):
             loss = F.mse_loss(model(x[s, m]), y[s, m])
-            losses.append(float(loss))
+            losses.append(float(loss.detach()))
             (loss / GAS).backward()
         if clip:
             torch.nn.utils.clip_grad_norm_(model.parameters(), clip)

@@ -88,7 +88,7 @@ def test_gpt_trains_on_gpu(dtype):
         loss = engine(data[:, :-1], targets=data[:, 1:])
         engine.backward(loss)
         engine.step()
-        losses.append(float(loss))
+        losses.append(float(loss.detach()))
     assert losses[-1] < losses[0] - 1.0, losses
 
 
