@@ -131,10 +131,28 @@ def all_reduce_flag(flag: bool) -> bool:
     return bool(t.item())
 
 
+_FORCE_STAGING = os.environ.get("MINISPEED_STAGE_COLLECTIVES", "0") == "1"
+
+
+def host_staged(*tensors: torch.Tensor) -> bool:
+    """Whether a reduce-scatter or all-gather over these tensors goes through
+    host copies: gloo (the backend of ranks that share a GPU) moves CUDA
+    tensors for broadcast, all-reduce and barrier, not for these two.
+    ``MINISPEED_STAGE_COLLECTIVES=1`` forces the host copies (tests)."""
+    if not _initialized():
+        return False
+    return _FORCE_STAGING or (dist.get_backend() == "gloo" and any(t.is_cuda for t in tensors))
+
+
 def reduce_scatter(output: torch.Tensor, input_: torch.Tensor) -> torch.Tensor:
     """SUM-reduce ``input_`` (world * output.numel()) and keep this rank's slice."""
     if is_distributed():
-        dist.reduce_scatter_tensor(output, input_)
+        if host_staged(output, input_):
+            out = output.to("cpu", copy=True)
+            dist.reduce_scatter_tensor(out, input_.to("cpu", copy=True))
+            output.copy_(out)
+        else:
+            dist.reduce_scatter_tensor(output, input_)
     else:
         output.copy_(input_)
     return output
@@ -143,7 +161,12 @@ def reduce_scatter(output: torch.Tensor, input_: torch.Tensor) -> torch.Tensor:
 def all_gather_flat(output: torch.Tensor, local_shard: torch.Tensor) -> torch.Tensor:
     """Concatenate every rank's shard, in rank order, into ``output``."""
     if is_distributed():
-        dist.all_gather_into_tensor(output, local_shard)
+        if host_staged(output, local_shard):
+            out = output.to("cpu", copy=True)
+            dist.all_gather_into_tensor(out, local_shard.to("cpu", copy=True))
+            output.copy_(out)
+        else:
+            dist.all_gather_into_tensor(output, local_shard)
     else:
         output.copy_(local_shard)
     return output

@@ -33,6 +33,7 @@ from typing import Tuple
 import torch
 import torch.distributed as dist
 
+from .. import comm
 from ..flat import FlatParamGroup
 from ..ops import kernels
 
@@ -122,7 +123,7 @@ class LibraryCollectives:
             g._grad = full
             return full, 1.0 / self.world_size, False
         out = self._shard_out(g)
-        dist.reduce_scatter_tensor(out, full)
+        comm.reduce_scatter(out, full)
         g._grad = None if g.zero_stage >= 3 else full
         return out, 1.0 / self.world_size, False
 
@@ -133,17 +134,17 @@ class LibraryCollectives:
         dist.all_reduce(out[:2])
 
     def _gather_into(self, full: torch.Tensor, shard: torch.Tensor) -> None:
-        if full.is_cuda and self.name == "nccl":
-            dist.all_gather_into_tensor(full, shard)
-        else:
-            dist.all_gather_into_tensor(full, shard.clone())
+        # ``shard`` is this rank's slice of ``full``: NCCL gathers in place,
+        # gloo needs a separate input
+        comm.all_gather_flat(full, shard if (full.is_cuda and self.name == "nccl")
+                             else shard.clone())
 
     def gather_params(self, g: FlatParamGroup) -> None:
         arena = g.param_arena
         self._gather_into(arena, arena[g.shard_start:g.shard_end])
 
     def gather_shards(self, g: FlatParamGroup) -> None:
-        dist.all_gather_into_tensor(g.param_arena, g.param_shard)
+        comm.all_gather_flat(g.param_arena, g.param_shard)
 
     def gather_masters(self, g: FlatParamGroup) -> None:
         if g._partitioned:

@@ -185,3 +185,20 @@ def test_surviving_rank_fails_cleanly_when_a_peer_leaves(tmp_path):
     out = torch.load(tmp_path / "r0.pt", weights_only=False)
     assert out["result"] != "no error"
     assert out["seconds"] < 60
+
+
+@pytest.mark.parametrize("stage", [0, 1, 2, 3])
+def test_host_staged_collectives_match(stage, tmp_path, monkeypatch):
+    """Ranks that share a GPU use gloo, which does not reduce-scatter or
+    all-gather CUDA tensors; those two then go through host copies.  Forced
+    here on CPU ranks, the staged path gives the same results bit for bit."""
+    (tmp_path / "a").mkdir()
+    (tmp_path / "b").mkdir()
+    plain = _spawn(stage, tmp_path / "a")
+    monkeypatch.setenv("MINISPEED_STAGE_COLLECTIVES", "1")
+    staged = _spawn(stage, tmp_path / "b")
+    for p, s in zip(plain, staged):
+        assert torch.equal(p["losses"], s["losses"])
+        for k in p["params"]:
+            assert torch.equal(p["params"][k], s["params"][k]), k
+        assert torch.equal(p["masters"], s["masters"])
