@@ -39,19 +39,20 @@
 //     streams, or different host threads) race on the array; serialize them.
 #include <mutex>
 
+#include "colsum_noalloc.h"
 #include "common.cuh"
 
 namespace {
 
-constexpr long long kScratchFloats = 1LL << 20;
+constexpr long long kScratchFloats = MSB_COLSUM_NOALLOC_MAX_N;
 constexpr int kMaxChunks = 256;
 constexpr int kMaxDevices = 64;
 
-// return codes of msb_colsum_noalloc
-constexpr int kNoallocOk = 0;
-constexpr int kNoallocBadArgs = -1;
-constexpr int kNoallocTooWide = -2;
-constexpr int kNoallocCudaError = -3;
+// return codes of msb_colsum_noalloc (declared in colsum_noalloc.h)
+constexpr int kNoallocOk = MSB_NOALLOC_OK;
+constexpr int kNoallocBadArgs = MSB_NOALLOC_BAD_ARGS;
+constexpr int kNoallocTooWide = MSB_NOALLOC_TOO_WIDE;
+constexpr int kNoallocCudaError = MSB_NOALLOC_CUDA_ERROR;
 
 static __device__ __align__(256) float g_noalloc_colsum_scratch[kScratchFloats];
 

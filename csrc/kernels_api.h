@@ -4,6 +4,10 @@
 
 #include <cuda_runtime.h>
 
+// C entry point that allocates nothing (msb_colsum_noalloc); no counterpart
+// in the reference
+#include "colsum_noalloc.h"
+
 namespace msb {
 
 enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
