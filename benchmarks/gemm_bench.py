@@ -2,10 +2,16 @@
 GPT-2-small training shapes (M = 16 x 1024 tokens).
 
     python benchmarks/gemm_bench.py [--tokens 16384] [--iters 20]
+    python benchmarks/gemm_bench.py --shape 16384,768,3072 --layout fwd [--iters 3]
 
 Times each product with CUDA events after warm-up; inputs are re-used, the
 operand set of each shape is < L2 for the small products, so this measures
 kernel throughput (compare with the cuBLAS column, same conditions).
+
+``--shape M,N,K`` runs one product of one layout (``fwd``: both operands
+K-major; ``dgrad``: B N-major; ``wgrad``: both M-major) ``--iters`` times
+without warm-up, each launch timed on its own, and prints one result line:
+the target of an ncu capture of the kernel.
 """
 
 import argparse
@@ -32,13 +38,43 @@ def timeit(fn, iters):
     return a.elapsed_time(b) / iters
 
 
+def one_shape(shape: str, layout: str, iters: int, dt) -> None:
+    """One product, launched ``iters`` times, each timed on its own."""
+    M, N, K = (int(v) for v in shape.split(","))
+    kmaj = {"fwd": (True, True), "dgrad": (True, False), "wgrad": (False, False)}[layout]
+    A = torch.randn(M, K, device="cuda").to(dt)
+    B = (torch.randn(N, K, device="cuda") * 0.02).to(dt)
+    A = A if kmaj[0] else A.t().contiguous()
+    B = B if kmaj[1] else B.t().contiguous()
+    out = torch.empty(M, N, device="cuda", dtype=dt)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    times = []
+    for _ in range(iters):
+        ev[0].record()
+        gemm.gemm(A, B, a_kmajor=kmaj[0], b_kmajor=kmaj[1], out=out)
+        ev[1].record()
+        torch.cuda.synchronize()
+        times.append(ev[0].elapsed_time(ev[1]))
+    gemm.check()
+    best = min(times)
+    print(json.dumps({"gemm": layout, "M_N_K": [M, N, K], "iters": iters,
+                      "ms": [round(t, 4) for t in times],
+                      "best_tflops": round(2.0 * M * N * K / best / 1e9, 1)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--embd", type=int, default=768)
     ap.add_argument("--dtype", default="fp16", choices=["fp16", "bf16"])
+    ap.add_argument("--shape", default=None, help="M,N,K: one product only")
+    ap.add_argument("--layout", default="fwd", choices=["fwd", "dgrad", "wgrad"])
     args = ap.parse_args()
+    if args.shape:
+        one_shape(args.shape, args.layout, args.iters,
+                  torch.float16 if args.dtype == "fp16" else torch.bfloat16)
+        return
     T, C, V = args.tokens, args.embd, 50257
     Vp = 50304
     dt = torch.float16 if args.dtype == "fp16" else torch.bfloat16

@@ -250,6 +250,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  // set-up above touches shared and tensor memory only: it overlaps the
+  // previous kernel's tail (programmatic dependent launch)
+  ::msb::pdl_begin();
   // Tensor memory.  D = 64: S of tile t at 128t, P at 256 + 64t, O at 384 + 64t,
   // so the next scores of a tile can be computed while its softmax still
   // runs.  D = 128: no room for that; P overwrites S (its next S waits for P V).
@@ -546,7 +549,7 @@ void launch_fwd(const CUtensorMap& tm, const Params& p, int B, int H, cudaStream
     attr = true;
   }
   dim3 grid(B * H, p.n_pairs);
-  kern<<<grid, kThreads, smem_bytes<D>(), st>>>(tm, p);
+  ::msb::launch(kern, grid, kThreads, smem_bytes<D>(), st, tm, p);
 }
 
 // ======================================================================
@@ -817,6 +820,9 @@ attn_bwd64_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  // set-up above touches shared and tensor memory only: it overlaps the
+  // previous kernel's tail (programmatic dependent launch)
+  ::msb::pdl_begin();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA
@@ -1212,6 +1218,7 @@ __global__ void __launch_bounds__(256)
 attn_delta_kernel(const T* __restrict__ dout, long long ld_do, const T* __restrict__ out,
                   long long ld_o, float* __restrict__ delta, float* __restrict__ dq_acc, int BT,
                   int seq, int H) {
+  ::msb::pdl_begin();
   constexpr int V = D / 64;   // 16-byte pieces of a head row per lane
   const long long n = (long long)BT * H;
   const int sub = threadIdx.x & 7;
@@ -1251,6 +1258,7 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 attn_dq_convert_kernel(const float* __restrict__ dq_acc, int BT, int HD, T* __restrict__ dqkv,
                        long long ld_dqkv, int q_col, float scale) {
+  ::msb::pdl_begin();
   const long long n = (long long)BT * HD / 8;
   for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
        idx += (long long)gridDim.x * blockDim.x) {
@@ -1280,7 +1288,7 @@ void launch_bwd64(const CUtensorMap& tkv, const CUtensorMap& tq, const CUtensorM
     attr = true;
   }
   const int items = p.n_q * p.B * p.Hkv;
-  kern<<<std::min(items, kNumSMs), kThreadsB, Layout64::BYTES, st>>>(tkv, tq, td, tdq, p);
+  ::msb::launch(kern, std::min(items, kNumSMs), kThreadsB, Layout64::BYTES, st, tkv, tq, td, tdq, p);
 }
 
 
@@ -1371,6 +1379,9 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  // set-up above touches shared and tensor memory only: it overlaps the
+  // previous kernel's tail (programmatic dependent launch)
+  ::msb::pdl_begin();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA
@@ -1640,7 +1651,7 @@ void launch_bwd128(const CUtensorMap& tq, const CUtensorMap& td, const CUtensorM
     attr = true;
   }
   dim3 grid(p.B * p.Hkv, p.n_q);
-  kern<<<grid, kThreads128, Layout128::BYTES, st>>>(tq, td, tdq, p);
+  ::msb::launch(kern, grid, kThreads128, Layout128::BYTES, st, tq, td, tdq, p);
 }
 
 }  // namespace bwd
@@ -1768,16 +1779,16 @@ void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
   auto run = [&](auto tag) {
     using T = decltype(tag);
     if (D == 64)
-      attn_delta_kernel<T, 64><<<blocks, 256, 0, st>>>(static_cast<const T*>(dout), ld_do,
+      ::msb::launch(attn_delta_kernel<T, 64>, blocks, 256, 0, st, static_cast<const T*>(dout), ld_do,
                                                        static_cast<const T*>(out), ld_out, delta,
                                                        dq_acc, BT, T_seq, H);
     else
-      attn_delta_kernel<T, 128><<<blocks, 256, 0, st>>>(static_cast<const T*>(dout), ld_do,
+      ::msb::launch(attn_delta_kernel<T, 128>, blocks, 256, 0, st, static_cast<const T*>(dout), ld_do,
                                                         static_cast<const T*>(out), ld_out, delta,
                                                         dq_acc, BT, T_seq, H);
     if (D == 64) launch_bwd64<T>(tq, tq64, td64, tdq16, p, st);
     else launch_bwd128<T>(tq, td, tdq, p, st);
-    attn_dq_convert_kernel<T><<<blocks_c, 256, 0, st>>>(dq_acc, BT, H * D, static_cast<T*>(dqkv),
+    ::msb::launch(attn_dq_convert_kernel<T>, blocks_c, 256, 0, st, dq_acc, BT, H * D, static_cast<T*>(dqkv),
                                                         ld_dqkv, q_col, scale);
   };
   if (dtype == kF16) {
@@ -1788,7 +1799,6 @@ void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
     throw std::runtime_error("attention takes fp16/bf16");
   }
   MSB_CHECK_LAUNCH("attention_bwd");
-  count_launch(2);
 }
 
 }  // namespace msb

@@ -232,6 +232,38 @@ void cross_entropy_fwd(const at::Tensor& logits, const at::Tensor& tgt, const at
                          dtype_code(logits), stream_of(logits));
 }
 
+void cross_entropy_fwd_grad(const at::Tensor& logits, const at::Tensor& tgt,
+                            const at::Tensor& lse, const at::Tensor& loss_rows,
+                            const at::Tensor& loss, const at::Tensor& inv_count,
+                            const at::Tensor& g_hint, int64_t ignore_index) {
+  check_rows(logits, "logits");
+  check_cuda_contig(tgt, "targets");
+  TORCH_CHECK(tgt.scalar_type() == at::kLong, "targets must be int64");
+  TORCH_CHECK(g_hint.is_cuda() && g_hint.scalar_type() == at::kFloat && g_hint.numel() >= 1,
+              "g_hint: fp32 CUDA scalar");
+  const int64_t V = logits.size(1), M = logits.size(0);
+  TORCH_CHECK(tgt.numel() == M && lse.numel() >= M && loss_rows.numel() >= M);
+  c10::cuda::CUDAGuard g(logits.device());
+  msb::cross_entropy_fwd_grad(logits.data_ptr(),
+                              reinterpret_cast<const long long*>(tgt.data_ptr<int64_t>()),
+                              lse.data_ptr<float>(), loss_rows.data_ptr<float>(),
+                              loss.data_ptr<float>(), inv_count.data_ptr<float>(),
+                              g_hint.data_ptr<float>(), M, (int)V, logits.stride(0),
+                              ignore_index, dtype_code(logits), stream_of(logits));
+}
+
+void cross_entropy_grad_rescale(const at::Tensor& dlogits, const at::Tensor& grad_out,
+                                const at::Tensor& g_hint) {
+  check_rows(dlogits, "dlogits");
+  TORCH_CHECK(grad_out.scalar_type() == at::kFloat && grad_out.is_cuda());
+  TORCH_CHECK(g_hint.scalar_type() == at::kFloat && g_hint.is_cuda());
+  c10::cuda::CUDAGuard g(dlogits.device());
+  msb::cross_entropy_grad_rescale(dlogits.data_ptr(), dlogits.size(0), (int)dlogits.size(1),
+                                  dlogits.stride(0), grad_out.data_ptr<float>(),
+                                  g_hint.data_ptr<float>(), dtype_code(dlogits),
+                                  stream_of(dlogits));
+}
+
 void cross_entropy_bwd(const at::Tensor& logits, const at::Tensor& tgt, const at::Tensor& lse,
                        const at::Tensor& grad_out, const at::Tensor& inv_count,
                        int64_t ignore_index) {
@@ -256,15 +288,30 @@ void embedding_fwd(const at::Tensor& idx, const at::Tensor& wte, const OptT& wpe
                      idx.numel(), (int)T, (int)C, wte.size(0), dtype_code(wte), stream_of(wte));
 }
 
-void embedding_bwd(const at::Tensor& dout, const at::Tensor& idx, const at::Tensor& dwte,
-                   const OptT& dwpe, int64_t T) {
+void embedding_bwd(const at::Tensor& dout, const at::Tensor& idx, const at::Tensor& acc,
+                   const at::Tensor& touched, const at::Tensor& dwte, bool acc_wte,
+                   const OptT& dwpe, bool acc_wpe, int64_t T) {
   check_cuda_contig(dout, "dout");
-  TORCH_CHECK(dwte.scalar_type() == at::kFloat);
+  check_cuda_contig(idx, "idx");
+  check_cuda_contig(acc, "acc");
+  check_cuda_contig(dwte, "dwte");
+  TORCH_CHECK(idx.scalar_type() == at::kLong);
   const int64_t C = dout.size(-1);
+  const int64_t V = dwte.size(0);
+  TORCH_CHECK(C % 8 == 0 && dwte.size(-1) == C && dwte.scalar_type() == dout.scalar_type());
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.numel() >= V * C, "acc: fp32 [V, C]");
+  TORCH_CHECK(touched.scalar_type() == at::kByte && touched.numel() >= V, "touched: uint8 [V]");
+  TORCH_CHECK(idx.numel() % T == 0, "tokens must be a whole number of sequences");
+  if (dwpe) {
+    check_cuda_contig(*dwpe, "dwpe");
+    TORCH_CHECK(dwpe->size(-1) == C && dwpe->size(0) >= T &&
+                dwpe->scalar_type() == dout.scalar_type());
+  }
   c10::cuda::CUDAGuard g(dout.device());
-  msb::embedding_bwd(dout.data_ptr(), reinterpret_cast<const long long*>(idx.data_ptr<int64_t>()), dwte.data_ptr<float>(),
-                     optr_f(dwpe), idx.numel(), (int)T, (int)C, dwte.size(0), dtype_code(dout),
-                     stream_of(dout));
+  msb::embedding_bwd(dout.data_ptr(), reinterpret_cast<const long long*>(idx.data_ptr<int64_t>()),
+                     acc.data_ptr<float>(), touched.data_ptr<uint8_t>(), dwte.data_ptr(),
+                     acc_wte ? 1 : 0, dwpe ? dwpe->data_ptr() : nullptr, acc_wpe ? 1 : 0,
+                     idx.numel(), (int)T, (int)C, V, dtype_code(dout), stream_of(dout));
 }
 
 void rope(const at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t, int64_t BT,
@@ -296,6 +343,33 @@ std::mutex g_plan_mutex;
 bool g_autotune = std::getenv("MSB_GEMM_AUTOTUNE") == nullptr ||
                   std::string(std::getenv("MSB_GEMM_AUTOTUNE")) != "0";
 
+bool g_stream_k = std::getenv("MSB_GEMM_STREAMK") == nullptr ||
+                 std::string(std::getenv("MSB_GEMM_STREAMK")) != "0";
+
+// fp32 partial-tile slots of a stream-K launch: one per resident CTA pair
+long long stream_k_ws_floats() { return 74LL * msb::kStreamKSlotFloats; }
+
+// Per-device zeroed tile counters of the stream-K GEMM (persistent: each
+// launch leaves them zero again).
+int* stream_k_counters(const at::Device& dev) {
+  static std::map<int, at::Tensor> bufs;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = bufs.find(dev.index());
+  if (it == bufs.end())
+    it = bufs.emplace(dev.index(), at::zeros({msb::kStreamKCounters},
+                                             at::TensorOptions().dtype(at::kInt).device(dev)))
+             .first;
+  return it->second.data_ptr<int>();
+}
+
+void gemm_reset_stream_k(const at::Tensor& like) {
+  c10::cuda::CUDAGuard g(like.device());
+  cuda_ok(cudaMemsetAsync(stream_k_counters(like.device()), 0,
+                          msb::kStreamKCounters * sizeof(int), stream_of(like)),
+          "stream-K counter reset");
+}
+
 std::pair<int, int> tune_gemm(const at::Tensor& a, const at::Tensor& b, int a_mn, int b_mn,
                               int64_t M, int64_t N, int64_t K, bool fused, const at::Tensor& err,
                               double timeout_s, cudaStream_t st) {
@@ -313,12 +387,18 @@ std::pair<int, int> tune_gemm(const at::Tensor& a, const at::Tensor& b, int a_mn
       if (s > 1 && (long long)s * M * N > (1LL << 31)) continue;
       cands.push_back({bn, s});
     }
+    // stream-K: the pair kernel over an even cut of all K slices
+    if (bn == 512 && g_stream_k && (M + 255) / 256 * ((N + 255) / 256) <= msb::kStreamKCounters)
+      cands.push_back({bn, -1});
   }
   if (cands.size() <= 1) return cands.empty() ? std::make_pair(0, 0) : cands[0];
   const int64_t ldn = (N + 7) / 8 * 8;  // aligned rows, as the real outputs use
   at::Tensor scratch = at::empty({M, ldn}, a.options());
   long long ws_need = 0;
-  for (auto& c : cands) ws_need = std::max<long long>(ws_need, c.second > 1 ? c.second * M * N : 0);
+  for (auto& c : cands)
+    ws_need = std::max<long long>(ws_need, c.second > 1 ? c.second * M * N
+                                           : (c.second == -1 ? stream_k_ws_floats() : 0));
+  int* ctr = stream_k_counters(a.device());
   at::Tensor ws;
   if (ws_need > 0) ws = at::empty({ws_need}, a.options().dtype(at::kFloat));
   cudaEvent_t e0, e1;
@@ -334,7 +414,7 @@ std::pair<int, int> tune_gemm(const at::Tensor& a, const at::Tensor& b, int a_mn
                         scratch.data_ptr(), ldn, nullptr, (int)M, (int)N, (int)K, dtype_code(a), 0,
                         0, nullptr, 0, ws_need > 0 ? ws.data_ptr<float>() : nullptr, ws_need,
                         reinterpret_cast<unsigned*>(err.data_ptr<int>()), timeout_s, st, c.first,
-                        c.second);
+                        c.second, ctr, msb::kStreamKCounters);
       cuda_ok(cudaEventRecord(e1, st), "event");
       cuda_ok(cudaEventSynchronize(e1), "event");
       float ms = 0.f;
@@ -396,9 +476,12 @@ void attention_bwd_py(const at::Tensor& qkv2d, int64_t q_col, int64_t k_col, int
 
 // C[M,N] (+)= A * B^T with A given as [M,K] (a_kmajor) or [K,M], B as [N,K]
 // (b_kmajor) or [K,N]; every matrix row-major with unit column stride.
+// force_bn > 0 picks the plan (bn 512 = 2-CTA pair, 256/128 = 1-CTA; splits
+// 1-8 split-K, -1 stream-K) instead of the tuned one (tests, benchmarks).
 void gemm(const at::Tensor& a, const at::Tensor& b, bool a_kmajor, bool b_kmajor,
           const OptT& bias, const at::Tensor& out, bool accumulate, const at::Tensor& err,
-          double timeout_s, int64_t mode, const OptT& aux) {
+          double timeout_s, int64_t mode, const OptT& aux, int64_t force_bn,
+          int64_t force_splits) {
   check_rows(a, "A");
   check_rows(b, "B");
   check_rows(out, "C");
@@ -431,7 +514,10 @@ void gemm(const at::Tensor& a, const at::Tensor& b, bool a_kmajor, bool b_kmajor
   cudaStream_t st = stream_of(a);
   const int a_mn = a_kmajor ? 0 : 1, b_mn = b_kmajor ? 0 : 1;
   int bn = 0, splits = 0;
-  if (g_autotune) {
+  if (force_bn > 0) {
+    bn = (int)force_bn;
+    splits = (int)force_splits;
+  } else if (g_autotune) {
     const PlanKey key{M, N, K, a_mn, b_mn, dtype_code(a), mode != 0 ? 1 : 0};
     std::lock_guard<std::mutex> lock(g_plan_mutex);
     auto it = g_plans.find(key);
@@ -451,19 +537,21 @@ void gemm(const at::Tensor& a, const at::Tensor& b, bool a_kmajor, bool b_kmajor
   }
   long long need = 0;
   if (bn > 0) {
-    need = splits > 1 ? (long long)splits * M * N : 0;
+    need = splits > 1 ? (long long)splits * M * N : (splits == -1 ? stream_k_ws_floats() : 0);
   } else {
     int pbn = 0, ps = 1;
     need = msb::gemm_plan((int)M, (int)N, (int)K, 148, &pbn, &ps);
   }
-  if (mode != 0) need = 0;
+  if (mode != 0 && splits != -1) need = 0;
   at::Tensor ws;
   if (need > 0) ws = at::empty({need}, a.options().dtype(at::kFloat));
   msb::gemm_tcgen05(a.data_ptr(), a.stride(0), a_mn, b.data_ptr(), b.stride(0), b_mn,
                     out.data_ptr(), out.stride(0), optr(bias), (int)M, (int)N, (int)K,
                     dtype_code(a), accumulate ? 1 : 0, (int)mode, auxp, ld_aux,
                     need > 0 ? ws.data_ptr<float>() : nullptr, need,
-                    reinterpret_cast<unsigned*>(err.data_ptr<int>()), timeout_s, st, bn, splits);
+                    reinterpret_cast<unsigned*>(err.data_ptr<int>()), timeout_s, st, bn, splits,
+                    splits == -1 ? stream_k_counters(a.device()) : nullptr,
+                    msb::kStreamKCounters);
 }
 
 std::vector<int64_t> gemm_cached_plan(int64_t M, int64_t N, int64_t K, int64_t a_mn,
@@ -613,6 +701,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, mod) {
   mod.def("swiglu_bwd", &swiglu_bwd);
   mod.def("cross_entropy_fwd", &cross_entropy_fwd);
   mod.def("cross_entropy_bwd", &cross_entropy_bwd);
+  mod.def("cross_entropy_fwd_grad", &cross_entropy_fwd_grad);
+  mod.def("cross_entropy_grad_rescale", &cross_entropy_grad_rescale);
   mod.def("embedding_fwd", &embedding_fwd);
   mod.def("embedding_bwd", &embedding_bwd);
   mod.def("rope", &rope);
@@ -621,6 +711,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, mod) {
   mod.def("attention_bwd", &attention_bwd_py);
   mod.def("gemm_plan", &gemm_plan_py);
   mod.def("gemm_cached_plan", &gemm_cached_plan);
+  mod.def("gemm_reset_stream_k", &gemm_reset_stream_k);
   mod.def("peer_alloc", &peer_alloc_py);
   mod.def("peer_free", &peer_free_py);
   mod.def("peer_handle", &peer_handle_py);

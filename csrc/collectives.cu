@@ -70,6 +70,7 @@ __device__ __forceinline__ Board* board_of(char* heap, long long sync_off) {
 __global__ void peer_barrier_kernel(char* const* heaps, long long sync_off, int rank, int world,
                                     unsigned* ctr, unsigned long long timeout_ns,
                                     unsigned* status) {
+  ::msb::pdl_begin();
   // make this device's earlier writes (local and peer stores of preceding
   // kernels) visible system-wide before announcing the epoch
   __threadfence_system();
@@ -101,6 +102,7 @@ rs_stats_kernel(char* const* heaps, long long grad_off, long long s0, long long 
                 float mul_host, const float* __restrict__ mul_dev, float* __restrict__ out,
                 long long fanout_off, float* __restrict__ partials,
                 unsigned* __restrict__ pflags) {
+  ::msb::pdl_begin();
   // the multiplier (1 / (loss scale * world)) may live on the device, so a
   // launch replayed from a CUDA graph follows the current loss scale
   const float mul = mul_dev != nullptr ? mul_host * *mul_dev : mul_host;
@@ -187,6 +189,7 @@ rs_stats_kernel(char* const* heaps, long long grad_off, long long s0, long long 
 __global__ void stats_exchange_kernel(char* const* heaps, long long sync_off, int rank, int world,
                                       unsigned* ctr, float* out, double max_norm,
                                       unsigned long long timeout_ns, unsigned* status) {
+  ::msb::pdl_begin();
   if (threadIdx.x == 0) {
     const unsigned epoch = *ctr + 1u;
     *ctr = epoch;
@@ -248,35 +251,44 @@ __device__ __forceinline__ float adam_one(float& p, float& mm, float& vv, float 
   return p;
 }
 
-// VECLOAD: master/m/v/grad are 16-byte aligned -> float4 accesses
+// VECLOAD: master/m/v/grad are 16-byte aligned -> float4 accesses.  Each
+// thread updates 16 bytes' worth of parameters (8 x 16-bit or 4 x fp32) and
+// stores them to every rank with one 16-byte store per rank; the rank order
+// starts at a different peer in each block, so the stores of one moment
+// spread over all peers' links instead of queueing on rank 0's.
 template <typename P, bool VECLOAD>
 __global__ void __launch_bounds__(256)
 adamw_fanout_kernel(float* __restrict__ master, float* __restrict__ m, float* __restrict__ v,
                     const float* __restrict__ grad, char* const* heaps, long long param_off,
                     long long s0, long long n, int world, const float* __restrict__ stats,
                     AdamArgs2 a) {
+  ::msb::pdl_begin();
   if (stats[0] != 0.f) return;  // overflow: nothing changes on any rank
   const float coef = stats[3];
-  constexpr int VEC = 4;
-  constexpr int BYTES = static_cast<int>(sizeof(P)) * VEC;
+  constexpr int VEC = 16 / static_cast<int>(sizeof(P));
   const long long groups = (n + VEC - 1) / VEC;
   const long long stride = (long long)gridDim.x * blockDim.x;
+  const int q0 = (int)(blockIdx.x % (unsigned)world);
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < groups; i += stride) {
     const long long e0 = i * VEC;
     const int cnt = (int)min((long long)VEC, n - e0);
     alignas(16) P outv[VEC];
     if (VECLOAD && cnt == VEC) {
-      float4 p4 = *reinterpret_cast<const float4*>(master + e0);
-      float4 m4 = *reinterpret_cast<const float4*>(m + e0);
-      float4 v4 = *reinterpret_cast<const float4*>(v + e0);
-      const float4 g4 = *reinterpret_cast<const float4*>(grad + e0);
-      outv[0] = from_f32<P>(adam_one(p4.x, m4.x, v4.x, g4.x, coef, a));
-      outv[1] = from_f32<P>(adam_one(p4.y, m4.y, v4.y, g4.y, coef, a));
-      outv[2] = from_f32<P>(adam_one(p4.z, m4.z, v4.z, g4.z, coef, a));
-      outv[3] = from_f32<P>(adam_one(p4.w, m4.w, v4.w, g4.w, coef, a));
-      *reinterpret_cast<float4*>(master + e0) = p4;
-      *reinterpret_cast<float4*>(m + e0) = m4;
-      *reinterpret_cast<float4*>(v + e0) = v4;
+#pragma unroll
+      for (int h = 0; h < VEC / 4; ++h) {
+        const long long e = e0 + 4 * h;
+        float4 p4 = *reinterpret_cast<const float4*>(master + e);
+        float4 m4 = *reinterpret_cast<const float4*>(m + e);
+        float4 v4 = *reinterpret_cast<const float4*>(v + e);
+        const float4 g4 = *reinterpret_cast<const float4*>(grad + e);
+        outv[4 * h + 0] = from_f32<P>(adam_one(p4.x, m4.x, v4.x, g4.x, coef, a));
+        outv[4 * h + 1] = from_f32<P>(adam_one(p4.y, m4.y, v4.y, g4.y, coef, a));
+        outv[4 * h + 2] = from_f32<P>(adam_one(p4.z, m4.z, v4.z, g4.z, coef, a));
+        outv[4 * h + 3] = from_f32<P>(adam_one(p4.w, m4.w, v4.w, g4.w, coef, a));
+        *reinterpret_cast<float4*>(master + e) = p4;
+        *reinterpret_cast<float4*>(m + e) = m4;
+        *reinterpret_cast<float4*>(v + e) = v4;
+      }
     } else {
 #pragma unroll
       for (int k = 0; k < VEC; ++k) {
@@ -290,17 +302,16 @@ adamw_fanout_kernel(float* __restrict__ master, float* __restrict__ m, float* __
         }
       }
     }
-    // one vector store per rank when the destination allows it: 4 x 16-bit
-    // = 8 bytes, 4 x fp32 = 16 bytes
-    for (int q = 0; q < world; ++q) {
+    for (int j = 0; j < world; ++j) {
+      int q = q0 + j;
+      if (q >= world) q -= world;
       P* dst = reinterpret_cast<P*>(heaps[q] + param_off) + s0 + e0;
-      const bool vec = cnt == VEC && (reinterpret_cast<uintptr_t>(dst) % BYTES) == 0;
-      if (vec && BYTES == 8) {
-        *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(outv);
-      } else if (vec && BYTES == 16) {
+      if (cnt == VEC && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
         *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(outv);
       } else {
-        for (int k = 0; k < cnt; ++k) dst[k] = outv[k];
+#pragma unroll
+        for (int k = 0; k < VEC; ++k)
+          if (k < cnt) dst[k] = outv[k];
       }
     }
   }
@@ -315,6 +326,7 @@ template <typename T, int VEC>
 __global__ void __launch_bounds__(256)
 gather_range_kernel(char* const* heaps, long long shard_off, long long shard, long long lo,
                     long long hi, T* __restrict__ dst) {
+  ::msb::pdl_begin();
   const long long nv = (hi - lo) / VEC;
   for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < nv;
        v += (long long)gridDim.x * blockDim.x) {
@@ -335,7 +347,7 @@ gather_range_kernel(char* const* heaps, long long shard_off, long long shard, lo
 // ------------------------------------------------------------- host API
 void peer_barrier(char* const* heaps, long long sync_off, int rank, int world, unsigned* ctr,
                   double timeout_s, unsigned* status, cudaStream_t st) {
-  peer_barrier_kernel<<<1, 32, 0, st>>>(heaps, sync_off, rank, world, ctr,
+  ::msb::launch(peer_barrier_kernel, 1, 32, 0, st, heaps, sync_off, rank, world, ctr,
                                         (unsigned long long)(timeout_s * 1e9), status);
   MSB_CHECK_LAUNCH("peer_barrier");
 }
@@ -353,11 +365,11 @@ int rs_stats(char* const* heaps, long long grad_off, int dtype, long long s0, lo
     // vector loads need 16-byte aligned sources, vector stores an aligned out
     if (aligned16 && V == 8 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
       blocks = grid_for(n / V, threads, max_blocks);
-      rs_stats_kernel<T, 8><<<blocks, threads, 0, st>>>(heaps, grad_off, s0, n, world, mul,
+      ::msb::launch(rs_stats_kernel<T, 8>, blocks, threads, 0, st, heaps, grad_off, s0, n, world, mul,
                                                         mul_dev, out, fanout_off, partials, pflags);
     } else {
       blocks = grid_for(n, threads, max_blocks);
-      rs_stats_kernel<T, 1><<<blocks, threads, 0, st>>>(heaps, grad_off, s0, n, world, mul,
+      ::msb::launch(rs_stats_kernel<T, 1>, blocks, threads, 0, st, heaps, grad_off, s0, n, world, mul,
                                                         mul_dev, out, fanout_off, partials, pflags);
     }
   });
@@ -368,7 +380,7 @@ int rs_stats(char* const* heaps, long long grad_off, int dtype, long long s0, lo
 void stats_exchange(char* const* heaps, long long sync_off, int rank, int world, unsigned* ctr,
                     float* out, double max_norm, double timeout_s, unsigned* status,
                     cudaStream_t st) {
-  stats_exchange_kernel<<<1, 32, 0, st>>>(heaps, sync_off, rank, world, ctr, out, max_norm,
+  ::msb::launch(stats_exchange_kernel, 1, 32, 0, st, heaps, sync_off, rank, world, ctr, out, max_norm,
                                           (unsigned long long)(timeout_s * 1e9), status);
   MSB_CHECK_LAUNCH("stats_exchange");
 }
@@ -388,15 +400,16 @@ void adamw_fanout(float* master, float* m, float* v, const float* grad, char* co
   a.bc2 = (float)bc2;
   a.eps = (float)eps;
   a.grad_mul = (float)grad_mul;
-  const int blocks = grid_for(n / 4 + 1, 256, kNumSMs * 16);
+  const int per = pdtype == kF32 ? 4 : 8;
+  const int blocks = grid_for(n / per + 1, 256, kNumSMs * 16);
   auto al = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
   const bool vl = al(master) && al(m) && al(v) && al(grad);
 #define MSB_FANOUT(P)                                                                        \
   if (vl)                                                                                    \
-    adamw_fanout_kernel<P, true><<<blocks, 256, 0, st>>>(master, m, v, grad, heaps, param_off, \
+    ::msb::launch(adamw_fanout_kernel<P, true>, blocks, 256, 0, st, master, m, v, grad, heaps, param_off, \
                                                          s0, n, world, stats, a);            \
   else                                                                                       \
-    adamw_fanout_kernel<P, false><<<blocks, 256, 0, st>>>(master, m, v, grad, heaps,         \
+    ::msb::launch(adamw_fanout_kernel<P, false>, blocks, 256, 0, st, master, m, v, grad, heaps,         \
                                                           param_off, s0, n, world, stats, a);
   if (pdtype == kF16) {
     MSB_FANOUT(__half)
@@ -416,11 +429,11 @@ void gather_range(char* const* heaps, long long shard_off, long long shard, long
     constexpr int V = 16 / sizeof(T);
     if (aligned16 && V == 8 && shard % V == 0 && lo % V == 0 && hi % V == 0) {
       const int blocks = grid_for((hi - lo) / V, 256, kNumSMs * 8);
-      gather_range_kernel<T, 8><<<blocks, 256, 0, st>>>(heaps, shard_off, shard, lo, hi,
+      ::msb::launch(gather_range_kernel<T, 8>, blocks, 256, 0, st, heaps, shard_off, shard, lo, hi,
                                                         static_cast<T*>(dst));
     } else {
       const int blocks = grid_for(hi - lo, 256, kNumSMs * 16);
-      gather_range_kernel<T, 1><<<blocks, 256, 0, st>>>(heaps, shard_off, shard, lo, hi,
+      ::msb::launch(gather_range_kernel<T, 1>, blocks, 256, 0, st, heaps, shard_off, shard, lo, hi,
                                                         static_cast<T*>(dst));
     }
   });

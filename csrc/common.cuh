@@ -29,11 +29,47 @@ inline void check_cuda(cudaError_t e, const char* what) {
   }
 }
 
+// Launch errors; the launches themselves are counted by launch() below.
 #define MSB_CHECK_LAUNCH(name)                                  \
   do {                                                          \
     ::msb::check_cuda(cudaGetLastError(), name);                \
-    ::msb::count_launch();                                      \
   } while (0)
+
+// Programmatic dependent launch (opt-in: MSB_PDL=1).  Every kernel of this
+// library is then launched with programmatic stream serialization allowed,
+// so the GPU may start it while the previous kernel of the stream is still
+// finishing; its launch latency and the set-up before pdl_begin() overlap
+// that tail.  Off by default: inside the replayed CUDA graph of a GPT-2 step
+// the kernels already run back to back, and the A/B runs measured no gain.  Every kernel calls pdl_begin() before its first access to
+// global memory: griddepcontrol.wait returns once the previous kernel has
+// completed and its writes are visible (at once when there is none or it was
+// launched without the attribute), and launch_dependents then lets the next
+// kernel start early in turn.  Inside a CUDA-graph capture the attribute
+// becomes a programmatic edge of the graph.
+bool pdl_enabled();
+
+__device__ __forceinline__ void pdl_begin() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                   cudaStream_t st, Args... args) {
+  static_assert(sizeof...(KArgs) == sizeof...(Args), "kernel argument count");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  check_cuda(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...), "kernel launch");
+  count_launch();
+}
 
 constexpr int kNumSMs = 148;
 

@@ -72,6 +72,14 @@ struct Params {
   long long ld_aux;
   int aux_vec;
   int staged;        // epilogue through shared memory + TMA stores (tmC / tmX valid)
+  // stream-K (2-CTA kernel): the tiles x kb_total K slices are cut into one
+  // contiguous range per pair (sk_per slices, one more for the first
+  // sk_extra pairs); a tile shared by several pairs is finished by the pair
+  // holding its first slice, after the others' fp32 partials (ws: one
+  // 256 x 256 slot per pair) and arrivals (sk_ctr[tile]) are in
+  int sk;
+  int sk_per, sk_extra;
+  int* sk_ctr;
   uint32_t idesc;
   unsigned* err;
   unsigned long long timeout_ns;
@@ -124,6 +132,50 @@ __device__ __forceinline__ void unit_coords(const Params& p, int u, int& m0, int
   }
   kb0 = split * p.kb_per_split;
   kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+}
+
+// Stream-K work of a pair: K-slice range [b, e) of the tiles * kb_total
+// slices, and the pair that holds slice `it`.
+__device__ __forceinline__ void sk_range(const Params& p, int pair, long long& b, long long& e) {
+  b = (long long)pair * p.sk_per + min(pair, p.sk_extra);
+  e = b + p.sk_per + (pair < p.sk_extra ? 1 : 0);
+}
+__device__ __forceinline__ int sk_pair_of(const Params& p, long long it) {
+  const long long big = (long long)p.sk_extra * (p.sk_per + 1);
+  if (it < big) return (int)(it / (p.sk_per + 1));
+  return p.sk_extra + (int)((it - big) / p.sk_per);
+}
+
+// The k-th work item of a pair: a tile and its K-slice range.  Units mode:
+// unit pair + k * npairs (unit_coords).  Stream-K: the k-th tile the pair's
+// slice range touches, cut to that range.
+template <int BN, int TM>
+__device__ __forceinline__ bool work_item(const Params& p, int pair, int npairs, int k, int& m0,
+                                          int& n0, int& kb0, int& kb1, int& split, int& tile) {
+  if (!p.sk) {
+    const int u = pair + k * npairs;
+    if (u >= p.units) return false;
+    unit_coords<BN, TM>(p, u, m0, n0, kb0, kb1, split);
+    tile = u % (p.tiles_m * p.tiles_n);
+    return true;
+  }
+  long long b, e;
+  sk_range(p, pair, b, e);
+  const long long t = b / p.kb_total + k;
+  const long long lo = max(b, t * p.kb_total), hi = min(e, (t + 1) * p.kb_total);
+  if (lo >= hi) return false;
+  tile = (int)t;
+  kb0 = (int)(lo - t * p.kb_total);
+  kb1 = (int)(hi - t * p.kb_total);
+  split = 0;
+  if (p.nfast) {
+    m0 = (tile / p.tiles_n) * TM;
+    n0 = (tile % p.tiles_n) * BN;
+  } else {
+    m0 = (tile % p.tiles_m) * TM;
+    n0 = (tile / p.tiles_m) * BN;
+  }
+  return true;
 }
 
 // 32 consecutive values of one row, 16-byte accesses when `vec`
@@ -344,6 +396,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
+  // set-up above touches shared and tensor memory only: it overlaps the
+  // previous kernel's tail (programmatic dependent launch)
+  ::msb::pdl_begin();
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -621,6 +676,34 @@ struct alignas(8) Bars2 {
   int abort;
 };
 
+// Bounded wait of a whole warp until *ctr >= target (lane 0 polls with
+// acquire loads; the warp then proceeds together).  False on abort/timeout.
+__device__ __forceinline__ bool sk_wait_w(int* ctr, int target, volatile int* abort,
+                                          const Params& p, unsigned code, int lane) {
+  int stop = 0;
+  if (lane == 0) {
+    const uint64_t t0 = gtime();
+    while (true) {
+      int v;
+      asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+      if (v >= target) break;
+      if (*abort) {
+        stop = 1;
+        break;
+      }
+      if (gtime() - t0 > p.timeout_ns) {
+        *abort = 1;
+        atomicCAS(p.err, 0u, code);
+        stop = 1;
+        break;
+      }
+    }
+  }
+  stop = __shfl_sync(0xffffffffu, stop, 0);
+  __syncwarp();
+  return stop == 0;
+}
+
 constexpr size_t smem_bytes2() {
   return 1024 + STAGES2 * (A2_BYTES + B2_BYTES) + kEpiStageBytes + sizeof(Bars2);
 }
@@ -670,6 +753,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
+  // set-up above touches shared and tensor memory only: it overlaps the
+  // previous kernel's tail (programmatic dependent launch)
+  ::msb::pdl_begin();
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -679,9 +765,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
 #pragma unroll
     for (int s = 0; s < STAGES2; ++s) pending[s] = -1;
     bool ok = true;
-    for (int u = pair_id; u < p.units && ok; u += npairs) {
-      int m0, n0, kb0, kb1, split;
-      unit_coords<BN2, TM>(p, u, m0, n0, kb0, kb1, split);
+    int m0, n0, kb0, kb1, split, tile;
+    for (int k = 0; ok && work_item<BN2, TM>(p, pair_id, npairs, k, m0, n0, kb0, kb1, split, tile);
+         ++k) {
       const int am = m0 + HALF * rank, bn = n0 + HALF * rank;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!wait2_w(smem_u32(&bars->empty[stage]), phase ^ 1, abort, p, 11, lane)) {
@@ -731,9 +817,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     int it = 0;
     bool ok = true;
     const uint32_t a_step = operand_step(p.a_mn), b_step = operand_step(p.b_mn);
-    for (int u = pair_id; u < p.units && ok; u += npairs, ++it) {
-      int m0, n0, kb0, kb1, split;
-      unit_coords<BN2, TM>(p, u, m0, n0, kb0, kb1, split);
+    int m0, n0, kb0, kb1, split, tile;
+    for (int k = 0; ok && work_item<BN2, TM>(p, pair_id, npairs, k, m0, n0, kb0, kb1, split, tile);
+         ++k, ++it) {
       const int buf = it & 1;
       const uint32_t tphase = (it >> 1) & 1;
       if (!wait2_w(smem_u32(&bars->tempty[buf]), tphase ^ 1, abort, p, 12, lane)) break;
@@ -773,13 +859,24 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     uint8_t* stg = sStage + (warp - 2) * 2 * kStageBytes;
     int sbuf = 0;
     int it = 0;
-    for (int u = pair_id; u < p.units; u += npairs, ++it) {
-      int m0, n0, kb0, kb1, split;
-      unit_coords<BN2, TM>(p, u, m0, n0, kb0, kb1, split);
+    int m0, n0, kb0, kb1, split, tile;
+    for (int k = 0; work_item<BN2, TM>(p, pair_id, npairs, k, m0, n0, kb0, kb1, split, tile);
+         ++k, ++it) {
       const int buf = it & 1;
       const uint32_t tphase = (it >> 1) & 1;
       if (!wait2_w(smem_u32(&bars->tfull[buf]), tphase, abort, p, 14, lane)) break;
       tc_fence_after();
+      // stream-K: a pair's first item may continue a tile another pair
+      // started (contribute the partial); its last item may start a tile
+      // that later pairs continue (finish it once their partials are in)
+      const bool contrib = p.sk && kb0 > 0;
+      const bool finish = p.sk && kb0 == 0 && kb1 < p.kb_total;
+      int ncontrib = 0;
+      if (finish) {
+        ncontrib = sk_pair_of(p, (long long)(tile + 1) * p.kb_total - 1) - pair_id;
+        // all 16 epilogue warps of each contributing pair have arrived
+        if (!sk_wait_w(p.sk_ctr + tile, 16 * ncontrib, abort, p, 15, lane)) break;
+      }
       const int row0 = m0 + HALF * rank + quarter * 32;
       const int row = m0 + row_in_tile;
 #pragma unroll 1
@@ -787,12 +884,36 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         uint32_t r[32];
         tmem_ld32(tmem_base + ((quarter * 32) << 16) + buf * BN2 + c * 32, r);
         tmem_ld_wait();
-        const int col = n0 + c * 32;
-        if (col >= p.N || row0 >= p.M) continue;
-        const int nvalid = min(32, p.N - col);
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        const long long slot_off = (long long)row_in_tile * BN2 + c * 32;
+        if (contrib) {
+          // the whole 32-column piece of the row, in or out of C: the
+          // finisher reads back exactly what it needs
+          float4* w = reinterpret_cast<float4*>(p.ws + (long long)pair_id * (TM * BN2) + slot_off);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            w[q] = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+          continue;
+        }
+        const int col = n0 + c * 32;
+        if (col >= p.N || row0 >= p.M) continue;
+        if (finish) {
+          for (int j = 1; j <= ncontrib; ++j) {
+            const float4* w = reinterpret_cast<const float4*>(
+                p.ws + (long long)(pair_id + j) * (TM * BN2) + slot_off);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 x = __ldcg(w + q);
+              v[q * 4] += x.x;
+              v[q * 4 + 1] += x.y;
+              v[q * 4 + 2] += x.z;
+              v[q * 4 + 3] += x.w;
+            }
+          }
+        }
+        const int nvalid = min(32, p.N - col);
         if (has_bias) add_bias<T>(p, col, nvalid, v);
         // TMA stores only for chunks wholly inside C: ragged edges are
         // stored per thread, so no write depends on the map's bound clipping
@@ -806,6 +927,18 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
       tc_fence_before();
       __syncwarp();
       if (lane == 0) remote_arrive(buf ? tempty_leader1 : tempty_leader0);
+      if (contrib) {
+        // release: this warp's partial rows are visible before its arrival
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(p.sk_ctr + tile, 1);
+      } else if (finish) {
+        // the 16 finishing warps count out; the last one clears the counter
+        // for the next launch
+        __syncwarp();
+        if (lane == 0 && atomicAdd(p.sk_ctr + tile, 1) == 16 * ncontrib + 15)
+          atomicExch(p.sk_ctr + tile, 0);
+      }
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
@@ -829,6 +962,7 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N, T* __restrict__ C,
                      long long ldc, const T* __restrict__ bias, int accumulate) {
+  ::msb::pdl_begin();
   const long long total = (long long)M * N;
   const int nq = N >> 2;  // N % 4 == 0 on this path
   const long long quads = (long long)M * nq;
@@ -861,6 +995,7 @@ __global__ void __launch_bounds__(256)
 splitk_reduce_scalar_kernel(const float* __restrict__ ws, int splits, int M, int N,
                             T* __restrict__ C, long long ldc, const T* __restrict__ bias,
                             int accumulate) {
+  ::msb::pdl_begin();
   const long long total = (long long)M * N;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -879,11 +1014,11 @@ void launch_reduce(const float* ws, int splits, int M, int N, void* C, long long
                    const void* bias, int accumulate, cudaStream_t st) {
   if (N % 4 == 0 && (reinterpret_cast<uintptr_t>(ws) & 15) == 0) {
     const int blocks = grid_for((long long)M * N / 4, 256, kNumSMs * 8);
-    splitk_reduce_kernel<T><<<blocks, 256, 0, st>>>(ws, splits, M, N, static_cast<T*>(C), ldc,
+    ::msb::launch(splitk_reduce_kernel<T>, blocks, 256, 0, st, ws, splits, M, N, static_cast<T*>(C), ldc,
                                                     static_cast<const T*>(bias), accumulate);
   } else {
     const int blocks = grid_for((long long)M * N, 256, kNumSMs * 8);
-    splitk_reduce_scalar_kernel<T><<<blocks, 256, 0, st>>>(ws, splits, M, N, static_cast<T*>(C),
+    ::msb::launch(splitk_reduce_scalar_kernel<T>, blocks, 256, 0, st, ws, splits, M, N, static_cast<T*>(C),
                                                            ldc, static_cast<const T*>(bias),
                                                            accumulate);
   }
@@ -906,7 +1041,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                "gemm smem attribute");
     attr_set = true;
   }
-  kern<<<grid, kThreads, smem_bytes<BN>(), st>>>(ta, tb, tc, tx, p);
+  ::msb::launch(kern, grid, kThreads, smem_bytes<BN>(), st, ta, tb, tc, tx, p);
 }
 
 template <typename T>
@@ -947,14 +1082,17 @@ void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = pair::smem_bytes2();
   cfg.stream = st;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = 2;
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   check_cuda(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, tx, p), "gemm2 launch");
+  count_launch();
 }
 
 }  // namespace tc
@@ -1003,12 +1141,14 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
                   void* C, long long ldc, const void* bias, int M, int N, int K, int dtype,
                   int accumulate, int mode, void* aux, long long ld_aux, float* ws,
                   long long ws_floats, unsigned* err, double timeout_s, cudaStream_t st,
-                  int force_bn, int force_splits) {
+                  int force_bn, int force_splits, int* sk_ctr, long long sk_ctr_n) {
   using namespace tc;
   int bn, splits;
   const long long need = gemm_plan(M, N, K, kNumSMs, &bn, &splits);
+  bool stream_k = false;
   if (force_bn > 0) {
     bn = force_bn;
+    stream_k = force_splits == -1 && bn == 512;
     splits = force_splits > 0 ? force_splits : 1;
     if (splits > 1 && (long long)splits * M * N > ws_floats) splits = 1;
   }
@@ -1068,12 +1208,34 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
                               ? make_map(aux, dtype, N, M, ld_aux, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
                               : ta;
   const int grid = std::min(p.units, kNumSMs);
+  p.sk = 0;
+  p.sk_per = 0;
+  p.sk_extra = 0;
+  p.sk_ctr = nullptr;
   if (two_cta) {
+    const int cap = dtype == kF16 ? pair_capacity<__half>(p, st)
+                                  : pair_capacity<__nv_bfloat16>(p, st);
+    int npairs = std::min(p.units, cap);
+    if (stream_k) {
+      // every pair must be resident at once (a finishing pair waits for
+      // pairs after it): one pair per resident slot, each with >= 1 slice
+      const long long tiles = (long long)p.tiles_m * p.tiles_n;
+      const long long total = tiles * p.kb_total;
+      npairs = cap;
+      if (total >= npairs && tiles <= sk_ctr_n && sk_ctr != nullptr && ws != nullptr &&
+          ws_floats >= (long long)npairs * pair::TM * pair::BN2 && p.splits == 1) {
+        p.sk = 1;
+        p.sk_per = static_cast<int>(total / npairs);
+        p.sk_extra = static_cast<int>(total % npairs);
+        p.sk_ctr = sk_ctr;
+        p.ws = ws;
+      } else {
+        npairs = std::min(p.units, cap);
+      }
+    }
     if (dtype == kF16) {
-      const int npairs = std::min(p.units, pair_capacity<__half>(p, st));
       launch_pair<__half>(ta, tb, tcm, txm, p, npairs, st);
     } else if (dtype == kBF16) {
-      const int npairs = std::min(p.units, pair_capacity<__nv_bfloat16>(p, st));
       launch_pair<__nv_bfloat16>(ta, tb, tcm, txm, p, npairs, st);
     } else {
       throw std::runtime_error("tcgen05 gemm takes fp16/bf16 operands");

@@ -53,10 +53,21 @@ void cross_entropy_fwd(const void* logits, const long long* tgt, float* lse, flo
 void cross_entropy_bwd(void* logits, const long long* tgt, const float* lse,
                        const float* grad_out, const float* inv_count, long long M, int V,
                        long long ld, long long ignore_index, int dtype, cudaStream_t st);
+// forward + gradient for an expected upstream gradient *g_hint (logits are
+// overwritten by the gradient); the rescale corrects it in backward when the
+// real upstream gradient differs
+void cross_entropy_fwd_grad(void* logits, const long long* tgt, float* lse, float* loss_rows,
+                            float* loss, float* inv_count, const float* g_hint, long long M, int V,
+                            long long ld, long long ignore_index, int dtype, cudaStream_t st);
+void cross_entropy_grad_rescale(void* dlogits, long long M, int V, long long ld,
+                                const float* grad_out, const float* g_hint, int dtype,
+                                cudaStream_t st);
 void embedding_fwd(const long long* idx, const void* wte, const void* wpe, void* out, long long M,
                    int T_len, int C, long long V, int dtype, cudaStream_t st);
-void embedding_bwd(const void* dout, const long long* idx, float* dwte, float* dwpe, long long M,
-                   int T_len, int C, long long V, int dtype, cudaStream_t st);
+// acc [V, C] fp32 and touched [V] must be all zero on entry and are left so
+void embedding_bwd(const void* dout, const long long* idx, float* acc, unsigned char* touched,
+                   void* dwte, int acc_wte, void* dwpe, int acc_wpe, long long M, int T_len,
+                   int C, long long V, int dtype, cudaStream_t st);
 void rope(void* x, const float* cos_t, const float* sin_t, long long BT, int T_len, int H, int D,
           long long row_stride, bool inverse, int dtype, cudaStream_t st);
 
@@ -77,7 +88,12 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
                   void* C, long long ldc, const void* bias, int M, int N, int K, int dtype,
                   int accumulate, int mode, void* aux, long long ld_aux, float* ws,
                   long long ws_floats, unsigned* err, double timeout_s, cudaStream_t st,
-                  int force_bn = 0, int force_splits = 0);
+                  int force_bn = 0, int force_splits = 0, int* sk_ctr = nullptr,
+                  long long sk_ctr_n = 0);
+// stream-K (force_bn 512, force_splits -1): fp32 slots ws >= kStreamKSlotFloats
+// per resident pair, and zeroed per-tile counters (left zero again)
+constexpr long long kStreamKSlotFloats = 256LL * 256;
+constexpr long long kStreamKCounters = 1LL << 16;
 
 // ---- NVLink peer heap + fused collectives (collectives.cu)
 // barrier-type kernels take this rank's device epoch counter (advanced by one each)

@@ -14,7 +14,9 @@
 //                      forward = one online-softmax pass per row (loss, lse),
 //                      backward = one pass writing dlogits in place; the fp32
 //                      logits the reference materializes never exist.
-//   embedding_*        token (+ position) gather-add and its scatter-add
+//   embedding_*        token (+ position) gather-add; backward: scatter-add into a
+//                      persistent fp32 accumulator, then only the touched rows are
+//                      added into the gradient and cleared
 //   rope_*             rotary position embedding on q/k in place
 #include <algorithm>
 
@@ -73,6 +75,7 @@ add_norm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ delta,
                     const T* __restrict__ w, const T* __restrict__ b, T* __restrict__ s_out,
                     T* __restrict__ y, float* __restrict__ mean_out,
                     float* __restrict__ rstd_out, int M, int C, float eps) {
+  ::msb::pdl_begin();
   const int warps = blockDim.x >> 5;
   const int row = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -146,6 +149,7 @@ __global__ void __launch_bounds__(256)
 norm_dx_kernel(const T* __restrict__ dy, const T* __restrict__ s, const T* __restrict__ w,
                const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
                const T* __restrict__ dres, T* __restrict__ dx, int M, int C) {
+  ::msb::pdl_begin();
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   const int nvec = C >> 3;
@@ -211,6 +215,7 @@ norm_dx_prefetch_kernel(const T* __restrict__ dy, const T* __restrict__ s,
                         const T* __restrict__ w, const float* __restrict__ mean_in,
                         const float* __restrict__ rstd_in, const T* __restrict__ dres,
                         T* __restrict__ dx, int M, int C) {
+  ::msb::pdl_begin();
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   const int nvec = C >> 3;
@@ -282,6 +287,7 @@ norm_dwdb_partial_kernel(const T* __restrict__ dy, const T* __restrict__ s,
                          const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
                          float* __restrict__ dw_part, float* __restrict__ db_part, int M, int C,
                          int rows_per_block) {
+  ::msb::pdl_begin();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c0 = blockIdx.x * 256 + lane * 8;
   const int r0 = blockIdx.y * rows_per_block;
@@ -340,6 +346,7 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 colsum_partial_kernel(const T* __restrict__ a, float* __restrict__ part, int M, int N,
                       long long ld, int rows_per_block) {
+  ::msb::pdl_begin();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c0 = blockIdx.x * 256 + lane * 8;
   const int r0 = blockIdx.y * rows_per_block;
@@ -397,6 +404,7 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 colsum_finish_kernel(const float* __restrict__ part, int nparts, int N, T* __restrict__ out,
                      int accumulate) {
+  ::msb::pdl_begin();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.x * 32 + lane;
   float t = 0.f;
@@ -418,6 +426,7 @@ colsum_finish_kernel(const float* __restrict__ part, int nparts, int N, T* __res
 template <typename T>
 __global__ void __launch_bounds__(256)
 accum_cast_kernel(const float* __restrict__ src, T* __restrict__ dst, long long n, int accumulate) {
+  ::msb::pdl_begin();
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
     float v = src[i];
@@ -431,6 +440,7 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 bias_gelu_fwd_kernel(T* __restrict__ u, const T* __restrict__ bias, T* __restrict__ h,
                      long long total, int N) {
+  ::msb::pdl_begin();
   const long long nvec = total >> 3;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
        i += (long long)gridDim.x * blockDim.x) {
@@ -456,6 +466,7 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 gelu_bwd_kernel(const T* __restrict__ dh, const T* __restrict__ u, T* __restrict__ du,
                 long long total) {
+  ::msb::pdl_begin();
   const long long nvec = total >> 3;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
        i += (long long)gridDim.x * blockDim.x) {
@@ -473,6 +484,7 @@ gelu_bwd_kernel(const T* __restrict__ dh, const T* __restrict__ u, T* __restrict
 template <typename T>
 __global__ void __launch_bounds__(256)
 swiglu_fwd_kernel(const T* __restrict__ gu, T* __restrict__ h, long long rows, int F) {
+  ::msb::pdl_begin();
   const long long nvec = rows * (F >> 3);
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
        i += (long long)gridDim.x * blockDim.x) {
@@ -491,6 +503,7 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 swiglu_bwd_kernel(const T* __restrict__ dh, const T* __restrict__ gu, T* __restrict__ dgu,
                   long long rows, int F) {
+  ::msb::pdl_begin();
   const long long nvec = rows * (F >> 3);
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
        i += (long long)gridDim.x * blockDim.x) {
@@ -544,6 +557,7 @@ __global__ void __launch_bounds__(512)
 ce_fwd_kernel(const T* __restrict__ logits, const long long* __restrict__ tgt,
               float* __restrict__ lse_out, float* __restrict__ loss_rows, int V, long long ld,
               long long ignore_index) {
+  ::msb::pdl_begin();
   const long long r = blockIdx.x;
   const T* row = logits + r * ld;
   float m = -INFINITY, s = 0.f;
@@ -595,6 +609,7 @@ __global__ void __launch_bounds__(1024)
 ce_reduce_kernel(const float* __restrict__ loss_rows, const long long* __restrict__ tgt,
                  long long M, int V, long long ignore_index, float* __restrict__ out_loss,
                  float* __restrict__ out_inv_count) {
+  ::msb::pdl_begin();
   double acc = 0.0;
   long long cnt = 0;
   for (long long i = threadIdx.x; i < M; i += blockDim.x) {
@@ -625,6 +640,7 @@ __global__ void __launch_bounds__(512)
 ce_bwd_kernel(T* __restrict__ logits, const long long* __restrict__ tgt,
               const float* __restrict__ lse, const float* __restrict__ grad_out,
               const float* __restrict__ inv_count, int V, long long ld, long long ignore_index) {
+  ::msb::pdl_begin();
   const long long r = blockIdx.x;
   T* row = logits + r * ld;
   const long long t = tgt[r];
@@ -650,12 +666,133 @@ ce_bwd_kernel(T* __restrict__ logits, const long long* __restrict__ tgt,
     row[i] = from_f32<T>(g(i, to_f32(row[i])));
 }
 
+// inv_count[0] = 1 / (number of valid targets) (0 when there is none),
+// before the fused forward that scales its gradient with it
+__global__ void __launch_bounds__(1024)
+ce_count_kernel(const long long* __restrict__ tgt, long long M, int V, long long ignore_index,
+                float* __restrict__ out_inv_count) {
+  ::msb::pdl_begin();
+  long long cnt = 0;
+  for (long long i = threadIdx.x; i < M; i += blockDim.x)
+    cnt += tgt[i] != ignore_index && tgt[i] >= 0 && tgt[i] < V;
+  __shared__ long long sc[1024];
+  sc[threadIdx.x] = cnt;
+  __syncthreads();
+  for (int w = 512; w > 0; w >>= 1) {
+    if (threadIdx.x < w) sc[threadIdx.x] += sc[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) out_inv_count[0] = sc[0] > 0 ? (float)(1.0 / (double)sc[0]) : 0.f;
+}
+
+// Forward and gradient of one row in one kernel: pass 1 is the online
+// softmax of ce_fwd_kernel (lse, the row's loss); pass 2 overwrites the
+// logits with their gradient for an expected upstream gradient g_hint (the
+// loss-scale seed of backward):
+//   dlogits[i] = (softmax[i] - [i == target]) * g_hint * inv_count.
+// The row was just read, so pass 2 mostly hits L2: the logits cross DRAM
+// once for reading and once for writing, against twice for reading when the
+// gradient waits for backward.  Backward checks the real upstream gradient
+// against g_hint (ce_grad_rescale_kernel).
+template <typename T>
+__global__ void __launch_bounds__(512)
+ce_fwd_grad_kernel(T* __restrict__ logits, const long long* __restrict__ tgt,
+                   float* __restrict__ lse_out, float* __restrict__ loss_rows, int V, long long ld,
+                   long long ignore_index, const float* __restrict__ g_hint,
+                   const float* __restrict__ inv_count) {
+  ::msb::pdl_begin();
+  const long long r = blockIdx.x;
+  T* row = logits + r * ld;
+  float m = -INFINITY, s = 0.f;
+  for_row(static_cast<const T*>(row), V, [&](int, float v) {
+    const float y = v * kLog2e;
+    if (y > m) {
+      s = s * ex2_approx(m - y) + 1.f;
+      m = y;
+    } else {
+      s += ex2_approx(y - m);
+    }
+  });
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    softmax_merge(m, s, m2, s2);
+  }
+  __shared__ float sm[32], ss[32];
+  __shared__ float s_lse;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sm[warp] = m;
+    ss[warp] = s;
+  }
+  __syncthreads();
+  const long long t = tgt[r];
+  const bool valid = t != ignore_index && t >= 0 && t < V;
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    m = lane < nw ? sm[lane] : -INFINITY;
+    s = lane < nw ? ss[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      softmax_merge(m, s, m2, s2);
+    }
+    if (lane == 0) {
+      const float lse = m * kLn2 + logf(s);
+      lse_out[r] = lse;
+      loss_rows[r] = valid ? lse - to_f32(row[t]) : 0.f;
+      s_lse = lse;
+    }
+  }
+  __syncthreads();   // every thread has read the row before it is overwritten
+  const float l = s_lse;
+  const float scale = valid ? g_hint[0] * inv_count[0] : 0.f;
+  const int head = (int)(((16 - (reinterpret_cast<uintptr_t>(row) & 15)) & 15) / sizeof(T));
+  const int h = min(head, V);
+  auto g = [&](int i, float v) {
+    return (ex2_approx((v - l) * kLog2e) - (i == t ? 1.f : 0.f)) * scale;
+  };
+  for (int i = threadIdx.x; i < h; i += blockDim.x) row[i] = from_f32<T>(g(i, to_f32(row[i])));
+  const int nvec = (V - h) / 8;
+  T* mid = row + h;
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    float v[8];
+    load8(mid + i * 8, v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = g(h + i * 8 + k, v[k]);
+    store8(mid + i * 8, v);
+  }
+  for (int i = h + nvec * 8 + threadIdx.x; i < V; i += blockDim.x)
+    row[i] = from_f32<T>(g(i, to_f32(row[i])));
+}
+
+// Backward of the fused forward: the stored gradient assumed the upstream
+// gradient g_hint; when the real one differs (a loss that was rescaled
+// before backward), multiply by grad_out / g_hint.  Otherwise every block
+// returns after reading two scalars.
+template <typename T>
+__global__ void __launch_bounds__(256)
+ce_grad_rescale_kernel(T* __restrict__ dlogits, long long M, int V, long long ld,
+                       const float* __restrict__ grad_out, const float* __restrict__ g_hint) {
+  ::msb::pdl_begin();
+  const float go = grad_out[0], gh = g_hint[0];
+  if (go == gh) return;
+  const float f = gh != 0.f ? go / gh : 0.f;
+  for (long long r = blockIdx.x; r < M; r += gridDim.x) {
+    T* row = dlogits + r * ld;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) row[i] = from_f32<T>(to_f32(row[i]) * f);
+  }
+}
+
 // ------------------------------------------------------------ embedding
 template <typename T>
 __global__ void __launch_bounds__(256)
 embedding_fwd_kernel(const long long* __restrict__ idx, const T* __restrict__ wte,
                      const T* __restrict__ wpe, T* __restrict__ out, long long M, int T_len,
                      int C, long long V) {
+  ::msb::pdl_begin();
   const int nvec = C >> 3;
   const long long total = M * nvec;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -675,30 +812,98 @@ embedding_fwd_kernel(const long long* __restrict__ idx, const T* __restrict__ wt
   }
 }
 
+// Token-embedding gradient, pass 1: scatter-add every row of dout into the
+// fp32 accumulator row of its token (atomics) and mark the row as touched.
+// The accumulator and the flags persist between steps and are all zero on
+// entry: pass 2 returns every row it reads to zero.
 template <typename T>
 __global__ void __launch_bounds__(256)
-embedding_bwd_kernel(const T* __restrict__ dout, const long long* __restrict__ idx,
-                     float* __restrict__ dwte, float* __restrict__ dwpe, long long M,
-                     int T_len, int C, long long V) {
+embedding_bwd_tok_kernel(const T* __restrict__ dout, const long long* __restrict__ idx,
+                         float* __restrict__ acc, unsigned char* __restrict__ touched,
+                         long long M, int C, long long V) {
+  ::msb::pdl_begin();
   const int nvec = C >> 3;
   const long long total = M * nvec;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
     const long long m = i / nvec;
     const int c = (int)(i % nvec) << 3;
+    const long long tok = idx[m];
+    if (tok < 0 || tok >= V) continue;
     float a[8];
     load8(dout + m * C + c, a);
-    const long long tok = idx[m];
-    if (tok >= 0 && tok < V) {
-      float* te = dwte + tok * C + c;
+    float* te = acc + tok * C + c;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) atomicAdd(te + k, a[k]);
-    }
-    if (dwpe != nullptr) {
-      float* pe = dwpe + (long long)(m % T_len) * C + c;
+    for (int k = 0; k < 8; ++k) atomicAdd(te + k, a[k]);
+    if (c == 0) touched[tok] = 1;
+  }
+}
+
+// Pass 2: one warp per vocabulary row; a touched row is added into the
+// gradient (model dtype, accumulating into what the head GEMM already put
+// there) and its accumulator row and flag are cleared.  Untouched rows cost
+// one byte read.
+template <typename T>
+__global__ void __launch_bounds__(256)
+embedding_bwd_finish_kernel(float* __restrict__ acc, unsigned char* __restrict__ touched,
+                            T* __restrict__ grad, long long V, int C, int accumulate) {
+  ::msb::pdl_begin();
+  const int lane = threadIdx.x & 31;
+  for (long long t = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); t < V;
+       t += (long long)gridDim.x * 8) {
+    if (!touched[t]) continue;
+    float* row = acc + t * C;
+    T* g = grad + t * C;
+    for (int c = lane * 8; c < C; c += 256) {
+      float a[8], o[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) atomicAdd(pe + k, a[k]);
+      for (int k = 0; k < 8; ++k) {
+        a[k] = row[c + k];
+        row[c + k] = 0.f;
+      }
+      if (accumulate) {
+        load8(g + c, o);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] += a[k];
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = a[k];
+      }
+      store8(g + c, o);
     }
+    __syncwarp();
+    if (lane == 0) touched[t] = 0;
+  }
+}
+
+// Position-embedding gradient: grad[p] (+)= sum over b of dout[b * T + p], in
+// batch order (deterministic, no atomics); one thread per 8 columns of a row.
+template <typename T>
+__global__ void __launch_bounds__(256)
+embedding_bwd_pos_kernel(const T* __restrict__ dout, T* __restrict__ grad, long long M,
+                         int T_len, int C, int accumulate) {
+  ::msb::pdl_begin();
+  const int nvec = C >> 3;
+  const long long total = (long long)T_len * nvec;
+  const long long B = M / T_len;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long p = i / nvec;
+    const int c = (int)(i % nvec) << 3;
+    float s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (long long b = 0; b < B; ++b) {
+      float a[8];
+      load8(dout + (b * T_len + p) * C + c, a);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s[k] += a[k];
+    }
+    if (accumulate) {
+      float o[8];
+      load8(grad + p * C + c, o);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s[k] += o[k];
+    }
+    store8(grad + p * C + c, s);
   }
 }
 
@@ -709,6 +914,7 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 rope_kernel(T* __restrict__ x, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
             long long BT, int T_len, int H, int D, long long row_stride, int inverse) {
+  ::msb::pdl_begin();
   const int half = D >> 1;
   const long long total = BT * H * half;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -735,11 +941,11 @@ static void launch_norm_fwd(const void* x, const void* delta, const void* w, con
                             void* s_out, void* y, float* mean, float* rstd, int M, int C,
                             float eps, bool rms, int blocks, cudaStream_t st) {
   if (rms)
-    add_norm_fwd_kernel<T, NVV, true><<<blocks, 256, 0, st>>>(
+    ::msb::launch(add_norm_fwd_kernel<T, NVV, true>, blocks, 256, 0, st, 
         (const T*)x, (const T*)delta, (const T*)w, (const T*)b, (T*)s_out, (T*)y, mean, rstd, M,
         C, eps);
   else
-    add_norm_fwd_kernel<T, NVV, false><<<blocks, 256, 0, st>>>(
+    ::msb::launch(add_norm_fwd_kernel<T, NVV, false>, blocks, 256, 0, st, 
         (const T*)x, (const T*)delta, (const T*)w, (const T*)b, (T*)s_out, (T*)y, mean, rstd, M,
         C, eps);
 }
@@ -770,19 +976,19 @@ static void launch_norm_dx(const void* dy, const void* s, const void* w, const f
   if constexpr (NVV <= 8) {
     if (C % 8 == 0 && al(dy) && al(s) && al(dx) && (dres == nullptr || al(dres))) {
       if (rms)
-        norm_dx_prefetch_kernel<T, NVV, true><<<blocks, 256, 0, st>>>(
+        ::msb::launch(norm_dx_prefetch_kernel<T, NVV, true>, blocks, 256, 0, st, 
             (const T*)dy, (const T*)s, (const T*)w, mean, rstd, (const T*)dres, (T*)dx, M, C);
       else
-        norm_dx_prefetch_kernel<T, NVV, false><<<blocks, 256, 0, st>>>(
+        ::msb::launch(norm_dx_prefetch_kernel<T, NVV, false>, blocks, 256, 0, st, 
             (const T*)dy, (const T*)s, (const T*)w, mean, rstd, (const T*)dres, (T*)dx, M, C);
       return;
     }
   }
   if (rms)
-    norm_dx_kernel<T, NVV, true><<<blocks, 256, 0, st>>>((const T*)dy, (const T*)s, (const T*)w,
+    ::msb::launch(norm_dx_kernel<T, NVV, true>, blocks, 256, 0, st, (const T*)dy, (const T*)s, (const T*)w,
                                                           mean, rstd, (const T*)dres, (T*)dx, M, C);
   else
-    norm_dx_kernel<T, NVV, false><<<blocks, 256, 0, st>>>((const T*)dy, (const T*)s, (const T*)w,
+    ::msb::launch(norm_dx_kernel<T, NVV, false>, blocks, 256, 0, st, (const T*)dy, (const T*)s, (const T*)w,
                                                            mean, rstd, (const T*)dres, (T*)dx, M,
                                                            C);
 }
@@ -805,10 +1011,10 @@ int norm_bwd(const void* dy, const void* s, const void* w, const float* mean, co
     else throw std::runtime_error("norm_bwd: hidden size too large");
     MSB_CHECK_LAUNCH("norm_dx");
     if (rms)
-      norm_dwdb_partial_kernel<T, true><<<grid, 256, 0, st>>>((const T*)dy, (const T*)s, mean,
+      ::msb::launch(norm_dwdb_partial_kernel<T, true>, grid, 256, 0, st, (const T*)dy, (const T*)s, mean,
                                                              rstd, dw_part, nullptr, M, C, rpb);
     else
-      norm_dwdb_partial_kernel<T, false><<<grid, 256, 0, st>>>((const T*)dy, (const T*)s, mean,
+      ::msb::launch(norm_dwdb_partial_kernel<T, false>, grid, 256, 0, st, (const T*)dy, (const T*)s, mean,
                                                               rstd, dw_part, db_part, M, C, rpb);
   });
   MSB_CHECK_LAUNCH("norm_dwdb_partial");
@@ -822,7 +1028,7 @@ int colsum_partial(const void* a, float* part, int M, int N, long long ld, int d
   chunks = (M + rpb - 1) / rpb;
   dim3 grid((N + 255) / 256, chunks);
   MSB_DISPATCH_FLOAT(dtype, T, {
-    colsum_partial_kernel<T><<<grid, 256, 0, st>>>((const T*)a, part, M, N, ld, rpb);
+    ::msb::launch(colsum_partial_kernel<T>, grid, 256, 0, st, (const T*)a, part, M, N, ld, rpb);
   });
   MSB_CHECK_LAUNCH("colsum_partial");
   return chunks;
@@ -831,7 +1037,7 @@ int colsum_partial(const void* a, float* part, int M, int N, long long ld, int d
 void colsum_finish(const float* part, int nparts, int N, void* out, int dtype, int accumulate,
                    cudaStream_t st) {
   MSB_DISPATCH_FLOAT(dtype, T, {
-    colsum_finish_kernel<T><<<(N + 31) / 32, 256, 0, st>>>(part, nparts, N, (T*)out, accumulate);
+    ::msb::launch(colsum_finish_kernel<T>, (N + 31) / 32, 256, 0, st, part, nparts, N, (T*)out, accumulate);
   });
   MSB_CHECK_LAUNCH("colsum_finish");
 }
@@ -840,7 +1046,7 @@ void accum_cast(const float* src, void* dst, long long n, int dtype, int accumul
                 cudaStream_t st) {
   const int blocks = grid_for(n, 256, kNumSMs * 16);
   MSB_DISPATCH_FLOAT(dtype, T, {
-    accum_cast_kernel<T><<<blocks, 256, 0, st>>>(src, (T*)dst, n, accumulate);
+    ::msb::launch(accum_cast_kernel<T>, blocks, 256, 0, st, src, (T*)dst, n, accumulate);
   });
   MSB_CHECK_LAUNCH("accum_cast");
 }
@@ -849,7 +1055,7 @@ void bias_gelu_fwd(void* u, const void* bias, void* h, long long total, int N, i
                    cudaStream_t st) {
   const int blocks = grid_for(total / 8, 256, kNumSMs * 16);
   MSB_DISPATCH_FLOAT(dtype, T, {
-    bias_gelu_fwd_kernel<T><<<blocks, 256, 0, st>>>((T*)u, (const T*)bias, (T*)h, total, N);
+    ::msb::launch(bias_gelu_fwd_kernel<T>, blocks, 256, 0, st, (T*)u, (const T*)bias, (T*)h, total, N);
   });
   MSB_CHECK_LAUNCH("bias_gelu_fwd");
 }
@@ -858,7 +1064,7 @@ void gelu_bwd(const void* dh, const void* u, void* du, long long total, int dtyp
               cudaStream_t st) {
   const int blocks = grid_for(total / 8, 256, kNumSMs * 16);
   MSB_DISPATCH_FLOAT(dtype, T, {
-    gelu_bwd_kernel<T><<<blocks, 256, 0, st>>>((const T*)dh, (const T*)u, (T*)du, total);
+    ::msb::launch(gelu_bwd_kernel<T>, blocks, 256, 0, st, (const T*)dh, (const T*)u, (T*)du, total);
   });
   MSB_CHECK_LAUNCH("gelu_bwd");
 }
@@ -866,7 +1072,7 @@ void gelu_bwd(const void* dh, const void* u, void* du, long long total, int dtyp
 void swiglu_fwd(const void* gu, void* h, long long rows, int F, int dtype, cudaStream_t st) {
   const int blocks = grid_for(rows * (F / 8), 256, kNumSMs * 16);
   MSB_DISPATCH_FLOAT(dtype, T, {
-    swiglu_fwd_kernel<T><<<blocks, 256, 0, st>>>((const T*)gu, (T*)h, rows, F);
+    ::msb::launch(swiglu_fwd_kernel<T>, blocks, 256, 0, st, (const T*)gu, (T*)h, rows, F);
   });
   MSB_CHECK_LAUNCH("swiglu_fwd");
 }
@@ -875,7 +1081,7 @@ void swiglu_bwd(const void* dh, const void* gu, void* dgu, long long rows, int F
                 cudaStream_t st) {
   const int blocks = grid_for(rows * (F / 8), 256, kNumSMs * 16);
   MSB_DISPATCH_FLOAT(dtype, T, {
-    swiglu_bwd_kernel<T><<<blocks, 256, 0, st>>>((const T*)dh, (const T*)gu, (T*)dgu, rows, F);
+    ::msb::launch(swiglu_bwd_kernel<T>, blocks, 256, 0, st, (const T*)dh, (const T*)gu, (T*)dgu, rows, F);
   });
   MSB_CHECK_LAUNCH("swiglu_bwd");
 }
@@ -884,11 +1090,11 @@ void cross_entropy_fwd(const void* logits, const long long* tgt, float* lse, flo
                        float* loss, float* inv_count, long long M, int V, long long ld,
                        long long ignore_index, int dtype, cudaStream_t st) {
   MSB_DISPATCH_FLOAT(dtype, T, {
-    ce_fwd_kernel<T><<<(unsigned)M, 512, 0, st>>>((const T*)logits, tgt, lse, loss_rows, V, ld,
+    ::msb::launch(ce_fwd_kernel<T>, (unsigned)M, 512, 0, st, (const T*)logits, tgt, lse, loss_rows, V, ld,
                                                  ignore_index);
   });
   MSB_CHECK_LAUNCH("ce_fwd");
-  ce_reduce_kernel<<<1, 1024, 0, st>>>(loss_rows, tgt, M, V, ignore_index, loss, inv_count);
+  ::msb::launch(ce_reduce_kernel, 1, 1024, 0, st, loss_rows, tgt, M, V, ignore_index, loss, inv_count);
   MSB_CHECK_LAUNCH("ce_reduce");
 }
 
@@ -896,28 +1102,55 @@ void cross_entropy_bwd(void* logits, const long long* tgt, const float* lse,
                        const float* grad_out, const float* inv_count, long long M, int V,
                        long long ld, long long ignore_index, int dtype, cudaStream_t st) {
   MSB_DISPATCH_FLOAT(dtype, T, {
-    ce_bwd_kernel<T><<<(unsigned)M, 512, 0, st>>>((T*)logits, tgt, lse, grad_out, inv_count, V,
+    ::msb::launch(ce_bwd_kernel<T>, (unsigned)M, 512, 0, st, (T*)logits, tgt, lse, grad_out, inv_count, V,
                                                  ld, ignore_index);
   });
   MSB_CHECK_LAUNCH("ce_bwd");
+}
+
+void cross_entropy_fwd_grad(void* logits, const long long* tgt, float* lse, float* loss_rows,
+                            float* loss, float* inv_count, const float* g_hint, long long M, int V,
+                            long long ld, long long ignore_index, int dtype, cudaStream_t st) {
+  ::msb::launch(ce_count_kernel, 1, 1024, 0, st, tgt, M, V, ignore_index, inv_count);
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    ::msb::launch(ce_fwd_grad_kernel<T>, (unsigned)M, 512, 0, st, (T*)logits, tgt, lse,
+                  loss_rows, V, ld, ignore_index, g_hint, (const float*)inv_count);
+  });
+  ::msb::launch(ce_reduce_kernel, 1, 1024, 0, st, (const float*)loss_rows, tgt, M, V,
+                ignore_index, loss, inv_count);
+  MSB_CHECK_LAUNCH("ce_fwd_grad");
+}
+
+void cross_entropy_grad_rescale(void* dlogits, long long M, int V, long long ld,
+                                const float* grad_out, const float* g_hint, int dtype,
+                                cudaStream_t st) {
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    ::msb::launch(ce_grad_rescale_kernel<T>, grid_for(M, 1, kNumSMs * 8), 256, 0, st, (T*)dlogits,
+                  M, V, ld, grad_out, g_hint);
+  });
+  MSB_CHECK_LAUNCH("ce_grad_rescale");
 }
 
 void embedding_fwd(const long long* idx, const void* wte, const void* wpe, void* out, long long M,
                    int T_len, int C, long long V, int dtype, cudaStream_t st) {
   const int blocks = grid_for(M * (C / 8), 256, kNumSMs * 16);
   MSB_DISPATCH_FLOAT(dtype, T, {
-    embedding_fwd_kernel<T><<<blocks, 256, 0, st>>>(idx, (const T*)wte, (const T*)wpe, (T*)out,
+    ::msb::launch(embedding_fwd_kernel<T>, blocks, 256, 0, st, idx, (const T*)wte, (const T*)wpe, (T*)out,
                                                     M, T_len, C, V);
   });
   MSB_CHECK_LAUNCH("embedding_fwd");
 }
 
-void embedding_bwd(const void* dout, const long long* idx, float* dwte, float* dwpe, long long M,
-                   int T_len, int C, long long V, int dtype, cudaStream_t st) {
-  const int blocks = grid_for(M * (C / 8), 256, kNumSMs * 16);
+void embedding_bwd(const void* dout, const long long* idx, float* acc, unsigned char* touched,
+                   void* dwte, int acc_wte, void* dwpe, int acc_wpe, long long M, int T_len,
+                   int C, long long V, int dtype, cudaStream_t st) {
   MSB_DISPATCH_FLOAT(dtype, T, {
-    embedding_bwd_kernel<T><<<blocks, 256, 0, st>>>((const T*)dout, idx, dwte, dwpe, M, T_len,
-                                                    C, V);
+    ::msb::launch(embedding_bwd_tok_kernel<T>, grid_for(M * (C / 8), 256, kNumSMs * 16), 256, 0, st, 
+        (const T*)dout, idx, acc, touched, M, C, V);
+    ::msb::launch(embedding_bwd_finish_kernel<T>, grid_for(V, 8, kNumSMs * 16), 256, 0, st, 
+        acc, touched, (T*)dwte, V, C, acc_wte);
+    if (dwpe != nullptr)
+      ::msb::launch(embedding_bwd_pos_kernel<T>, grid_for((long long)T_len * (C / 8), 256, kNumSMs * 8), 256, 0, st, (const T*)dout, (T*)dwpe, M, T_len, C, acc_wpe);
   });
   MSB_CHECK_LAUNCH("embedding_bwd");
 }
@@ -926,7 +1159,7 @@ void rope(void* x, const float* cos_t, const float* sin_t, long long BT, int T_l
           long long row_stride, bool inverse, int dtype, cudaStream_t st) {
   const int blocks = grid_for(BT * H * (D / 2), 256, kNumSMs * 16);
   MSB_DISPATCH_FLOAT(dtype, T, {
-    rope_kernel<T><<<blocks, 256, 0, st>>>((T*)x, cos_t, sin_t, BT, T_len, H, D, row_stride,
+    ::msb::launch(rope_kernel<T>, blocks, 256, 0, st, (T*)x, cos_t, sin_t, BT, T_len, H, D, row_stride,
                                            inverse ? 1 : 0);
   });
   MSB_CHECK_LAUNCH("rope");

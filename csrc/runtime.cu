@@ -1,5 +1,8 @@
-// Library-wide runtime state: the launch counter used as bench evidence.
+// Library-wide runtime state: the launch counter used as bench evidence and
+// the programmatic-dependent-launch switch (MSB_PDL=1 turns it on).
 #include <atomic>
+#include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 
@@ -10,5 +13,13 @@ static std::atomic<long long> g_launches{0};
 void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("MSB_PDL");
+    return v != nullptr && std::strcmp(v, "1") == 0;
+  }();
+  return on;
+}
 
 }  // namespace msb

@@ -42,6 +42,7 @@ template <typename T, int VEC>
 __global__ void __launch_bounds__(kStatThreads)
 grad_stats_kernel(const T* __restrict__ x, long long n, float mul,
                   float* __restrict__ partials, unsigned* __restrict__ flags) {
+  ::msb::pdl_begin();
   float ss = 0.f;
   unsigned bad = 0u;
   const long long nvec = n / VEC;
@@ -91,6 +92,7 @@ __device__ void compute_norm_coef(float* out, double max_norm) {
 __global__ void __launch_bounds__(kFinThreads)
 stats_finalize_kernel(const float* __restrict__ partials, const unsigned* __restrict__ flags,
                       int n, float* __restrict__ out, double max_norm, int epilogue) {
+  ::msb::pdl_begin();
   // fixed assignment of partials to threads + fixed tree => deterministic
   double acc = 0.0;
   unsigned bad = 0u;
@@ -118,6 +120,7 @@ stats_finalize_kernel(const float* __restrict__ partials, const unsigned* __rest
 }
 
 __global__ void stats_epilogue_kernel(float* out, double max_norm) {
+  ::msb::pdl_begin();
   if (threadIdx.x == 0 && blockIdx.x == 0) {
     out[0] = out[0] > 0.f ? 1.f : 0.f;
     compute_norm_coef(out, max_norm);
@@ -152,6 +155,7 @@ adamw_kernel(float* __restrict__ master, float* __restrict__ exp_avg,
              float* __restrict__ exp_avg_sq, const G* __restrict__ grad,
              P* __restrict__ param_out, long long n, const float* __restrict__ stats,
              AdamArgs a) {
+  ::msb::pdl_begin();
   float coef = 1.f;
   if (stats != nullptr) {
     if (stats[0] != 0.f) return;  // overflow: the whole step is skipped
@@ -190,6 +194,7 @@ adamw_kernel(float* __restrict__ master, float* __restrict__ exp_avg,
 template <typename S, typename D, int VEC>
 __global__ void __launch_bounds__(256)
 cast_scale_kernel(const S* __restrict__ src, D* __restrict__ dst, long long n, float mul) {
+  ::msb::pdl_begin();
   const long long nvec = n / VEC;
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
@@ -219,10 +224,10 @@ int grad_stats(const void* x, int dtype, long long n, float mul, float* partials
     const long long items = vec ? n / V : n;
     blocks = grid_for(items, kStatThreads, max_blocks < 1 ? 1 : max_blocks);
     if (vec)
-      grad_stats_kernel<T, V><<<blocks, kStatThreads, 0, stream>>>(
+      ::msb::launch(grad_stats_kernel<T, V>, blocks, kStatThreads, 0, stream, 
           static_cast<const T*>(x), n, mul, partials, flags);
     else
-      grad_stats_kernel<T, 1><<<blocks, kStatThreads, 0, stream>>>(
+      ::msb::launch(grad_stats_kernel<T, 1>, blocks, kStatThreads, 0, stream, 
           static_cast<const T*>(x), n, mul, partials, flags);
   });
   MSB_CHECK_LAUNCH("grad_stats");
@@ -231,13 +236,13 @@ int grad_stats(const void* x, int dtype, long long n, float mul, float* partials
 
 void stats_finalize(const float* partials, const unsigned* flags, int n, float* out,
                     double max_norm, bool epilogue, cudaStream_t stream) {
-  stats_finalize_kernel<<<1, kFinThreads, 0, stream>>>(partials, flags, n, out, max_norm,
+  ::msb::launch(stats_finalize_kernel, 1, kFinThreads, 0, stream, partials, flags, n, out, max_norm,
                                                        epilogue ? 1 : 0);
   MSB_CHECK_LAUNCH("stats_finalize");
 }
 
 void stats_epilogue(float* out, double max_norm, cudaStream_t stream) {
-  stats_epilogue_kernel<<<1, 32, 0, stream>>>(out, max_norm);
+  ::msb::launch(stats_epilogue_kernel, 1, 32, 0, stream, out, max_norm);
   MSB_CHECK_LAUNCH("stats_epilogue");
 }
 
@@ -265,19 +270,19 @@ void adamw(float* master, float* m, float* v, const void* grad, int gdtype, void
   MSB_DISPATCH_FLOAT(gdtype, G, {
     if (param_out == nullptr) {
       if (vec)
-        adamw_kernel<G, float, 4, false><<<blocks, threads, 0, stream>>>(
+        ::msb::launch(adamw_kernel<G, float, 4, false>, blocks, threads, 0, stream, 
             master, m, v, static_cast<const G*>(grad), nullptr, n, stats, a);
       else
-        adamw_kernel<G, float, 1, false><<<blocks, threads, 0, stream>>>(
+        ::msb::launch(adamw_kernel<G, float, 1, false>, blocks, threads, 0, stream, 
             master, m, v, static_cast<const G*>(grad), nullptr, n, stats, a);
     } else {
       MSB_DISPATCH_FLOAT(pdtype, P, {
         if (vec)
-          adamw_kernel<G, P, 4, true><<<blocks, threads, 0, stream>>>(
+          ::msb::launch(adamw_kernel<G, P, 4, true>, blocks, threads, 0, stream, 
               master, m, v, static_cast<const G*>(grad), static_cast<P*>(param_out), n, stats,
               a);
         else
-          adamw_kernel<G, P, 1, true><<<blocks, threads, 0, stream>>>(
+          ::msb::launch(adamw_kernel<G, P, 1, true>, blocks, threads, 0, stream, 
               master, m, v, static_cast<const G*>(grad), static_cast<P*>(param_out), n, stats,
               a);
       });
@@ -295,10 +300,10 @@ void cast_scale(const void* src, int sdtype, void* dst, int ddtype, long long n,
   MSB_DISPATCH_FLOAT(sdtype, S, {
     MSB_DISPATCH_FLOAT(ddtype, D, {
       if (vec)
-        cast_scale_kernel<S, D, 4><<<blocks, threads, 0, stream>>>(
+        ::msb::launch(cast_scale_kernel<S, D, 4>, blocks, threads, 0, stream, 
             static_cast<const S*>(src), static_cast<D*>(dst), n, mul);
       else
-        cast_scale_kernel<S, D, 1><<<blocks, threads, 0, stream>>>(
+        ::msb::launch(cast_scale_kernel<S, D, 1>, blocks, threads, 0, stream, 
             static_cast<const S*>(src), static_cast<D*>(dst), n, mul);
     });
   });

@@ -36,6 +36,7 @@ from . import checkpoint as ckpt
 from . import comm
 from .config import DeepSpeedConfig, load_config
 from .flat import FlatParamGroup, build_flat_groups
+from .ops.nn import expected_loss_grad
 from .optim import build_scheduler
 from .precision import DynamicLossScaler
 from .utils import DeviceTimers, Timers
@@ -82,6 +83,10 @@ class DeepSpeedEngine:
         self.world_size = comm.get_world_size()
         self.device = comm.resolve_device()
         if self.device.type == "cuda":
+            if self.device.index is None:
+                # MINISPEED_DEVICE=cuda: the current device (as the reference,
+                # which uses the bare "cuda" device)
+                self.device = torch.device("cuda", torch.cuda.current_device())
             torch.cuda.set_device(self.device)
         self.timers = Timers()
         # CUDA-event times of the same phases plus "forward" (b200.device_timers)
@@ -253,8 +258,25 @@ class DeepSpeedEngine:
                     self.optimizer.gather_parameters()
         self._open_window()
         self._begin_micro_step()
-        with self._device_phase("forward"):
+        with self._device_phase("forward"), expected_loss_grad(self._loss_grad_hint()):
             return self.module(*self._cast_inputs(args), **self._cast_inputs(kwargs))
+
+    def _loss_grad_hint(self) -> Optional[torch.Tensor]:
+        """The upstream gradient :meth:`backward` will give the module's loss
+        (loss scale / gradient-accumulation steps), as a device scalar: the
+        fused cross-entropy computes its gradient in the forward for it."""
+        if self.device.type != "cuda" or not self.module.training:
+            return None
+        factor = self.loss_scaler.loss_scale_factor
+        if self.gas > 1:
+            factor /= self.gas
+        if getattr(self, "_hint_dev", None) is None:
+            self._hint_dev = torch.empty(1, dtype=torch.float32, device=self.device)
+            self._hint_val = None
+        if self._hint_val != factor:
+            self._hint_dev.fill_(factor)
+            self._hint_val = factor
+        return self._hint_dev
 
     @contextmanager
     def _phase(self, name: str):

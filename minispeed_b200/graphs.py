@@ -37,6 +37,7 @@ from typing import Any, List, Optional, Tuple
 import torch
 
 from .ops import _ext
+from .ops.nn import expected_loss_grad
 
 
 def _flatten(obj, out: List[torch.Tensor]):
@@ -119,7 +120,9 @@ class MicroStepGraph:
         g = torch.cuda.CUDAGraph()
         n0 = _ext.launch_count()
         with torch.cuda.graph(g, stream=stream):
-            loss = eng.module(*eng._cast_inputs(self.args), **eng._cast_inputs(self.kwargs))
+            # the fused cross-entropy computes its gradient for this seed
+            with expected_loss_grad(self.seed):
+                loss = eng.module(*eng._cast_inputs(self.args), **eng._cast_inputs(self.kwargs))
             if not isinstance(loss, torch.Tensor) or loss.dim() != 0:
                 raise RuntimeError("train_batch: the module must return a scalar loss")
             torch.autograd.backward(loss, self.seed.to(loss.dtype))

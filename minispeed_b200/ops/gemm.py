@@ -9,7 +9,8 @@ accumulation:
 
 On CUDA they run the tcgen05/TMEM kernel of ``csrc/gemm_tcgen05.cu``
 (TMA-fed shared-memory ring, accumulators in tensor memory, epilogue with
-bias / accumulate, split-K for small outputs).  TMA needs 16-byte aligned
+bias / accumulate; split-K or stream-K where the output has too few tiles
+for whole waves, chosen per shape by timing the candidates once).  TMA needs 16-byte aligned
 operand bases and row strides; an operand that is not (e.g. a parameter view
 at an odd arena offset) is copied into an aligned buffer first.
 ``MSB_GEMM=torch`` selects the library product instead (comparison baseline
@@ -58,11 +59,17 @@ def check(device: Optional[torch.device] = None) -> None:
     code = int(w[0].item())
     if code:
         w.zero_()
+        # an aborted stream-K launch can leave its tile counters raised
+        _ext.get().gemm_reset_stream_k(w)
         raise KernelTimeoutError(f"tcgen05 gemm wait expired (code {code})")
 
 
 def native_enabled() -> bool:
-    return _MODE != "torch" and _ext.available() and hasattr(_ext.get(), "gemm")
+    """True unless ``MSB_GEMM=torch`` asked for the library product.
+
+    With the native path selected, a missing or broken extension raises on
+    the first CUDA GEMM (``_ext.get``) instead of falling back silently."""
+    return _MODE != "torch"
 
 
 def _tma_ready(t: torch.Tensor) -> torch.Tensor:
@@ -84,20 +91,26 @@ EPI_PLAIN, EPI_BIAS_GELU, EPI_DGELU = 0, 1, 2
 def gemm(a: torch.Tensor, b: torch.Tensor, *, a_kmajor: bool, b_kmajor: bool,
          bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
          accumulate: bool = False, mode: int = EPI_PLAIN,
-         aux: Optional[torch.Tensor] = None) -> torch.Tensor:
+         aux: Optional[torch.Tensor] = None, plan: Optional[tuple] = None) -> torch.Tensor:
     """C[M,N] (+)= A @ B^T (+ bias) in the tcgen05 operand convention.
 
     ``a`` holds A as [M,K] (``a_kmajor``) or [K,M]; ``b`` holds B as [N,K]
     (``b_kmajor``) or [K,N].  Epilogue modes: ``EPI_BIAS_GELU`` stores
     u = A@B^T + bias into ``out`` and gelu(u) into ``aux``; ``EPI_DGELU``
-    stores (A@B^T) * gelu'(aux) into ``out``."""
+    stores (A@B^T) * gelu'(aux) into ``out``.  ``plan=(bn, splits)`` replaces
+    the tuned plan: bn 512 is the 2-CTA pair kernel (256 x 256 tiles), 256 or
+    128 the 1-CTA kernel; splits 1-8 split K, -1 is stream-K (an even cut of
+    all K slices over the resident pairs, pair kernel only)."""
     M = a.shape[0] if a_kmajor else a.shape[1]
     N = b.shape[0] if b_kmajor else b.shape[1]
     if out is None:
         out = torch.empty(M, N, dtype=a.dtype, device=a.device)
-    if a.is_cuda and a.dtype in (torch.float16, torch.bfloat16) and native_enabled():
+    if a.is_cuda and native_enabled():
+        if a.dtype not in (torch.float16, torch.bfloat16):
+            raise TypeError(f"tcgen05 gemm takes fp16 or bf16 operands, got {a.dtype}")
+        bn, splits = plan if plan is not None else (0, 0)
         _ext.get().gemm(_tma_ready(a), _tma_ready(b), a_kmajor, b_kmajor, bias, out,
-                        accumulate, error_word(a.device), TIMEOUT_S, mode, aux)
+                        accumulate, error_word(a.device), TIMEOUT_S, mode, aux, bn, splits)
         return out
     A = a if a_kmajor else a.t()
     B = b.t() if b_kmajor else b

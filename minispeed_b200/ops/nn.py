@@ -25,6 +25,7 @@ Llama family, which the reference has no model for.
 from __future__ import annotations
 
 import math
+from contextlib import contextmanager
 from typing import Optional, Tuple
 
 import torch
@@ -38,6 +39,13 @@ _NORM_BLOCKS = 256     # row chunks of the norm-backward dw/db column sums
 
 def _C():
     return _ext.get()
+
+
+def _tc(x: torch.Tensor) -> bool:
+    """GEMM-bearing ops run the tcgen05 kernels for 16-bit CUDA tensors; fp32
+    models (a debugging configuration of the reference's GPU tests) run
+    PyTorch's fp32 GEMM, since tcgen05 ``kind::f16`` takes 16-bit operands."""
+    return x.is_cuda and x.dtype in (torch.float16, torch.bfloat16)
 
 
 def _scratch(device, n: int) -> torch.Tensor:
@@ -247,7 +255,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
     """``x @ w.T + b``.  ``pad_out`` > 0 allocates the output with its row
     stride rounded up to a multiple of ``pad_out`` (the returned tensor is a
     view with the logical width)."""
-    if x.is_cuda:
+    if _tc(x):
         return _Linear.apply(x, w, b, pad_out)
     return F.linear(x, w, b)
 
@@ -255,7 +263,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
 def mlp_gelu(x: torch.Tensor, w1: torch.Tensor, b1: Optional[torch.Tensor], w2: torch.Tensor,
              b2: Optional[torch.Tensor]) -> torch.Tensor:
     """``fc2(gelu(fc(x)))`` (exact erf GELU)."""
-    if x.is_cuda:
+    if _tc(x):
         return _MlpGelu.apply(x, w1, b1, w2, b2)
     return F.linear(F.gelu(F.linear(x, w1, b1)), w2, b2)
 
@@ -263,7 +271,7 @@ def mlp_gelu(x: torch.Tensor, w1: torch.Tensor, b1: Optional[torch.Tensor], w2: 
 def linear_gelu(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None
                 ) -> torch.Tensor:
     """``gelu(x @ w.T + b)`` (pre-activation kept for backward)."""
-    if x.is_cuda:
+    if _tc(x):
         return _LinearGelu.apply(x, w, b)
     return F.gelu(F.linear(x, w, b))
 
@@ -320,9 +328,28 @@ def swiglu(gu: torch.Tensor) -> torch.Tensor:
 
 
 # -------------------------------------------------------- cross entropy
+_LOSS_GRAD_HINT: list = [None]
+
+
+@contextmanager
+def expected_loss_grad(seed: Optional[torch.Tensor]):
+    """Within this context, :func:`cross_entropy` on CUDA computes its
+    gradient during the forward, for the upstream gradient ``seed`` (an fp32
+    CUDA scalar: the backward seed the engine will use, i.e. loss scale /
+    gradient-accumulation steps).  The backward then only checks the real
+    upstream gradient against ``seed`` and rescales when they differ.  The
+    logits are read from DRAM once instead of twice.  ``None`` turns it off."""
+    prev = _LOSS_GRAD_HINT[0]
+    _LOSS_GRAD_HINT[0] = seed
+    try:
+        yield
+    finally:
+        _LOSS_GRAD_HINT[0] = prev
+
+
 class _CrossEntropy(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, logits, targets, ignore_index):
+    def forward(ctx, logits, targets, ignore_index, hint):
         V = logits.shape[-1]
         l2 = as_matrix(logits, V)
         M = l2.shape[0]
@@ -331,8 +358,13 @@ class _CrossEntropy(torch.autograd.Function):
         rows = torch.empty(M, dtype=torch.float32, device=logits.device)
         loss = torch.empty((), dtype=torch.float32, device=logits.device)
         inv = torch.empty(1, dtype=torch.float32, device=logits.device)
-        _C().cross_entropy_fwd(l2, t, lse, rows, loss, inv, ignore_index)
+        if hint is not None:
+            # the logits buffer becomes the gradient for upstream gradient `hint`
+            _C().cross_entropy_fwd_grad(l2, t, lse, rows, loss, inv, hint, ignore_index)
+        else:
+            _C().cross_entropy_fwd(l2, t, lse, rows, loss, inv, ignore_index)
         ctx.save_for_backward(l2, t, lse, inv)
+        ctx.hint = hint
         ctx.ignore_index = ignore_index
         ctx.shape = logits.shape
         return loss
@@ -340,20 +372,29 @@ class _CrossEntropy(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         l2, t, lse, inv = ctx.saved_tensors
-        # the logits buffer is consumed in place: it becomes dlogits
-        _C().cross_entropy_bwd(l2, t, lse, g.float().reshape(1).contiguous(), inv,
-                               ctx.ignore_index)
-        return l2.view(ctx.shape), None, None
+        go = g.float().reshape(1).contiguous()
+        if ctx.hint is not None:
+            _C().cross_entropy_grad_rescale(l2, go, ctx.hint)
+        else:
+            # the logits buffer is consumed in place: it becomes dlogits
+            _C().cross_entropy_bwd(l2, t, lse, go, inv, ctx.ignore_index)
+        ctx.hint = None
+        return l2.view(ctx.shape), None, None, None
 
 
 def cross_entropy(logits: torch.Tensor, targets: torch.Tensor, ignore_index: int = -100
                   ) -> torch.Tensor:
     """Mean softmax cross-entropy in fp32 math over model-dtype logits.
 
-    On CUDA the logits tensor is overwritten by its gradient during backward
-    (it must not be used after ``loss.backward()``)."""
+    On CUDA the logits tensor is overwritten by its gradient (during backward,
+    or during the forward inside :func:`expected_loss_grad`): it must not be
+    used after the loss is computed."""
     if logits.is_cuda:
-        return _CrossEntropy.apply(logits, targets, ignore_index)
+        hint = _LOSS_GRAD_HINT[0]
+        if hint is not None and not (torch.is_grad_enabled() and logits.requires_grad
+                                     and hint.device == logits.device):
+            hint = None
+        return _CrossEntropy.apply(logits, targets, ignore_index, hint)
     return F.cross_entropy(logits.reshape(-1, logits.shape[-1]).float(), targets.reshape(-1),
                            ignore_index=ignore_index)
 
@@ -377,21 +418,39 @@ class _Embedding(torch.autograd.Function):
         (idx,) = ctx.saved_tensors
         wte_shape, wpe_shape, dtype, T = ctx.shapes
         wte_p, wpe_p = ctx.params
-        dwte = torch.zeros(wte_shape, dtype=torch.float32, device=dout.device)
-        dwpe = None if wpe_shape is None else torch.zeros(wpe_shape, dtype=torch.float32,
-                                                          device=dout.device)
-        _C().embedding_bwd(dout.contiguous(), idx, dwte, dwpe, T)
-        return None, _to_sink(dwte, wte_p, dtype), (None if dwpe is None
-                                                     else _to_sink(dwpe, wpe_p, dtype))
+        acc, touched = _embedding_accumulator(dout.device, wte_shape)
+        # straight into the gradient arena when the parameter has a sink
+        # (tied with the LM head: added to the head GEMM's wgrad), else into
+        # a fresh zero gradient
+        sink_te = grad_sink(wte_p)
+        sink_pe = grad_sink(wpe_p) if wpe_shape is not None else None
+        dwte = sink_te if sink_te is not None else torch.zeros(wte_shape, dtype=dtype,
+                                                               device=dout.device)
+        dwpe = None
+        if wpe_shape is not None:
+            dwpe = sink_pe if sink_pe is not None else torch.zeros(wpe_shape, dtype=dtype,
+                                                                   device=dout.device)
+        _C().embedding_bwd(dout.contiguous(), idx, acc, touched, dwte, True, dwpe, True, T)
+        return (None, None if sink_te is not None else dwte,
+                None if sink_pe is not None or dwpe is None else dwpe)
 
 
-def _to_sink(g32: torch.Tensor, param, dtype) -> Optional[torch.Tensor]:
-    """Add an fp32 gradient into the param's sink, or return it cast."""
-    sink = grad_sink(param)
-    if sink is not None:
-        _C().accum_cast(g32, sink, True)
-        return None
-    return g32.to(dtype)
+_EMB_ACC = {}
+
+
+def _embedding_accumulator(device, shape) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The persistent fp32 scatter accumulator [V, C] and touched-row flags
+    [V] of a device, zero between uses (the backward kernel clears the rows
+    it reads).  Created on the first (eager) backward, before any CUDA-graph
+    capture of the step."""
+    key = (device, tuple(shape))
+    buf = _EMB_ACC.get(key)
+    if buf is None:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("embedding backward: run one eager step before capturing")
+        buf = _EMB_ACC[key] = (torch.zeros(shape, dtype=torch.float32, device=device),
+                               torch.zeros(shape[0], dtype=torch.uint8, device=device))
+    return buf
 
 
 def embedding(idx: torch.Tensor, wte: torch.Tensor, wpe: Optional[torch.Tensor] = None

@@ -153,3 +153,62 @@ def test_mlp_gelu_op_and_grad_sinks(dtype):
     _check(x.grad, xf.grad, F)
     for p, r in zip(params, ref_params):
         _check(p.grad, r.grad + 0.25, 4 * 64)
+
+
+SK = (512, -1)   # the 2-CTA pair kernel with stream-K
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("a_k,b_k", [(True, True), (True, False), (False, False)])
+@pytest.mark.parametrize("M,N,K", [(16384, 768, 3072), (2304, 768, 16384), (300, 200, 4160),
+                                   (1000, 768, 768), (512, 512, 64)])
+def test_stream_k(dtype, a_k, b_k, M, N, K, _variant):
+    """Stream-K cuts tiles x K-slices evenly over the resident pairs; a tile
+    split between pairs is finished by the pair holding its first slice.
+    Two launches in a row: the tile counters must be back at zero."""
+    if _variant != "auto":
+        pytest.skip("forced plan; one variant is enough")
+    torch.manual_seed(M + N + K)
+    A = (torch.randn(M, K, device="cuda") * 0.1).to(dtype)
+    B = (torch.randn(N, K, device="cuda") * 0.1).to(dtype)
+    a = A if a_k else A.t().contiguous()
+    b = B if b_k else B.t().contiguous()
+    ref = _ref(A, B)
+    for _ in range(2):
+        out = gemm.gemm(a, b, a_kmajor=a_k, b_kmajor=b_k, plan=SK)
+        torch.cuda.synchronize()
+        _check(out, ref, K)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_stream_k_epilogues(dtype, _variant):
+    """Bias, accumulate and the GELU modes are applied once, by the pair that
+    finishes each tile."""
+    if _variant != "auto":
+        pytest.skip("forced plan; one variant is enough")
+    M, N, K = 2000, 1000, 2112
+    torch.manual_seed(5)
+    A = (torch.randn(M, K, device="cuda") * 0.05).to(dtype)
+    B = (torch.randn(N, K, device="cuda") * 0.05).to(dtype)
+    bias = torch.randn(N, device="cuda").to(dtype)
+    out = gemm.gemm(A, B, a_kmajor=True, b_kmajor=True, bias=bias, plan=SK)
+    _check(out, _ref(A, B, bias), K)
+    C0 = torch.randn(M, N, device="cuda").to(dtype)
+    C = C0.clone()
+    gemm.gemm(A, B, a_kmajor=True, b_kmajor=True, out=C, accumulate=True, plan=SK)
+    _check(C, C0.float() + _ref(A, B), K)
+    u = torch.empty(M, N, device="cuda", dtype=dtype)
+    h = torch.empty_like(u)
+    gemm.gemm(A, B, a_kmajor=True, b_kmajor=True, bias=bias, out=u, mode=gemm.EPI_BIAS_GELU,
+              aux=h, plan=SK)
+    uref = _ref(A, B, bias)
+    _check(u, uref, K)
+    _check(h, torch.nn.functional.gelu(u.float()), K)
+    dY = (torch.randn(M, K, device="cuda") * 0.05).to(dtype)
+    W = (torch.randn(K, N, device="cuda") * 0.05).to(dtype)
+    du = torch.empty(M, N, device="cuda", dtype=dtype)
+    gemm.gemm(dY, W, a_kmajor=True, b_kmajor=False, out=du, mode=gemm.EPI_DGELU, aux=u,
+              plan=SK)
+    from minispeed_b200.ops.nn import gelu_grad_reference
+    want = (dY.float() @ W.float()).to(dtype).float() * gelu_grad_reference(u.float())
+    _check(du, want, K)

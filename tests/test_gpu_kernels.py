@@ -236,3 +236,54 @@ def test_rope(dtype):
     # rotation is orthogonal: the backward is the inverse rotation
     back = ops.rope(g.float().cpu(), cos.cpu(), -sin.cpu()).cuda()
     torch.testing.assert_close(x.grad.float(), back, rtol=rt, atol=at * 2)
+
+
+@pytest.mark.parametrize("dtype", DT)
+def test_embedding_backward_into_sink_twice(dtype):
+    """Parameters whose ``.grad`` is bound (the engine's arena views) get the
+    token and position gradients added in place; the persistent fp32
+    accumulator is clean again for the second backward (other tokens)."""
+    V, C, B, T = 211, 128, 4, 48
+    wte = torch.nn.Parameter(torch.randn(V, C, device="cuda", dtype=dtype))
+    wpe = torch.nn.Parameter(torch.randn(T + 3, C, device="cuda", dtype=dtype))
+    wte.grad = torch.randn_like(wte) * 0.1
+    wpe.grad = torch.randn_like(wpe) * 0.1
+    want_te, want_pe = wte.grad.float().clone(), wpe.grad.float().clone()
+    for seed in (1, 2):
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        idx = torch.randint(0, V // seed, (B, T), device="cuda", generator=gen)
+        out = ops.embedding(idx, wte, wpe)
+        g = torch.randn(out.shape, device="cuda", generator=gen).to(dtype)
+        out.backward(g)
+        want_te.index_add_(0, idx.reshape(-1), g.float().reshape(-1, C))
+        want_pe[:T] += g.float().sum(0)
+        rt, at = _tol(dtype)
+        torch.testing.assert_close(wte.grad.float(), want_te, rtol=rt * 4, atol=at * 8)
+        torch.testing.assert_close(wpe.grad.float(), want_pe, rtol=rt * 4, atol=at * 8)
+        want_te, want_pe = wte.grad.float().clone(), wpe.grad.float().clone()
+
+
+@pytest.mark.parametrize("dtype", DT)
+@pytest.mark.parametrize("mult", [7.0, 3.0])
+@pytest.mark.parametrize("V,ld", [(50257, 50304), (1003, 1008)])
+def test_cross_entropy_gradient_in_forward(dtype, mult, V, ld):
+    """Inside ``expected_loss_grad(seed)`` the forward writes the gradient for
+    upstream gradient ``seed`` (here 7); a backward with that gradient leaves
+    it as is, one with another (3) rescales it.  Both match the fp32 oracle,
+    ignored targets included."""
+    torch.manual_seed(4)
+    M = 133
+    logits = (torch.randn(M, ld, device="cuda") * 3).to(dtype)[:, :V]
+    tgt = torch.randint(0, V, (M,), device="cuda")
+    tgt[7] = -100
+    ref_l = logits.detach().float().requires_grad_()
+    ref = F.cross_entropy(ref_l, tgt)
+    (ref * mult).backward()
+    lg = logits.requires_grad_()
+    seed = torch.full((1,), 7.0, device="cuda")
+    with ops.expected_loss_grad(seed):
+        loss = ops.cross_entropy(lg, tgt)
+    assert float(loss) == pytest.approx(float(ref), rel=1e-5, abs=1e-5)
+    (loss * mult).backward()
+    rt, at = _tol(dtype)
+    torch.testing.assert_close(lg.grad.float(), ref_l.grad, rtol=rt, atol=at * 0.05)
