@@ -106,14 +106,25 @@ def save_checkpoint(engine, save_dir: str, tag: Optional[str] = None) -> str:
             raise err
         raise RuntimeError(f"checkpoint {ckpt_dir}: another rank failed to write its files; "
                            "latest still names the previous checkpoint")
+    latest_err: Optional[BaseException] = None
     if engine.rank == 0:
-        latest = os.path.join(save_dir, LATEST)
-        with open(latest + ".tmp", "w", encoding="utf-8") as fh:
-            fh.write(tag)
-        os.replace(latest + ".tmp", latest)
-    comm.barrier()
+        try:
+            latest = os.path.join(save_dir, LATEST)
+            with open(latest + ".tmp", "w", encoding="utf-8") as fh:
+                fh.write(tag)
+            os.replace(latest + ".tmp", latest)
+        except Exception as e:  # reported to every rank by the flag below
+            latest_err = e
+    # the flag doubles as the final barrier: no rank waits on a rank 0 that
+    # raised, and every rank frees stage-3 parameters on either outcome
+    latest_failed = comm.all_reduce_flag(latest_err is not None)
     if not was_gathered:
         engine.optimizer.free_parameters()
+    if latest_failed:
+        if latest_err is not None:
+            raise latest_err
+        raise RuntimeError(f"checkpoint {ckpt_dir}: rank 0 failed to update {LATEST}; the "
+                           "files are written but latest still names the previous checkpoint")
     return ckpt_dir
 
 

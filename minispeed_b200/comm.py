@@ -93,7 +93,10 @@ def init_distributed(timeout_s: float | None = None) -> None:
     backend = resolve_backend()
     if backend == "nccl":
         dev = resolve_device()
-        torch.cuda.set_device(dev if dev.type == "cuda" else 0)
+        if dev.type != "cuda":
+            torch.cuda.set_device(0)
+        elif dev.index is not None:     # a bare "cuda" keeps the current device
+            torch.cuda.set_device(dev)
     if timeout_s is None:
         timeout_s = float(os.environ.get("MINISPEED_PG_TIMEOUT_S", 600))
     kwargs = {"timeout": datetime.timedelta(seconds=timeout_s)}
@@ -132,6 +135,9 @@ def all_reduce_flag(flag: bool) -> bool:
 
 
 _FORCE_STAGING = os.environ.get("MINISPEED_STAGE_COLLECTIVES", "0") == "1"
+# how many reduce-scatters / all-gathers took the host-staged path (tests
+# check that the path they force is the one that ran)
+staged_calls = {"reduce_scatter": 0, "all_gather": 0}
 
 
 def host_staged(*tensors: torch.Tensor) -> bool:
@@ -148,9 +154,11 @@ def reduce_scatter(output: torch.Tensor, input_: torch.Tensor) -> torch.Tensor:
     """SUM-reduce ``input_`` (world * output.numel()) and keep this rank's slice."""
     if is_distributed():
         if host_staged(output, input_):
-            out = output.to("cpu", copy=True)
+            # the receive buffer is written whole: no need to copy output down
+            out = torch.empty_like(output, device="cpu")
             dist.reduce_scatter_tensor(out, input_.to("cpu", copy=True))
             output.copy_(out)
+            staged_calls["reduce_scatter"] += 1
         else:
             dist.reduce_scatter_tensor(output, input_)
     else:
@@ -162,9 +170,10 @@ def all_gather_flat(output: torch.Tensor, local_shard: torch.Tensor) -> torch.Te
     """Concatenate every rank's shard, in rank order, into ``output``."""
     if is_distributed():
         if host_staged(output, local_shard):
-            out = output.to("cpu", copy=True)
+            out = torch.empty_like(output, device="cpu")
             dist.all_gather_into_tensor(out, local_shard.to("cpu", copy=True))
             output.copy_(out)
+            staged_calls["all_gather"] += 1
         else:
             dist.all_gather_into_tensor(output, local_shard)
     else:

@@ -95,9 +95,12 @@ class Timers:
 class DeviceTimers:
     """CUDA-event section timers (no-ops on CPU).
 
-    Intervals whose end event has completed are folded into the totals
-    without a sync once more than ``fold_after`` are pending, so a long run
-    that never reads the timers holds a bounded number of events."""
+    Once more than ``fold_after`` intervals of a section are pending, the
+    oldest ones whose end event has completed are folded into the totals
+    (events recorded on one stream complete in order, so the scan stops at
+    the first that has not).  If the GPU is so far behind that more than
+    ``2 * fold_after`` stay pending, the oldest half is waited for: a long
+    run that never reads the timers holds a bounded number of events."""
 
     def __init__(self, fold_after: int = 256) -> None:
         self._pending: Dict[str, list] = {}
@@ -105,17 +108,23 @@ class DeviceTimers:
         self._fold_after = fold_after
 
     def _fold_completed(self, name: str) -> None:
-        keep = []
-        for a, b in self._pending.get(name, []):
-            if b.query():
-                self._done[name] = self._done.get(name, 0.0) + a.elapsed_time(b)
-            else:
-                keep.append((a, b))
-        self._pending[name] = keep
+        pend = self._pending.get(name, [])
+        if len(pend) > 2 * self._fold_after:
+            pend[len(pend) // 2][1].synchronize()
+        n = 0
+        total = self._done.get(name, 0.0)
+        for a, b in pend:
+            if not b.query():
+                break
+            total += a.elapsed_time(b)
+            n += 1
+        self._done[name] = total
+        del pend[:n]
 
     @contextmanager
     def timer(self, name: str) -> Iterator[None]:
-        if not torch.cuda.is_available():
+        if not torch.cuda.is_available() or torch.cuda.is_current_stream_capturing():
+            # inside a CUDA-graph capture the replay is timed as a whole
             yield
             return
         a = torch.cuda.Event(enable_timing=True)

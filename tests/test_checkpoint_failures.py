@@ -227,3 +227,42 @@ def test_failed_write_on_one_rank_fails_all_and_keeps_latest(tmp_path):
     assert (tmp_path / "w0.txt").read_text() == "other rank"
     assert (tmp_path / "w1.txt").read_text() == "own error"
     assert (tmp_path / "latest").read_text() == "good"
+
+
+def _failed_latest_worker(rank, port, out_dir):
+    set_rank_env(rank, WORLD, port, "gloo", "cpu")
+    x, y = make_data(2, GAS, WORLD, MICRO)
+    x, y = rank_slice(x, rank, MICRO), rank_slice(y, rank, MICRO)
+    eng = ms.initialize(model=make_net(), config=config(micro=MICRO, gas=GAS, stage=3))
+    run(eng, x, y, 1, GAS)
+    eng.save_checkpoint(out_dir, tag="good")
+    if rank == 0:
+        real_replace = ckpt.os.replace
+
+        def failing_replace(src, dst):
+            if os.path.basename(dst) == "latest":
+                raise OSError(5, "Input/output error")
+            return real_replace(src, dst)
+        ckpt.os.replace = failing_replace
+    try:
+        eng.save_checkpoint(out_dir, tag="bad")
+        outcome = "saved"
+    except OSError:
+        outcome = "own error"
+    except RuntimeError as e:
+        outcome = "other rank" if "failed to update latest" in str(e) else repr(e)
+    gathered = eng.optimizer.params_gathered
+    ms.comm.barrier()      # still in lockstep
+    with open(os.path.join(out_dir, f"l{rank}.txt"), "w") as fh:
+        fh.write(f"{outcome} gathered={gathered}")
+    ms.comm.destroy()
+
+
+def test_failed_latest_update_on_rank0_fails_all(tmp_path):
+    """Rank 0 fails to move ``latest`` after every shard is written: every
+    rank raises at once (none waits for a barrier rank 0 never reaches), and
+    stage-3 parameters are freed again on every rank."""
+    mp.spawn(_failed_latest_worker, args=(free_port(), str(tmp_path)), nprocs=WORLD, join=True)
+    assert (tmp_path / "l0.txt").read_text() == "own error gathered=False"
+    assert (tmp_path / "l1.txt").read_text() == "other rank gathered=False"
+    assert (tmp_path / "latest").read_text() == "good"

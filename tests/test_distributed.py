@@ -31,7 +31,7 @@ def _worker(rank, stage, port, out_dir, clip, dtype):
                 "exp_avg": [s["exp_avg"].clone() for s in engine.optimizer.state],
                 "opt_step": engine.optimizer.state[0]["step"],
                 "masters": engine.flat_groups[0].data.clone(),
-                "coll": engine.collectives},
+                "coll": engine.collectives, "staged": dict(ms.comm.staged_calls)},
                os.path.join(out_dir, f"r{rank}.pt"))
     ms.comm.destroy()
 
@@ -198,6 +198,11 @@ def test_host_staged_collectives_match(stage, tmp_path, monkeypatch):
     monkeypatch.setenv("MINISPEED_STAGE_COLLECTIVES", "1")
     staged = _spawn(stage, tmp_path / "b")
     for p, s in zip(plain, staged):
+        assert sum(p["staged"].values()) == 0
+        # stage 0 only all-reduces; stages 1-3 reduce-scatter the gradient
+        # and all-gather the parameters
+        for kind in ("reduce_scatter", "all_gather"):
+            assert (s["staged"][kind] > 0) == (stage >= 1), kind
         assert torch.equal(p["losses"], s["losses"])
         for k in p["params"]:
             assert torch.equal(p["params"][k], s["params"][k]), k

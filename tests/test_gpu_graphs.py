@@ -112,3 +112,41 @@ def test_graph_is_captured_once():
             first = eng._graph
     assert eng._graph is first and first.replays == len(data) - 2
     eng.close()
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_device_timers_on_gpu(graph):
+    """``b200.device_timers``: CUDA-event phase times over a few
+    ``train_batch`` steps are positive and add up to less than the wall
+    time of those steps (eager, and with the micro-step replayed as a graph,
+    where the replay is timed under ``backward``)."""
+    import time
+
+    import minispeed_b200 as ms
+    from minispeed_b200.models import GPT, GPTConfig, init_gpt2_
+
+    torch.manual_seed(0)
+    model = init_gpt2_(GPT(GPTConfig(vocab_size=512, block_size=128, n_layer=2, n_head=4,
+                                     n_embd=256))).cuda()
+    engine = ms.initialize(model=model, config={
+        "train_micro_batch_size_per_gpu": 4, "gradient_accumulation_steps": 1,
+        "fp16": {"enabled": True, "initial_scale_power": 8},
+        "zero_optimization": {"stage": 2},
+        "optimizer": {"type": "AdamW", "params": {"lr": 1e-3}},
+        "b200": {"device_timers": True, "cuda_graph": graph}})
+    x = torch.randint(0, 512, (4, 129), device="cuda")
+    for _ in range(4):                      # eager warm-up (and the capture)
+        engine.train_batch(x[:, :-1], targets=x[:, 1:])
+    engine.device_time_ms()
+    engine.device_timers.reset()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(5):
+        engine.train_batch(x[:, :-1], targets=x[:, 1:])
+    torch.cuda.synchronize()
+    wall_ms = (time.perf_counter() - t0) * 1e3
+    times = engine.device_time_ms()
+    assert times.get("backward", 0) > 0 and times.get("step", 0) > 0, times
+    if not graph:
+        assert times.get("forward", 0) > 0, times
+    assert sum(times.values()) < wall_ms, (times, wall_ms)

@@ -77,10 +77,10 @@ def test_fused_matches_nccl_path(dtype, tmp_path):
                                    atol=tol)
 
 
-def _gpt_worker(rank, stage, overlap, graph, port, out_dir):
+def _gpt_worker(rank, stage, overlap, graph, port, out_dir, world=WORLD, comm_mode="fused"):
     os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port),
-                       "RANK": str(rank), "WORLD_SIZE": str(WORLD), "LOCAL_RANK": str(rank),
-                       "LOCAL_WORLD_SIZE": str(WORLD), "MINISPEED_DEVICE": f"cuda:{rank}",
+                       "RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank),
+                       "LOCAL_WORLD_SIZE": str(world), "MINISPEED_DEVICE": f"cuda:{rank}",
                        "MINISPEED_PG_TIMEOUT_S": "120", "NCCL_NVLS_ENABLE": "0"})
     os.environ.pop("MINISPEED_BACKEND", None)
     torch.cuda.set_device(rank)
@@ -93,11 +93,11 @@ def _gpt_worker(rank, stage, overlap, graph, port, out_dir):
            "fp16": {"enabled": True, "initial_scale_power": 10, "loss_scale_window": 3},
            "optimizer": {"type": "AdamW", "params": {"lr": 1e-3, "weight_decay": 0.1}},
            "zero_optimization": {"stage": stage},
-           "b200": {"comm": "fused", "overlap": overlap, "cuda_graph": graph,
+           "b200": {"comm": comm_mode, "overlap": overlap, "cuda_graph": graph,
                     "wait_timeout_ms": 20000}}
     engine = ms.initialize(model=model, config=cfg)
     g = torch.Generator().manual_seed(11)
-    data = [torch.randint(0, 512, (WORLD * 4, 65), generator=g) for _ in range(12)]
+    data = [torch.randint(0, 512, (world * 4, 65), generator=g) for _ in range(12)]
     losses = []
     for t in data:
         t = t[rank * 4:(rank + 1) * 4].cuda()
@@ -105,7 +105,8 @@ def _gpt_worker(rank, stage, overlap, graph, port, out_dir):
     params = {k: v.detach().float().cpu() for k, v in engine.state_dict().items()}
     torch.save({"losses": torch.tensor(losses), "params": params,
                 "slots": engine.optimizer.overlap_slots, "steps": engine.global_steps,
-                "scale": engine.get_loss_scale()}, os.path.join(out_dir, f"r{rank}.pt"))
+                "scale": engine.get_loss_scale(), "coll": engine.collectives},
+               os.path.join(out_dir, f"r{rank}.pt"))
     engine.close()
     ms.comm.destroy()
 
@@ -148,3 +149,30 @@ def test_stage3_layer_gather_matches_stage2(tmp_path):
     for k in s2[0]["params"]:
         torch.testing.assert_close(s3[0]["params"][k], s2[0]["params"][k], rtol=2e-3, atol=6e-3)
         torch.testing.assert_close(s3[0]["params"][k], s3[1]["params"][k], rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("stage", [2, 3])
+def test_all_gpus_fused_matches_nccl(stage, tmp_path):
+    """Every visible GPU as one rank (8 on a full box): the fused NVLink step
+    and the NCCL step give the same GPT training trajectory, and every rank
+    holds the same parameters."""
+    world = torch.cuda.device_count()
+    if world <= 2:
+        pytest.skip("covered by the two-GPU tests")
+    runs = {}
+    for mode in ("fused", "nccl"):
+        d = tmp_path / mode
+        d.mkdir()
+        mp.spawn(_gpt_worker, args=(stage, False, stage < 3, free_port(), str(d), world, mode),
+                 nprocs=world, join=True)
+        runs[mode] = [torch.load(d / f"r{r}.pt", weights_only=False) for r in range(world)]
+    fused, nccl = runs["fused"], runs["nccl"]
+    assert fused[0]["coll"] == "fused-nvlink" and nccl[0]["coll"] == "nccl"
+    assert fused[0]["steps"] == nccl[0]["steps"] == 6
+    torch.testing.assert_close(fused[0]["losses"], nccl[0]["losses"], rtol=2e-3, atol=2e-3)
+    for k in fused[0]["params"]:
+        for r in range(1, world):
+            torch.testing.assert_close(fused[r]["params"][k], fused[0]["params"][k], rtol=0,
+                                       atol=0)
+        torch.testing.assert_close(fused[0]["params"][k], nccl[0]["params"][k], rtol=2e-3,
+                                   atol=6e-3)
