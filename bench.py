@@ -383,13 +383,17 @@ def main():
     l1 = launches()
     ms_local = start.elapsed_time(end)
     ms_total = _max_over_ranks(ms_local, distributed, device)
-    comm_ms = None
+    comm_ms, phases = None, None
     if args.impl == "ours" and world > 1 and getattr(opt, "phase_log", None):
-        # everything between the end of backward and the next forward that is
-        # communication (no bucketed overlap with backward yet: all exposed)
+        # the optimizer step's phases, device-timed per step (mean over the
+        # timed steps, max over ranks); the exposed communication is the step
+        # tail outside the AdamW kernel: peer barriers, the fused
+        # reduce-scatter + statistics, the statistics exchange, the gather
         log = opt.phase_log
-        mean = sum(r[0] + r[2] for r in log) / len(log)
-        comm_ms = _max_over_ranks(mean, distributed, device)
+        names = sorted({k for r in log for k in r})
+        phases = {k: round(_max_over_ranks(sum(r.get(k, 0.0) for r in log) / len(log),
+                                           distributed, device), 4) for k in names}
+        comm_ms = sum(v for k, v in phases.items() if k != "adamw")
         opt.phase_log = None
     skipped_timed = engine.skipped_steps - skipped_before
 
@@ -437,11 +441,12 @@ def main():
                                      if spec["dtype"] == "fp16" else "bf16 + fp32 masters"),
                        "optimizer": "AdamW + WarmupDecayLR" + (
                            f", clip {spec['clip']}" if spec["clip"] else ""),
-                       "l2": "per-step working set > L2 (fp32 optimizer state streamed)",
-                       "collectives": getattr(engine, "collectives", "reference comm")},
+                       "l2": "per-step working set > L2 (fp32 optimizer state streamed)"},
             "impl": args.impl,
+            "collectives": getattr(engine, "collectives", "reference comm"),
             "exposed_comm_ms": 0.0 if world == 1 else (
                 round(comm_ms, 4) if comm_ms is not None else None),
+            "step_phases_ms": phases,
             "skipped_steps_timed": skipped_timed,
             "clocks": sampler.summary(),
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",

@@ -1,16 +1,22 @@
-"""Run one memory-bound kernel a few times (profiling target, one GPU).
+"""Bandwidth of the memory-bound kernels on one GPU.
 
-    python benchmarks/kernels_one.py --kernel adamw|rs_stats|grad_stats|cross_entropy|norm_bwd|add_norm
-                                     [--n 268435456] [--iters 3]
+    python benchmarks/kernels_bench.py --kernel adamw|rs_stats|grad_stats|cross_entropy|norm_bwd|add_norm
+                                       [--n 268435456] [--iters 3]
 
 ``rs_stats`` runs the fused reduce-scatter + statistics kernel over a
 one-rank peer table (this GPU's own heap), i.e. the kernel's load/compute
-structure without NVLink traffic.  Each launch is timed with CUDA events and
-reported with its algorithmic bytes and achieved bandwidth.
+structure without NVLink traffic.  Each launch is timed with CUDA events
+(the working set of the default size is larger than L2); the result line
+gives its algorithmic bytes, the median time and the achieved bandwidth as
+a fraction of the measured HBM copy bandwidth (``MEASURED_PEAKS.json``,
+else 6650 GB/s).  With few iterations it is also the target of an ncu
+capture of one kernel.
 """
 
 import argparse
+import json
 import os
+import statistics
 import sys
 
 import torch
@@ -20,15 +26,32 @@ from minispeed_b200.ops import _ext, kernels  # noqa: E402
 from minispeed_b200.ops import nn as ops  # noqa: E402
 
 
+def _hbm_gbs() -> float:
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                        "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return float(json.load(fh)["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return 6650.0
+
+
 def timed(fn, iters, nbytes, label):
+    """Time ``iters`` launches one by one; print one JSON result line."""
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    for i in range(iters):
+    times = []
+    for _ in range(iters):
         ev[0].record()
         fn()
         ev[1].record()
         torch.cuda.synchronize()
-        ms = ev[0].elapsed_time(ev[1])
-        print(f"{label} iter {i}: {ms:.4f} ms  {nbytes / ms / 1e6:.1f} GB/s")
+        times.append(ev[0].elapsed_time(ev[1]))
+    ms = statistics.median(times)
+    gbs = nbytes / ms / 1e6
+    print(json.dumps({"kernel": label, "bytes": int(nbytes), "iters": iters,
+                      "ms_median": round(ms, 4), "ms_min": round(min(times), 4),
+                      "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / _hbm_gbs(), 3)}),
+          flush=True)
 
 
 def main():

@@ -1,6 +1,7 @@
 """Per-kernel device time of one training step (torch.profiler, CUDA activity).
 
     python benchmarks/step_profile.py [--model gpt2-small|gpt2-xl|llama3-8b] [--impl ours|reference]
+                                      [--host]
 
 Builds the same model and config as ``bench.py`` (synthetic tokens, random
 weights), runs three warm-up steps, profiles one step and prints the step's
@@ -9,6 +10,10 @@ device's idle gaps between them (count and time by length, the longest with
 their neighbours).  Profiler
 timings are for shares, not for the headline number (``bench.py`` times
 without a profiler).
+
+``--host`` profiles the host instead: cProfile over ten steps, the functions
+by own time (the host's share of the step boundary: what runs between the
+optimizer's device-to-host read and the next replay).
 """
 
 import argparse
@@ -59,6 +64,7 @@ def main():
     ap.add_argument("--model", choices=sorted(bench.SPECS), default="gpt2-small")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--top", type=int, default=25)
+    ap.add_argument("--host", action="store_true")
     a = ap.parse_args()
     spec = bench.SPECS[a.model]
     torch.cuda.set_device(0)
@@ -96,6 +102,24 @@ def main():
     for _ in range(3):
         step()
     torch.cuda.synchronize()
+    if a.host:
+        import cProfile
+        import pstats
+        import time
+
+        prof = cProfile.Profile()
+        t0 = time.perf_counter()
+        prof.enable()
+        for _ in range(10):
+            step()
+        prof.disable()
+        torch.cuda.synchronize()
+        print(f"{a.model} {a.impl}: {(time.perf_counter() - t0) * 100:.2f} ms per step (wall, "
+              "under cProfile)")
+        st = pstats.Stats(prof)
+        st.sort_stats("tottime").print_stats(a.top)
+        st.sort_stats("cumulative").print_stats(a.top)
+        return
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         step()
         torch.cuda.synchronize()

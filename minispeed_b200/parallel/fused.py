@@ -117,6 +117,8 @@ class FusedCollectives:
         self.epoch_dev = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._shard32 = {}
         self._step_open = False
+        # phase marker of the optimizer's step timing (None: timing off)
+        self.marker = None
 
     # ------------------------------------------------------------ set-up
     def attach(self, groups: List[FlatParamGroup], zero_stage: int) -> None:
@@ -249,6 +251,8 @@ class FusedCollectives:
         if not self._step_open:
             self.barrier()          # every rank's gradient arena is final
             self._step_open = True
+            if self.marker is not None:
+                self.marker("barrier")
         if g.grad_arena is not arena:
             raise RuntimeError("gradient arena left the peer heap")
         if overlapped:
@@ -276,6 +280,8 @@ class FusedCollectives:
                                  inv_scale / self.world_size, None, fan, stats.partials,
                                  stats.flags, stats.used, min(left, 148 * 8), aligned, 256)
         stats.used += int(nb)
+        if self.marker is not None:
+            self.marker("rs_stats")
         if self.stage == 0:
             return g._grad, 1.0, True
         return out, 1.0, True

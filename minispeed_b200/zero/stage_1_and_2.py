@@ -81,9 +81,10 @@ class ZeROOptimizer:
         # stages 1-2 only all-gather the model-dtype params each step; the
         # fp32 masters outside this rank's shard are refreshed on demand
         self._masters_stale = False
-        # optional CUDA-event timing of the communication phases of each step
-        # (list of (reduce_ms, gather_ms)); enabled by the engine
+        # optional CUDA-event timing of the phases of each step: a list that
+        # gets one {phase: ms} dict per step (set it to [] to enable)
         self.phase_log = None
+        self._marks = None
         # bucketed reduction overlapped with backward (fused collectives)
         self.overlap_slots = 0
         self._overlap_ran = False
@@ -202,10 +203,10 @@ class ZeROOptimizer:
         if overlapped:
             self.join_comm()
             st.used = self.overlap_slots
-        ev = None
-        if self.phase_log is not None and st.device.type == "cuda":
-            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-            ev[0].record()
+        timing = self.phase_log is not None and st.device.type == "cuda"
+        self._marks = [] if timing else None
+        self.coll.marker = self._mark if timing else None
+        self._mark("start")
         grads, mul = [], 1.0
         for g in self.flat_groups:
             arena = g.collect_grads()
@@ -216,36 +217,56 @@ class ZeROOptimizer:
             if not stats_done:
                 st.accumulate(red, mul)
             grads.append(red)
+        self._mark("reduce")
         if self.coll.stats_need_allreduce(self.zero_stage):
             st.finalize(max_norm, epilogue=False)
             self.coll.all_reduce_stats(st.out)
             out = st.epilogue(max_norm)
         else:
             out = st.finalize(max_norm)
-        if ev is not None:
-            ev[1].record()
+        self._mark("stats")
         targets = [self._param_target(g) for g in self.flat_groups]
         fanouts = [self.coll.fanout(g) for g in self.flat_groups]
         self.adam.fused_step(grads, out, mul, max_norm, targets, fanouts)
-        if ev is not None:
-            ev[2].record()
+        self._mark("adamw")
         if 1 <= self.zero_stage <= 2 and self.world_size > 1:
             for g in self.flat_groups:
                 self.coll.gather_params(g)
             self._masters_stale = True
         self.coll.end_step()
-        if ev is not None:
-            ev[3].record()
+        self._mark("gather")
         flag, norm = self._read_stats(out)
         self.coll.check()
-        if ev is not None:
-            self.phase_log.append((ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]),
-                                   ev[2].elapsed_time(ev[3])))
+        if timing:
+            self.phase_log.append(self._phase_times())
+            self.coll.marker = None
+        self._marks = None
         if flag:
             return False, None
         self.adam.commit_step()
         self.grad_norm = norm
         return True, norm
+
+    def _mark(self, name: str) -> None:
+        """Record a CUDA event that ends phase ``name`` of this step (timing on)."""
+        if self._marks is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self._marks.append((name, ev))
+
+    def _phase_times(self) -> dict:
+        """Milliseconds from each mark to the next, under the later mark's
+        name (after the step's one host read, so every event has completed).
+        Phases: ``barrier`` (peer barrier: every rank's backward is done),
+        ``rs_stats`` (fused reduce-scatter + statistics), ``reduce`` (what
+        else the reduction took: library collectives, local statistics),
+        ``stats`` (statistics exchange / finalize), ``adamw`` (fused AdamW,
+        with the parameter fan-out at stages 1-2), ``gather`` (parameter
+        all-gather or the final peer barrier)."""
+        out = {}
+        for (_, a), (name, b) in zip(self._marks, self._marks[1:]):
+            out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        return out
 
     def _read_stats(self, out: torch.Tensor) -> Tuple[bool, float]:
         if out.is_cuda:

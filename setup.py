@@ -23,8 +23,6 @@ NVCC_FLAGS = [
 ]
 if os.environ.get("MSB_PTXAS_VERBOSE"):
     NVCC_FLAGS.append("-Xptxas=-v")
-if os.environ.get("MSB_BOUNDS_CHECK"):
-    NVCC_FLAGS.append("-DMSB_BOUNDS_CHECK=1")
 
 
 def sources():
