@@ -3,7 +3,8 @@
     python benchmarks/kernels_bench.py --kernel adamw|rs_stats|grad_stats|cross_entropy|norm_bwd|add_norm
                                        [--n 268435456] [--iters 3]
 
-``rs_stats`` runs the fused reduce-scatter + statistics kernel over a
+``cross_entropy`` times the forward + backward pair and then the forward
+that writes the gradient itself (the engine's path).  ``rs_stats`` runs the fused reduce-scatter + statistics kernel over a
 one-rank peer table (this GPU's own heap), i.e. the kernel's load/compute
 structure without NVLink traffic.  Each launch is timed with CUDA events
 (the working set of the default size is larger than L2); the result line
@@ -108,6 +109,16 @@ def main():
             loss = ops.cross_entropy(lg, tgt)
             loss.backward()
         timed(fn, a.iters, M * V * 2 * 3, "cross_entropy fwd+bwd")
+        # the engine's path: gradient written by the forward for the seed,
+        # logits read once and written once
+        seed = torch.ones(1, device=dev)
+
+        def fused():
+            lg = logits.detach().requires_grad_()
+            with ops.expected_loss_grad(seed):
+                loss = ops.cross_entropy(lg, tgt)
+            loss.backward()
+        timed(fused, a.iters, M * V * 2 * 2, "cross_entropy fwd+grad (one kernel)")
     elif a.kernel in ("norm_bwd", "add_norm"):
         Cd = 768
         M = n // Cd

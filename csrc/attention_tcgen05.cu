@@ -32,6 +32,8 @@
 // flight, frees its tensor memory and returns.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
+#include <type_traits>
 
 #include "common.cuh"
 #include "tcgen05.cuh"
@@ -71,6 +73,7 @@ struct Params {
   uint32_t idesc_s, idesc_o;
   unsigned* err;
   unsigned long long timeout_ns;
+  int poly;                  // of every 4 exponentials of P, how many exp2_poly computes (0-2)
 };
 
 template <int D>
@@ -170,22 +173,7 @@ __device__ __forceinline__ void sts_f(uint32_t a, float v) {
 #define MSB_EXP2_POLY 0   // of every 4 backward exponentials, how many use exp2_poly
 #endif
 
-// 2^x on the FMA and integer pipes (the special-function unit that ex2 uses
-// is the softmax's bottleneck).  Range reduction x = n + f, n = rint(x),
-// f in [-1/2, 1/2]: adding 1.5 * 2^23 leaves rint(x) in the low mantissa
-// bits.  2^f is a degree-3 polynomial whose coefficients minimise the maximum
-// relative error on [-1/2, 1/2] (a linear program over 4001 points):
-// 7.5e-5, below half an fp16 ulp.  n is added to the exponent field; x is
-// clamped at -125 so the result stays a normal number.
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -125.f);
-  const float t = x + 12582912.f;
-  const float f = x - (t - 12582912.f);
-  float q = fmaf(0.05517222f, f, 0.24261115f);
-  q = fmaf(q, f, 0.69326085f);
-  q = fmaf(q, f, 0.99992806f);
-  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
-}
+// exp2_poly (2^x on the FMA and integer pipes) lives in common.cuh.
 
 // One CTA: query tiles 2c and 2c+1 of one (batch, head).  The MMA warp
 // alternates between them (ping-pong): while warps 2-5 run the softmax of
@@ -466,19 +454,30 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
         }
         tc_fence_after();
       }
-      // P = 2^(s - m) as packed 16-bit pairs
+      // P = 2^(s - m) as packed 16-bit pairs.  The special-function unit
+      // that ex2 runs on bounds this loop at head dim 64 (128 exponentials
+      // per row per key tile against 2 x 64-deep MMAs), so a share of the
+      // exponentials (p.poly of every 4) goes to exp2_poly on the FMA pipe.
+      auto write_p = [&](auto share) {
+        constexpr int PC = decltype(share)::value;
 #pragma unroll
-      for (int hh = 0; hh < 4; ++hh) {
-        uint32_t pk[16];
+        for (int hh = 0; hh < 4; ++hh) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float a = ex2(fmaf(__uint_as_float(sv[hh * 32 + 2 * e]), p.scale_log2, -mref));
-          const float bb = ex2(fmaf(__uint_as_float(sv[hh * 32 + 2 * e + 1]), p.scale_log2, -mref));
-          l += a + bb;
-          pk[e] = pack2<T>(a, bb);
+          for (int e = 0; e < 16; ++e) {
+            const float xa = fmaf(__uint_as_float(sv[hh * 32 + 2 * e]), p.scale_log2, -mref);
+            const float xb = fmaf(__uint_as_float(sv[hh * 32 + 2 * e + 1]), p.scale_log2, -mref);
+            const float a = ex2(xa);
+            const float bb = (PC >= 2 || (PC == 1 && (e & 1))) ? exp2_poly(xb) : ex2(xb);
+            l += a + bb;
+            pk[e] = pack2<T>(a, bb);
+          }
+          tmem_st16(lane_base + cp + hh * 16, pk);
         }
-        tmem_st16(lane_base + cp + hh * 16, pk);
-      }
+      };
+      if (p.poly <= 0) write_p(std::integral_constant<int, 0>{});
+      else if (p.poly == 1) write_p(std::integral_constant<int, 1>{});
+      else write_p(std::integral_constant<int, 2>{});
       if (__any_sync(0xffffffffu, grow && j > 0)) {
         // O is stable: this tile's previous P V retired (waited for above, or
         // before its S was issued), and its next P V waits for p_full
@@ -1696,6 +1695,13 @@ void attention_fwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
   p.out = out;
   p.ld_out = ld_out;
   p.lse = lse;
+  // share of the forward's exponentials on the FMA pipe (MSB_ATTN_POLY=0-2 of 4)
+  static const int poly_share = [] {
+    const char* v = std::getenv("MSB_ATTN_POLY");
+    const int n = v ? std::atoi(v) : 1;
+    return n < 0 ? 0 : (n > 2 ? 2 : n);
+  }();
+  p.poly = poly_share;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.n_qtiles = (T + BQ - 1) / BQ;
   p.n_pairs = (p.n_qtiles + 1) / 2;

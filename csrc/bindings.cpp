@@ -6,6 +6,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdio>
 #include <cstdlib>
 #include <map>
 #include <mutex>
@@ -343,6 +344,9 @@ std::mutex g_plan_mutex;
 bool g_autotune = std::getenv("MSB_GEMM_AUTOTUNE") == nullptr ||
                   std::string(std::getenv("MSB_GEMM_AUTOTUNE")) != "0";
 
+// MSB_GEMM_TUNE_LOG=1: print every candidate's time to stderr
+bool g_tune_log = std::getenv("MSB_GEMM_TUNE_LOG") != nullptr &&
+                  std::string(std::getenv("MSB_GEMM_TUNE_LOG")) == "1";
 bool g_stream_k = std::getenv("MSB_GEMM_STREAMK") == nullptr ||
                  std::string(std::getenv("MSB_GEMM_STREAMK")) != "0";
 
@@ -421,6 +425,9 @@ std::pair<int, int> tune_gemm(const at::Tensor& a, const at::Tensor& b, int a_mn
       cuda_ok(cudaEventElapsedTime(&ms, e0, e1), "event");
       if (rep > 0) t = std::min(t, ms);
     }
+    if (g_tune_log)
+      std::fprintf(stderr, "gemm tune M=%lld N=%lld K=%lld a_mn=%d b_mn=%d bn=%d splits=%d: %.4f ms\n",
+                   (long long)M, (long long)N, (long long)K, a_mn, b_mn, c.first, c.second, t);
     if (t < best) {
       best = t;
       pick = c;
@@ -481,7 +488,7 @@ void attention_bwd_py(const at::Tensor& qkv2d, int64_t q_col, int64_t k_col, int
 void gemm(const at::Tensor& a, const at::Tensor& b, bool a_kmajor, bool b_kmajor,
           const OptT& bias, const at::Tensor& out, bool accumulate, const at::Tensor& err,
           double timeout_s, int64_t mode, const OptT& aux, int64_t force_bn,
-          int64_t force_splits) {
+          int64_t force_splits, const OptT& colsum_part) {
   check_rows(a, "A");
   check_rows(b, "B");
   check_rows(out, "C");
@@ -509,6 +516,14 @@ void gemm(const at::Tensor& a, const at::Tensor& b, bool a_kmajor, bool b_kmajor
     auxp = aux->data_ptr();
     ld_aux = aux->stride(0);
     TORCH_CHECK(!accumulate, "gemm epilogue modes do not accumulate");
+  }
+  float* csp = nullptr;
+  if (colsum_part.has_value() && colsum_part->defined()) {
+    TORCH_CHECK(mode == 2, "gemm column sums come with the dGELU epilogue (mode 2)");
+    TORCH_CHECK(colsum_part->is_cuda() && colsum_part->scalar_type() == at::kFloat &&
+                    colsum_part->is_contiguous() && colsum_part->numel() >= (M + 31) / 32 * N,
+                "gemm column-sum partials: fp32 [ceil(M/32), N]");
+    csp = colsum_part->data_ptr<float>();
   }
   c10::cuda::CUDAGuard g(a.device());
   cudaStream_t st = stream_of(a);
@@ -551,7 +566,7 @@ void gemm(const at::Tensor& a, const at::Tensor& b, bool a_kmajor, bool b_kmajor
                     need > 0 ? ws.data_ptr<float>() : nullptr, need,
                     reinterpret_cast<unsigned*>(err.data_ptr<int>()), timeout_s, st, bn, splits,
                     splits == -1 ? stream_k_counters(a.device()) : nullptr,
-                    msb::kStreamKCounters);
+                    msb::kStreamKCounters, csp);
 }
 
 std::vector<int64_t> gemm_cached_plan(int64_t M, int64_t N, int64_t K, int64_t a_mn,

@@ -80,6 +80,9 @@ struct Params {
   int sk;
   int sk_per, sk_extra;
   int* sk_ctr;
+  // mode 2: column sums of the stored output (the fc bias gradient), one
+  // fp32 partial row per 32 output rows: [ceil(M / 32), N]
+  float* colsum_part;
   uint32_t idesc;
   unsigned* err;
   unsigned long long timeout_ns;
@@ -342,6 +345,30 @@ __device__ __forceinline__ void staged_chunk(const Params& p, const CUtensorMap*
   sbuf ^= 1;
 }
 
+// Column sums of one 32 x 32 output chunk (lane = row) into its partial
+// row: the values as stored (rounded to the model dtype), rows past M as
+// zero.  A transpose-reduce: at each of five steps every lane sends the half
+// of its remaining columns that its partner keeps and adds the half it
+// receives (31 shuffles); lane j ends with column j's sum.
+template <typename T>
+__device__ __forceinline__ void chunk_colsum(const Params& p, int row0, int col, int nvalid,
+                                             bool valid_row, const float (&v)[32], int lane) {
+  float x[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) x[j] = valid_row ? to_f32(from_f32<T>(v[j])) : 0.f;
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1) {
+    const bool up = (lane & w) != 0;
+#pragma unroll
+    for (int j = 0; j < w; ++j) {
+      const float send = up ? x[j] : x[j + w];
+      const float keep = up ? x[j + w] : x[j];
+      x[j] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+    }
+  }
+  if (lane < nvalid) p.colsum_part[(long long)(row0 >> 5) * p.N + col + lane] = x[0];
+}
+
 __device__ __forceinline__ void store_ws_chunk(const Params& p, int split, int row, int col,
                                                const float (&v)[32], int nvalid) {
   float* w = p.ws + ((long long)split * p.M + row) * p.N + col;
@@ -529,6 +556,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           if (p.splits > 1) store_ws_chunk(p, split, row, col, v, nvalid);
           else store_chunk<T>(p, row, col, v, nvalid);
         }
+        if (p.colsum_part != nullptr) chunk_colsum<T>(p, row0, col, nvalid, row < p.M, v, lane);
       }
       tc_fence_before();
       __syncwarp();
@@ -923,6 +951,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
           if (p.splits > 1) store_ws_chunk(p, split, row, col, v, nvalid);
           else store_chunk<T>(p, row, col, v, nvalid);
         }
+        if (p.colsum_part != nullptr) chunk_colsum<T>(p, row0, col, nvalid, row < p.M, v, lane);
       }
       tc_fence_before();
       __syncwarp();
@@ -1141,7 +1170,8 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
                   void* C, long long ldc, const void* bias, int M, int N, int K, int dtype,
                   int accumulate, int mode, void* aux, long long ld_aux, float* ws,
                   long long ws_floats, unsigned* err, double timeout_s, cudaStream_t st,
-                  int force_bn, int force_splits, int* sk_ctr, long long sk_ctr_n) {
+                  int force_bn, int force_splits, int* sk_ctr, long long sk_ctr_n,
+                  float* colsum_part) {
   using namespace tc;
   int bn, splits;
   const long long need = gemm_plan(M, N, K, kNumSMs, &bn, &splits);
@@ -1212,6 +1242,7 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
   p.sk_per = 0;
   p.sk_extra = 0;
   p.sk_ctr = nullptr;
+  p.colsum_part = mode == 2 ? colsum_part : nullptr;
   if (two_cta) {
     const int cap = dtype == kF16 ? pair_capacity<__half>(p, st)
                                   : pair_capacity<__nv_bfloat16>(p, st);

@@ -89,7 +89,9 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
                   int accumulate, int mode, void* aux, long long ld_aux, float* ws,
                   long long ws_floats, unsigned* err, double timeout_s, cudaStream_t st,
                   int force_bn = 0, int force_splits = 0, int* sk_ctr = nullptr,
-                  long long sk_ctr_n = 0);
+                  long long sk_ctr_n = 0, float* colsum_part = nullptr);
+// colsum_part (mode 2 only): fp32 [ceil(M / 32), N] column sums of the stored
+// output, one row per 32 output rows (finished by colsum_finish)
 // stream-K (force_bn 512, force_splits -1): fp32 slots ws >= kStreamKSlotFloats
 // per resident pair, and zeroed per-tile counters (left zero again)
 constexpr long long kStreamKSlotFloats = 256LL * 256;

@@ -279,6 +279,116 @@ norm_dx_prefetch_kernel(const T* __restrict__ dy, const T* __restrict__ s,
   }
 }
 
+// The prefetch pass above plus the weight and bias gradients' column
+// partials in the same sweep: while a warp has a row's dy and s in
+// registers it also adds dy * xhat and dy into per-lane accumulators for its
+// 8-column groups.  Each block then reduces its 8 warps in shared memory (a
+// fixed order, 256 columns at a time) and writes one partial row of dw and
+// one of db; colsum_finish sums the gridDim.x partial rows.  The separate
+// partial kernel, which read dy and s a second time, is not launched.
+template <typename T, int NV, bool RMS>
+__global__ void __launch_bounds__(256)
+norm_bwd_fused_kernel(const T* __restrict__ dy, const T* __restrict__ s,
+                      const T* __restrict__ w, const float* __restrict__ mean_in,
+                      const float* __restrict__ rstd_in, const T* __restrict__ dres,
+                      T* __restrict__ dx, float* __restrict__ dw_part,
+                      float* __restrict__ db_part, int M, int C) {
+  ::msb::pdl_begin();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nvec = C >> 3;
+  float aw[NV][8], ab[NV][8];
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      aw[i][k] = 0.f;
+      ab[i][k] = 0.f;
+    }
+  for (int row = blockIdx.x * 8 + warp; row < M; row += gridDim.x * 8) {
+    const size_t base = (size_t)row * C;
+    Pack8<T> sp[NV], dp[NV], rp[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (lane + i * 32) << 3;
+      if ((lane + i * 32) < nvec) {
+        sp[i] = *reinterpret_cast<const Pack8<T>*>(s + base + c);
+        dp[i] = *reinterpret_cast<const Pack8<T>*>(dy + base + c);
+        if (dres != nullptr) rp[i] = *reinterpret_cast<const Pack8<T>*>(dres + base + c);
+      }
+    }
+    const float mean = RMS ? 0.f : mean_in[row];
+    const float rstd = rstd_in[row];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (lane + i * 32) << 3;
+      if ((lane + i * 32) < nvec) {
+        float sv[8], dyv[8], wv[8];
+        unpack8(sp[i], sv);
+        unpack8(dp[i], dyv);
+        load8(w + c, wv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float xh = (sv[k] - mean) * rstd;
+          const float g = dyv[k] * wv[k];
+          s1 += g;
+          s2 += g * xh;
+          aw[i][k] += dyv[k] * xh;
+          ab[i][k] += dyv[k];
+        }
+      }
+    }
+    s1 = warp_sum(s1) / (float)C;
+    s2 = warp_sum(s2) / (float)C;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (lane + i * 32) << 3;
+      if ((lane + i * 32) < nvec) {
+        float sv[8], dyv[8], wv[8], o[8];
+        unpack8(sp[i], sv);
+        unpack8(dp[i], dyv);
+        load8(w + c, wv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float xh = (sv[k] - mean) * rstd;
+          const float g = dyv[k] * wv[k];
+          o[k] = RMS ? rstd * (g - xh * s2) : rstd * (g - s1 - xh * s2);
+        }
+        if (dres != nullptr) {
+          float r[8];
+          unpack8(rp[i], r);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) o[k] += r[k];
+        }
+        store8(dx + base + c, o);
+      }
+    }
+  }
+  // per-block column partials: lane l of vector group i owns columns
+  // (l + 32 i) * 8 .. +7; reduce the 8 warps 256 columns (32 groups) at a time
+  __shared__ float red[8][256 + 8];
+#pragma unroll
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1 && (RMS || db_part == nullptr)) break;
+    float* out = pass == 0 ? dw_part : db_part;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) red[warp][lane * 8 + k] = pass == 0 ? aw[i][k] : ab[i][k];
+      __syncthreads();
+      const int c = i * 256 + threadIdx.x;
+      if (c < C) {
+        float t = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t += red[q][threadIdx.x];
+        out[(size_t)blockIdx.x * C + c] = t;
+      }
+      __syncthreads();
+    }
+  }
+}
+
 // Column partials of dw = sum_rows dy * xhat and db = sum_rows dy, tiled like
 // colsum_partial_kernel: block (256-column slab, row chunk).
 template <typename T, bool RMS>
@@ -754,14 +864,21 @@ ce_fwd_grad_kernel(T* __restrict__ logits, const long long* __restrict__ tgt,
   auto g = [&](int i, float v) {
     return (ex2_approx((v - l) * kLog2e) - (i == t ? 1.f : 0.f)) * scale;
   };
+  // the same with 2^x on the FMA pipe (exp2_poly: relative error 7.5e-5,
+  // under half a 16-bit ulp of the stored gradient)
+  auto gp = [&](int i, float v) {
+    return (exp2_poly((v - l) * kLog2e) - (i == t ? 1.f : 0.f)) * scale;
+  };
   for (int i = threadIdx.x; i < h; i += blockDim.x) row[i] = from_f32<T>(g(i, to_f32(row[i])));
   const int nvec = (V - h) / 8;
   T* mid = row + h;
   for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
     float v[8];
     load8(mid + i * 8, v);
+    // half of the exponentials on the special-function unit, half on the
+    // FMA pipe: pass 1 already keeps the special-function unit busy
 #pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = g(h + i * 8 + k, v[k]);
+    for (int k = 0; k < 8; ++k) v[k] = (k & 1) ? gp(h + i * 8 + k, v[k]) : g(h + i * 8 + k, v[k]);
     store8(mid + i * 8, v);
   }
   for (int i = h + nvec * 8 + threadIdx.x; i < V; i += blockDim.x)
@@ -993,10 +1110,47 @@ static void launch_norm_dx(const void* dy, const void* s, const void* w, const f
                                                            C);
 }
 
+template <typename T, int NVV>
+static bool launch_norm_fused(const void* dy, const void* s, const void* w, const float* mean,
+                              const float* rstd, const void* dres, void* dx, float* dw_part,
+                              float* db_part, int M, int C, bool rms, int blocks,
+                              cudaStream_t st) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  // the accumulators take 16 registers per vector group: up to 1024 columns
+  // the kernel stays without spills
+  if constexpr (NVV <= 4) {
+    if (C % 8 == 0 && al(dy) && al(s) && al(dx) && (dres == nullptr || al(dres))) {
+      if (rms)
+        ::msb::launch(norm_bwd_fused_kernel<T, NVV, true>, blocks, 256, 0, st, (const T*)dy,
+                      (const T*)s, (const T*)w, mean, rstd, (const T*)dres, (T*)dx, dw_part,
+                      (float*)nullptr, M, C);
+      else
+        ::msb::launch(norm_bwd_fused_kernel<T, NVV, false>, blocks, 256, 0, st, (const T*)dy,
+                      (const T*)s, (const T*)w, mean, rstd, (const T*)dres, (T*)dx, dw_part,
+                      db_part, M, C);
+      return true;
+    }
+  }
+  return false;
+}
+
 int norm_bwd(const void* dy, const void* s, const void* w, const float* mean, const float* rstd,
              const void* dres, void* dx, float* dw_part, float* db_part, int M, int C, bool rms,
              int dtype, int max_blocks, cudaStream_t st) {
   const int nv = (C / 8 + 31) / 32;
+  // one pass (dx and the dw/db partials) when the rows allow 16-byte access
+  const int fused_blocks = std::max(1, std::min({max_blocks, 2 * kNumSMs, (M + 7) / 8}));
+  bool fused = false;
+  MSB_DISPATCH_FLOAT(dtype, T, {
+    if (nv <= 1) fused = launch_norm_fused<T, 1>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, fused_blocks, st);
+    else if (nv <= 2) fused = launch_norm_fused<T, 2>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, fused_blocks, st);
+    else if (nv <= 3) fused = launch_norm_fused<T, 3>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, fused_blocks, st);
+    else if (nv <= 4) fused = launch_norm_fused<T, 4>(dy, s, w, mean, rstd, dres, dx, dw_part, db_part, M, C, rms, fused_blocks, st);
+  });
+  if (fused) {
+    MSB_CHECK_LAUNCH("norm_bwd_fused");
+    return fused_blocks;
+  }
   int chunks = std::min(max_blocks, std::max(1, (M + 63) / 64));
   const int rpb = (M + chunks - 1) / chunks;
   chunks = (M + rpb - 1) / rpb;

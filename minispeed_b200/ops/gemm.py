@@ -91,7 +91,8 @@ EPI_PLAIN, EPI_BIAS_GELU, EPI_DGELU = 0, 1, 2
 def gemm(a: torch.Tensor, b: torch.Tensor, *, a_kmajor: bool, b_kmajor: bool,
          bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
          accumulate: bool = False, mode: int = EPI_PLAIN,
-         aux: Optional[torch.Tensor] = None, plan: Optional[tuple] = None) -> torch.Tensor:
+         aux: Optional[torch.Tensor] = None, plan: Optional[tuple] = None,
+         colsum: Optional[torch.Tensor] = None) -> torch.Tensor:
     """C[M,N] (+)= A @ B^T (+ bias) in the tcgen05 operand convention.
 
     ``a`` holds A as [M,K] (``a_kmajor``) or [K,M]; ``b`` holds B as [N,K]
@@ -100,7 +101,10 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_kmajor: bool, b_kmajor: bool,
     stores (A@B^T) * gelu'(aux) into ``out``.  ``plan=(bn, splits)`` replaces
     the tuned plan: bn 512 is the 2-CTA pair kernel (256 x 256 tiles), 256 or
     128 the 1-CTA kernel; splits 1-8 split K, -1 is stream-K (an even cut of
-    all K slices over the resident pairs, pair kernel only)."""
+    all K slices over the resident pairs, pair kernel only).  ``colsum``
+    (``EPI_DGELU`` only): an fp32 buffer of ceil(M/32) x N that receives the
+    column sums of the stored output, one row per 32 output rows (finish
+    with ``colsum_finish``): the bias gradient without re-reading C."""
     M = a.shape[0] if a_kmajor else a.shape[1]
     N = b.shape[0] if b_kmajor else b.shape[1]
     if out is None:
@@ -110,7 +114,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_kmajor: bool, b_kmajor: bool,
             raise TypeError(f"tcgen05 gemm takes fp16 or bf16 operands, got {a.dtype}")
         bn, splits = plan if plan is not None else (0, 0)
         _ext.get().gemm(_tma_ready(a), _tma_ready(b), a_kmajor, b_kmajor, bias, out,
-                        accumulate, error_word(a.device), TIMEOUT_S, mode, aux, bn, splits)
+                        accumulate, error_word(a.device), TIMEOUT_S, mode, aux, bn, splits,
+                        colsum)
         return out
     A = a if a_kmajor else a.t()
     B = b.t() if b_kmajor else b
@@ -126,6 +131,11 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_kmajor: bool, b_kmajor: bool,
         from .nn import gelu_grad_reference
 
         r = r.to(out.dtype).float() * gelu_grad_reference(aux.float())
+        if colsum is not None:
+            rows = r.to(out.dtype).float()
+            pad = (-rows.shape[0]) % 32
+            rows = torch.cat([rows, rows.new_zeros(pad, rows.shape[1])]) if pad else rows
+            colsum.view(-1, N)[: rows.shape[0] // 32].copy_(rows.view(-1, 32, N).sum(1))
     if accumulate:
         out.copy_((out.float() + r).to(out.dtype))
     else:

@@ -34,7 +34,7 @@ import torch.nn.functional as F
 from . import _ext, gemm
 
 _COLSUM_CHUNKS = 256   # row chunks of a column-sum reduction
-_NORM_BLOCKS = 256     # row chunks of the norm-backward dw/db column sums
+_NORM_BLOCKS = 296     # row chunks (blocks) of the norm-backward dw/db column sums
 
 
 def _C():
@@ -243,9 +243,21 @@ class _MlpGelu(torch.autograd.Function):
         dw2 = _wgrad(d2, a, w2_p)
         db2 = _colsum(d2, w2.dtype, grad_sink(b2_p)) if b2_p is not None else None
         du = torch.empty_like(u)
-        gemm.gemm(d2, w2, a_kmajor=True, b_kmajor=False, out=du, mode=gemm.EPI_DGELU, aux=u)
+        M, F_ = du.shape
+        # the dGELU epilogue also leaves the column sums of du (fc bias
+        # gradient), one partial row per 32 rows: no second read of du
+        part = _scratch(du.device, -(-M // 32) * F_) if b1_p is not None else None
+        gemm.gemm(d2, w2, a_kmajor=True, b_kmajor=False, out=du, mode=gemm.EPI_DGELU, aux=u,
+                  colsum=part)
         dw1 = _wgrad(du, x2, w1_p)
-        db1 = _colsum(du, w1.dtype, grad_sink(b1_p)) if b1_p is not None else None
+        db1 = None
+        if b1_p is not None:
+            sink = grad_sink(b1_p)
+            if sink is not None:
+                _C().colsum_finish(part, -(-M // 32), sink, True)
+            else:
+                db1 = torch.empty(F_, dtype=w1.dtype, device=du.device)
+                _C().colsum_finish(part, -(-M // 32), db1, False)
         dx = gemm.linear_dgrad(du, w1).view(ctx.shape) if ctx.needs_input_grad[0] else None
         return dx, dw1, db1, dw2, db2
 

@@ -212,3 +212,27 @@ def test_stream_k_epilogues(dtype, _variant):
     from minispeed_b200.ops.nn import gelu_grad_reference
     want = (dY.float() @ W.float()).to(dtype).float() * gelu_grad_reference(u.float())
     _check(du, want, K)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M,N,K", [(4096, 3072, 768), (1000, 520, 256)])
+def test_dgelu_epilogue_column_sums(dtype, M, N, K, _variant):
+    """The dGELU epilogue also writes the column sums of its stored output,
+    one fp32 partial row per 32 rows (ragged last group included); their
+    finished sum is the bias gradient of the column sums of du itself."""
+    torch.manual_seed(M + N)
+    dY = (torch.randn(M, K, device="cuda") * 0.05).to(dtype)
+    W = (torch.randn(K, N, device="cuda") * 0.05).to(dtype)
+    u = torch.randn(M, N, device="cuda").to(dtype)
+    du = torch.empty(M, N, device="cuda", dtype=dtype)
+    groups = -(-M // 32)
+    part = torch.full((groups * N,), float("nan"), device="cuda")
+    gemm.gemm(dY, W, a_kmajor=True, b_kmajor=False, out=du, mode=gemm.EPI_DGELU, aux=u,
+              colsum=part)
+    torch.cuda.synchronize()
+    want = du.float().sum(0)
+    got = part.view(groups, N).sum(0)
+    torch.testing.assert_close(got, want, rtol=1e-3, atol=1e-3 * K ** 0.5)
+    out = torch.zeros(N, device="cuda", dtype=dtype)
+    _ext.get().colsum_finish(part, groups, out, False)
+    torch.testing.assert_close(out.float(), want, rtol=1e-2, atol=1e-2)
