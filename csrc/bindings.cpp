@@ -12,6 +12,7 @@
 #include <mutex>
 #include <string>
 #include <tuple>
+#include <vector>
 
 #include "kernels_api.h"
 
@@ -353,6 +354,16 @@ bool g_stream_k = std::getenv("MSB_GEMM_STREAMK") == nullptr ||
 // fp32 partial-tile slots of a stream-K launch: one per resident CTA pair
 long long stream_k_ws_floats() { return 74LL * msb::kStreamKSlotFloats; }
 
+// split-K workspace: [splits][M][N] for the reduce kernel, or (pair kernel,
+// in-kernel fixup) one 256 x 256 slot per tile of every split but the last
+long long split_ws_floats(int64_t M, int64_t N, int splits, int bn) {
+  long long need = (long long)splits * M * N;
+  if (bn == 512)
+    need = std::max<long long>(need, (long long)(splits - 1) * ((M + 255) / 256) *
+                                         ((N + 255) / 256) * msb::kStreamKSlotFloats);
+  return need;
+}
+
 // Per-device zeroed tile counters of the stream-K GEMM (persistent: each
 // launch leaves them zero again).
 int* stream_k_counters(const at::Device& dev) {
@@ -400,7 +411,7 @@ std::pair<int, int> tune_gemm(const at::Tensor& a, const at::Tensor& b, int a_mn
   at::Tensor scratch = at::empty({M, ldn}, a.options());
   long long ws_need = 0;
   for (auto& c : cands)
-    ws_need = std::max<long long>(ws_need, c.second > 1 ? c.second * M * N
+    ws_need = std::max<long long>(ws_need, c.second > 1 ? split_ws_floats(M, N, c.second, c.first)
                                            : (c.second == -1 ? stream_k_ws_floats() : 0));
   int* ctr = stream_k_counters(a.device());
   at::Tensor ws;
@@ -552,7 +563,8 @@ void gemm(const at::Tensor& a, const at::Tensor& b, bool a_kmajor, bool b_kmajor
   }
   long long need = 0;
   if (bn > 0) {
-    need = splits > 1 ? (long long)splits * M * N : (splits == -1 ? stream_k_ws_floats() : 0);
+    need = splits > 1 ? split_ws_floats(M, N, splits, bn)
+                      : (splits == -1 ? stream_k_ws_floats() : 0);
   } else {
     int pbn = 0, ps = 1;
     need = msb::gemm_plan((int)M, (int)N, (int)K, 148, &pbn, &ps);
@@ -565,7 +577,7 @@ void gemm(const at::Tensor& a, const at::Tensor& b, bool a_kmajor, bool b_kmajor
                     dtype_code(a), accumulate ? 1 : 0, (int)mode, auxp, ld_aux,
                     need > 0 ? ws.data_ptr<float>() : nullptr, need,
                     reinterpret_cast<unsigned*>(err.data_ptr<int>()), timeout_s, st, bn, splits,
-                    splits == -1 ? stream_k_counters(a.device()) : nullptr,
+                    (splits == -1 || splits > 1) ? stream_k_counters(a.device()) : nullptr,
                     msb::kStreamKCounters, csp);
 }
 
@@ -609,6 +621,22 @@ at::Tensor tensor_from_ptr(int64_t ptr, int64_t numel, int64_t dtype, int64_t de
   TORCH_CHECK(dtype >= 0 && dtype < 3);
   auto opts = at::TensorOptions().dtype(types[dtype]).device(at::kCUDA, (int)device);
   return at::from_blob(reinterpret_cast<void*>(ptr), {numel}, opts);
+}
+
+// Device-to-device copies on the current stream of `like`'s device, one
+// cudaMemcpyAsync each (peer pointers mapped into this process included:
+// the copy engines move those over NVLink without using SMs).
+void copy_many(const at::Tensor& like, const std::vector<int64_t>& dst,
+               const std::vector<int64_t>& src, const std::vector<int64_t>& nbytes) {
+  TORCH_CHECK(dst.size() == src.size() && src.size() == nbytes.size(), "copy lists differ");
+  c10::cuda::CUDAGuard g(like.device());
+  cudaStream_t st = stream_of(like);
+  for (size_t k = 0; k < dst.size(); ++k) {
+    if (nbytes[k] <= 0) continue;
+    cuda_ok(cudaMemcpyAsync(reinterpret_cast<void*>(dst[k]), reinterpret_cast<const void*>(src[k]),
+                            static_cast<size_t>(nbytes[k]), cudaMemcpyDeviceToDevice, st),
+            "peer copy");
+  }
 }
 
 unsigned* epoch_counter(const at::Tensor& ctr) {
@@ -733,6 +761,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, mod) {
   mod.def("peer_open", &peer_open_py);
   mod.def("peer_close", &peer_close_py);
   mod.def("tensor_from_ptr", &tensor_from_ptr);
+  mod.def("copy_many", &copy_many);
   mod.def("peer_barrier", &peer_barrier_py);
   mod.def("rs_stats", &rs_stats_py);
   mod.def("stats_exchange", &stats_exchange_py);

@@ -80,6 +80,10 @@ struct Params {
   int sk;
   int sk_per, sk_extra;
   int* sk_ctr;
+  // split-K with in-kernel fixup (pair kernel, all units resident at once):
+  // splits 0..S-2 of a tile store fp32 partials (ws slot split * tiles +
+  // tile) and arrive on sk_ctr[tile]; split S-1 adds them and finishes
+  int fix;
   // mode 2: column sums of the stored output (the fc bias gradient), one
   // fp32 partial row per 32 output rows: [ceil(M / 32), N]
   float* colsum_part;
@@ -881,7 +885,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     const int quarter = warp & 3;
     const int half = (warp - 2) / 4;
     const int row_in_tile = HALF * rank + quarter * 32 + lane;
-    const bool has_bias = p.bias != nullptr && p.splits == 1;
+    const bool has_bias = p.bias != nullptr && (p.splits == 1 || p.fix);
     const uint32_t tempty_leader0 = mapa(smem_u32(&bars->tempty[0]), 0);
     const uint32_t tempty_leader1 = mapa(smem_u32(&bars->tempty[1]), 0);
     uint8_t* stg = sStage + (warp - 2) * 2 * kStageBytes;
@@ -897,11 +901,16 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
       // stream-K: a pair's first item may continue a tile another pair
       // started (contribute the partial); its last item may start a tile
       // that later pairs continue (finish it once their partials are in)
-      const bool contrib = p.sk && kb0 > 0;
-      const bool finish = p.sk && kb0 == 0 && kb1 < p.kb_total;
+      // split-K fixup: the last split of a tile finishes it from the others
+      const int ntiles = p.tiles_m * p.tiles_n;
+      const bool contrib = (p.sk && kb0 > 0) || (p.fix && split < p.splits - 1);
+      const bool finish =
+          (p.sk && kb0 == 0 && kb1 < p.kb_total) || (p.fix && split == p.splits - 1);
+      const long long my_slot = p.fix ? (long long)split * ntiles + tile : pair_id;
       int ncontrib = 0;
       if (finish) {
-        ncontrib = sk_pair_of(p, (long long)(tile + 1) * p.kb_total - 1) - pair_id;
+        ncontrib = p.fix ? p.splits - 1
+                         : sk_pair_of(p, (long long)(tile + 1) * p.kb_total - 1) - pair_id;
         // all 16 epilogue warps of each contributing pair have arrived
         if (!sk_wait_w(p.sk_ctr + tile, 16 * ncontrib, abort, p, 15, lane)) break;
       }
@@ -915,25 +924,30 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        const long long slot_off = (long long)row_in_tile * BN2 + c * 32;
+        // a partial tile is stored chunk by chunk in register order: float4
+        // q of lane l of chunk (row block, c) at ((rb * 8 + c) * 8 + q) * 32
+        // + l, so every warp-wide store and load moves 512 contiguous bytes
+        const long long slot_off =
+            (((long long)(row_in_tile >> 5) * (BN2 / 32) + c) * 8) * 32 + lane;
         if (contrib) {
           // the whole 32-column piece of the row, in or out of C: the
           // finisher reads back exactly what it needs
-          float4* w = reinterpret_cast<float4*>(p.ws + (long long)pair_id * (TM * BN2) + slot_off);
+          float4* w = reinterpret_cast<float4*>(p.ws + my_slot * (TM * BN2)) + slot_off;
 #pragma unroll
           for (int q = 0; q < 8; ++q)
-            w[q] = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+            w[q * 32] = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
           continue;
         }
         const int col = n0 + c * 32;
         if (col >= p.N || row0 >= p.M) continue;
         if (finish) {
           for (int j = 1; j <= ncontrib; ++j) {
-            const float4* w = reinterpret_cast<const float4*>(
-                p.ws + (long long)(pair_id + j) * (TM * BN2) + slot_off);
+            const long long slot =
+                p.fix ? (long long)(j - 1) * ntiles + tile : (long long)(pair_id + j);
+            const float4* w = reinterpret_cast<const float4*>(p.ws + slot * (TM * BN2)) + slot_off;
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
-              const float4 x = __ldcg(w + q);
+              const float4 x = __ldcg(w + q * 32);
               v[q * 4] += x.x;
               v[q * 4 + 1] += x.y;
               v[q * 4 + 2] += x.z;
@@ -948,7 +962,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         if (p.staged && nvalid == 32 && row0 + 32 <= p.M) {
           staged_chunk<T>(p, &tmC, &tmX, stg, sbuf, row0, lane, col, nvalid, v);
         } else if (row < p.M) {
-          if (p.splits > 1) store_ws_chunk(p, split, row, col, v, nvalid);
+          if (p.splits > 1 && !p.fix) store_ws_chunk(p, split, row, col, v, nvalid);
           else store_chunk<T>(p, row, col, v, nvalid);
         }
         if (p.colsum_part != nullptr) chunk_colsum<T>(p, row0, col, nvalid, row < p.M, v, lane);
@@ -1200,13 +1214,26 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
   p.tiles_n = (N + tn - 1) / tn;
   p.nfast = (long long)M > (long long)N ? 1 : 0;  // A (M x K) larger than B (N x K)
   p.units = p.tiles_m * p.tiles_n * p.splits;
+  // split-K on the pair kernel finishes in the kernel (no reduce launch)
+  // when every unit is resident at once and the tile counters and the
+  // per-tile partial slots are available
+  p.fix = 0;
+  if (two_cta && p.splits > 1 && sk_ctr != nullptr && ws != nullptr) {
+    const int cap = dtype == kF16 ? pair_capacity<__half>(p, st)
+                                  : pair_capacity<__nv_bfloat16>(p, st);
+    const long long tiles = (long long)p.tiles_m * p.tiles_n;
+    if (p.units <= cap && tiles <= sk_ctr_n &&
+        ws_floats >= (long long)(p.splits - 1) * tiles * pair::TM * pair::BN2)
+      p.fix = 1;
+  }
+  const bool reduce_launch = p.splits > 1 && !p.fix;
   p.C = C;
   p.ldc = ldc;
-  p.bias = p.splits > 1 ? nullptr : bias;
+  p.bias = reduce_launch ? nullptr : bias;
   p.ws = ws;
   p.a_mn = a_mn;
   p.b_mn = b_mn;
-  p.accumulate = p.splits > 1 ? 0 : accumulate;
+  p.accumulate = reduce_launch ? 0 : accumulate;
   p.c_vec = ((reinterpret_cast<uintptr_t>(C) & 15) == 0 && (ldc % 8) == 0) ? 1 : 0;
   p.mode = mode;
   p.aux = aux;
@@ -1230,7 +1257,8 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
                               : make_map(B, dtype, K, N, ldb, 64, b_rows);
   // output maps for the staged epilogue: 32 x 32 boxes, 64-byte swizzle
   // (plain and GELU/dGELU outputs; accumulation and split-K store per thread)
-  p.staged = (p.splits == 1 && p.c_vec && (mode != 1 || p.aux_vec) && (!p.accumulate || mode == 0))
+  p.staged = (!reduce_launch && p.c_vec && (mode != 1 || p.aux_vec) &&
+              (!p.accumulate || mode == 0))
                  ? 1 : 0;
   const CUtensorMap tcm = p.staged ? make_map(C, dtype, N, M, ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
                                    : ta;
@@ -1241,7 +1269,7 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
   p.sk = 0;
   p.sk_per = 0;
   p.sk_extra = 0;
-  p.sk_ctr = nullptr;
+  p.sk_ctr = p.fix ? sk_ctr : nullptr;
   p.colsum_part = mode == 2 ? colsum_part : nullptr;
   if (two_cta) {
     const int cap = dtype == kF16 ? pair_capacity<__half>(p, st)
@@ -1281,7 +1309,7 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
     throw std::runtime_error("tcgen05 gemm takes fp16/bf16 operands");
   }
   MSB_CHECK_LAUNCH("gemm_tcgen05");
-  if (p.splits > 1) {
+  if (reduce_launch) {
     if (dtype == kF16)
       launch_reduce<__half>(ws, p.splits, M, N, C, ldc, bias, accumulate, st);
     else

@@ -100,6 +100,54 @@ def supported(device: torch.device) -> Tuple[bool, str]:
     return True, ""
 
 
+def dma_plan(buckets, shards, pers, world: int, rank: int):
+    """Ranges of the copy-engine overlap (stages 1-2: rank q owns flat
+    elements [q * S, (q + 1) * S) of each group).
+
+    ``buckets[k]`` lists ``(group, lo, hi)`` arena ranges.  Returns
+    ``(sends, covered, remaining)``: ``sends[k]`` lists ``(group, q, e0,
+    e1)``, the part of bucket k that this rank copies to peer q; ``covered``
+    maps each group to the merged parts of this rank's own shard that the
+    buckets bring in, cut to ``pers[group]``-element (16-byte) boundaries;
+    ``remaining`` to the rest of the shard, reduced from the peers' arenas at
+    the step."""
+    sends, mine = [], {i: [] for i in range(len(shards))}
+    for ranges in buckets:
+        out = []
+        for (i, lo, hi) in ranges:
+            S = shards[i]
+            for q in range(world):
+                e0, e1 = max(lo, q * S), min(hi, (q + 1) * S)
+                if e1 <= e0:
+                    continue
+                if q == rank:
+                    mine[i].append((e0, e1))
+                else:
+                    out.append((i, q, e0, e1))
+        sends.append(out)
+    covered, remaining = {}, {}
+    for i, S in enumerate(shards):
+        a, b = rank * S, (rank + 1) * S
+        per = pers[i]
+        merged = []
+        for s0, e0 in sorted(mine[i]):
+            if merged and s0 <= merged[-1][1]:
+                merged[-1] = (merged[-1][0], max(merged[-1][1], e0))
+            else:
+                merged.append((s0, e0))
+        cut = [(-(-s0 // per) * per, e0 // per * per) for s0, e0 in merged]
+        covered[i] = [(s0, e0) for s0, e0 in cut if e0 > s0]
+        rest, pos = [], a
+        for s0, e0 in covered[i]:
+            if s0 > pos:
+                rest.append((pos, s0))
+            pos = max(pos, e0)
+        if pos < b:
+            rest.append((pos, b))
+        remaining[i] = rest
+    return sends, covered, remaining
+
+
 class FusedCollectives:
     name = "fused-nvlink"
 
@@ -117,6 +165,8 @@ class FusedCollectives:
         self.epoch_dev = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._shard32 = {}
         self._step_open = False
+        self.dma = False
+        self.recv: Optional[PeerHeap] = None
         # phase marker of the optimizer's step timing (None: timing off)
         self.marker = None
 
@@ -174,7 +224,71 @@ class FusedCollectives:
             return self.rank * g.shard_size, (self.rank + 1) * g.shard_size
         return g.shard_start, g.shard_end
 
+    # how the buckets reach their owners: "dma" (default) copies each peer's
+    # part of a bucket into that peer's receive slot with the copy engines
+    # as soon as backward has produced it, and the step reduces local slots;
+    # "kernel" runs the fused reduce-scatter kernel per bucket on a second
+    # stream (it competes with backward for the SMs)
+    OVERLAP_MODE = os.environ.get("MINISPEED_OVERLAP_MODE", "dma")
+
     def plan_buckets(self, buckets: List[List[Tuple[int, int, int]]]) -> int:
+        if self.OVERLAP_MODE == "dma" and self.stage in (1, 2):
+            return self._plan_dma(buckets)
+        self.dma = False
+        return self._plan_kernel(buckets)
+
+    def _slot_layout(self, g: FlatParamGroup) -> Tuple[int, int]:
+        """(elements per receive slot, element size).  A slot holds one source
+        rank's copy of an owner's shard, shifted so that every element sits
+        at the same address modulo 16 as in the gradient arena."""
+        esz = g.grad_arena.element_size()
+        return g.shard_size + 16 // esz, esz
+
+    def _plan_dma(self, buckets: List[List[Tuple[int, int, int]]]) -> int:
+        """Copy-engine overlap.  Bucket k's part that rank q owns goes, once
+        backward has produced the bucket, straight into q's receive slot for
+        this rank (one cudaMemcpyAsync per peer, no SMs).  At the step each
+        rank reduces the covered part of its shard from its own arena and its
+        local slots (the fused statistics kernel over a table of local
+        addresses), and the rest (parameters outside the buckets, the
+        unaligned edges) from the peers' arenas as before."""
+        self.dma = True
+        W, me = self.world_size, self.rank
+        regions = []
+        for i, g in enumerate(self.groups):
+            slot, esz = self._slot_layout(g)
+            regions.append((f"recv{i}", W * slot * esz))
+        self.recv = PeerHeap(self.device, regions, me, W)   # collective
+        shards = [g.shard_size for g in self.groups]
+        pers = [16 // g.grad_arena.element_size() for g in self.groups]
+        sends, self.covered, self.remaining = dma_plan(buckets, shards, pers, W, me)
+        self.dma_copies = []
+        for bucket in sends:
+            dst, src, nbytes = [], [], []
+            for (i, q, e0, e1) in bucket:
+                g = self.groups[i]
+                slot, esz = self._slot_layout(g)
+                align = (q * shards[i]) // pers[i] * pers[i]
+                base = self.recv.ptrs[q] + self.recv.offsets[f"recv{i}"] + me * slot * esz
+                dst.append(base + (e0 - align) * esz)
+                src.append(self.heap.ptrs[me] + self.heap.offsets[f"grad{i}"] + e0 * esz)
+                nbytes.append((e1 - e0) * esz)
+            self.dma_copies.append((dst, src, nbytes))
+        self.recv_tab = {}
+        for i, g in enumerate(self.groups):
+            slot, esz = self._slot_layout(g)
+            # local source table: this rank's arena, and for every peer its
+            # slot here, offset so that table[q] + grad_off + e * esz is the
+            # address of element e of this rank's shard
+            align = (me * shards[i]) // pers[i] * pers[i]
+            mine = self.recv.ptrs[me] + self.recv.offsets[f"recv{i}"]
+            goff = self.heap.offsets[f"grad{i}"]
+            tab = [self.heap.ptrs[me] if q == me else
+                   mine + q * slot * esz - goff - align * esz for q in range(W)]
+            self.recv_tab[i] = torch.tensor(tab, dtype=torch.int64, device=self.device)
+        return 0
+
+    def _plan_kernel(self, buckets: List[List[Tuple[int, int, int]]]) -> int:
         """Fix the reduction of gradient buckets that become final during
         backward.  ``buckets[k]`` lists ``(group, lo, hi)`` arena ranges.  Each
         rank reduces ``[lo, hi)`` cut to its shard and to 8-element (16-byte)
@@ -213,21 +327,28 @@ class FusedCollectives:
         return self._shard_out(i, g)[s0 - a:e0 - a]
 
     def _reduce_segment(self, i: int, s0: int, e0: int, mul: float, mul_dev, stats,
-                        slot: int, max_blocks: int, threads: int = 256) -> int:
+                        slot: int, max_blocks: int, threads: int = 256, table=None) -> int:
         g = self.groups[i]
         out = self._out_slice(i, g, s0, e0)
         esz = g.grad_arena.element_size()
         aligned = (s0 * esz) % 16 == 0 and (self.heap.offsets[f"grad{i}"] % 16) == 0
         fan = self.heap.offsets[f"grad32_{i}"] if self.stage == 0 else -1
-        return int(_ext.get().rs_stats(self.heap.heaps, self.heap.offsets[f"grad{i}"],
+        heaps = self.heap.heaps if table is None else table
+        return int(_ext.get().rs_stats(heaps, self.heap.offsets[f"grad{i}"],
                                        DTYPE_CODE[g.grad_arena.dtype], s0, out, self.world_size,
                                        mul, mul_dev, fan, stats.partials, stats.flags, slot,
                                        max_blocks, aligned, threads))
 
     def launch_bucket(self, k: int, mul_dev: torch.Tensor, stats) -> None:
-        """Barrier (every rank has this bucket's gradients), then the
-        reduction of this rank's part of bucket k, on the current stream.
-        The multiplier 1 / loss scale is read from ``mul_dev``."""
+        """Copy mode: bucket k's parts to their owners' receive slots (copy
+        engines, current stream).  Kernel mode: barrier (every rank has this
+        bucket's gradients), then the reduction of this rank's part of bucket
+        k, on the current stream; the multiplier 1 / loss scale is read from
+        ``mul_dev``."""
+        if self.dma:
+            dst, src, nbytes = self.dma_copies[k]
+            _ext.get().copy_many(self.status, dst, src, nbytes)
+            return
         self.barrier()
         slot = k * self.BUCKET_SLOTS
         end = slot + self.BUCKET_SLOTS
@@ -255,8 +376,18 @@ class FusedCollectives:
                 self.marker("barrier")
         if g.grad_arena is not arena:
             raise RuntimeError("gradient arena left the peer heap")
+        if overlapped and self.dma:
+            # the peers' parts of the buckets are in the local slots (their
+            # copies completed before they reached the barrier above)
+            tab = self.recv_tab[i]
+            for s0, e0 in self.covered[i]:
+                left = stats.partials.numel() - stats.used
+                stats.used += self._reduce_segment(i, s0, e0, inv_scale / self.world_size, None,
+                                                   stats, stats.used, min(left, 148 * 8),
+                                                   table=tab)
         if overlapped:
-            # the buckets were reduced during backward: only the rest remains
+            # the buckets were reduced during backward (or sit in the local
+            # slots): the rest comes from the peers' arenas
             for s0, e0 in self.remaining[i]:
                 left = stats.partials.numel() - stats.used
                 stats.used += self._reduce_segment(i, s0, e0, inv_scale / self.world_size, None,
@@ -361,3 +492,6 @@ class FusedCollectives:
         comm.barrier()
         self.heap.close()
         self.heap = None
+        if self.recv is not None:
+            self.recv.close()
+            self.recv = None

@@ -124,6 +124,7 @@ def test_bucket_plan_covers_each_shard_exactly():
     for stage in (0, 2):
         for rank in range(3):
             fc = FusedCollectives.__new__(FusedCollectives)
+            fc.OVERLAP_MODE = "kernel"
             fc.rank, fc.world_size, fc.stage = rank, 3, stage
             g = types.SimpleNamespace(shard_size=1000, shard_start=1000 * rank,
                                       shard_end=1000 * (rank + 1))
@@ -207,3 +208,32 @@ def test_host_staged_collectives_match(stage, tmp_path, monkeypatch):
         for k in p["params"]:
             assert torch.equal(p["params"][k], s["params"][k]), k
         assert torch.equal(p["masters"], s["masters"])
+
+
+def test_dma_plan_sends_each_element_to_its_owner_once():
+    """Copy-engine overlap: every bucket element outside this rank's shard is
+    sent to exactly its owner, and the shard is split into the covered part
+    (16-byte aligned) and the rest without gaps or overlaps."""
+    from minispeed_b200.parallel.fused import dma_plan
+
+    S, W, per = 1000, 3, 8
+    buckets = [[(0, 5, 733)], [(0, 733, 1501)], [(0, 1501, 2999)]]
+    for rank in range(W):
+        sends, covered, remaining = dma_plan(buckets, [S], [per], W, rank)
+        seen = []
+        for k, bucket in enumerate(sends):
+            for (i, q, e0, e1) in bucket:
+                assert q != rank and q * S <= e0 < e1 <= (q + 1) * S
+                lo, hi = buckets[k][0][1], buckets[k][0][2]
+                assert lo <= e0 and e1 <= hi
+                seen.append((e0, e1))
+        seen.sort()
+        total = sum(e1 - e0 for e0, e1 in seen)
+        mine = max(0, min(2999, (rank + 1) * S) - max(5, rank * S))
+        assert total == (2999 - 5) - mine
+        segs = sorted(covered[0] + remaining[0])
+        assert segs[0][0] == rank * S and segs[-1][1] == (rank + 1) * S
+        for (s0, e0), (s1, _) in zip(segs, segs[1:]):
+            assert e0 == s1
+        for s0, e0 in covered[0]:
+            assert s0 % per == 0 and e0 % per == 0

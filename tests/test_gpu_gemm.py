@@ -236,3 +236,27 @@ def test_dgelu_epilogue_column_sums(dtype, M, N, K, _variant):
     out = torch.zeros(N, device="cuda", dtype=dtype)
     _ext.get().colsum_finish(part, groups, out, False)
     torch.testing.assert_close(out.float(), want, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("splits", [2, 4])
+@pytest.mark.parametrize("M,N,K", [(3072, 768, 16384), (2304, 768, 16384), (700, 300, 4096)])
+def test_pair_split_k_fixup(dtype, splits, M, N, K, _variant):
+    """Split-K on the pair kernel with every unit resident: the last split of
+    each tile adds the others' fp32 partials and finishes it (bias and
+    accumulation applied once); two launches in a row (counters reset)."""
+    if _variant != "auto":
+        pytest.skip("forced plan; one variant is enough")
+    torch.manual_seed(M + splits)
+    dy = (torch.randn(K, M, device="cuda") * 0.05).to(dtype)
+    x = (torch.randn(K, N, device="cuda") * 0.05).to(dtype)
+    bias = torch.randn(N, device="cuda").to(dtype)
+    ref = dy.float().t() @ x.float()
+    for _ in range(2):
+        out = gemm.gemm(dy, x, a_kmajor=False, b_kmajor=False, bias=bias, plan=(512, splits))
+        torch.cuda.synchronize()
+        _check(out, ref + bias.float(), K)
+    C0 = torch.randn(M, N, device="cuda").to(dtype)
+    C = C0.clone()
+    gemm.gemm(dy, x, a_kmajor=False, b_kmajor=False, out=C, accumulate=True, plan=(512, splits))
+    _check(C, C0.float() + ref, K)

@@ -104,16 +104,22 @@ def _gpt_worker(rank, stage, overlap, graph, port, out_dir, world=WORLD, comm_mo
         losses.append(float(engine.train_batch(t[:, :-1], targets=t[:, 1:])))
     params = {k: v.detach().float().cpu() for k, v in engine.state_dict().items()}
     torch.save({"losses": torch.tensor(losses), "params": params,
-                "slots": engine.optimizer.overlap_slots, "steps": engine.global_steps,
+                "slots": engine.optimizer.overlap_slots,
+                "planned": engine.optimizer.comm_stream is not None,
+                "dma": bool(getattr(engine.optimizer.coll, "dma", False)),
+                "steps": engine.global_steps,
                 "scale": engine.get_loss_scale(), "coll": engine.collectives},
                os.path.join(out_dir, f"r{rank}.pt"))
     engine.close()
     ms.comm.destroy()
 
 
-@pytest.mark.parametrize("stage,graph", [(0, False), (0, True), (2, False), (2, True),
-                                         (3, False)])
+@pytest.mark.parametrize("stage,graph", [(0, False), (0, True), (1, False), (2, False),
+                                         (2, True), (3, False)])
 def test_overlapped_bucket_reduction_matches_step_reduction(stage, graph, tmp_path):
+    """Buckets reduced during backward (stages 1-2: copied to their owners by
+    the copy engines; stages 0 and 3: the reduction kernel on a second
+    stream) give the same trajectory as the reduction at the step."""
     runs = {}
     for overlap in (False, True):
         d = tmp_path / f"o{int(overlap)}"
@@ -122,7 +128,8 @@ def test_overlapped_bucket_reduction_matches_step_reduction(stage, graph, tmp_pa
                  join=True)
         runs[overlap] = [torch.load(d / f"r{r}.pt", weights_only=False) for r in range(WORLD)]
     off, on = runs[False], runs[True]
-    assert off[0]["slots"] == 0 and on[0]["slots"] > 0       # the buckets were planned
+    assert not off[0]["planned"] and on[0]["planned"]       # the buckets were planned
+    assert on[0]["dma"] == (stage in (1, 2))
     assert on[0]["steps"] == off[0]["steps"] == 6 and on[0]["scale"] == off[0]["scale"]
     torch.testing.assert_close(on[0]["losses"], off[0]["losses"], rtol=2e-3, atol=2e-3)
     for k in off[0]["params"]:
