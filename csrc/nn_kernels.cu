@@ -813,16 +813,35 @@ ce_fwd_grad_kernel(T* __restrict__ logits, const long long* __restrict__ tgt,
   ::msb::pdl_begin();
   const long long r = blockIdx.x;
   T* row = logits + r * ld;
+  const int head = (int)(((16 - (reinterpret_cast<uintptr_t>(row) & 15)) & 15) / sizeof(T));
+  const int h = min(head, V);
+  const int nvec = (V - h) / 8;
+  T* mid = row + h;
+  // Pass 1: running (max, sum) in base-2 units.  The kernel is bound by
+  // instruction issue, not by DRAM, so the middle of the row goes 8 values
+  // at a time: one max and one rescale per vector, then one fma + ex2 + add
+  // per value, without a data-dependent branch.
   float m = -INFINITY, s = 0.f;
-  for_row(static_cast<const T*>(row), V, [&](int, float v) {
+  auto add1 = [&](float v) {
     const float y = v * kLog2e;
-    if (y > m) {
-      s = s * ex2_approx(m - y) + 1.f;
-      m = y;
-    } else {
-      s += ex2_approx(y - m);
-    }
-  });
+    const float mn = fmaxf(m, y);
+    s = s * ex2_approx(m - mn) + ex2_approx(y - mn);
+    m = mn;
+  };
+  for (int i = threadIdx.x; i < h; i += blockDim.x) add1(to_f32(row[i]));
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    float v[8];
+    load8(mid + i * 8, v);
+    float mx = v[0];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) mx = fmaxf(mx, v[k]);
+    const float mn = fmaxf(m, mx * kLog2e);
+    s *= ex2_approx(m - mn);   // m = -inf: 0 (s is 0 then)
+    m = mn;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += ex2_approx(fmaf(v[k], kLog2e, -mn));
+  }
+  for (int i = h + nvec * 8 + threadIdx.x; i < V; i += blockDim.x) add1(to_f32(row[i]));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
@@ -857,32 +876,30 @@ ce_fwd_grad_kernel(T* __restrict__ logits, const long long* __restrict__ tgt,
     }
   }
   __syncthreads();   // every thread has read the row before it is overwritten
-  const float l = s_lse;
+  // Pass 2: dlogits[i] = softmax[i] * scale (- scale at the target), with the
+  // scale folded into the exponent: 2^(v log2 e - lse log2 e + log2 scale).
+  // scale = 0 (an ignored target) gives -inf there and zeros.
   const float scale = valid ? g_hint[0] * inv_count[0] : 0.f;
-  const int head = (int)(((16 - (reinterpret_cast<uintptr_t>(row) & 15)) & 15) / sizeof(T));
-  const int h = min(head, V);
-  auto g = [&](int i, float v) {
-    return (ex2_approx((v - l) * kLog2e) - (i == t ? 1.f : 0.f)) * scale;
+  const float base = (scale > 0.f ? log2f(scale) : -INFINITY) - s_lse * kLog2e;
+  auto g1 = [&](int i, float v) {
+    return ex2_approx(fmaf(v, kLog2e, base)) - (i == t ? scale : 0.f);
   };
-  // the same with 2^x on the FMA pipe (exp2_poly: relative error 7.5e-5,
-  // under half a 16-bit ulp of the stored gradient)
-  auto gp = [&](int i, float v) {
-    return (exp2_poly((v - l) * kLog2e) - (i == t ? 1.f : 0.f)) * scale;
-  };
-  for (int i = threadIdx.x; i < h; i += blockDim.x) row[i] = from_f32<T>(g(i, to_f32(row[i])));
-  const int nvec = (V - h) / 8;
-  T* mid = row + h;
+  for (int i = threadIdx.x; i < h; i += blockDim.x) row[i] = from_f32<T>(g1(i, to_f32(row[i])));
   for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
     float v[8];
     load8(mid + i * 8, v);
-    // half of the exponentials on the special-function unit, half on the
-    // FMA pipe: pass 1 already keeps the special-function unit busy
 #pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = (k & 1) ? gp(h + i * 8 + k, v[k]) : g(h + i * 8 + k, v[k]);
+    for (int k = 0; k < 8; ++k) v[k] = ex2_approx(fmaf(v[k], kLog2e, base));
+    const long long kt = t - (h + (long long)i * 8);   // the target inside this vector?
+    if (kt >= 0 && kt < 8) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k == kt) v[k] -= scale;
+    }
     store8(mid + i * 8, v);
   }
   for (int i = h + nvec * 8 + threadIdx.x; i < V; i += blockDim.x)
-    row[i] = from_f32<T>(g(i, to_f32(row[i])));
+    row[i] = from_f32<T>(g1(i, to_f32(row[i])));
 }
 
 // Backward of the fused forward: the stored gradient assumed the upstream

@@ -65,11 +65,11 @@ class B200Options:
     rank owns a distinct GPU of one node and falls back to NCCL otherwise;
     ``"nccl"`` forces the library path; ``"fused"`` requires the fused path.
     ``bucket_mb``: gradient bucket size for backward/communication overlap.
-    ``overlap``: reduce each model block's gradients (fused collectives) as
+    ``overlap``: move each model block's gradients (fused collectives) as
     soon as backward has produced them, on a second stream, instead of after
-    backward (env ``MINISPEED_OVERLAP=1``).  Off by default: on 2 B200s it
-    hides 0.55 of 0.77 ms of exposed communication but slows the concurrent
-    backward kernels by more (23.2 -> 24.0 ms per GPT-2 step).
+    backward (env ``MINISPEED_OVERLAP=1``).  At stages 1-2 the copy engines
+    send each peer its part of the block (the step then reduces local
+    copies); at stages 0 and 3 the reduction kernel runs per block.
     ``wait_timeout_ms``: bound on every cross-GPU spin inside fused kernels;
     past it the kernel reports an error status instead of waiting forever.
     ``cuda_graph``: ``engine.train_batch`` replays forward + backward as one
