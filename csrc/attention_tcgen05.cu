@@ -446,6 +446,27 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
       if (warp == 2 && lane == 0) ATTN_ADD(2, t_rs);
       ATTN_T0(t_p2);
       const float mref = m_used == -INFINITY ? 0.f : m_used;
+      // P = 2^(s - m) as packed 16-bit pairs, first into registers: the
+      // exponentials do not depend on the tile's previous P V, only the
+      // store of P into its (single) tensor-memory buffer does, so they run
+      // while that P V is still on the tensor core.  A share of them (p.poly
+      // of every 4, off by default) can go to exp2_poly on the FMA pipe.
+      uint32_t pk[64];
+      auto make_p = [&](auto share) {
+        constexpr int PC = decltype(share)::value;
+#pragma unroll
+        for (int e = 0; e < 64; ++e) {
+          const float xa = fmaf(__uint_as_float(sv[2 * e]), p.scale_log2, -mref);
+          const float xb = fmaf(__uint_as_float(sv[2 * e + 1]), p.scale_log2, -mref);
+          const float a = ex2(xa);
+          const float bb = (PC >= 2 || (PC == 1 && (e & 1))) ? exp2_poly(xb) : ex2(xb);
+          l += a + bb;
+          pk[e] = pack2<T>(a, bb);
+        }
+      };
+      if (p.poly <= 0) make_p(std::integral_constant<int, 0>{});
+      else if (p.poly == 1) make_p(std::integral_constant<int, 1>{});
+      else make_p(std::integral_constant<int, 2>{});
       if (SEP_P && j > 0) {
         // P and O of this tile are free once its previous P V retired
         if (!warp_wait_f(smem_u32(&bars->pv_done[t]), (j - 1) & 1, abort, p, 30, lane)) {
@@ -454,30 +475,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
         }
         tc_fence_after();
       }
-      // P = 2^(s - m) as packed 16-bit pairs.  The special-function unit
-      // that ex2 runs on bounds this loop at head dim 64 (128 exponentials
-      // per row per key tile against 2 x 64-deep MMAs), so a share of the
-      // exponentials (p.poly of every 4) goes to exp2_poly on the FMA pipe.
-      auto write_p = [&](auto share) {
-        constexpr int PC = decltype(share)::value;
 #pragma unroll
-        for (int hh = 0; hh < 4; ++hh) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float xa = fmaf(__uint_as_float(sv[hh * 32 + 2 * e]), p.scale_log2, -mref);
-            const float xb = fmaf(__uint_as_float(sv[hh * 32 + 2 * e + 1]), p.scale_log2, -mref);
-            const float a = ex2(xa);
-            const float bb = (PC >= 2 || (PC == 1 && (e & 1))) ? exp2_poly(xb) : ex2(xb);
-            l += a + bb;
-            pk[e] = pack2<T>(a, bb);
-          }
-          tmem_st16(lane_base + cp + hh * 16, pk);
-        }
-      };
-      if (p.poly <= 0) write_p(std::integral_constant<int, 0>{});
-      else if (p.poly == 1) write_p(std::integral_constant<int, 1>{});
-      else write_p(std::integral_constant<int, 2>{});
+      for (int hh = 0; hh < 4; ++hh)
+        tmem_st16(lane_base + cp + hh * 16, *reinterpret_cast<uint32_t(*)[16]>(pk + hh * 16));
       if (__any_sync(0xffffffffu, grow && j > 0)) {
         // O is stable: this tile's previous P V retired (waited for above, or
         // before its S was issued), and its next P V waits for p_full
