@@ -131,8 +131,12 @@ class DeepSpeedEngine:
         self._consumed_boundary = -1
         self.grad_norm: Optional[float] = None
         self._window_open = False
-        self._graph = None          # MicroStepGraph of train_batch (CUDA graphs)
-        self._graph_eager = 0       # eager micro-steps run for the current signature
+        # captured micro-steps of train_batch (CUDA graphs), one per signature:
+        # with gradient accumulation and overlap, the window's last micro-step
+        # (which launches the bucket transfers) differs from the others
+        self._graphs = {}
+        self._graph = None          # the graph replayed last
+        self._graph_eager = {}      # eager micro-steps run per signature
         self._overlap_now = False   # this micro-step's backward reduces buckets
         self._bucket_hooks = self._setup_overlap() + self._setup_layer_gather()
 
@@ -366,30 +370,38 @@ class DeepSpeedEngine:
         self._begin_micro_step()
         sig, _ = signature(args, kwargs)
         sig = (sig, self._overlap_now)
-        st = self._graph
-        if st is None or st.sig != sig or (st.graph is not None and not st.valid()):
-            if st is not None:
-                st.release()
-            self._graph = st = None
+        st = self._graphs.get(sig)
+        if st is not None and st.graph is not None and not st.valid():
+            st.release()
+            del self._graphs[sig]
+            st = None
+        if st is None:
             side = self._graph_stream()
             cur = torch.cuda.current_stream(self.device)
             side.wait_stream(cur)
-            if self._graph_eager < self.config.b200.graph_warmup:
+            n = self._graph_eager.get(sig, 0)
+            if n < self.config.b200.graph_warmup:
                 # eager micro-steps first (GEMM autotuning, lazy library
                 # state), on the stream the capture will use
-                self._graph_eager += 1
+                self._graph_eager[sig] = n + 1
                 with torch.cuda.stream(side):
                     loss = self.forward(*self._to_device(args), **self._to_device(kwargs))
                     self.backward(loss)
                 cur.wait_stream(side)
                 return loss
+            if len(self._graphs) >= self.MAX_GRAPHS:
+                # the signature replayed longest ago goes (inputs of new shapes)
+                old = next(iter(self._graphs))
+                self._graphs.pop(old).release()
             torch.cuda.empty_cache()
             st = MicroStepGraph(self, args, kwargs)
             st.sig = sig            # inputs and whether the bucket reductions are captured
             st.capture(side)
             cur.wait_stream(side)
-            self._graph = st
-        self._graph_eager = 0
+            self._graphs[sig] = st
+        else:
+            self._graphs[sig] = self._graphs.pop(sig)   # most recently used last
+        self._graph = st
         factor = self.loss_scaler.loss_scale_factor
         if self.gas > 1:
             factor /= self.gas
@@ -413,12 +425,15 @@ class DeepSpeedEngine:
             self._side_stream = torch.cuda.Stream(self.device)
         return self._side_stream
 
+    MAX_GRAPHS = 4      # captured micro-step signatures kept at once
+
     def release_graphs(self) -> None:
-        """Drop the captured micro-step graph and its memory pool."""
-        if self._graph is not None:
-            self._graph.release()
-            self._graph = None
-        self._graph_eager = 0
+        """Drop the captured micro-step graphs and their memory pools."""
+        for st in self._graphs.values():
+            st.release()
+        self._graphs = {}
+        self._graph = None
+        self._graph_eager = {}
 
     # ---------------------------------------------------------------- step
     def step(self) -> bool:

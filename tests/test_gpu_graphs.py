@@ -150,3 +150,25 @@ def test_device_timers_on_gpu(graph):
     if not graph:
         assert times.get("forward", 0) > 0, times
     assert sum(times.values()) < wall_ms, (times, wall_ms)
+
+
+def test_alternating_signatures_keep_their_graphs():
+    """Two input shapes used in turn: each gets its own captured graph once
+    (after its eager warm-up micro-steps) and both are replayed from then on,
+    with the same losses as the eager engine."""
+    data = _batches(12)
+    runs = []
+    for graph in (False, True):
+        eng, _ = _engine(2, 1, graph)
+        losses = []
+        for k, t in enumerate(data):
+            t = t.cuda()
+            if k % 2:
+                t = t[:, : CFG["block_size"] // 2 + 1]     # the other signature
+            losses.append(float(eng.train_batch(t[:, :-1], targets=t[:, 1:])))
+        if graph:
+            assert len(eng._graphs) == 2
+            assert sorted(g.replays for g in eng._graphs.values()) == [4, 4]
+        runs.append(torch.tensor(losses))
+        eng.close()
+    torch.testing.assert_close(runs[1], runs[0], rtol=2e-3, atol=2e-3)
