@@ -2,8 +2,9 @@
 persistent head-dim-64 attention backward (``attn_bwd64_kernel``), the
 head-dim-128 backward (``attn_bwd128_kernel``) and the attention forward's
 event loop (``attn_fwd_kernel``), all in ``csrc/attention_tcgen05.cu``,
-the 1-CTA and 2-CTA GEMMs (``csrc/gemm_tcgen05.cu``), and the cross-GPU
-epoch protocol of the fused NVLink step (``csrc/collectives.cu``).
+the 1-CTA and 2-CTA GEMMs (``csrc/gemm_tcgen05.cu``, including the
+stream-K and split-K fixup tile hand-off between CTA pairs), and the
+cross-GPU epoch protocol of the fused NVLink step (``csrc/collectives.cu``).
 
 The kernel's roles (TMA warp, MMA warp, softmax warps, dQ warps) synchronise
 only through mbarriers whose waits name a phase parity.  A wrong parity is a
@@ -761,3 +762,139 @@ def test_fused_step_needs_the_closing_barrier():
         except AssertionError:
             failures += 1
     assert failures > 0
+
+
+# ---------------------------------------------------------------------------
+# Stream-K and split-K fixup of the pair GEMM (gemm2_kernel): which pair
+# finishes which tile, the per-tile counters, and termination.  Mirrors
+# sk_range / sk_pair_of / work_item and the epilogue's contrib / finish roles.
+
+WARPS = 16          # epilogue warps of a CTA pair: each arrives once
+
+
+def sk_range(pair, per, extra):
+    b = pair * per + min(pair, extra)
+    return b, b + per + (1 if pair < extra else 0)
+
+
+def sk_pair_of(it, per, extra):
+    big = extra * (per + 1)
+    if it < big:
+        return it // (per + 1)
+    return extra + (it - big) // per
+
+
+def sk_items(pair, kbt, per, extra):
+    b, e = sk_range(pair, per, extra)
+    k, out = 0, []
+    while True:
+        t = b // kbt + k
+        lo, hi = max(b, t * kbt), min(e, (t + 1) * kbt)
+        if lo >= hi:
+            return out
+        out.append((t, lo - t * kbt, hi - t * kbt))
+        k += 1
+
+
+def stream_k_plan(tiles, kbt, npairs):
+    total = tiles * kbt
+    per, extra = total // npairs, total % npairs
+    plan = []
+    for pair in range(npairs):
+        items = []
+        for (t, kb0, kb1) in sk_items(pair, kbt, per, extra):
+            contrib = kb0 > 0
+            finish = kb0 == 0 and kb1 < kbt
+            n = sk_pair_of((t + 1) * kbt - 1, per, extra) - pair if finish else 0
+            items.append(dict(tile=t, kb0=kb0, kb1=kb1, contrib=contrib, finish=finish,
+                              wait=WARPS * n, slots=[pair + j for j in range(1, n + 1)],
+                              slot=pair))
+        plan.append(items)
+    return plan
+
+
+def fixup_plan(tiles, splits):
+    """Split-K with every unit resident: unit = split * tiles + tile, one per pair."""
+    plan = []
+    for u in range(tiles * splits):
+        split, t = divmod(u, tiles)
+        last = split == splits - 1
+        plan.append([dict(tile=t, kb0=split, kb1=split + 1, contrib=not last, finish=last,
+                          wait=WARPS * (splits - 1) if last else 0,
+                          slots=[s * tiles + t for s in range(splits - 1)] if last else [],
+                          slot=split * tiles + t)])
+    return plan
+
+
+def run_tiles(plan, tiles, kbt, seed):
+    """Execute every pair's items in order under a random interleaving of
+    the pairs (warps of a pair step together); a finisher blocks until its
+    counter reaches the target.  Returns the K slices each tile summed."""
+    rng = random.Random(seed)
+    ctr = [0] * tiles
+    slots = {}
+    summed = {t: [] for t in range(tiles)}
+    pos = [0] * len(plan)
+    while True:
+        live = [p for p in range(len(plan)) if pos[p] < len(plan[p])]
+        if not live:
+            break
+        ready = []
+        for p in live:
+            it = plan[p][pos[p]]
+            if not it["finish"] or ctr[it["tile"]] >= it["wait"]:
+                ready.append(p)
+        assert ready, "deadlock: every live pair waits"
+        p = rng.choice(ready)
+        it = plan[p][pos[p]]
+        rng_slices = list(range(it["kb0"], it["kb1"]))
+        t = it["tile"]
+        if it["contrib"]:
+            assert it["slot"] not in slots          # a slot holds one partial at a time
+            slots[it["slot"]] = (t, rng_slices)
+            ctr[t] += WARPS
+        elif it["finish"]:
+            got = list(rng_slices)
+            for s in it["slots"]:
+                tt, sl = slots.pop(s)
+                assert tt == t                      # the slot holds this tile's partial
+                got += sl
+            summed[t].append(sorted(got))
+            # the 16 finishing warps count out; the last one clears the counter
+            ctr[t] += WARPS
+            assert ctr[t] == it["wait"] + WARPS
+            ctr[t] = 0
+        else:
+            summed[t].append(rng_slices)
+        pos[p] += 1
+    assert all(c == 0 for c in ctr), "a counter was left raised"
+    assert not slots, "a partial was never consumed"
+    for t in range(tiles):
+        assert summed[t] == [list(range(kbt))], (t, summed[t])
+
+
+@pytest.mark.parametrize("tiles,kbt,npairs", [(36, 256, 74), (27, 256, 74), (2, 65, 74),
+                                              (192, 48, 74), (9, 256, 74), (5, 7, 31)])
+def test_stream_k_finishes_every_tile_once(tiles, kbt, npairs):
+    if tiles * kbt < npairs:
+        pytest.skip("the host falls back to units below one slice per pair")
+    plan = stream_k_plan(tiles, kbt, npairs)
+    # a finisher is always its pair's last item and waits only for later
+    # pairs' first items, which never wait: no cycle is possible
+    for p, items in enumerate(plan):
+        for k, it in enumerate(items):
+            if it["finish"]:
+                assert k == len(items) - 1
+                for q in it["slots"]:
+                    assert q > p and plan[q][0]["contrib"] and plan[q][0]["tile"] == it["tile"]
+            if it["contrib"]:
+                assert k == 0
+    for seed in range(20):
+        run_tiles(plan, tiles, kbt, seed)
+
+
+@pytest.mark.parametrize("tiles,splits", [(36, 2), (27, 2), (9, 8), (18, 4)])
+def test_split_k_fixup_finishes_every_tile_once(tiles, splits):
+    plan = fixup_plan(tiles, splits)
+    for seed in range(20):
+        run_tiles(plan, tiles, splits, seed)
