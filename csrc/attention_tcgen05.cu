@@ -1191,7 +1191,7 @@ attn_bwd64_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_consta
         fence_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_reduce_add_2d(&tm_dq, smem_u32(stg), h * D + 16 * cc, row);
+          tma_reduce_add_2d<4>(&tm_dq, smem_u32(stg), h * D + 16 * cc, row);
           bulk_commit();
         }
       }
@@ -1616,7 +1616,7 @@ attn_bwd128_kernel(const __grid_constant__ CUtensorMap tm_qkv,
         if (lane == 0) {
 #pragma unroll
           for (int c = 0; c < 2; ++c)
-            tma_reduce_add_2d(&tm_dq, smem_u32(stg + c * 4096), h * D + half * 64 + 32 * c,
+            tma_reduce_add_2d<4>(&tm_dq, smem_u32(stg + c * 4096), h * D + half * 64 + 32 * c,
                               row0 + i * 128 + quarter * 32);
           bulk_commit();
         }
@@ -1808,5 +1808,7 @@ void attention_bwd(const void* qkv, long long ld_qkv, long long n_cols, int q_co
   }
   MSB_CHECK_LAUNCH("attention_bwd");
 }
+
+MSB_BOUNDS_TU(attention)
 
 }  // namespace msb

@@ -176,6 +176,31 @@ void colsum_finish(const at::Tensor& part, int64_t nparts, const at::Tensor& out
                      dtype_code(out), accumulate ? 1 : 0, stream_of(out));
 }
 
+// Several column-sum finishes in as few launches as possible (one per
+// kMaxColsumJobs); every output has the same dtype and device.
+void colsum_finish_many(const std::vector<at::Tensor>& parts, const std::vector<int64_t>& nparts,
+                        const std::vector<at::Tensor>& outs, const std::vector<bool>& accumulate) {
+  const size_t n = outs.size();
+  TORCH_CHECK(parts.size() == n && nparts.size() == n && accumulate.size() == n,
+              "colsum_finish_many: list lengths differ");
+  if (n == 0) return;
+  std::vector<msb::ColsumJob> jobs(n);
+  for (size_t i = 0; i < n; ++i) {
+    check_cuda_contig(outs[i], "out");
+    TORCH_CHECK(outs[i].scalar_type() == outs[0].scalar_type() &&
+                    outs[i].device() == outs[0].device(),
+                "colsum_finish_many: outputs differ in dtype or device");
+    TORCH_CHECK(parts[i].scalar_type() == at::kFloat && parts[i].is_contiguous() &&
+                    parts[i].device() == outs[0].device(),
+                "colsum_finish_many: partials must be contiguous fp32 on the outputs' device");
+    TORCH_CHECK(parts[i].numel() >= nparts[i] * outs[i].numel(), "partial buffer too small");
+    jobs[i] = {parts[i].data_ptr<float>(), outs[i].data_ptr(), (int)nparts[i],
+               (int)outs[i].numel(), accumulate[i] ? 1 : 0};
+  }
+  c10::cuda::CUDAGuard g(outs[0].device());
+  msb::colsum_finish_many(jobs.data(), (int)n, dtype_code(outs[0]), stream_of(outs[0]));
+}
+
 void accum_cast(const at::Tensor& src, const at::Tensor& dst, bool accumulate) {
   check_cuda_contig(src, "src");
   check_cuda_contig(dst, "dst");
@@ -723,6 +748,25 @@ void gather_range_py(const at::Tensor& heaps, int64_t shard_off, int64_t shard, 
 
 }  // namespace
 
+// Records of the bounds-checked debug build, one per translation unit with
+// checks: (unit, failed checks, site of the first failure, its index, its
+// limit).  All zero in the release build.
+std::vector<std::tuple<std::string, int64_t, int64_t, int64_t, int64_t>> bounds_status(
+    bool reset) {
+  using Reader = void (*)(msb::BoundsRecord*, bool);
+  const std::pair<const char*, Reader> units[] = {{"nn", &msb::bounds_read_nn},
+                                                  {"gemm", &msb::bounds_read_gemm},
+                                                  {"attention", &msb::bounds_read_attention}};
+  std::vector<std::tuple<std::string, int64_t, int64_t, int64_t, int64_t>> out;
+  for (const auto& u : units) {
+    msb::BoundsRecord r{};
+    u.second(&r, reset);
+    out.emplace_back(u.first, (int64_t)r.count, (int64_t)r.site, (int64_t)r.index,
+                     (int64_t)r.limit);
+  }
+  return out;
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, mod) {
   mod.doc() = "minispeed_b200 sm_100a kernels";
   mod.def("grad_stats", &grad_stats);
@@ -731,12 +775,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, mod) {
   mod.def("adamw", &adamw);
   mod.def("cast_scale", &cast_scale);
   mod.def("launch_count", &msb::launch_count);
+  mod.def("bounds_check_build", &msb::bounds_check_build);
+  mod.def("bounds_status", &bounds_status);
   mod.def("count_launches", [](int64_t n) { msb::count_launch((int)n); },
           "add n to the launch counter (kernels replayed from a captured CUDA graph)");
   mod.def("add_norm_fwd", &add_norm_fwd);
   mod.def("norm_bwd", &norm_bwd);
   mod.def("colsum_partial", &colsum_partial);
   mod.def("colsum_finish", &colsum_finish);
+  mod.def("colsum_finish_many", &colsum_finish_many);
   mod.def("accum_cast", &accum_cast);
   mod.def("bias_gelu_fwd", &bias_gelu_fwd);
   mod.def("gelu_bwd", &gelu_bwd);

@@ -73,6 +73,44 @@ inline void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
 
 constexpr int kNumSMs = 148;
 
+// Bounds checks (see BoundsRecord).  MSB_INB(i, n, site): i in [0, n);
+// MSB_CHECK(cond, site, i, n): an invariant.  Both are `true` in the release
+// build.  MSB_OK(cond, site, i, n): a condition the release build tests as
+// well (an out-of-range token id reads as a zero row there); the debug build
+// also records its failure.  MSB_BOUNDS_TU(name) defines the translation
+// unit's bounds_read_<name>.
+#ifdef MSB_BOUNDS_CHECK
+static __device__ BoundsRecord g_bounds;
+static __device__ __noinline__ bool bounds_fail(int site, long long index, long long limit) {
+  if (atomicAdd(&g_bounds.count, 1ull) == 0ull) {
+    g_bounds.site = site;
+    g_bounds.index = index;
+    g_bounds.limit = limit;
+  }
+  return false;
+}
+#define MSB_INB(i, n, site)                                                  \
+  (((long long)(i) >= 0 && (long long)(i) < (long long)(n)) ||               \
+   ::msb::bounds_fail((site), (long long)(i), (long long)(n)))
+#define MSB_CHECK(cond, site, i, n) \
+  ((cond) || ::msb::bounds_fail((site), (long long)(i), (long long)(n)))
+#define MSB_OK(cond, site, i, n) MSB_CHECK(cond, site, i, n)
+#define MSB_BOUNDS_TU(NAME)                                                          \
+  void bounds_read_##NAME(BoundsRecord* out, bool reset) {                           \
+    check_cuda(cudaMemcpyFromSymbol(out, g_bounds, sizeof(BoundsRecord)), "bounds"); \
+    if (reset) {                                                                     \
+      const BoundsRecord z = {0ull, 0, 0, 0};                                        \
+      check_cuda(cudaMemcpyToSymbol(g_bounds, &z, sizeof z), "bounds reset");        \
+    }                                                                                \
+  }
+#else
+#define MSB_INB(i, n, site) true
+#define MSB_CHECK(cond, site, i, n) true
+#define MSB_OK(cond, site, i, n) (cond)
+#define MSB_BOUNDS_TU(NAME) \
+  void bounds_read_##NAME(BoundsRecord* out, bool) { *out = BoundsRecord{0ull, 0, 0, 0}; }
+#endif
+
 __device__ __forceinline__ float to_f32(float x) { return x; }
 __device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
 __device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }

@@ -87,6 +87,8 @@ struct Params {
   // mode 2: column sums of the stored output (the fc bias gradient), one
   // fp32 partial row per 32 output rows: [ceil(M / 32), N]
   float* colsum_part;
+  long long ws_floats;  // workspace and counter sizes (bounds checks of the debug build)
+  long long sk_ctr_n;
   uint32_t idesc;
   unsigned* err;
   unsigned long long timeout_ns;
@@ -370,12 +372,16 @@ __device__ __forceinline__ void chunk_colsum(const Params& p, int row0, int col,
       x[j] = keep + __shfl_xor_sync(0xffffffffu, send, w);
     }
   }
-  if (lane < nvalid) p.colsum_part[(long long)(row0 >> 5) * p.N + col + lane] = x[0];
+  const long long ci = (long long)(row0 >> 5) * p.N + col + lane;
+  if (lane < nvalid && MSB_INB(ci, (long long)((p.M + 31) >> 5) * p.N, kSiteGemmColsum))
+    p.colsum_part[ci] = x[0];
 }
 
 __device__ __forceinline__ void store_ws_chunk(const Params& p, int split, int row, int col,
                                                const float (&v)[32], int nvalid) {
-  float* w = p.ws + ((long long)split * p.M + row) * p.N + col;
+  const long long wi = ((long long)split * p.M + row) * p.N + col;
+  if (!MSB_INB(wi + nvalid - 1, p.ws_floats, kSiteGemmSlot)) return;
+  float* w = p.ws + wi;
   if (nvalid == 32 && p.ws_vec) {
 #pragma unroll
     for (int q = 0; q < 8; ++q)
@@ -652,6 +658,7 @@ __device__ __forceinline__ bool wait2_w(uint32_t bar, uint32_t parity, volatile 
 }
 __device__ __forceinline__ void tma_load_pair_w(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                                 int x, int y) {
+  if (!MSB_CHECK((x & 7) == 0, kSiteTmaLoadX, x, 8)) x &= ~7;   // as tma_load_2d_w
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"
@@ -912,7 +919,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         ncontrib = p.fix ? p.splits - 1
                          : sk_pair_of(p, (long long)(tile + 1) * p.kb_total - 1) - pair_id;
         // all 16 epilogue warps of each contributing pair have arrived
-        if (!sk_wait_w(p.sk_ctr + tile, 16 * ncontrib, abort, p, 15, lane)) break;
+        if (MSB_INB(tile, p.sk_ctr_n, kSiteGemmCounter) &&
+            !sk_wait_w(p.sk_ctr + tile, 16 * ncontrib, abort, p, 15, lane))
+          break;
       }
       const int row0 = m0 + HALF * rank + quarter * 32;
       const int row = m0 + row_in_tile;
@@ -933,9 +942,12 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
           // the whole 32-column piece of the row, in or out of C: the
           // finisher reads back exactly what it needs
           float4* w = reinterpret_cast<float4*>(p.ws + my_slot * (TM * BN2)) + slot_off;
+          if (MSB_INB(my_slot * (TM * BN2) + (slot_off + 7 * 32) * 4 + 3, p.ws_floats,
+                      kSiteGemmSlot)) {
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            w[q * 32] = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+            for (int q = 0; q < 8; ++q)
+              w[q * 32] = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+          }
           continue;
         }
         const int col = n0 + c * 32;
@@ -945,6 +957,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
             const long long slot =
                 p.fix ? (long long)(j - 1) * ntiles + tile : (long long)(pair_id + j);
             const float4* w = reinterpret_cast<const float4*>(p.ws + slot * (TM * BN2)) + slot_off;
+            if (!MSB_INB(slot * (TM * BN2) + (slot_off + 7 * 32) * 4 + 3, p.ws_floats,
+                         kSiteGemmSlot))
+              continue;
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
               const float4 x = __ldcg(w + q * 32);
@@ -974,12 +989,13 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         // release: this warp's partial rows are visible before its arrival
         __threadfence();
         __syncwarp();
-        if (lane == 0) atomicAdd(p.sk_ctr + tile, 1);
+        if (lane == 0 && MSB_INB(tile, p.sk_ctr_n, kSiteGemmCounter)) atomicAdd(p.sk_ctr + tile, 1);
       } else if (finish) {
         // the 16 finishing warps count out; the last one clears the counter
         // for the next launch
         __syncwarp();
-        if (lane == 0 && atomicAdd(p.sk_ctr + tile, 1) == 16 * ncontrib + 15)
+        if (lane == 0 && MSB_INB(tile, p.sk_ctr_n, kSiteGemmCounter) &&
+            atomicAdd(p.sk_ctr + tile, 1) == 16 * ncontrib + 15)
           atomicExch(p.sk_ctr + tile, 0);
       }
     }
@@ -1246,6 +1262,8 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
             (static_cast<uint32_t>(tm >> 4) << 24);
   p.err = err;
   p.timeout_ns = static_cast<unsigned long long>(timeout_s * 1e9);
+  p.ws_floats = ws != nullptr ? ws_floats : 0;
+  p.sk_ctr_n = sk_ctr != nullptr ? sk_ctr_n : 0;
 
   // operand maps: K-major [rows, K] -> box {64, rows staged per CTA};
   // MN-major [K, rows] -> box {64, 64}
@@ -1317,5 +1335,7 @@ void gemm_tcgen05(const void* A, long long lda, int a_mn, const void* B, long lo
     MSB_CHECK_LAUNCH("splitk_reduce");
   }
 }
+
+MSB_BOUNDS_TU(gemm)
 
 }  // namespace msb

@@ -15,6 +15,34 @@ enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
 long long launch_count();
 void count_launch(int n);
 
+// ---- bounds-checked debug build (-DMSB_BOUNDS_CHECK: the extension
+// minispeed_b200._C_debug).  Every translation unit with checks keeps one
+// record on the device: how many checks failed, and the site, index and
+// limit of the first failure.  A failed check skips its access (a TMA load
+// moves its x coordinate down to the aligned one, so its barrier still
+// completes) and the kernel runs on; nothing traps.  The release build
+// compiles every check away.
+enum BoundsSite : int {
+  kSiteNone = 0,
+  kSiteEmbeddingToken = 1,  // token id outside [0, vocab) (embedding forward / backward)
+  kSiteTarget = 2,          // cross-entropy target outside [0, V), not ignore_index
+  kSiteTmaLoadX = 3,        // TMA load whose x coordinate is not 16-byte aligned
+  kSiteTmaStoreXY = 4,      // TMA store / reduce at a negative or unaligned coordinate
+  kSiteGemmSlot = 5,        // split-K / stream-K partial beyond the workspace
+  kSiteGemmCounter = 6,     // stream-K / fixup tile counter beyond the counter array
+  kSiteGemmColsum = 7,      // dGELU column-sum partial beyond [ceil(M / 32), N]
+  kSiteCount = 8
+};
+struct BoundsRecord {
+  unsigned long long count;
+  long long site, index, limit;
+};
+bool bounds_check_build();
+// one per translation unit: copy its record out, zero it when reset
+void bounds_read_nn(BoundsRecord* out, bool reset);
+void bounds_read_gemm(BoundsRecord* out, bool reset);
+void bounds_read_attention(BoundsRecord* out, bool reset);
+
 // ---- step pipeline (step_kernels.cu)
 int grad_stats(const void* x, int dtype, long long n, float mul, float* partials,
                unsigned* flags, int max_blocks, cudaStream_t stream);
@@ -38,6 +66,19 @@ int colsum_partial(const void* a, float* part, int M, int N, long long ld, int d
                    int max_chunks, cudaStream_t st);
 void colsum_finish(const float* part, int nparts, int N, void* out, int dtype, int accumulate,
                    cudaStream_t st);
+// One finish of a column-sum reduction: out[c] (+)= sum over the nparts fp32
+// partial rows part[p * N + c].  colsum_finish_many runs up to
+// kMaxColsumJobs of them (one output dtype) per launch; the jobs travel as
+// the kernel's parameter, so a captured CUDA graph holds them by value.
+struct ColsumJob {
+  const float* part;
+  void* out;
+  int nparts;
+  int N;
+  int accumulate;
+};
+constexpr int kMaxColsumJobs = 48;
+void colsum_finish_many(const ColsumJob* jobs, int njobs, int dtype, cudaStream_t st);
 void accum_cast(const float* src, void* dst, long long n, int dtype, int accumulate,
                 cudaStream_t st);
 void bias_gelu_fwd(void* u, const void* bias, void* h, long long total, int N, int dtype,

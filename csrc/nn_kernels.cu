@@ -509,14 +509,14 @@ colsum_partial_kernel(const T* __restrict__ a, float* __restrict__ part, int M, 
   }
 }
 
-// out[c] (+)= sum_p part[p][c]: block = 32 columns x 8 warps over the parts.
+// out[c] (+)= sum_p part[p][c] for the 32 columns of column block `cb`:
+// 8 warps over the parts, then one warp adds the 8 sums in warp order.
 template <typename T>
-__global__ void __launch_bounds__(256)
-colsum_finish_kernel(const float* __restrict__ part, int nparts, int N, T* __restrict__ out,
-                     int accumulate) {
-  ::msb::pdl_begin();
+__device__ __forceinline__ void colsum_finish_block(const float* __restrict__ part, int nparts,
+                                                    int N, T* __restrict__ out, int accumulate,
+                                                    int cb) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = blockIdx.x * 32 + lane;
+  const int c = cb * 32 + lane;
   float t = 0.f;
   if (c < N)
     for (int q = warp; q < nparts; q += 8) t += part[(size_t)q * N + c];
@@ -530,6 +530,34 @@ colsum_finish_kernel(const float* __restrict__ part, int nparts, int N, T* __res
     if (accumulate) acc += to_f32(out[c]);
     out[c] = from_f32<T>(acc);
   }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+colsum_finish_kernel(const float* __restrict__ part, int nparts, int N, T* __restrict__ out,
+                     int accumulate) {
+  ::msb::pdl_begin();
+  colsum_finish_block<T>(part, nparts, N, out, accumulate, blockIdx.x);
+}
+
+// Several finishes in one launch: job j owns the blocks first[j] ..
+// first[j + 1] - 1 (ceil(N_j / 32) of them); the same sums in the same order
+// as one colsum_finish_kernel launch per job.
+struct ColsumBatch {
+  ColsumJob job[kMaxColsumJobs];
+  int first[kMaxColsumJobs + 1];
+  int njobs;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+colsum_finish_many_kernel(const __grid_constant__ ColsumBatch b) {
+  ::msb::pdl_begin();
+  int j = 0;
+  while (j + 1 < b.njobs && (int)blockIdx.x >= b.first[j + 1]) ++j;
+  const ColsumJob& jb = b.job[j];
+  colsum_finish_block<T>(jb.part, jb.nparts, jb.N, static_cast<T*>(jb.out), jb.accumulate,
+                         (int)blockIdx.x - b.first[j]);
 }
 
 // dst (+)= float(src) for a float32 source (accumulating gradients in place)
@@ -708,7 +736,7 @@ ce_fwd_kernel(const T* __restrict__ logits, const long long* __restrict__ tgt,
       lse_out[r] = lse;
       const long long t = tgt[r];
       // ignored (or out-of-range) targets contribute nothing
-      const bool valid = t != ignore_index && t >= 0 && t < V;
+      const bool valid = t != ignore_index && MSB_OK(t >= 0 && t < V, kSiteTarget, t, V);
       loss_rows[r] = valid ? lse - to_f32(row[t]) : 0.f;
     }
   }
@@ -858,6 +886,7 @@ ce_fwd_grad_kernel(T* __restrict__ logits, const long long* __restrict__ tgt,
   __syncthreads();
   const long long t = tgt[r];
   const bool valid = t != ignore_index && t >= 0 && t < V;
+  if (threadIdx.x == 0 && t != ignore_index) (void)MSB_OK(t >= 0 && t < V, kSiteTarget, t, V);
   if (warp == 0) {
     const int nw = blockDim.x >> 5;
     m = lane < nw ? sm[lane] : -INFINITY;
@@ -935,6 +964,7 @@ embedding_fwd_kernel(const long long* __restrict__ idx, const T* __restrict__ wt
     const int c = (int)(i % nvec) << 3;
     const long long tok = idx[m];
     float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (c == 0) (void)MSB_OK(tok >= 0 && tok < V, kSiteEmbeddingToken, tok, V);
     if (tok >= 0 && tok < V) load8(wte + tok * C + c, a);
     if (wpe != nullptr) {
       float b[8];
@@ -963,7 +993,10 @@ embedding_bwd_tok_kernel(const T* __restrict__ dout, const long long* __restrict
     const long long m = i / nvec;
     const int c = (int)(i % nvec) << 3;
     const long long tok = idx[m];
-    if (tok < 0 || tok >= V) continue;
+    if (tok < 0 || tok >= V) {
+      if (c == 0) (void)MSB_OK(false, kSiteEmbeddingToken, tok, V);
+      continue;
+    }
     float a[8];
     load8(dout + m * C + c, a);
     float* te = acc + tok * C + c;
@@ -1213,6 +1246,25 @@ void colsum_finish(const float* part, int nparts, int N, void* out, int dtype, i
   MSB_CHECK_LAUNCH("colsum_finish");
 }
 
+void colsum_finish_many(const ColsumJob* jobs, int njobs, int dtype, cudaStream_t st) {
+  for (int j0 = 0; j0 < njobs; j0 += kMaxColsumJobs) {
+    ColsumBatch b;
+    b.njobs = std::min(kMaxColsumJobs, njobs - j0);
+    int blocks = 0;
+    for (int j = 0; j < b.njobs; ++j) {
+      b.job[j] = jobs[j0 + j];
+      b.first[j] = blocks;
+      blocks += (jobs[j0 + j].N + 31) / 32;
+    }
+    b.first[b.njobs] = blocks;
+    if (blocks == 0) continue;
+    MSB_DISPATCH_FLOAT(dtype, T, {
+      ::msb::launch(colsum_finish_many_kernel<T>, blocks, 256, 0, st, b);
+    });
+    MSB_CHECK_LAUNCH("colsum_finish_many");
+  }
+}
+
 void accum_cast(const float* src, void* dst, long long n, int dtype, int accumulate,
                 cudaStream_t st) {
   const int blocks = grid_for(n, 256, kNumSMs * 16);
@@ -1335,5 +1387,7 @@ void rope(void* x, const float* cos_t, const float* sin_t, long long BT, int T_l
   });
   MSB_CHECK_LAUNCH("rope");
 }
+
+MSB_BOUNDS_TU(nn)
 
 }  // namespace msb

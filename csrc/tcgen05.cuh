@@ -97,8 +97,13 @@ __device__ __forceinline__ bool warp_test(uint32_t bar, uint32_t parity) {
   return __all_sync(0xffffffffu, mbar_test(bar, parity));
 }
 // warp-wide forms (one elected lane issues; see umma_f16_w)
+// Every TMA load of this library reads 16-bit elements: x must be a
+// multiple of 8 (16 bytes).  The debug build records an unaligned x and
+// loads from the aligned coordinate below it, so the barrier still gets
+// its bytes.
 __device__ __forceinline__ void tma_load_2d_w(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                               int x, int y) {
+  if (!MSB_CHECK((x & 7) == 0, kSiteTmaLoadX, x, 8)) x &= ~7;
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"
@@ -195,15 +200,22 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
 
 
 // ------------------------------------------------ TMA bulk tensor stores
+// XA: the elements in 16 bytes (8 for 16-bit tiles, 4 for fp32).  A store
+// or reduce must not start at a negative coordinate; the debug build records
+// one that would (or an unaligned x) and skips it.
+template <int XA = 8>
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  if (!MSB_CHECK(x >= 0 && y >= 0 && x % XA == 0, kSiteTmaStoreXY, x, XA)) return;
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
                "r"(x), "r"(y), "r"(src)
                : "memory");
 }
 // global (fp32) += shared tile, element-wise, by the TMA unit
+template <int XA = 8>
 __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32_t src, int x,
                                                   int y) {
+  if (!MSB_CHECK(x >= 0 && y >= 0 && x % XA == 0, kSiteTmaStoreXY, x, XA)) return;
   asm volatile(
       "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
           reinterpret_cast<uint64_t>(map)),

@@ -36,7 +36,8 @@ from . import checkpoint as ckpt
 from . import comm
 from .config import DeepSpeedConfig, load_config
 from .flat import FlatParamGroup, build_flat_groups
-from .ops.nn import expected_loss_grad
+from .ops import _ext
+from .ops.nn import batched_colsums, expected_loss_grad
 from .optim import build_scheduler
 from .precision import DynamicLossScaler
 from .utils import DeviceTimers, Timers
@@ -137,6 +138,9 @@ class DeepSpeedEngine:
         self._graphs = {}
         self._graph = None          # the graph replayed last
         self._graph_eager = {}      # eager micro-steps run per signature
+        # the bounds-checked debug build: its device records are read (and a
+        # failure raised) after every step
+        self._debug_bounds = self.device.type == "cuda" and _ext.debug_build()
         self._overlap_now = False   # this micro-step's backward reduces buckets
         self._bucket_hooks = self._setup_overlap() + self._setup_layer_gather()
 
@@ -322,7 +326,8 @@ class DeepSpeedEngine:
 
     def backward(self, loss: torch.Tensor, scale_wrt_gas: bool = True,
                  retain_graph: bool = False, create_graph: bool = False) -> None:
-        with self._phase("backward"):
+        # bias and norm-weight gradient finishes run batched (ops.nn)
+        with self._phase("backward"), batched_colsums():
             self._scale_loss(loss, scale_wrt_gas).backward(retain_graph=retain_graph,
                                                            create_graph=create_graph)
         self.micro_steps += 1
@@ -444,7 +449,10 @@ class DeepSpeedEngine:
             return False
         self._consumed_boundary = self.micro_steps
         with self._phase("step"):
-            return self._take_optimizer_step()
+            applied = self._take_optimizer_step()
+        if self._debug_bounds:
+            _ext.check_bounds()
+        return applied
 
     @torch.no_grad()
     def _take_optimizer_step(self) -> bool:

@@ -37,7 +37,7 @@ from typing import Any, List, Optional, Tuple
 import torch
 
 from .ops import _ext
-from .ops.nn import expected_loss_grad
+from .ops.nn import batched_colsums, expected_loss_grad
 
 
 def _flatten(obj, out: List[torch.Tensor]):
@@ -125,7 +125,8 @@ class MicroStepGraph:
                 loss = eng.module(*eng._cast_inputs(self.args), **eng._cast_inputs(self.kwargs))
             if not isinstance(loss, torch.Tensor) or loss.dim() != 0:
                 raise RuntimeError("train_batch: the module must return a scalar loss")
-            torch.autograd.backward(loss, self.seed.to(loss.dtype))
+            with batched_colsums():
+                torch.autograd.backward(loss, self.seed.to(loss.dtype))
             if self.overlap:
                 eng.optimizer.join_comm()   # the bucket reductions rejoin the graph
         if self.overlap:

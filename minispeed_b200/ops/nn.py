@@ -77,6 +77,95 @@ def grad_sink(p: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
     return g
 
 
+class _FinishQueue:
+    """Column-sum finishes into gradient sinks, batched.
+
+    A bias or norm-weight gradient is the column sum of fp32 partial rows
+    that its backward kernel leaves; the finish that adds them into the
+    gradient is a launch of its own, tiny and latency-bound (a GPT-2 small
+    step has 98 of them).  Inside :func:`batched_colsums` (the engine's
+    backward) finishes into sinks are queued instead and run together by
+    ``colsum_finish_many``: one launch per flush.  A flush happens when the
+    context exits normally, before a gradient bucket is handed to the
+    collectives (:func:`flush_colsums`), when ``_BATCH`` finishes are queued,
+    and before a finish whose sink, stream or dtype conflicts with the queue
+    (two finishes into one sink in one launch would race).  The queue keeps
+    each partial buffer alive until its flush has been launched.
+
+    Autograd runs CUDA backward functions on its own thread while the caller
+    waits in ``backward()``; the queue is shared module state, touched by one
+    thread at a time."""
+
+    _BATCH = 48
+
+    def __init__(self):
+        self.depth = 0
+        self.clear()
+
+    def clear(self):
+        self.parts, self.nparts, self.outs = [], [], []
+        self.sinks = set()
+        self.stream = None
+
+    def add(self, part: torch.Tensor, nparts: int, sink: torch.Tensor) -> None:
+        st = torch.cuda.current_stream(sink.device)
+        key = sink.data_ptr()
+        if self.outs and (key in self.sinks or st != self.stream
+                          or sink.dtype != self.outs[0].dtype):
+            self.flush()
+        if not self.outs:
+            self.stream = st
+        self.parts.append(part)
+        self.nparts.append(int(nparts))
+        self.outs.append(sink)
+        self.sinks.add(key)
+        if len(self.outs) >= self._BATCH:
+            self.flush()
+
+    def flush(self) -> None:
+        if not self.outs:
+            return
+        with torch.cuda.stream(self.stream):
+            _C().colsum_finish_many(self.parts, self.nparts, self.outs,
+                                    [True] * len(self.outs))
+        self.clear()
+
+
+_finishes = _FinishQueue()
+
+
+@contextmanager
+def batched_colsums():
+    """Queue column-sum finishes into gradient sinks while the block runs
+    (a backward pass) and launch them batched; nests."""
+    _finishes.depth += 1
+    ok = False
+    try:
+        yield
+        ok = True
+    finally:
+        _finishes.depth -= 1
+        if _finishes.depth == 0:
+            if ok:
+                _finishes.flush()
+            else:
+                _finishes.clear()
+
+
+def flush_colsums() -> None:
+    """Launch the queued finishes now (the gradients they complete are about
+    to be read)."""
+    _finishes.flush()
+
+
+def _finish_into(part: torch.Tensor, nparts: int, sink: torch.Tensor) -> None:
+    """sink += the column sums of ``part``'s first ``nparts`` rows."""
+    if _finishes.depth > 0:
+        _finishes.add(part, nparts, sink)
+    else:
+        _C().colsum_finish(part, nparts, sink, True)
+
+
 def _colsum(a2d: torch.Tensor, dtype, sink: Optional[torch.Tensor] = None
             ) -> Optional[torch.Tensor]:
     """Column sums of a [M, N] CUDA matrix (bias gradients); accumulated into
@@ -85,7 +174,7 @@ def _colsum(a2d: torch.Tensor, dtype, sink: Optional[torch.Tensor] = None
     part = _scratch(a2d.device, _COLSUM_CHUNKS * n)
     nb = _C().colsum_partial(a2d, part, _COLSUM_CHUNKS)
     if sink is not None:
-        _C().colsum_finish(part, nb, sink, True)
+        _finish_into(part, nb, sink)
         return None
     out = torch.empty(n, dtype=dtype, device=a2d.device)
     _C().colsum_finish(part, nb, out, False)
@@ -143,14 +232,14 @@ class _AddNorm(torch.autograd.Function):
         dw = db = None
         sink = grad_sink(w_p)
         if sink is not None:
-            _C().colsum_finish(dw_part, nb, sink, True)
+            _finish_into(dw_part, nb, sink)
         else:
             dw = torch.empty_like(w)
             _C().colsum_finish(dw_part, nb, dw, False)
         if ctx.has_bias:
             sink = grad_sink(b_p)
             if sink is not None:
-                _C().colsum_finish(db_part, nb, sink, True)
+                _finish_into(db_part, nb, sink)
             else:
                 db = torch.empty_like(w)
                 _C().colsum_finish(db_part, nb, db, False)
@@ -254,7 +343,7 @@ class _MlpGelu(torch.autograd.Function):
         if b1_p is not None:
             sink = grad_sink(b1_p)
             if sink is not None:
-                _C().colsum_finish(part, -(-M // 32), sink, True)
+                _finish_into(part, -(-M // 32), sink)
             else:
                 db1 = torch.empty(F_, dtype=w1.dtype, device=du.device)
                 _C().colsum_finish(part, -(-M // 32), db1, False)

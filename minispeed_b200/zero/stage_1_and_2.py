@@ -40,6 +40,7 @@ import torch
 from .. import comm
 from ..flat import FlatParamGroup
 from ..ops import kernels
+from ..ops.nn import flush_colsums
 from ..optim.adam import FlatAdam
 from ..parallel.collectives import LibraryCollectives, LocalCollectives
 
@@ -146,6 +147,7 @@ class ZeROOptimizer:
     def launch_bucket(self, k: int) -> None:
         """Reduce bucket k on the communication stream, after the work the
         current (backward) stream has queued so far."""
+        flush_colsums()   # the bucket's bias and norm-weight gradients are complete
         cur = torch.cuda.current_stream(self.stats.device)
         self.comm_stream.wait_stream(cur)
         with torch.cuda.stream(self.comm_stream):

@@ -3,6 +3,11 @@
 Produces ``minispeed_b200/_C*.so``.  Every CUDA source is compiled for
 Blackwell only (``-gencode arch=compute_100a,code=sm_100a``); giving an arch
 flag in the nvcc arguments stops torch from adding its own arch list.
+
+``MSB_DEBUG_BUILD=1`` builds the bounds-checked variant instead,
+``minispeed_b200/_C_debug*.so`` (the same sources with ``-DMSB_BOUNDS_CHECK``,
+objects under their own build folder); ``MSB_DEBUG_BUILD=1`` at run time
+makes the package load it.
 """
 
 import glob
@@ -24,6 +29,20 @@ NVCC_FLAGS = [
 if os.environ.get("MSB_PTXAS_VERBOSE"):
     NVCC_FLAGS.append("-Xptxas=-v")
 
+DEBUG = os.environ.get("MSB_DEBUG_BUILD") == "1"
+EXT_NAME = "minispeed_b200._C_debug" if DEBUG else "minispeed_b200._C"
+DEFINES = ["-DMSB_BOUNDS_CHECK"] if DEBUG else []
+
+
+class BuildExt(BuildExtension.with_options(use_ninja=True)):
+    """The debug variant compiles into its own object folder, so the two
+    builds do not overwrite each other's objects."""
+
+    def finalize_options(self):
+        super().finalize_options()
+        if DEBUG:
+            self.build_temp = os.path.join(self.build_temp, "bounds_check")
+
 
 def sources():
     cu = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
@@ -37,11 +56,12 @@ setup(
     packages=find_packages(include=["minispeed_b200*"]),
     ext_modules=[
         CUDAExtension(
-            name="minispeed_b200._C",
+            name=EXT_NAME,
             sources=sources(),
             include_dirs=[CSRC],
-            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"] + DEFINES,
+                                "nvcc": NVCC_FLAGS + DEFINES},
         )
     ],
-    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    cmdclass={"build_ext": BuildExt},
 )
