@@ -19,6 +19,10 @@
 //                      added into the gradient and cleared
 //   rope_*             rotary position embedding on q/k in place
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -65,6 +69,41 @@ __device__ __forceinline__ void store8(T* p, const float (&f)[8]) {
 #pragma unroll
     for (int k = 0; k < 8; ++k) p[k] = from_f32<T>(f[k]);
   }
+}
+
+// 8 16-bit values as one 16-byte quad of registers, unpacked and packed two
+// at a time (a bf16 is the upper half of an fp32; element 0 is the low half
+// of the first word), so packed rows take 4 registers per 8 values.
+template <typename T>
+__device__ __forceinline__ void unpack_u4(const uint4& r, float (&f)[8]) {
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      f[2 * q] = __uint_as_float(w[q] << 16);
+      f[2 * q + 1] = __uint_as_float(w[q] & 0xffff0000u);
+    } else {
+      const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&w[q]));
+      f[2 * q] = v.x;
+      f[2 * q + 1] = v.y;
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack_u4(const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * q], f[2 * q + 1]);
+      w[q] = *reinterpret_cast<const uint32_t*>(&h);
+    } else {
+      const __half2 h = __floats2half2_rn(f[2 * q], f[2 * q + 1]);
+      w[q] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 // ------------------------------------------------------------ layernorm
@@ -132,12 +171,114 @@ add_norm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ delta,
 #pragma unroll
         for (int k = 0; k < 8; ++k) o[k] = (v[i][k] * rstd) * wf[k];
       } else {
-        float bf[8];
-        load8(b + c, bf);
+        float bf[8] = {0, 0, 0, 0, 0, 0, 0, 0};   // a LayerNorm without bias: b == nullptr
+        if (b != nullptr) load8(b + c, bf);
 #pragma unroll
         for (int k = 0; k < 8; ++k) o[k] = ((v[i][k] - mean) * rstd) * wf[k] + bf[k];
       }
       store8(y + base + c, o);
+    }
+  }
+}
+
+// Forward for 16-byte aligned rows (every row pointer aligned, C % 8 == 0):
+// each warp issues all of its row's loads before it uses any, so a row costs
+// one memory round trip rather than one per vector (the per-vector loads
+// above sit behind a bounds branch and a store, and are not hoisted); the
+// rounded residual sum stays packed in the model dtype (4 registers per 8
+// values), and the weight and bias are read from shared memory, staged once
+// per block as fp32.  Blocks loop over groups of 8 rows.
+template <typename T, int NV, bool RMS>
+__global__ void __launch_bounds__(256, 2)
+add_norm_fwd_rows_kernel(const T* __restrict__ x, const T* __restrict__ delta,
+                         const T* __restrict__ w, const T* __restrict__ b, T* __restrict__ s_out,
+                         T* __restrict__ y, float* __restrict__ mean_out,
+                         float* __restrict__ rstd_out, int M, int C, float eps) {
+  extern __shared__ float4 norm_smem4[];
+  float* sw = reinterpret_cast<float*>(norm_smem4);
+  float* sb = sw + C;
+  ::msb::pdl_begin();
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    sw[c] = to_f32(w[c]);
+    if (!RMS) sb[c] = b != nullptr ? to_f32(b[c]) : 0.f;   // LayerNorm without bias
+  }
+  __syncthreads();
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int nvec = C >> 3;
+  const uint4* x4 = reinterpret_cast<const uint4*>(x);
+  const uint4* d4 = reinterpret_cast<const uint4*>(delta);
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+    const size_t base = (size_t)row * nvec;   // in 8-value vectors
+    uint4 xr[NV], dr[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int j = lane + i * 32;
+      if (j < nvec) {
+        xr[i] = x4[base + j];
+        if (delta != nullptr) dr[i] = d4[base + j];
+      }
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int j = lane + i * 32;
+      if (j < nvec) {
+        float v[8];
+        unpack_u4<T>(xr[i], v);
+        if (delta != nullptr) {
+          // the residual stream is stored in the model dtype: normalise the
+          // rounded value so that forward and backward see the same input
+          float d[8];
+          unpack_u4<T>(dr[i], d);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) v[k] += d[k];
+          xr[i] = pack_u4<T>(v);
+          unpack_u4<T>(xr[i], v);
+          if (s_out != nullptr) reinterpret_cast<uint4*>(s_out)[base + j] = xr[i];
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) sum += v[k];
+      }
+    }
+    const float mean = RMS ? 0.f : warp_sum(sum) / (float)C;
+    float sq = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+      if (lane + i * 32 < nvec) {
+        float v[8];
+        unpack_u4<T>(xr[i], v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float d = v[k] - mean;
+          sq += d * d;
+        }
+      }
+    const float rstd = rsqrtf(warp_sum(sq) / (float)C + eps);
+    if (lane == 0) {
+      if (mean_out != nullptr) mean_out[row] = mean;
+      rstd_out[row] = rstd;
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int j = lane + i * 32;
+      if (j < nvec) {
+        float v[8], o[8];
+        unpack_u4<T>(xr[i], v);
+        const float4* w4 = reinterpret_cast<const float4*>(sw + j * 8);
+        const float4 wa = w4[0], wb = w4[1];
+        const float wf[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        if (RMS) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) o[k] = (v[k] * rstd) * wf[k];
+        } else {
+          const float4* b4 = reinterpret_cast<const float4*>(sb + j * 8);
+          const float4 ba = b4[0], bb = b4[1];
+          const float bf[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+          for (int k = 0; k < 8; ++k) o[k] = ((v[k] - mean) * rstd) * wf[k] + bf[k];
+        }
+        reinterpret_cast<uint4*>(y)[base + j] = pack_u4<T>(o);
+      }
     }
   }
 }
@@ -201,8 +342,8 @@ norm_dx_kernel(const T* __restrict__ dy, const T* __restrict__ s, const T* __res
 // Same computation with every load of a row issued before the row
 // reductions: the raw 16-byte packs of s, dy and the residual gradient stay in
 // registers (4 registers per 8 values) and x-hat / g are recomputed in the
-// second pass.  Used when the activation rows are 16-byte aligned and a row
-// is at most 2048 wide (NV <= 8).
+// second pass.  Used for 16-bit activations whose rows are 16-byte aligned
+// and at most 2048 wide (NV <= 8); blocks of 4 warps loop over rows.
 template <typename T>
 __device__ __forceinline__ void unpack8(const Pack8<T>& r, float (&f)[8]) {
 #pragma unroll
@@ -210,25 +351,40 @@ __device__ __forceinline__ void unpack8(const Pack8<T>& r, float (&f)[8]) {
 }
 
 template <typename T, int NV, bool RMS>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(128, 3)
 norm_dx_prefetch_kernel(const T* __restrict__ dy, const T* __restrict__ s,
                         const T* __restrict__ w, const float* __restrict__ mean_in,
                         const float* __restrict__ rstd_in, const T* __restrict__ dres,
                         T* __restrict__ dx, int M, int C) {
+  // the weight, staged once per block as fp32 (it was re-read from L2 per
+  // vector in both passes, one round trip each)
+  extern __shared__ float4 norm_smem4[];
+  float* sw = reinterpret_cast<float*>(norm_smem4);
   ::msb::pdl_begin();
+  for (int c = threadIdx.x; c < C; c += blockDim.x) sw[c] = to_f32(w[c]);
+  __syncthreads();
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   const int nvec = C >> 3;
+  auto wvec = [&](int j, float (&wv)[8]) {
+    const float4* w4 = reinterpret_cast<const float4*>(sw + j * 8);
+    const float4 a = w4[0], b = w4[1];
+    wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
+    wv[4] = b.x; wv[5] = b.y; wv[6] = b.z; wv[7] = b.w;
+  };
+  const uint4* s4 = reinterpret_cast<const uint4*>(s);
+  const uint4* dy4 = reinterpret_cast<const uint4*>(dy);
+  const uint4* r4 = reinterpret_cast<const uint4*>(dres);
   for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
-    const size_t base = (size_t)row * C;
-    Pack8<T> sp[NV], dp[NV], rp[NV];
+    const size_t base = (size_t)row * nvec;   // in 8-value vectors
+    uint4 sp[NV], dp[NV], rp[NV];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const int c = (lane + i * 32) << 3;
-      if ((lane + i * 32) < nvec) {
-        sp[i] = *reinterpret_cast<const Pack8<T>*>(s + base + c);
-        dp[i] = *reinterpret_cast<const Pack8<T>*>(dy + base + c);
-        if (dres != nullptr) rp[i] = *reinterpret_cast<const Pack8<T>*>(dres + base + c);
+      const int j = lane + i * 32;
+      if (j < nvec) {
+        sp[i] = s4[base + j];
+        dp[i] = dy4[base + j];
+        if (dres != nullptr) rp[i] = r4[base + j];
       }
     }
     const float mean = RMS ? 0.f : mean_in[row];
@@ -236,12 +392,12 @@ norm_dx_prefetch_kernel(const T* __restrict__ dy, const T* __restrict__ s,
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const int c = (lane + i * 32) << 3;
-      if ((lane + i * 32) < nvec) {
+      const int j = lane + i * 32;
+      if (j < nvec) {
         float sv[8], dyv[8], wv[8];
-        unpack8(sp[i], sv);
-        unpack8(dp[i], dyv);
-        load8(w + c, wv);
+        unpack_u4<T>(sp[i], sv);
+        unpack_u4<T>(dp[i], dyv);
+        wvec(j, wv);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const float xh = (sv[k] - mean) * rstd;
@@ -255,12 +411,12 @@ norm_dx_prefetch_kernel(const T* __restrict__ dy, const T* __restrict__ s,
     s2 = warp_sum(s2) / (float)C;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const int c = (lane + i * 32) << 3;
-      if ((lane + i * 32) < nvec) {
+      const int j = lane + i * 32;
+      if (j < nvec) {
         float sv[8], dyv[8], wv[8], o[8];
-        unpack8(sp[i], sv);
-        unpack8(dp[i], dyv);
-        load8(w + c, wv);
+        unpack_u4<T>(sp[i], sv);
+        unpack_u4<T>(dp[i], dyv);
+        wvec(j, wv);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const float xh = (sv[k] - mean) * rstd;
@@ -269,11 +425,11 @@ norm_dx_prefetch_kernel(const T* __restrict__ dy, const T* __restrict__ s,
         }
         if (dres != nullptr) {
           float r[8];
-          unpack8(rp[i], r);
+          unpack_u4<T>(rp[i], r);
 #pragma unroll
           for (int k = 0; k < 8; ++k) o[k] += r[k];
         }
-        store8(dx + base + c, o);
+        reinterpret_cast<uint4*>(dx)[base + j] = pack_u4<T>(o);
       }
     }
   }
@@ -1103,10 +1259,41 @@ rope_kernel(T* __restrict__ x, const float* __restrict__ cos_t, const float* __r
 }  // namespace
 
 // =============================================================== host API
+// Blocks of `kernel` resident on the whole GPU at once (its registers and
+// shared memory per block); a row-looping kernel launches that many.
+template <typename K>
+static int resident_blocks(K kernel, int threads, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, size_t>, int> cache;
+  const auto key = std::make_tuple(reinterpret_cast<const void*>(kernel), threads, smem);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int per_sm = 0;
+  check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem),
+             "occupancy");
+  return cache[key] = std::max(1, per_sm) * kNumSMs;
+}
+
 template <typename T, int NVV>
 static void launch_norm_fwd(const void* x, const void* delta, const void* w, const void* b,
                             void* s_out, void* y, float* mean, float* rstd, int M, int C,
                             float eps, bool rms, int blocks, cudaStream_t st) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if constexpr (NVV <= 8 && !std::is_same<T, float>::value) {
+    if (C % 8 == 0 && al(x) && al(y) && (delta == nullptr || al(delta)) &&
+        (s_out == nullptr || al(s_out))) {
+      // as many blocks of 8 warps as are resident at once, each looping
+      // over groups of 8 rows
+      const size_t smem = (rms ? 1 : 2) * (size_t)C * sizeof(float);
+      auto kern = rms ? add_norm_fwd_rows_kernel<T, NVV, true>
+                      : add_norm_fwd_rows_kernel<T, NVV, false>;
+      const int grid = std::min(blocks, resident_blocks(kern, 256, smem));
+      ::msb::launch(kern, grid, 256, smem, st, (const T*)x, (const T*)delta, (const T*)w,
+                    (const T*)b, (T*)s_out, (T*)y, mean, rstd, M, C, eps);
+      return;
+    }
+  }
   if (rms)
     ::msb::launch(add_norm_fwd_kernel<T, NVV, true>, blocks, 256, 0, st, 
         (const T*)x, (const T*)delta, (const T*)w, (const T*)b, (T*)s_out, (T*)y, mean, rstd, M,
@@ -1140,14 +1327,15 @@ static void launch_norm_dx(const void* dy, const void* s, const void* w, const f
                            cudaStream_t st) {
   const int blocks = grid_for((M + 7) / 8, 1, kNumSMs * 16);
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  if constexpr (NVV <= 8) {
+  if constexpr (NVV <= 8 && !std::is_same<T, float>::value) {
     if (C % 8 == 0 && al(dy) && al(s) && al(dx) && (dres == nullptr || al(dres))) {
-      if (rms)
-        ::msb::launch(norm_dx_prefetch_kernel<T, NVV, true>, blocks, 256, 0, st, 
-            (const T*)dy, (const T*)s, (const T*)w, mean, rstd, (const T*)dres, (T*)dx, M, C);
-      else
-        ::msb::launch(norm_dx_prefetch_kernel<T, NVV, false>, blocks, 256, 0, st, 
-            (const T*)dy, (const T*)s, (const T*)w, mean, rstd, (const T*)dres, (T*)dx, M, C);
+      // as many blocks of 4 warps as are resident at once, each looping
+      // over groups of 4 rows
+      const size_t smem = (size_t)C * sizeof(float);
+      auto kern = rms ? norm_dx_prefetch_kernel<T, NVV, true> : norm_dx_prefetch_kernel<T, NVV, false>;
+      const int grid = std::min((M + 3) / 4, resident_blocks(kern, 128, smem));
+      ::msb::launch(kern, grid, 128, smem, st, (const T*)dy, (const T*)s, (const T*)w, mean, rstd,
+                    (const T*)dres, (T*)dx, M, C);
       return;
     }
   }

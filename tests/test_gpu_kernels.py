@@ -145,6 +145,51 @@ def test_add_norm_fwd_bwd(dtype, rms, C):
 
 
 @pytest.mark.parametrize("dtype", DT)
+@pytest.mark.parametrize("rms,C", [(False, 1600), (True, 1600), (True, 4096), (False, 768)])
+@pytest.mark.parametrize("with_delta", [True, False])
+@pytest.mark.parametrize("offset", [0, 1])
+def test_norm_row_kernels(dtype, rms, C, with_delta, offset):
+    """The row-looping norm kernels (all of a row's loads issued first; the
+    weight and bias staged in shared memory) on 5000 rows, so every block
+    loops over several row groups; offset 1 misaligns the rows (the
+    per-vector kernels run instead); width 4096 uses 16 vectors per lane."""
+    torch.manual_seed(C + offset)
+    M = 5000
+
+    def rows(scale=1.0):
+        buf = (torch.randn(M * C + offset, device="cuda") * scale).to(dtype)
+        return buf[offset:].view(M, C).requires_grad_()
+
+    x = rows()
+    d = rows() if with_delta else None
+    w = (1 + 0.1 * torch.randn(C, device="cuda")).to(dtype).requires_grad_()
+    b = None if rms else (0.1 * torch.randn(C, device="cuda")).to(dtype).requires_grad_()
+    if with_delta:
+        s, y = ops.add_norm(x, d, w, b, 1e-5, rms)
+    else:
+        s, y = x, ops.norm(x, w, b, 1e-5, rms)
+    gy = torch.randn(M, C, device="cuda").to(dtype)
+    y.backward(gy)
+    leaves = [t for t in (x, d, w, b) if t is not None]
+    xs = [t.detach().float().requires_grad_() for t in leaves]
+    sr = (xs[0] + xs[1]).to(dtype).float() if with_delta else xs[0]
+    wi = 2 if with_delta else 1
+    if rms:
+        yr = sr * torch.rsqrt(sr.pow(2).mean(-1, keepdim=True) + 1e-5) * xs[wi]
+    else:
+        yr = F.layer_norm(sr, (C,), xs[wi], xs[wi + 1], 1e-5)
+    yr.backward(gy.float())
+    rt, at = _tol(dtype)
+    if with_delta:
+        torch.testing.assert_close(s.float(), sr.detach(), rtol=0, atol=0)
+    torch.testing.assert_close(y.float(), yr.detach(), rtol=rt, atol=at * 4)
+    for got, ref in zip(leaves, xs):
+        scale = float(ref.grad.abs().max())
+        torch.testing.assert_close(got.grad.float(), ref.grad, rtol=rt * 4,
+                                   atol=at * 2 * scale)
+
+
+@pytest.mark.parametrize("dtype", DT)
 def test_linear_gelu_and_linear(dtype):
     torch.manual_seed(2)
     x = torch.randn(256, 128, device="cuda", dtype=dtype, requires_grad=True)
