@@ -1,6 +1,8 @@
-"""The FMA-pipe exp2 the attention backward can use for part of its
-exponentials (``exp2_poly`` in ``csrc/attention_tcgen05.cu``, selected at
-build time with ``-DMSB_EXP2_POLY=n``), evaluated step by step in float32:
+"""The FMA-pipe exp2 (``exp2_poly`` in ``csrc/common.cuh``) that the
+attention kernels can use for part of their exponentials (the forward at run
+time with ``MSB_ATTN_POLY=1|2``, the backward at build time with
+``-DMSB_EXP2_POLY=n``; both off by default, where measured slower), evaluated
+step by step in float32:
 range reduction through the 1.5 * 2^23 rounding constant, degree-3 minimax
 polynomial, exponent-field add.  Checks the relative error bound the kernel
 comment states and the clamp at -125."""
