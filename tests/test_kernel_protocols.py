@@ -898,3 +898,57 @@ def test_split_k_fixup_finishes_every_tile_once(tiles, splits):
     plan = fixup_plan(tiles, splits)
     for seed in range(20):
         run_tiles(plan, tiles, splits, seed)
+
+
+# ------------------------------------------------- batched column-sum finishes
+# colsum_finish_many (csrc/nn_kernels.cu): the host cuts the job list into
+# launches of at most MAX_JOBS; a launch's job j owns the blocks
+# first[j] .. first[j + 1] - 1 (ceil(N_j / 32) of them), and a block finds
+# its job by scanning first[] upward from 0.
+MAX_JOBS = 48
+
+
+def colsum_launches(widths):
+    """Host plan: per launch, (first[], block count), as colsum_finish_many."""
+    launches = []
+    for j0 in range(0, len(widths), MAX_JOBS):
+        chunk = widths[j0:j0 + MAX_JOBS]
+        first, blocks = [], 0
+        for n in chunk:
+            first.append(blocks)
+            blocks += (n + 31) // 32
+        first.append(blocks)
+        launches.append((j0, first, blocks))
+    return launches
+
+
+def block_job(first, njobs, block):
+    """Device scan: the job that owns `block` (the kernel's while loop)."""
+    j = 0
+    while j + 1 < njobs and block >= first[j + 1]:
+        j += 1
+    return j, block - first[j]
+
+
+@pytest.mark.parametrize("seed", range(8))
+def test_colsum_batches_cover_every_column_once(seed):
+    """Every column of every job is finished by exactly one thread of one
+    block, across launches, for ragged widths (including 1 and multiples
+    of 32) and job counts around the per-launch limit."""
+    import random
+
+    rng = random.Random(seed)
+    njobs = rng.choice([1, 47, 48, 49, 98, 100])
+    widths = [rng.choice([1, 31, 32, 33, 768, 1600, 3072, 6400]) for _ in range(njobs)]
+    seen = [[0] * n for n in widths]
+    for j0, first, blocks in colsum_launches(widths):
+        nj = len(first) - 1
+        for b in range(blocks):
+            j, cb = block_job(first, nj, b)
+            for lane in range(32):
+                c = cb * 32 + lane
+                if c < widths[j0 + j]:          # the kernel's `c < N` guard
+                    seen[j0 + j][c] += 1
+    assert all(all(x == 1 for x in cols) for cols in seen)
+    # one launch per MAX_JOBS jobs, as the GPU profile shows (98 -> 3)
+    assert len(colsum_launches(widths)) == -(-njobs // MAX_JOBS)
