@@ -43,6 +43,40 @@ def test_build_flags():
     assert dbg.bounds_check_build() is True
 
 
+class _FakeBounds:
+    """Stands in for an extension: records as bounds_status(reset) returns."""
+
+    def __init__(self, records):
+        self.records = records
+        self.resets = 0
+
+    def bounds_status(self, reset):
+        out = list(self.records)
+        if reset:
+            self.resets += 1
+            self.records = [(u, 0, 0, 0, 0) for u, *_ in self.records]
+        return out
+
+
+def test_check_bounds_names_the_first_failure_per_unit():
+    """check_bounds raises with each failing unit's count, site and index,
+    resets the records, and is silent when nothing failed."""
+    fake = _FakeBounds([("nn", 3, 1, 102, 100), ("gemm", 0, 0, 0, 0),
+                        ("attention", 1, 3, 13, 8)])
+    with pytest.raises(_ext.BoundsError) as e:
+        _ext.check_bounds(mod=fake)
+    msg = str(e.value)
+    assert "nn: 3 failed check(s), first: embedding token id" in msg
+    assert "(index 102, limit 100)" in msg
+    assert "attention: 1 failed check(s), first: TMA load x coordinate" in msg
+    assert "gemm" not in msg
+    assert fake.resets == 1
+    _ext.check_bounds(mod=fake)          # reset: nothing left to report
+    rows = _ext.bounds_status(reset=False, mod=fake)
+    assert [r["unit"] for r in rows] == ["nn", "gemm", "attention"]
+    assert all(r["count"] == 0 and r["what"] == "none" for r in rows)
+
+
 class _FakeC:
     def __init__(self):
         self.single, self.batches = [], []
