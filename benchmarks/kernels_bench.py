@@ -2,6 +2,7 @@
 
     python benchmarks/kernels_bench.py --kernel adamw|rs_stats|grad_stats|cross_entropy|norm_bwd|add_norm
                                        [--n 268435456] [--iters 3]
+                                       [--hidden 768] [--dtype fp16|bf16]   (norm kernels)
 
 ``cross_entropy`` times the forward + backward pair and then the forward
 that writes the gradient itself (the engine's path).  ``rs_stats`` runs the fused reduce-scatter + statistics kernel over a
@@ -60,6 +61,9 @@ def main():
     ap.add_argument("--kernel", required=True)
     ap.add_argument("--n", type=int, default=1 << 28)
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--hidden", type=int, default=768, help="row width of the norm kernels")
+    ap.add_argument("--dtype", choices=["fp16", "bf16"], default="fp16",
+                    help="activation dtype of the norm kernels")
     a = ap.parse_args()
     C = _ext.get()
     dev = torch.device("cuda")
@@ -120,20 +124,21 @@ def main():
             loss.backward()
         timed(fused, a.iters, M * V * 2 * 2, "cross_entropy fwd+grad (one kernel)")
     elif a.kernel in ("norm_bwd", "add_norm"):
-        Cd = 768
+        Cd = a.hidden
         M = n // Cd
-        x = torch.randn(M, Cd, device=dev).half().requires_grad_()
-        d = torch.randn(M, Cd, device=dev).half().requires_grad_()
-        w = torch.ones(Cd, device=dev).half().requires_grad_()
-        b = torch.zeros(Cd, device=dev).half().requires_grad_()
+        dt = torch.bfloat16 if a.dtype == "bf16" else torch.float16
+        x = torch.randn(M, Cd, device=dev).to(dt).requires_grad_()
+        d = torch.randn(M, Cd, device=dev).to(dt).requires_grad_()
+        w = torch.ones(Cd, device=dev).to(dt).requires_grad_()
+        b = torch.zeros(Cd, device=dev).to(dt).requires_grad_()
         if a.kernel == "add_norm":
             fn = lambda: ops.add_norm(x.detach(), d.detach(), w, b)
-            timed(fn, a.iters, M * Cd * 2 * 4, "add_norm fwd")
+            timed(fn, a.iters, M * Cd * 2 * 4, f"add_norm fwd {M}x{Cd} {a.dtype}")
         else:
             s, y = ops.add_norm(x, d, w, b)
             gy, gs = torch.randn_like(y), torch.randn_like(s)
             fn = lambda: torch.autograd.grad((s, y), (x,), (gs, gy), retain_graph=True)
-            timed(fn, a.iters, M * Cd * 2 * 6, "norm bwd")
+            timed(fn, a.iters, M * Cd * 2 * 6, f"norm bwd {M}x{Cd} {a.dtype}")
     else:
         raise SystemExit(f"unknown kernel {a.kernel}")
 
