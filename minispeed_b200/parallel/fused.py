@@ -269,6 +269,13 @@ class FusedCollectives:
                 g = self.groups[i]
                 slot, esz = self._slot_layout(g)
                 align = (q * shards[i]) // pers[i] * pers[i]
+                # the copy writes peer memory: it must stay inside q's slot
+                # for this rank and read inside this rank's arena (checked
+                # once here, not per step)
+                if not (q * shards[i] <= e0 < e1 <= min((q + 1) * shards[i], g.numel_padded)
+                        and e1 - align <= slot):
+                    raise RuntimeError(f"copy-engine plan: group {i} range [{e0}, {e1}) "
+                                       f"leaves rank {q}'s receive slot")
                 base = self.recv.ptrs[q] + self.recv.offsets[f"recv{i}"] + me * slot * esz
                 dst.append(base + (e0 - align) * esz)
                 src.append(self.heap.ptrs[me] + self.heap.offsets[f"grad{i}"] + e0 * esz)

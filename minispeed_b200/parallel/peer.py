@@ -37,9 +37,11 @@ class PeerHeap:
         self.device = torch.device(device)
         self.rank, self.world = rank, world
         self.offsets: Dict[str, int] = {}
+        self.sizes: Dict[str, int] = {}
         off = 0
         for name, nbytes in regions:
             self.offsets[name] = off
+            self.sizes[name] = int(nbytes)
             off += _round(max(nbytes, 1))
         self.offsets["__sync__"] = off
         self.nbytes = off + SYNC_BYTES
@@ -64,7 +66,13 @@ class PeerHeap:
         return self.offsets["__sync__"]
 
     def view(self, name: str, dtype: torch.dtype, numel: int) -> torch.Tensor:
-        """This rank's copy of region ``name`` as a tensor (heap-owned memory)."""
+        """This rank's copy of region ``name`` as a tensor (heap-owned memory).
+        A view larger than the region is refused: peers address the same
+        layout, so an overrun would land in the next region of every rank."""
+        nbytes = numel * (torch.finfo(dtype).bits // 8)
+        if numel < 0 or nbytes > self.sizes[name]:
+            raise ValueError(f"peer heap: {numel} x {dtype} ({nbytes} bytes) does not fit "
+                             f"region {name!r} ({self.sizes[name]} bytes)")
         return _ext.get().tensor_from_ptr(self.base + self.offsets[name], numel,
                                           DTYPE_CODE[dtype], self.device.index)
 

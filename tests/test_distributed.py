@@ -237,3 +237,21 @@ def test_dma_plan_sends_each_element_to_its_owner_once():
             assert e0 == s1
         for s0, e0 in covered[0]:
             assert s0 % per == 0 and e0 % per == 0
+
+
+def test_peer_heap_view_refuses_an_overrun():
+    """A view of a peer-heap region larger than the region is refused before
+    any device call (every rank addresses the same layout, so an overrun
+    would write into the next region of every peer)."""
+    import torch
+
+    from minispeed_b200.parallel.peer import PeerHeap
+
+    heap = object.__new__(PeerHeap)          # the layout alone, no device memory
+    heap.offsets = {"grad0": 0, "pshard0": 512}
+    heap.sizes = {"grad0": 400, "pshard0": 100}
+    heap.base, heap.device = 0, torch.device("cpu")
+    with pytest.raises(ValueError, match="does not fit region 'grad0'"):
+        heap.view("grad0", torch.float16, 201)
+    with pytest.raises(ValueError, match="does not fit region 'pshard0'"):
+        heap.view("pshard0", torch.float32, 26)
