@@ -952,3 +952,36 @@ def test_colsum_batches_cover_every_column_once(seed):
     assert all(all(x == 1 for x in cols) for cols in seen)
     # one launch per MAX_JOBS jobs, as the GPU profile shows (98 -> 3)
     assert len(colsum_launches(widths)) == -(-njobs // MAX_JOBS)
+
+
+# ----------------------------------------- partial-tile slot of the pair kernel
+# gemm2_kernel's epilogue (csrc/gemm_tcgen05.cu): 8 epilogue warps per CTA
+# (warps 2..9), quarter = warp & 3, half = (warp - 2) / 4; CTA `rank` of the
+# pair owns tile rows 128 * rank + 32 * quarter + lane and 32-column chunks
+# c = half, half + 2, ...; a partial is stored in register order, float4 q of
+# lane l of (row block rb, chunk c) at ((rb * 8 + c) * 8 + q) * 32 + l.
+PAIR_TM, PAIR_BN2, PAIR_HALF = 256, 256, 128
+
+
+def test_pair_partial_slot_is_a_bijection():
+    """Every fp32 value of a 256 x 256 partial tile has its own float4 slot
+    entry inside the slot (65536 floats), so contributing pairs and splits
+    never overwrite one another and never leave their slot."""
+    seen = {}
+    for rank in range(2):
+        for warp in range(2, 10):
+            quarter, half = warp & 3, (warp - 2) // 4
+            for lane in range(32):
+                row = PAIR_HALF * rank + quarter * 32 + lane
+                for c in range(half, PAIR_BN2 // 32, 2):
+                    slot_off = ((row >> 5) * (PAIR_BN2 // 32) + c) * 8 * 32 + lane
+                    for q in range(8):
+                        f4 = slot_off + q * 32
+                        assert 0 <= f4 and f4 * 4 + 3 < PAIR_TM * PAIR_BN2
+                        for k in range(4):          # the four floats of the float4
+                            key = f4 * 4 + k
+                            assert key not in seen, (rank, warp, lane, c, q)
+                            seen[key] = (row, c * 32 + q * 4 + k)
+    assert len(seen) == PAIR_TM * PAIR_BN2
+    # every (row, column) of the tile appears once
+    assert len(set(seen.values())) == PAIR_TM * PAIR_BN2
